@@ -1,0 +1,251 @@
+/*
+ * qsml_cuda.h -- extern "C" ABI of the B200 (sm_100a) backend for QuasarML.
+ *
+ * libqsml_cuda.so replaces QuasarML's Vulkan backend (the abstract Backend of
+ * QuasarML/src/Backend/BackendInterface.h:43-85 with its VulkanBackend
+ * implementation) together with the per-op GLSL generation of
+ * QuasarML/src/Ops/*.cpp.  The C++ QuasarML layer (Tensor, Device, Ops::*,
+ * qsml::) calls these entry points; any other host language can bind them
+ * directly (plain pointers, sizes and POD descriptors, no C++ types).
+ *
+ * Conventions
+ *  - Every entry point returns a qsml_status_t and never throws or aborts.
+ *    On failure qsml_last_error(ctx) gives a message; the C++ layer turns it
+ *    into std::runtime_error, the reference's error convention
+ *    (QuasarML/src/Common/Assert.h:8-13).
+ *  - Work is enqueued on the context's CUDA stream and is asynchronous with
+ *    respect to the host until qsml_synchronize() or a device->host copy,
+ *    as in the reference (QuasarML/src/Core/Device.cpp:96-102).
+ *  - Tensors are described by qsml_tdesc: `data` points at the view's first
+ *    element (storage offset already applied), shape/stride are in elements,
+ *    strides may be 0 (broadcast) or negative on inputs.  Outputs must be
+ *    contiguous row-major and must not partially overlap an input.
+ *  - Outputs are caller-allocated (the reference's Ops allocate the result
+ *    tensor first, e.g. QuasarML/src/Ops/Elementwise.cpp:143).
+ *  - There is no CPU fallback: an unsupported case returns an error status.
+ */
+#ifndef QSML_CUDA_H
+#define QSML_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define QSML_API __declspec(dllexport)
+#else
+#define QSML_API __attribute__((visibility("default")))
+#endif
+
+typedef int32_t qsml_status_t;
+
+#define QSML_OK 0
+#define QSML_E_INVALID 1     /* bad argument (null pointer, bad enum)         */
+#define QSML_E_SHAPE 2       /* incompatible shapes / axis out of range       */
+#define QSML_E_DTYPE 3       /* dtype not supported by this op                */
+#define QSML_E_OOM 4         /* device allocation failed                      */
+#define QSML_E_CUDA 5        /* CUDA runtime error                            */
+#define QSML_E_NCCL 6        /* collective error                              */
+#define QSML_E_TIMEOUT 7     /* bounded device-side wait expired              */
+#define QSML_E_UNSUPPORTED 8 /* valid request this build does not implement   */
+
+/* Element types, same order and sizes as QuasarML::DataType
+ * (QuasarML/src/Common/Types.h:80-103). */
+#define QSML_F32 0
+#define QSML_F16 1
+#define QSML_I32 2
+#define QSML_I16 3
+#define QSML_I8 4
+#define QSML_U32 5
+#define QSML_U16 6
+#define QSML_U8 7
+
+#define QSML_MAX_DIMS 8
+
+typedef struct qsml_tdesc {
+    void* data;                      /* device pointer to element [0,...,0]   */
+    int32_t dtype;                   /* QSML_F32 ...                          */
+    int32_t ndim;                    /* 0..QSML_MAX_DIMS (0 = scalar)         */
+    int64_t shape[QSML_MAX_DIMS];
+    int64_t stride[QSML_MAX_DIMS];   /* in elements                           */
+} qsml_tdesc;
+
+typedef struct qsml_ctx qsml_ctx;
+
+/* Binary element ops (qsml_binary, qsml_binary_scalar). */
+#define QSML_OP_ADD 0
+#define QSML_OP_SUB 1
+#define QSML_OP_MUL 2
+#define QSML_OP_DIV 3
+#define QSML_OP_POW 4
+
+/* Unary element ops (qsml_unary). */
+#define QSML_UN_RELU 0
+#define QSML_UN_NEG 1
+#define QSML_UN_ABS 2
+#define QSML_UN_SQRT 3
+#define QSML_UN_EXP 4
+#define QSML_UN_LOG 5
+#define QSML_UN_SIN 6
+#define QSML_UN_COS 7
+#define QSML_UN_TANH 8
+#define QSML_UN_SIGMOID 9
+#define QSML_UN_GELU 10
+
+/* Reductions (qsml_reduce). */
+#define QSML_RED_SUM 0
+#define QSML_RED_MEAN 1
+#define QSML_RED_MAX 2
+#define QSML_RED_MIN 3
+#define QSML_AXIS_ALL (-1000)
+
+/* Matmul precisions (qsml_matmul). */
+#define QSML_MM_AUTO 0          /* F32 inputs -> FP32_FFMA, F16 -> FP16_F32ACC */
+#define QSML_MM_FP32_FFMA 1     /* fp32 CUDA-core fma, k ascending             */
+#define QSML_MM_FP32_3XTF32 2   /* fp32 via three tf32 tensor-core products    */
+#define QSML_MM_FP16_F32ACC 3   /* fp16 inputs, fp32 accumulate (tcgen05)      */
+
+/* ---- device / context ------------------------------------------------- */
+
+/* Number of CUDA devices.  Replaces DeviceManager::enumerate
+ * (QuasarML/src/Core/DeviceManager.cpp:20-50). */
+QSML_API qsml_status_t qsml_device_count(int32_t* count);
+
+/* Device name into buf (NUL-terminated).  Replaces
+ * DeviceManager::device_names (QuasarML/src/Core/DeviceManager.cpp:68-106). */
+QSML_API qsml_status_t qsml_device_name(int32_t device, char* buf, size_t len);
+
+/* Creates a context on `device`: a CUDA stream, a caching allocator and the
+ * op scratch space.  Replaces Device::Device -> create_vulkan_backend ->
+ * VulkanBackend::init (QuasarML/src/Core/Device.cpp:9-17,
+ * QuasarML/src/Backend/Vulkan/VulkanBackend.cpp:82-180). */
+QSML_API qsml_status_t qsml_init(int32_t device, qsml_ctx** ctx);
+
+/* Releases the context, its cached blocks and its stream.  Replaces
+ * Device::~Device (QuasarML/src/Core/Device.cpp:19-23). */
+QSML_API qsml_status_t qsml_destroy(qsml_ctx* ctx);
+
+/* Makes the context enqueue on `stream` (a cudaStream_t; NULL restores the
+ * context's own stream).  Pending work on the previous stream is waited for
+ * first, so cached blocks stay stream-ordered.  No reference counterpart
+ * (the reference owns one Vulkan queue per device). */
+QSML_API qsml_status_t qsml_set_stream(qsml_ctx* ctx, void* stream);
+QSML_API qsml_status_t qsml_get_stream(qsml_ctx* ctx, void** stream);
+
+/* Blocks until all work enqueued on the context has finished.  Replaces
+ * Device::synchronize / flush_pending (QuasarML/src/Core/Device.cpp:96-102,
+ * QuasarML/src/Backend/Vulkan/VulkanBackend.cpp:613-658). */
+QSML_API qsml_status_t qsml_synchronize(qsml_ctx* ctx);
+
+/* Message of the last failed call on ctx (or of the last failed
+ * context-free call when ctx is NULL).  Never NULL. */
+QSML_API const char* qsml_last_error(qsml_ctx* ctx);
+
+/* ---- memory ------------------------------------------------------------ */
+
+/* Device allocation from the context's caching allocator (256-byte aligned,
+ * size-binned, reused in stream order).  Replaces
+ * Backend::create_storage_buffer / destroy_buffer
+ * (QuasarML/src/Backend/Vulkan/VulkanBackend.cpp:254-325). */
+QSML_API qsml_status_t qsml_alloc(qsml_ctx* ctx, size_t bytes, void** ptr);
+QSML_API qsml_status_t qsml_free(qsml_ctx* ctx, void* ptr);
+/* Returns every cached, unused block to the driver. */
+QSML_API qsml_status_t qsml_empty_cache(qsml_ctx* ctx);
+
+/* Host<->device copies on the context stream.  qsml_h2d is asynchronous for
+ * pinned host memory; qsml_d2h waits for the copy before returning.
+ * Replace Backend::upload_buffer / download_buffer / copy_buffer
+ * (QuasarML/src/Backend/Vulkan/VulkanBackend.cpp:327-373). */
+QSML_API qsml_status_t qsml_h2d(qsml_ctx* ctx, void* dst, const void* src, size_t bytes);
+QSML_API qsml_status_t qsml_d2h(qsml_ctx* ctx, void* dst, const void* src, size_t bytes);
+QSML_API qsml_status_t qsml_d2h_async(qsml_ctx* ctx, void* dst, const void* src, size_t bytes);
+QSML_API qsml_status_t qsml_d2d(qsml_ctx* ctx, void* dst, const void* src, size_t bytes);
+
+/* Page-locked host memory for fast, asynchronous transfers. */
+QSML_API qsml_status_t qsml_host_alloc(size_t bytes, void** ptr);
+QSML_API qsml_status_t qsml_host_free(void* ptr);
+
+/* Fills `count` elements of `elem_size` bytes (1, 2, 4 or 8) with the
+ * pattern at `value`.  Replaces Tensor::fill / Tensor::zero, which upload a
+ * host-built buffer (QuasarML/src/Core/Tensor.cpp:100-112). */
+QSML_API qsml_status_t qsml_fill(qsml_ctx* ctx, void* dst, const void* value,
+                                 int32_t elem_size, int64_t count);
+
+/* ---- ops --------------------------------------------------------------- */
+
+/* out = a (op) b with NumPy broadcasting; out.shape must equal the
+ * broadcast shape.  F32, F16 (computed in fp32, rounded once) and I32
+ * (add/sub/mul/div).  Add/sub/mul/div are IEEE-correctly rounded with no FMA
+ * contraction; POW uses x*x for exponent 2 and a binary64 pow rounded once
+ * otherwise.  Replaces Ops::add/subtract/multiply/divide
+ * (QuasarML/src/Ops/Elementwise.cpp:139-205, shader
+ * QuasarML/src/Ops/ShaderGen.cpp:40-53), which require equal shapes. */
+QSML_API qsml_status_t qsml_binary(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a,
+                                   const qsml_tdesc* b, const qsml_tdesc* out);
+
+/* out = a (op) s.  Replaces Ops::add_scalar / multiply_scalar
+ * (QuasarML/src/Ops/Elementwise.cpp:207-241, shader :39-51); SUB, DIV and
+ * POW (scalar exponent, the new qsml::pow(x, f32)) use the same kernel. */
+QSML_API qsml_status_t qsml_binary_scalar(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a,
+                                          float s, const qsml_tdesc* out);
+
+/* out = f(a).  Replaces Ops::relu (QuasarML/src/Ops/Elementwise.cpp:347-361,
+ * shader :53-66) and neg/abs/sqrt/exp/log/sin/cos/tanh/sigmoid/gelu
+ * (QuasarML/src/Ops/Elementwise.cpp:243-345,363-395).  relu(NaN) = NaN,
+ * relu(-0) = +0. */
+QSML_API qsml_status_t qsml_unary(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a,
+                                  const qsml_tdesc* out);
+
+/* Sum / mean / max / min over one axis (negative counts from the end) or
+ * over all elements (axis = QSML_AXIS_ALL).  out has the reduced shape
+ * (keepdims keeps the axis as 1; the full reduction gives shape [1]) and the
+ * input's dtype; F16 input accumulates in fp32.  mean = sum * (1.0f/(float)n).
+ * max/min follow IEEE 754-2019 maximum/minimum (NaN propagates as 0x7fffffff,
+ * -0 < +0).  The combine order is fixed by the shape alone, so results are
+ * run-to-run deterministic.  Replaces Ops::sum/mean/max/min
+ * (QuasarML/src/Ops/Reduction.cpp:285-382), whose axis max/min are stubs. */
+QSML_API qsml_status_t qsml_reduce(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a,
+                                   int32_t axis, int32_t keepdims, const qsml_tdesc* out);
+
+/* Materialises a strided view (any strides, including 0 and negative) into
+ * the contiguous `out` of the same shape and dtype, bit-exactly.  Replaces
+ * Ops::copy (QuasarML/src/Ops/Manipulation.cpp:171-184), Ops::slice's host
+ * round trip (QuasarML/src/Ops/Manipulation.cpp:146-161) and the
+ * materialising transpose (QuasarML/src/Ops/LinAlg.cpp:329-351). */
+QSML_API qsml_status_t qsml_gather(qsml_ctx* ctx, const qsml_tdesc* src, const qsml_tdesc* out);
+
+/* y = (x - mean) / sqrt(var + eps) * gamma + beta over the last dim (biased
+ * variance).  x/y F32 or F16; gamma/beta F32 or the dtype of x, shape
+ * [last dim].  No reference counterpart (layer norm is absent from the
+ * reference snapshot). */
+QSML_API qsml_status_t qsml_layer_norm(qsml_ctx* ctx, const qsml_tdesc* x, const qsml_tdesc* gamma,
+                                       const qsml_tdesc* beta, float eps, const qsml_tdesc* y);
+
+/* C = A * B for rank-2 A[M,K], B[K,N] -> C[M,N], or batched rank-3
+ * A[b,M,K], B[b,K,N] -> C[b,M,N] (batch strides may be 0).  A and B must have
+ * unit stride in their last dim.  F32 inputs give F32 C; F16 inputs give
+ * F32 (or F16) C with fp32 accumulation.  Replaces Ops::matmul and
+ * Ops::batch_matmul (QuasarML/src/Ops/LinAlg.cpp:221-290; the reference's
+ * batched version is broken). */
+QSML_API qsml_status_t qsml_matmul(qsml_ctx* ctx, const qsml_tdesc* a, const qsml_tdesc* b,
+                                   const qsml_tdesc* c, int32_t precision);
+
+/* ---- counters ---------------------------------------------------------- */
+
+/* Kernels this context has launched since qsml_init. */
+QSML_API qsml_status_t qsml_launch_count(qsml_ctx* ctx, uint64_t* count);
+/* Ops that ran on the CPU instead of the GPU: always 0 (there is no CPU
+ * path).  Backs qsml::cpu_fallback_count(). */
+QSML_API qsml_status_t qsml_cpu_fallback_count(qsml_ctx* ctx, uint64_t* count);
+/* Caching-allocator statistics: cudaMalloc calls (misses), cache hits,
+ * bytes currently held from the driver, bytes currently handed out. */
+QSML_API qsml_status_t qsml_allocator_stats(qsml_ctx* ctx, uint64_t* misses, uint64_t* hits,
+                                            uint64_t* reserved_bytes, uint64_t* live_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,274 @@
+"""ctypes binding of libqsml_cuda.so, the extern "C" ABI of include/qsml_cuda.h.
+
+This is how Python code (the test suite and bench.py) reaches the CUDA
+backend: every call goes through the same C entry points the C++ QuasarML
+layer uses.  Device buffers may come from the library's own caching
+allocator (``Context.alloc``) or from torch tensors (``desc_of``); torch is
+only plumbing for memory, streams and events.
+
+There is no fallback: if the shared library is missing the import of this
+module raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Iterable, Optional, Sequence
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libqsml_cuda.so")
+HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "qsml_cuda.h")
+
+# ---- constants (mirror include/qsml_cuda.h; tests check they agree) -------
+OK, E_INVALID, E_SHAPE, E_DTYPE, E_OOM, E_CUDA, E_NCCL, E_TIMEOUT, E_UNSUPPORTED = range(9)
+F32, F16, I32, I16, I8, U32, U16, U8 = range(8)
+MAX_DIMS = 8
+OP_ADD, OP_SUB, OP_MUL, OP_DIV, OP_POW = range(5)
+(UN_RELU, UN_NEG, UN_ABS, UN_SQRT, UN_EXP, UN_LOG, UN_SIN, UN_COS, UN_TANH,
+ UN_SIGMOID, UN_GELU) = range(11)
+RED_SUM, RED_MEAN, RED_MAX, RED_MIN = range(4)
+AXIS_ALL = -1000
+MM_AUTO, MM_FP32_FFMA, MM_FP32_3XTF32, MM_FP16_F32ACC = range(4)
+
+DTYPE_SIZE = {F32: 4, F16: 2, I32: 4, I16: 2, I8: 1, U32: 4, U16: 2, U8: 1}
+STATUS_NAME = {OK: "OK", E_INVALID: "E_INVALID", E_SHAPE: "E_SHAPE", E_DTYPE: "E_DTYPE",
+               E_OOM: "E_OOM", E_CUDA: "E_CUDA", E_NCCL: "E_NCCL", E_TIMEOUT: "E_TIMEOUT",
+               E_UNSUPPORTED: "E_UNSUPPORTED"}
+
+
+class TDesc(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("dtype", ctypes.c_int32),
+        ("ndim", ctypes.c_int32),
+        ("shape", ctypes.c_int64 * MAX_DIMS),
+        ("stride", ctypes.c_int64 * MAX_DIMS),
+    ]
+
+
+class QsmlError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAME.get(status, status)}: {message}")
+        self.status = status
+
+
+_P = ctypes.POINTER
+_c = ctypes
+# name -> (restype, argtypes)
+_SIGS = {
+    "qsml_device_count": (_c.c_int32, [_P(_c.c_int32)]),
+    "qsml_device_name": (_c.c_int32, [_c.c_int32, _c.c_char_p, _c.c_size_t]),
+    "qsml_init": (_c.c_int32, [_c.c_int32, _P(_c.c_void_p)]),
+    "qsml_destroy": (_c.c_int32, [_c.c_void_p]),
+    "qsml_set_stream": (_c.c_int32, [_c.c_void_p, _c.c_void_p]),
+    "qsml_get_stream": (_c.c_int32, [_c.c_void_p, _P(_c.c_void_p)]),
+    "qsml_synchronize": (_c.c_int32, [_c.c_void_p]),
+    "qsml_last_error": (_c.c_char_p, [_c.c_void_p]),
+    "qsml_alloc": (_c.c_int32, [_c.c_void_p, _c.c_size_t, _P(_c.c_void_p)]),
+    "qsml_free": (_c.c_int32, [_c.c_void_p, _c.c_void_p]),
+    "qsml_empty_cache": (_c.c_int32, [_c.c_void_p]),
+    "qsml_h2d": (_c.c_int32, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t]),
+    "qsml_d2h": (_c.c_int32, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t]),
+    "qsml_d2h_async": (_c.c_int32, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t]),
+    "qsml_d2d": (_c.c_int32, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t]),
+    "qsml_host_alloc": (_c.c_int32, [_c.c_size_t, _P(_c.c_void_p)]),
+    "qsml_host_free": (_c.c_int32, [_c.c_void_p]),
+    "qsml_fill": (_c.c_int32, [_c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int64]),
+    "qsml_binary": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _P(TDesc), _P(TDesc)]),
+    "qsml_binary_scalar": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_float, _P(TDesc)]),
+    "qsml_unary": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _P(TDesc)]),
+    "qsml_reduce": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_int32, _c.c_int32, _P(TDesc)]),
+    "qsml_gather": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc)]),
+    "qsml_layer_norm": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_float, _P(TDesc)]),
+    "qsml_matmul": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_int32]),
+    "qsml_launch_count": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64)]),
+    "qsml_cpu_fallback_count": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64)]),
+    "qsml_allocator_stats": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64), _P(_c.c_uint64),
+                                          _P(_c.c_uint64), _P(_c.c_uint64)]),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads libqsml_cuda.so once; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise OSError(f"{LIB_PATH} is missing: build it with `make -C quasarml_b200` "
+                      "(or __graft_entry__.build()); there is no CPU fallback")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def declared_functions() -> list:
+    """Names of the functions include/qsml_cuda.h declares."""
+    import re
+    text = open(HEADER_PATH).read()
+    return sorted(set(re.findall(r"QSML_API\s+[\w\s\*]+?\b(qsml_\w+)\s*\(", text)))
+
+
+def make_desc(ptr: int, dtype: int, shape: Sequence[int], strides: Optional[Sequence[int]] = None) -> TDesc:
+    shape = [int(s) for s in shape]
+    if len(shape) > MAX_DIMS:
+        raise ValueError("too many dims")
+    if strides is None:
+        strides, s = [0] * len(shape), 1
+        for i in range(len(shape) - 1, -1, -1):
+            strides[i] = s
+            s *= shape[i]
+    d = TDesc()
+    d.data = ctypes.c_void_p(int(ptr)) if ptr else None
+    d.dtype = dtype
+    d.ndim = len(shape)
+    for i, (n, st) in enumerate(zip(shape, strides)):
+        d.shape[i] = n
+        d.stride[i] = int(st)
+    return d
+
+
+def torch_dtype_code(dt) -> int:
+    import torch
+    table = {torch.float32: F32, torch.float16: F16, torch.int32: I32, torch.int16: I16,
+             torch.int8: I8, torch.uint8: U8}
+    if hasattr(torch, "uint16"):
+        table[torch.uint16] = U16
+        table[torch.uint32] = U32
+    return table[dt]
+
+
+def desc_of(t) -> TDesc:
+    """Descriptor of a torch CUDA tensor (any strides; storage offset applied)."""
+    return make_desc(t.data_ptr(), torch_dtype_code(t.dtype), tuple(t.shape), tuple(t.stride()))
+
+
+class Context:
+    """One qsml_ctx: a device, a stream and a caching allocator."""
+
+    def __init__(self, device: int = 0, use_torch_stream: bool = True):
+        self.lib = load()
+        h = ctypes.c_void_p()
+        st = self.lib.qsml_init(int(device), ctypes.byref(h))
+        if st != OK:
+            raise QsmlError(st, self.lib.qsml_last_error(None).decode())
+        self.h = h
+        self.device = device
+        if use_torch_stream:
+            import torch
+            self.set_stream(torch.cuda.current_stream(device).cuda_stream)
+
+    # -- plumbing ------------------------------------------------------------
+    def check(self, st: int) -> None:
+        if st != OK:
+            raise QsmlError(st, self.lib.qsml_last_error(self.h).decode())
+
+    def close(self) -> None:
+        if self.h:
+            self.check(self.lib.qsml_destroy(self.h))
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_ptr: int) -> None:
+        self.check(self.lib.qsml_set_stream(self.h, ctypes.c_void_p(int(stream_ptr)) if stream_ptr else None))
+
+    def stream(self) -> int:
+        s = ctypes.c_void_p()
+        self.check(self.lib.qsml_get_stream(self.h, ctypes.byref(s)))
+        return s.value or 0
+
+    def synchronize(self) -> None:
+        self.check(self.lib.qsml_synchronize(self.h))
+
+    def launch_count(self) -> int:
+        n = ctypes.c_uint64()
+        self.check(self.lib.qsml_launch_count(self.h, ctypes.byref(n)))
+        return n.value
+
+    def cpu_fallback_count(self) -> int:
+        n = ctypes.c_uint64()
+        self.check(self.lib.qsml_cpu_fallback_count(self.h, ctypes.byref(n)))
+        return n.value
+
+    def allocator_stats(self) -> dict:
+        v = [ctypes.c_uint64() for _ in range(4)]
+        self.check(self.lib.qsml_allocator_stats(self.h, *[ctypes.byref(x) for x in v]))
+        return dict(zip(["misses", "hits", "reserved_bytes", "live_bytes"], [x.value for x in v]))
+
+    # -- memory --------------------------------------------------------------
+    def alloc(self, nbytes: int) -> int:
+        p = ctypes.c_void_p()
+        self.check(self.lib.qsml_alloc(self.h, int(nbytes), ctypes.byref(p)))
+        return p.value
+
+    def free(self, ptr: int) -> None:
+        self.check(self.lib.qsml_free(self.h, ctypes.c_void_p(ptr)))
+
+    def h2d(self, dst: int, src: int, nbytes: int) -> None:
+        self.check(self.lib.qsml_h2d(self.h, ctypes.c_void_p(dst), ctypes.c_void_p(src), int(nbytes)))
+
+    def d2h(self, dst: int, src: int, nbytes: int, sync: bool = True) -> None:
+        fn = self.lib.qsml_d2h if sync else self.lib.qsml_d2h_async
+        self.check(fn(self.h, ctypes.c_void_p(dst), ctypes.c_void_p(src), int(nbytes)))
+
+    def fill(self, dst: int, value_bytes: bytes, count: int) -> None:
+        buf = ctypes.create_string_buffer(value_bytes, len(value_bytes))
+        self.check(self.lib.qsml_fill(self.h, ctypes.c_void_p(dst), buf, len(value_bytes), int(count)))
+
+    # -- ops (descriptors) ---------------------------------------------------
+    def binary(self, op: int, a: TDesc, b: TDesc, out: TDesc) -> None:
+        self.check(self.lib.qsml_binary(self.h, op, ctypes.byref(a), ctypes.byref(b), ctypes.byref(out)))
+
+    def binary_scalar(self, op: int, a: TDesc, s: float, out: TDesc) -> None:
+        self.check(self.lib.qsml_binary_scalar(self.h, op, ctypes.byref(a), ctypes.c_float(s), ctypes.byref(out)))
+
+    def unary(self, op: int, a: TDesc, out: TDesc) -> None:
+        self.check(self.lib.qsml_unary(self.h, op, ctypes.byref(a), ctypes.byref(out)))
+
+    def reduce(self, op: int, a: TDesc, axis: int, keepdims: bool, out: TDesc) -> None:
+        self.check(self.lib.qsml_reduce(self.h, op, ctypes.byref(a), int(axis), int(bool(keepdims)), ctypes.byref(out)))
+
+    def gather(self, src: TDesc, out: TDesc) -> None:
+        self.check(self.lib.qsml_gather(self.h, ctypes.byref(src), ctypes.byref(out)))
+
+    def layer_norm(self, x: TDesc, g: TDesc, b: TDesc, eps: float, y: TDesc) -> None:
+        self.check(self.lib.qsml_layer_norm(self.h, ctypes.byref(x), ctypes.byref(g), ctypes.byref(b),
+                                            ctypes.c_float(eps), ctypes.byref(y)))
+
+    def matmul(self, a: TDesc, b: TDesc, c: TDesc, precision: int = MM_AUTO) -> None:
+        self.check(self.lib.qsml_matmul(self.h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), precision))
+
+
+def broadcast_shape(a: Iterable[int], b: Iterable[int]) -> tuple:
+    """NumPy broadcasting of two shapes (raises ValueError if incompatible)."""
+    a, b = list(a), list(b)
+    n = max(len(a), len(b))
+    a = [1] * (n - len(a)) + a
+    b = [1] * (n - len(b)) + b
+    out = []
+    for x, y in zip(a, b):
+        if x != y and x != 1 and y != 1:
+            raise ValueError(f"shapes {a} and {b} do not broadcast")
+        out.append(y if x == 1 else x)
+    return tuple(out)
+
+
+def reduced_shape(shape: Sequence[int], axis: Optional[int], keepdims: bool) -> tuple:
+    """Output shape of a reduction, following Ops/Reduction.cpp:297-305."""
+    if axis is None or axis == AXIS_ALL:
+        return (1,)
+    ax = axis + len(shape) if axis < 0 else axis
+    if not 0 <= ax < len(shape):
+        raise ValueError("invalid axis")
+    out = [d if i != ax else 1 for i, d in enumerate(shape) if i != ax or keepdims]
+    return tuple(out) if out else (1,)

@@ -1,0 +1,596 @@
+// Elementwise kernels: broadcast binary ops, scalar-operand ops, unary ops
+// and fill.
+//
+// Reference: Ops/Elementwise.cpp:139-417 builds one GLSL shader per op with
+// one element per invocation (`result[idx] = a[idx] op b[idx]`,
+// Ops/ShaderGen.cpp:40-53) and requires equal shapes.  Here every op shares
+// one host planner and three kernels:
+//   * the planner applies NumPy broadcasting (stride 0 on broadcast dims) and
+//     collapses dims that are contiguous for every operand, so
+//     A[4096,4096] + B[1,4096] becomes a [4096 rows x 4096 cols] problem;
+//   * k_ew_rows: 16-byte vector loads/stores along the collapsed inner dim,
+//     per-row broadcast offsets computed once per vector (the inner stride of
+//     each operand is 0 or 1), several independent vectors per thread;
+//   * k_ew_flat: the 1-D contiguous case with a scalar tail;
+//   * k_ew_generic: any strides (one element per thread), always correct.
+// Arithmetic is IEEE binary32 with explicit round-to-nearest intrinsics, so
+// no multiply-add contraction can happen (bit-exact with the oracle).
+#include "qsml_internal.cuh"
+
+namespace qsml {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+// ---------------------------------------------------------------------------
+// Element types: storage type T, compute type C.
+// ---------------------------------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+    using C = float;
+    static __device__ __forceinline__ float ld(float v) { return v; }
+    static __device__ __forceinline__ float st(float v) { return v; }
+};
+template <> struct Elem<__half> {
+    using C = float;
+    static __device__ __forceinline__ float ld(__half v) { return __half2float(v); }
+    static __device__ __forceinline__ __half st(float v) { return __float2half_rn(v); }
+};
+template <> struct Elem<int32_t> {
+    using C = int32_t;
+    static __device__ __forceinline__ int32_t ld(int32_t v) { return v; }
+    static __device__ __forceinline__ int32_t st(int32_t v) { return v; }
+};
+
+template <typename T> struct alignas(16) Pack {
+    static constexpr int N = 16 / sizeof(T);
+    T v[N];
+};
+
+// ---------------------------------------------------------------------------
+// Operators
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float pow_f32(float x, float y) {
+    // Exponent 2 is the single correctly rounded product; any other exponent
+    // goes through binary64 pow (error far below 1 binary32 ulp) rounded once.
+    if (y == 2.0f) return __fmul_rn(x, x);
+    return __double2float_rn(pow(static_cast<double>(x), static_cast<double>(y)));
+}
+
+template <int OP> struct BinOp {
+    __device__ __forceinline__ float operator()(float a, float b) const {
+        if (OP == QSML_OP_ADD) return __fadd_rn(a, b);
+        if (OP == QSML_OP_SUB) return __fsub_rn(a, b);
+        if (OP == QSML_OP_MUL) return __fmul_rn(a, b);
+        if (OP == QSML_OP_DIV) return __fdiv_rn(a, b);
+        return pow_f32(a, b);
+    }
+    __device__ __forceinline__ int32_t operator()(int32_t a, int32_t b) const {
+        uint32_t ua = static_cast<uint32_t>(a), ub = static_cast<uint32_t>(b);
+        if (OP == QSML_OP_ADD) return static_cast<int32_t>(ua + ub);
+        if (OP == QSML_OP_SUB) return static_cast<int32_t>(ua - ub);
+        if (OP == QSML_OP_MUL) return static_cast<int32_t>(ua * ub);
+        if (OP == QSML_OP_DIV) {
+            if (b == 0) return 0;
+            if (a == INT32_MIN && b == -1) return INT32_MIN;
+            return a / b;
+        }
+        return 0;
+    }
+};
+
+// Scalar right operand held by value.
+template <int OP> struct ScalarOp {
+    float s;
+    __device__ __forceinline__ float operator()(float a) const { return BinOp<OP>()(a, s); }
+    __device__ __forceinline__ int32_t operator()(int32_t a) const {
+        return BinOp<OP>()(a, static_cast<int32_t>(s));
+    }
+};
+
+template <int OP> struct UnOp {
+    __device__ __forceinline__ float operator()(float x) const {
+        switch (OP) {
+            case QSML_UN_RELU: return (x != x) ? x : (x > 0.0f ? x : 0.0f);
+            case QSML_UN_NEG: return -x;
+            case QSML_UN_ABS: return fabsf(x);
+            case QSML_UN_SQRT: return __fsqrt_rn(x);
+            case QSML_UN_EXP: return expf(x);
+            case QSML_UN_LOG: return logf(x);
+            case QSML_UN_SIN: return sinf(x);
+            case QSML_UN_COS: return cosf(x);
+            case QSML_UN_TANH: return tanhf(x);
+            case QSML_UN_SIGMOID:
+                // Ops/Elementwise.cpp:77: 1 / (1 + exp(-x))
+                return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+            case QSML_UN_GELU: {
+                // Ops/Elementwise.cpp:93, evaluated left to right:
+                // 0.5*x*(1 + tanh(0.7978845608*(x + 0.044715*x*x*x)))
+                float c = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+                float t = tanhf(__fmul_rn(0.7978845608f, __fadd_rn(x, c)));
+                return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
+            }
+        }
+        return x;
+    }
+    __device__ __forceinline__ int32_t operator()(int32_t x) const {
+        switch (OP) {
+            case QSML_UN_RELU: return x > 0 ? x : 0;
+            case QSML_UN_NEG: return static_cast<int32_t>(0u - static_cast<uint32_t>(x));
+            case QSML_UN_ABS: return x < 0 ? static_cast<int32_t>(0u - static_cast<uint32_t>(x)) : x;
+        }
+        return x;
+    }
+};
+
+// relu on binary16 keeps NaN payloads and maps every non-positive to +0,
+// exactly like the binary32 rule (conversion is exact both ways).
+
+// ---------------------------------------------------------------------------
+// Plan: collapsed output shape and per-operand element strides.
+// ---------------------------------------------------------------------------
+struct EwPlan {
+    int nd;
+    int64_t shape[kMaxDims];
+    int64_t st[2][kMaxDims];  // input strides (0 = broadcast)
+};
+
+template <typename T, int NIN> struct Ptrs {
+    const T* in[2];
+    T* out;
+};
+
+template <typename C, int NIN, typename Op>
+__device__ __forceinline__ C apply(const Op& op, C a, C b) {
+    if constexpr (NIN == 2) return op(a, b);
+    else return op(a);
+}
+
+// Offset of the first element of collapsed row `row` for input j.
+template <typename IDX>
+__device__ __forceinline__ int64_t row_offset(const EwPlan& p, int j, IDX row) {
+    int64_t off = 0;
+    for (int d = p.nd - 2; d >= 1; --d) {
+        IDX e = static_cast<IDX>(p.shape[d]);
+        IDX c = row % e;
+        row /= e;
+        off += static_cast<int64_t>(c) * p.st[j][d];
+    }
+    if (p.nd >= 2) off += static_cast<int64_t>(row) * p.st[j][0];
+    return off;
+}
+
+// Row kernel: out is [R, Cn] with Cn % VEC == 0; each input's inner stride is
+// 0 (one value per row, splatted) or 1 (16-byte vectors).
+template <typename T, int NIN, typename Op, typename IDX>
+__global__ void __launch_bounds__(kThreads) k_ew_rows(Ptrs<T, NIN> P, EwPlan plan, IDX items, IDX cpr, Op op) {
+    using E = Elem<T>;
+    using CT = typename E::C;
+    constexpr int V = Pack<T>::N;
+    const IDX base = static_cast<IDX>(blockIdx.x) * (kThreads * kUnroll) + threadIdx.x;
+    Pack<T> r[2][kUnroll];
+    IDX outoff[kUnroll];
+    bool ok[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+        IDX it = base + static_cast<IDX>(u) * kThreads;
+        ok[u] = it < items;
+        if (!ok[u]) continue;
+        IDX row = it / cpr;
+        IDX cv = it - row * cpr;
+        outoff[u] = it;
+#pragma unroll
+        for (int j = 0; j < NIN; ++j) {
+            int64_t off = row_offset<IDX>(plan, j, row);
+            if (plan.st[j][plan.nd - 1] != 0) {
+                r[j][u] = *reinterpret_cast<const Pack<T>*>(P.in[j] + off + static_cast<int64_t>(cv) * V);
+            } else {
+                T s = P.in[j][off];
+#pragma unroll
+                for (int e = 0; e < V; ++e) r[j][u].v[e] = s;
+            }
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+        if (!ok[u]) continue;
+        Pack<T> o;
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+            CT a = E::ld(r[0][u].v[e]);
+            CT b = NIN == 2 ? E::ld(r[NIN - 1][u].v[e]) : a;
+            o.v[e] = E::st(apply<CT, NIN>(op, a, b));
+        }
+        reinterpret_cast<Pack<T>*>(P.out)[outoff[u]] = o;
+    }
+}
+
+// 1-D contiguous (or scalar-broadcast) operands: vector body + scalar tail.
+template <typename T, int NIN, typename Op, bool VEC>
+__global__ void __launch_bounds__(kThreads) k_ew_flat(Ptrs<T, NIN> P, EwPlan plan, int64_t n, Op op) {
+    using E = Elem<T>;
+    using CT = typename E::C;
+    constexpr int V = VEC ? Pack<T>::N : 1;
+    const int64_t npk = n / V;
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * (kThreads * kUnroll) + threadIdx.x;
+    bool bc[2];
+    T sv[2];
+#pragma unroll
+    for (int j = 0; j < NIN; ++j) {
+        bc[j] = plan.st[j][0] == 0;
+        sv[j] = bc[j] ? P.in[j][0] : T();
+    }
+    if constexpr (VEC) {
+        Pack<T> r[2][kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            int64_t pk = base + static_cast<int64_t>(u) * kThreads;
+            if (pk >= npk) continue;
+#pragma unroll
+            for (int j = 0; j < NIN; ++j) {
+                if (!bc[j]) {
+                    r[j][u] = reinterpret_cast<const Pack<T>*>(P.in[j])[pk];
+                } else {
+#pragma unroll
+                    for (int e = 0; e < Pack<T>::N; ++e) r[j][u].v[e] = sv[j];
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            int64_t pk = base + static_cast<int64_t>(u) * kThreads;
+            if (pk >= npk) continue;
+            Pack<T> o;
+#pragma unroll
+            for (int e = 0; e < Pack<T>::N; ++e) {
+                CT a = E::ld(r[0][u].v[e]);
+                CT b = NIN == 2 ? E::ld(r[NIN - 1][u].v[e]) : a;
+                o.v[e] = E::st(apply<CT, NIN>(op, a, b));
+            }
+            reinterpret_cast<Pack<T>*>(P.out)[pk] = o;
+        }
+        // tail: the last n % V elements, handled by the first threads of block 0
+        if (blockIdx.x == 0) {
+            int64_t i = npk * V + threadIdx.x;
+            if (i < n) {
+                CT a = E::ld(bc[0] ? sv[0] : P.in[0][i]);
+                CT b = a;
+                if (NIN == 2) b = E::ld(bc[NIN - 1] ? sv[NIN - 1] : P.in[NIN - 1][i]);
+                P.out[i] = E::st(apply<CT, NIN>(op, a, b));
+            }
+        }
+    } else {
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            int64_t i = base + static_cast<int64_t>(u) * kThreads;
+            if (i >= n) continue;
+            CT a = E::ld(bc[0] ? sv[0] : P.in[0][i]);
+            CT b = a;
+            if (NIN == 2) b = E::ld(bc[NIN - 1] ? sv[NIN - 1] : P.in[NIN - 1][i]);
+            P.out[i] = E::st(apply<CT, NIN>(op, a, b));
+        }
+    }
+}
+
+// Any strides, one element per thread (grid-stride).
+template <typename T, int NIN, typename Op>
+__global__ void __launch_bounds__(kThreads) k_ew_generic(Ptrs<T, NIN> P, EwPlan plan, int64_t n, Op op) {
+    using E = Elem<T>;
+    using CT = typename E::C;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * kThreads) {
+        int64_t rem = i, off[2] = {0, 0};
+        for (int d = plan.nd - 1; d >= 0; --d) {
+            int64_t c = rem % plan.shape[d];
+            rem /= plan.shape[d];
+#pragma unroll
+            for (int j = 0; j < NIN; ++j) off[j] += c * plan.st[j][d];
+        }
+        CT a = E::ld(P.in[0][off[0]]);
+        CT b = NIN == 2 ? E::ld(P.in[NIN - 1][off[NIN - 1]]) : a;
+        P.out[i] = E::st(apply<CT, NIN>(op, a, b));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host planning
+// ---------------------------------------------------------------------------
+
+// Aligns each input's shape/strides to out's dims (NumPy broadcasting) and
+// collapses.  Returns QSML_OK or a shape error.
+qsml_status_t make_plan(Context* ctx, const qsml_tdesc* out, const qsml_tdesc* const* ins, int nin, EwPlan* p) {
+    const int nd = out->ndim;
+    int64_t shape[kMaxDims];
+    int64_t st[2][kMaxDims];
+    for (int d = 0; d < nd; ++d) shape[d] = out->shape[d];
+    for (int j = 0; j < nin; ++j) {
+        const qsml_tdesc* a = ins[j];
+        if (a->ndim > nd) return set_error(ctx, QSML_E_SHAPE, "input has more dims than the output");
+        for (int d = 0; d < nd; ++d) {
+            int ad = a->ndim - nd + d;
+            if (ad < 0) { st[j][d] = 0; continue; }
+            if (a->shape[ad] == out->shape[d]) st[j][d] = out->shape[d] == 1 ? 0 : a->stride[ad];
+            else if (a->shape[ad] == 1) st[j][d] = 0;
+            else return set_error(ctx, QSML_E_SHAPE, "operand shape does not broadcast to the output shape");
+        }
+    }
+    // Output shape must be exactly the broadcast of the inputs: every out
+    // extent > 1 must come from some input.
+    for (int d = 0; d < nd; ++d) {
+        if (out->shape[d] == 1) continue;
+        bool from_input = false;
+        for (int j = 0; j < nin; ++j) {
+            int ad = ins[j]->ndim - nd + d;
+            if (ad >= 0 && ins[j]->shape[ad] == out->shape[d]) from_input = true;
+        }
+        if (!from_input) return set_error(ctx, QSML_E_SHAPE, "output shape is not the broadcast shape of the inputs");
+    }
+    // Drop size-1 dims, then merge dims contiguous for every operand
+    // (out is contiguous, so only the inputs decide).
+    int n = 0;
+    for (int d = 0; d < nd; ++d) {
+        if (shape[d] == 1) continue;
+        if (n > 0) {
+            bool merge = true;
+            for (int j = 0; j < nin; ++j)
+                if (p->st[j][n - 1] != st[j][d] * shape[d]) merge = false;
+            if (merge) {
+                p->shape[n - 1] *= shape[d];
+                for (int j = 0; j < nin; ++j) p->st[j][n - 1] = st[j][d];
+                continue;
+            }
+        }
+        p->shape[n] = shape[d];
+        for (int j = 0; j < nin; ++j) p->st[j][n] = st[j][d];
+        ++n;
+    }
+    if (n == 0) {
+        p->shape[0] = 1;
+        for (int j = 0; j < 2; ++j) p->st[j][0] = 0;
+        n = 1;
+    }
+    for (int j = nin; j < 2; ++j)
+        for (int d = 0; d < n; ++d) p->st[j][d] = 0;
+    p->nd = n;
+    return QSML_OK;
+}
+
+template <typename T, int NIN, typename Op>
+qsml_status_t launch_ew(Context* ctx, const EwPlan& p, const qsml_tdesc* const* ins, const qsml_tdesc* out, Op op) {
+    constexpr int V = Pack<T>::N;
+    Ptrs<T, NIN> P;
+    for (int j = 0; j < 2; ++j) P.in[j] = static_cast<const T*>(ins[j < NIN ? j : 0]->data);
+    P.out = static_cast<T*>(out->data);
+    int64_t n = 1;
+    for (int d = 0; d < p.nd; ++d) n *= p.shape[d];
+    if (n == 0) return QSML_OK;
+
+    const int last = p.nd - 1;
+    bool inner_ok = true;  // every inner stride is 0 or 1
+    for (int j = 0; j < NIN; ++j)
+        if (p.st[j][last] != 0 && p.st[j][last] != 1) inner_ok = false;
+
+    if (inner_ok && p.nd == 1) {
+        bool vec = aligned16(P.out);
+        for (int j = 0; j < NIN; ++j)
+            if (p.st[j][0] == 1 && !aligned16(P.in[j])) vec = false;
+        if (vec) {
+            int64_t npk = n / V;
+            int64_t blocks = (npk + kThreads * kUnroll - 1) / (kThreads * kUnroll);
+            if (blocks < 1) blocks = 1;
+            k_ew_flat<T, NIN, Op, true><<<static_cast<unsigned>(blocks), kThreads, 0, ctx->stream>>>(P, p, n, op);
+        } else {
+            int64_t blocks = (n + kThreads * kUnroll - 1) / (kThreads * kUnroll);
+            k_ew_flat<T, NIN, Op, false><<<static_cast<unsigned>(blocks), kThreads, 0, ctx->stream>>>(P, p, n, op);
+        }
+        return after_launch(ctx, "k_ew_flat");
+    }
+
+    if (inner_ok && p.shape[last] % V == 0 && aligned16(P.out)) {
+        bool vec = true;
+        for (int j = 0; j < NIN; ++j) {
+            if (p.st[j][last] != 1) continue;
+            if (!aligned16(P.in[j])) vec = false;
+            for (int d = 0; d < last; ++d)
+                if (p.st[j][d] % V != 0) vec = false;
+        }
+        if (vec) {
+            int64_t cpr = p.shape[last] / V;
+            int64_t items = n / V;
+            int64_t blocks = (items + kThreads * kUnroll - 1) / (kThreads * kUnroll);
+            bool small = items < (int64_t(1) << 31);
+            for (int d = 0; d < p.nd; ++d)
+                if (p.shape[d] >= (int64_t(1) << 31)) small = false;
+            if (small) {
+                k_ew_rows<T, NIN, Op, uint32_t><<<static_cast<unsigned>(blocks), kThreads, 0, ctx->stream>>>(
+                    P, p, static_cast<uint32_t>(items), static_cast<uint32_t>(cpr), op);
+            } else {
+                k_ew_rows<T, NIN, Op, int64_t><<<static_cast<unsigned>(blocks), kThreads, 0, ctx->stream>>>(
+                    P, p, items, cpr, op);
+            }
+            return after_launch(ctx, "k_ew_rows");
+        }
+    }
+
+    int64_t blocks = (n + kThreads - 1) / kThreads;
+    int64_t cap = static_cast<int64_t>(ctx->num_sms) * 16;
+    if (blocks > cap) blocks = cap;
+    k_ew_generic<T, NIN, Op><<<static_cast<unsigned>(blocks), kThreads, 0, ctx->stream>>>(P, p, n, op);
+    return after_launch(ctx, "k_ew_generic");
+}
+
+template <typename T, int NIN, template <int> class OpT, int... OPS>
+struct OpDispatch;
+
+template <typename T, int NIN, typename Op>
+qsml_status_t run_typed(Context* ctx, const EwPlan& p, const qsml_tdesc* const* ins, const qsml_tdesc* out, Op op) {
+    return launch_ew<T, NIN, Op>(ctx, p, ins, out, op);
+}
+
+template <typename T>
+qsml_status_t binary_typed(Context* ctx, int op, const EwPlan& p, const qsml_tdesc* const* ins, const qsml_tdesc* out) {
+    switch (op) {
+        case QSML_OP_ADD: return run_typed<T, 2>(ctx, p, ins, out, BinOp<QSML_OP_ADD>());
+        case QSML_OP_SUB: return run_typed<T, 2>(ctx, p, ins, out, BinOp<QSML_OP_SUB>());
+        case QSML_OP_MUL: return run_typed<T, 2>(ctx, p, ins, out, BinOp<QSML_OP_MUL>());
+        case QSML_OP_DIV: return run_typed<T, 2>(ctx, p, ins, out, BinOp<QSML_OP_DIV>());
+        case QSML_OP_POW:
+            if constexpr (std::is_same<T, int32_t>::value) return set_error(ctx, QSML_E_DTYPE, "pow needs a float dtype");
+            else return run_typed<T, 2>(ctx, p, ins, out, BinOp<QSML_OP_POW>());
+    }
+    return set_error(ctx, QSML_E_INVALID, "unknown binary op");
+}
+
+template <typename T>
+qsml_status_t scalar_typed(Context* ctx, int op, float s, const EwPlan& p, const qsml_tdesc* const* ins, const qsml_tdesc* out) {
+    switch (op) {
+        case QSML_OP_ADD: return run_typed<T, 1>(ctx, p, ins, out, ScalarOp<QSML_OP_ADD>{s});
+        case QSML_OP_SUB: return run_typed<T, 1>(ctx, p, ins, out, ScalarOp<QSML_OP_SUB>{s});
+        case QSML_OP_MUL: return run_typed<T, 1>(ctx, p, ins, out, ScalarOp<QSML_OP_MUL>{s});
+        case QSML_OP_DIV: return run_typed<T, 1>(ctx, p, ins, out, ScalarOp<QSML_OP_DIV>{s});
+        case QSML_OP_POW:
+            if constexpr (std::is_same<T, int32_t>::value) return set_error(ctx, QSML_E_DTYPE, "pow needs a float dtype");
+            else return run_typed<T, 1>(ctx, p, ins, out, ScalarOp<QSML_OP_POW>{s});
+    }
+    return set_error(ctx, QSML_E_INVALID, "unknown scalar op");
+}
+
+template <typename T>
+qsml_status_t unary_typed(Context* ctx, int op, const EwPlan& p, const qsml_tdesc* const* ins, const qsml_tdesc* out) {
+    if constexpr (std::is_same<T, int32_t>::value) {
+        switch (op) {
+            case QSML_UN_RELU: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_RELU>());
+            case QSML_UN_NEG: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_NEG>());
+            case QSML_UN_ABS: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_ABS>());
+        }
+        return set_error(ctx, QSML_E_DTYPE, "this unary op needs a float dtype");
+    } else {
+        switch (op) {
+            case QSML_UN_RELU: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_RELU>());
+            case QSML_UN_NEG: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_NEG>());
+            case QSML_UN_ABS: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_ABS>());
+            case QSML_UN_SQRT: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_SQRT>());
+            case QSML_UN_EXP: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_EXP>());
+            case QSML_UN_LOG: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_LOG>());
+            case QSML_UN_SIN: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_SIN>());
+            case QSML_UN_COS: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_COS>());
+            case QSML_UN_TANH: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_TANH>());
+            case QSML_UN_SIGMOID: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_SIGMOID>());
+            case QSML_UN_GELU: return run_typed<T, 1>(ctx, p, ins, out, UnOp<QSML_UN_GELU>());
+        }
+        return set_error(ctx, QSML_E_INVALID, "unknown unary op");
+    }
+}
+
+qsml_status_t check_out(Context* ctx, const qsml_tdesc* out) {
+    QSML_TRY_STATUS(check_desc(ctx, out, "out"));
+    if (!is_contiguous(out)) return set_error(ctx, QSML_E_SHAPE, "out must be contiguous");
+    return QSML_OK;
+}
+
+template <typename T>
+__global__ void k_fill(T* p, T v, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        p[i] = v;
+}
+
+}  // namespace
+}  // namespace qsml
+
+using namespace qsml;
+
+extern "C" {
+
+qsml_status_t qsml_binary(qsml_ctx* handle, int32_t op, const qsml_tdesc* a, const qsml_tdesc* b,
+                          const qsml_tdesc* out) {
+    QSML_CTX(handle);
+    QSML_TRY_STATUS(check_desc(C_, a, "a"));
+    QSML_TRY_STATUS(check_desc(C_, b, "b"));
+    QSML_TRY_STATUS(check_out(C_, out));
+    if (a->dtype != b->dtype || a->dtype != out->dtype)
+        return set_error(C_, QSML_E_DTYPE, "qsml_binary: dtypes of a, b and out must match");
+    if (op < QSML_OP_ADD || op > QSML_OP_POW) return set_error(C_, QSML_E_INVALID, "qsml_binary: unknown op");
+    const qsml_tdesc* ins[2] = {a, b};
+    EwPlan p;
+    QSML_TRY_STATUS(make_plan(C_, out, ins, 2, &p));
+    switch (a->dtype) {
+        case QSML_F32: return binary_typed<float>(C_, op, p, ins, out);
+        case QSML_F16: return binary_typed<__half>(C_, op, p, ins, out);
+        case QSML_I32: return binary_typed<int32_t>(C_, op, p, ins, out);
+    }
+    return set_error(C_, QSML_E_DTYPE, "qsml_binary: dtype must be F32, F16 or I32");
+}
+
+qsml_status_t qsml_binary_scalar(qsml_ctx* handle, int32_t op, const qsml_tdesc* a, float s,
+                                 const qsml_tdesc* out) {
+    QSML_CTX(handle);
+    QSML_TRY_STATUS(check_desc(C_, a, "a"));
+    QSML_TRY_STATUS(check_out(C_, out));
+    if (a->dtype != out->dtype) return set_error(C_, QSML_E_DTYPE, "qsml_binary_scalar: dtype mismatch");
+    if (op < QSML_OP_ADD || op > QSML_OP_POW) return set_error(C_, QSML_E_INVALID, "qsml_binary_scalar: unknown op");
+    const qsml_tdesc* ins[1] = {a};
+    EwPlan p;
+    QSML_TRY_STATUS(make_plan(C_, out, ins, 1, &p));
+    switch (a->dtype) {
+        case QSML_F32: return scalar_typed<float>(C_, op, s, p, ins, out);
+        case QSML_F16: return scalar_typed<__half>(C_, op, s, p, ins, out);
+        case QSML_I32: return scalar_typed<int32_t>(C_, op, s, p, ins, out);
+    }
+    return set_error(C_, QSML_E_DTYPE, "qsml_binary_scalar: dtype must be F32, F16 or I32");
+}
+
+qsml_status_t qsml_unary(qsml_ctx* handle, int32_t op, const qsml_tdesc* a, const qsml_tdesc* out) {
+    QSML_CTX(handle);
+    QSML_TRY_STATUS(check_desc(C_, a, "a"));
+    QSML_TRY_STATUS(check_out(C_, out));
+    if (a->dtype != out->dtype) return set_error(C_, QSML_E_DTYPE, "qsml_unary: dtype mismatch");
+    const qsml_tdesc* ins[1] = {a};
+    EwPlan p;
+    QSML_TRY_STATUS(make_plan(C_, out, ins, 1, &p));
+    switch (a->dtype) {
+        case QSML_F32: return unary_typed<float>(C_, op, p, ins, out);
+        case QSML_F16: return unary_typed<__half>(C_, op, p, ins, out);
+        case QSML_I32: return unary_typed<int32_t>(C_, op, p, ins, out);
+    }
+    return set_error(C_, QSML_E_DTYPE, "qsml_unary: dtype must be F32, F16 or I32");
+}
+
+qsml_status_t qsml_fill(qsml_ctx* handle, void* dst, const void* value, int32_t elem_size, int64_t count) {
+    QSML_CTX(handle);
+    if (count <= 0) return QSML_OK;
+    if (!dst || !value) return set_error(C_, QSML_E_INVALID, "qsml_fill: null pointer");
+    int64_t blocks = (count + 255) / 256;
+    int64_t cap = static_cast<int64_t>(C_->num_sms) * 16;
+    if (blocks > cap) blocks = cap;
+    switch (elem_size) {
+        case 1:
+            return check_cuda(C_, cudaMemsetAsync(dst, *static_cast<const uint8_t*>(value), count, C_->stream),
+                              "qsml_fill");
+        case 2: {
+            uint16_t v;
+            std::memcpy(&v, value, 2);
+            if ((reinterpret_cast<uintptr_t>(dst) & 1) != 0) return set_error(C_, QSML_E_INVALID, "qsml_fill: misaligned");
+            k_fill<uint16_t><<<static_cast<unsigned>(blocks), 256, 0, C_->stream>>>(static_cast<uint16_t*>(dst), v, count);
+            return after_launch(C_, "k_fill");
+        }
+        case 4: {
+            uint32_t v;
+            std::memcpy(&v, value, 4);
+            if ((reinterpret_cast<uintptr_t>(dst) & 3) != 0) return set_error(C_, QSML_E_INVALID, "qsml_fill: misaligned");
+            k_fill<uint32_t><<<static_cast<unsigned>(blocks), 256, 0, C_->stream>>>(static_cast<uint32_t*>(dst), v, count);
+            return after_launch(C_, "k_fill");
+        }
+        case 8: {
+            uint64_t v;
+            std::memcpy(&v, value, 8);
+            if ((reinterpret_cast<uintptr_t>(dst) & 7) != 0) return set_error(C_, QSML_E_INVALID, "qsml_fill: misaligned");
+            k_fill<uint64_t><<<static_cast<unsigned>(blocks), 256, 0, C_->stream>>>(static_cast<uint64_t*>(dst), v, count);
+            return after_launch(C_, "k_fill");
+        }
+    }
+    return set_error(C_, QSML_E_INVALID, "qsml_fill: elem_size must be 1, 2, 4 or 8");
+}
+
+}  // extern "C"

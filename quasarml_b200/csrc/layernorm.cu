@@ -1,0 +1,230 @@
+// Layer norm over the last dim: y = (x - mean) / sqrt(var + eps) * gamma + beta
+// with the biased (population) variance.  The reference snapshot has no
+// layer norm; this is a new op of the same API family.
+//
+// k_layer_norm_reg: one CTA per row, the row held in registers (16-byte
+// loads), so x is read from HBM exactly once and y written once.  Each
+// thread's values give a local (mean, M2); warps merge them with Chan's
+// pairwise update (equal counts, written symmetrically so partner lanes
+// hold identical bits), then the warps' results merge in warp order.
+// k_layer_norm_generic: any width or alignment, Welford over global memory
+// (reads x twice).
+#include "qsml_internal.cuh"
+
+namespace qsml {
+namespace {
+
+template <typename T> struct alignas(16) Pack {
+    static constexpr int N = 16 / sizeof(T);
+    T v[N];
+};
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+__device__ __forceinline__ float from_f_tag(float v, float*) { return v; }
+__device__ __forceinline__ __half from_f_tag(float v, __half*) { return __float2half_rn(v); }
+
+// Merge (mean, m2) statistics of two equal-count halves of n elements each.
+__device__ __forceinline__ void chan_equal(float& mean, float& m2, float mo, float m2o, float n) {
+    float d = __fsub_rn(mo, mean);
+    float dd = __fmul_rn(d, d);  // (a-b)^2 == (b-a)^2 bit for bit
+    mean = __fmul_rn(__fadd_rn(mean, mo), 0.5f);
+    m2 = __fadd_rn(__fadd_rn(m2, m2o), __fmul_rn(dd, __fmul_rn(n, 0.5f)));
+}
+
+template <typename T, typename GT, int NV>
+__global__ void k_layer_norm_reg(const T* __restrict__ x, const GT* __restrict__ gamma, const GT* __restrict__ beta,
+                                 T* __restrict__ y, int64_t rows, int cols, float eps) {
+    constexpr int PV = Pack<T>::N;
+    constexpr int E = NV * PV;  // elements per thread
+    __shared__ float s_mean[32], s_m2[32];
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5, nw = blockDim.x >> 5;
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + row * cols);
+        float v[E];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            Pack<T> p = xr[t + i * blockDim.x];
+#pragma unroll
+            for (int e = 0; e < PV; ++e) v[i * PV + e] = to_f(p.v[e]);
+        }
+        // Thread-local statistics (two passes over registers).
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) s = __fadd_rn(s, v[i]);
+        float mean = __fdiv_rn(s, static_cast<float>(E));
+        float m2 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            float d = __fsub_rn(v[i], mean);
+            m2 = __fmaf_rn(d, d, m2);
+        }
+        // Warp: butterfly merge, counts double each step.
+        float n = static_cast<float>(E);
+#pragma unroll
+        for (int m = 1; m < 32; m <<= 1) {
+            float mo = __shfl_xor_sync(0xffffffffu, mean, m);
+            float m2o = __shfl_xor_sync(0xffffffffu, m2, m);
+            chan_equal(mean, m2, mo, m2o, n);
+            n = __fmul_rn(n, 2.0f);
+        }
+        __syncthreads();  // previous row's readers are done with s_mean/s_m2
+        if (lane == 0) {
+            s_mean[w] = mean;
+            s_m2[w] = m2;
+        }
+        __syncthreads();
+        // Merge warps in order 0..nw-1 (general Chan update, equal counts).
+        float gm = s_mean[0], gm2 = s_m2[0], gn = n;
+        for (int j = 1; j < nw; ++j) {
+            float mb = s_mean[j], m2b = s_m2[j];
+            float tot = __fadd_rn(gn, n);
+            float d = __fsub_rn(mb, gm);
+            gm = __fadd_rn(gm, __fmul_rn(d, __fdiv_rn(n, tot)));
+            gm2 = __fadd_rn(__fadd_rn(gm2, m2b), __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(gn, n), tot)));
+            gn = tot;
+        }
+        const float var = __fdiv_rn(gm2, static_cast<float>(cols));
+        const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+        Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c0 = (t + i * blockDim.x) * PV;
+            Pack<T> o;
+#pragma unroll
+            for (int e = 0; e < PV; ++e) {
+                float g = to_f(gamma[c0 + e]), b = to_f(beta[c0 + e]);
+                float z = __fmul_rn(__fsub_rn(v[i * PV + e], gm), rstd);
+                o.v[e] = from_f_tag(__fmaf_rn(z, g, b), static_cast<T*>(nullptr));
+            }
+            yr[t + i * blockDim.x] = o;
+        }
+    }
+}
+
+template <typename T, typename GT>
+__global__ void __launch_bounds__(256) k_layer_norm_generic(const T* __restrict__ x, const GT* __restrict__ gamma,
+                                                            const GT* __restrict__ beta, T* __restrict__ y,
+                                                            int64_t rows, int64_t cols, float eps) {
+    __shared__ float s_n[8], s_mean[8], s_m2[8];
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const T* xr = x + row * cols;
+        float n = 0.0f, mean = 0.0f, m2 = 0.0f;
+        for (int64_t c = t; c < cols; c += 256) {
+            float v = to_f(xr[c]);
+            n = __fadd_rn(n, 1.0f);
+            float d = __fsub_rn(v, mean);
+            mean = __fadd_rn(mean, __fdiv_rn(d, n));
+            m2 = __fmaf_rn(d, __fsub_rn(v, mean), m2);
+        }
+        // General Chan merge down a fixed tree (lane i absorbs lane i+m).
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1) {
+            float nb = __shfl_down_sync(0xffffffffu, n, m);
+            float mb = __shfl_down_sync(0xffffffffu, mean, m);
+            float m2b = __shfl_down_sync(0xffffffffu, m2, m);
+            if (lane < m && nb > 0.0f) {
+                float tot = __fadd_rn(n, nb);
+                float d = __fsub_rn(mb, mean);
+                mean = __fadd_rn(mean, __fmul_rn(d, __fdiv_rn(nb, tot)));
+                m2 = __fadd_rn(__fadd_rn(m2, m2b), __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(n, nb), tot)));
+                n = tot;
+            }
+        }
+        __syncthreads();
+        if (lane == 0) {
+            s_n[w] = n;
+            s_mean[w] = mean;
+            s_m2[w] = m2;
+        }
+        __syncthreads();
+        float gn = s_n[0], gm = s_mean[0], gm2 = s_m2[0];
+        for (int j = 1; j < 8; ++j) {
+            float nb = s_n[j];
+            if (nb <= 0.0f) continue;
+            float tot = __fadd_rn(gn, nb);
+            float d = __fsub_rn(s_mean[j], gm);
+            gm = __fadd_rn(gm, __fmul_rn(d, __fdiv_rn(nb, tot)));
+            gm2 = __fadd_rn(__fadd_rn(gm2, s_m2[j]), __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(gn, nb), tot)));
+            gn = tot;
+        }
+        const float var = __fdiv_rn(gm2, static_cast<float>(cols));
+        const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+        T* yr = y + row * cols;
+        for (int64_t c = t; c < cols; c += 256) {
+            float z = __fmul_rn(__fsub_rn(to_f(xr[c]), gm), rstd);
+            yr[c] = from_f_tag(__fmaf_rn(z, to_f(gamma[c]), to_f(beta[c])), static_cast<T*>(nullptr));
+        }
+    }
+}
+
+template <typename T, typename GT>
+qsml_status_t run_ln(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int64_t cols, float eps) {
+    constexpr int PV = Pack<T>::N;
+    int64_t grid = rows < 65535 * 16 ? rows : 65535 * 16;
+    if (cols % PV == 0 && aligned16(x) && aligned16(y) && cols <= INT32_MAX) {
+        const int64_t packs = cols / PV;
+        int nv = 0;
+        for (int cand : {1, 2, 4, 8}) {
+            if (packs % cand) continue;
+            int64_t th = packs / cand;
+            if (th % 32 == 0 && th <= 512) {
+                nv = cand;
+                break;
+            }
+        }
+        if (nv) {
+            const unsigned th = static_cast<unsigned>(packs / nv);
+            const int c = static_cast<int>(cols);
+            switch (nv) {
+                case 1: k_layer_norm_reg<T, GT, 1><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, g, b, y, rows, c, eps); break;
+                case 2: k_layer_norm_reg<T, GT, 2><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, g, b, y, rows, c, eps); break;
+                case 4: k_layer_norm_reg<T, GT, 4><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, g, b, y, rows, c, eps); break;
+                default: k_layer_norm_reg<T, GT, 8><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, g, b, y, rows, c, eps); break;
+            }
+            return after_launch(ctx, "k_layer_norm_reg");
+        }
+    }
+    k_layer_norm_generic<T, GT><<<static_cast<unsigned>(grid), 256, 0, ctx->stream>>>(x, g, b, y, rows, cols, eps);
+    return after_launch(ctx, "k_layer_norm_generic");
+}
+
+}  // namespace
+}  // namespace qsml
+
+using namespace qsml;
+
+extern "C" qsml_status_t qsml_layer_norm(qsml_ctx* handle, const qsml_tdesc* x, const qsml_tdesc* gamma,
+                                         const qsml_tdesc* beta, float eps, const qsml_tdesc* y) {
+    QSML_CTX(handle);
+    QSML_TRY_STATUS(check_desc(C_, x, "x"));
+    QSML_TRY_STATUS(check_desc(C_, gamma, "gamma"));
+    QSML_TRY_STATUS(check_desc(C_, beta, "beta"));
+    QSML_TRY_STATUS(check_desc(C_, y, "y"));
+    if (x->ndim < 1) return set_error(C_, QSML_E_SHAPE, "qsml_layer_norm: x needs at least one dim");
+    if (x->dtype != QSML_F32 && x->dtype != QSML_F16)
+        return set_error(C_, QSML_E_DTYPE, "qsml_layer_norm: x must be F32 or F16");
+    if (y->dtype != x->dtype) return set_error(C_, QSML_E_DTYPE, "qsml_layer_norm: y dtype must equal x dtype");
+    if (gamma->dtype != beta->dtype || (gamma->dtype != QSML_F32 && gamma->dtype != x->dtype))
+        return set_error(C_, QSML_E_DTYPE, "qsml_layer_norm: gamma/beta must be F32 or x's dtype");
+    if (!is_contiguous(x) || !is_contiguous(y) || !is_contiguous(gamma) || !is_contiguous(beta))
+        return set_error(C_, QSML_E_UNSUPPORTED, "qsml_layer_norm: x, y, gamma and beta must be contiguous");
+    const int64_t cols = x->shape[x->ndim - 1];
+    if (numel(gamma) != cols || numel(beta) != cols)
+        return set_error(C_, QSML_E_SHAPE, "qsml_layer_norm: gamma/beta must have the last dim's size");
+    if (y->ndim != x->ndim) return set_error(C_, QSML_E_SHAPE, "qsml_layer_norm: y shape must equal x shape");
+    for (int d = 0; d < x->ndim; ++d)
+        if (y->shape[d] != x->shape[d]) return set_error(C_, QSML_E_SHAPE, "qsml_layer_norm: y shape must equal x shape");
+    const int64_t n = numel(x);
+    if (n == 0) return QSML_OK;
+    const int64_t rows = n / cols;
+    if (x->dtype == QSML_F32)
+        return run_ln<float, float>(C_, static_cast<const float*>(x->data), static_cast<const float*>(gamma->data),
+                                    static_cast<const float*>(beta->data), static_cast<float*>(y->data), rows, cols, eps);
+    if (gamma->dtype == QSML_F32)
+        return run_ln<__half, float>(C_, static_cast<const __half*>(x->data), static_cast<const float*>(gamma->data),
+                                     static_cast<const float*>(beta->data), static_cast<__half*>(y->data), rows, cols, eps);
+    return run_ln<__half, __half>(C_, static_cast<const __half*>(x->data), static_cast<const __half*>(gamma->data),
+                                  static_cast<const __half*>(beta->data), static_cast<__half*>(y->data), rows, cols, eps);
+}

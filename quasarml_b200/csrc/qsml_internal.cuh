@@ -1,0 +1,115 @@
+// Internal declarations shared by the libqsml_cuda translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "qsml_cuda.h"
+
+namespace qsml {
+
+// ---------------------------------------------------------------------------
+// Caching allocator: size-binned blocks reused in the order of the context's
+// single stream.  Replaces one VMA allocation per tensor
+// (Backend/Vulkan/VulkanBackend.cpp:254-281 in the reference), which has no
+// pooling at all.
+// ---------------------------------------------------------------------------
+class CachingAllocator {
+public:
+    explicit CachingAllocator(int device) : device_(device) {}
+    ~CachingAllocator();
+    qsml_status_t alloc(size_t bytes, void** ptr, std::string* err);
+    qsml_status_t free(void* ptr, std::string* err);
+    void release_cached();
+    void stats(uint64_t* misses, uint64_t* hits, uint64_t* reserved, uint64_t* live);
+    static size_t round_size(size_t bytes);
+
+private:
+    int device_;
+    std::mutex mu_;
+    std::multimap<size_t, void*> free_;          // rounded size -> block
+    std::unordered_map<void*, size_t> live_;     // block -> rounded size
+    uint64_t misses_ = 0, hits_ = 0, reserved_ = 0, live_bytes_ = 0;
+    uint64_t malloc_calls_ = 0;
+};
+
+// Per-device execution context: what a reference Device owned through its
+// Backend (queue, allocator, kernel cache), on CUDA.
+struct Context {
+    int device = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    CachingAllocator* allocator = nullptr;
+    // Scratch space for multi-CTA reductions: partials + a self-resetting
+    // ticket counter.  Grown on demand, zero-initialised once.
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+    uint64_t launches = 0;
+    std::mutex err_mu;
+    std::string last_error;
+};
+
+// Error recording helpers ----------------------------------------------------
+qsml_status_t set_error(Context* ctx, qsml_status_t st, const std::string& msg);
+qsml_status_t check_cuda(Context* ctx, cudaError_t e, const char* what);
+// Checks the launch that was just enqueued and counts it.
+qsml_status_t after_launch(Context* ctx, const char* kernel);
+
+// Scratch of at least `bytes` (the first 256 bytes hold zeroed counters).
+qsml_status_t get_scratch(Context* ctx, size_t bytes, void** ptr);
+
+// Descriptor helpers ---------------------------------------------------------
+inline int dtype_size(int32_t dt) {
+    switch (dt) {
+        case QSML_F32: case QSML_I32: case QSML_U32: return 4;
+        case QSML_F16: case QSML_I16: case QSML_U16: return 2;
+        case QSML_I8: case QSML_U8: return 1;
+    }
+    return 0;
+}
+
+inline int64_t numel(const qsml_tdesc* d) {
+    int64_t n = 1;
+    for (int i = 0; i < d->ndim; ++i) n *= d->shape[i];
+    return n;
+}
+
+inline bool is_contiguous(const qsml_tdesc* d) {
+    int64_t s = 1;
+    for (int i = d->ndim - 1; i >= 0; --i) {
+        if (d->shape[i] != 1 && d->stride[i] != s) return false;
+        s *= d->shape[i];
+    }
+    return true;
+}
+
+// Validates ndim, shape and dtype; data may be null only when empty.
+qsml_status_t check_desc(Context* ctx, const qsml_tdesc* d, const char* name);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int kMaxDims = QSML_MAX_DIMS;
+
+}  // namespace qsml
+
+// Every entry point validates its context with this.
+#define QSML_CTX(ctx_)                                                   \
+    qsml::Context* C_ = reinterpret_cast<qsml::Context*>(ctx_);          \
+    if (!C_) return QSML_E_INVALID;                                      \
+    if (cudaSetDevice(C_->device) != cudaSuccess)                        \
+        return qsml::set_error(C_, QSML_E_CUDA, "cudaSetDevice failed");
+
+#define QSML_TRY_STATUS(expr)                \
+    do {                                     \
+        qsml_status_t st__ = (expr);         \
+        if (st__ != QSML_OK) return st__;    \
+    } while (0)

@@ -1,0 +1,429 @@
+// Reductions: sum / mean / max / min over one axis or over all elements.
+//
+// Reference: Ops/Reduction.cpp.  Full reductions there loop a one-element-
+// per-thread workgroup tree (or subgroup) shader until one value is left
+// (Reduction.cpp:213-281), allocating and zero-uploading a tensor per pass;
+// axis sums run one thread per output with a serial k loop
+// (Reduction.cpp:293-345); axis max/min are stubs (Reduction.cpp:366-382).
+//
+// Here the input is viewed as [outer, k, inner] (Reduction.cpp:310-312) and
+// one of three kernels runs, chosen from the shape alone:
+//   * k_reduce_seg   -- inner == 1 with few long rows, including the full
+//                       reduction (one row).  Each row is cut into fixed
+//                       chunks; a chunk is reduced by one CTA in a fixed
+//                       order and its partial stored; the CTA that completes
+//                       the last chunk of a row (atomic ticket per row)
+//                       combines that row's partials in chunk order.  One
+//                       launch, deterministic for a given shape whatever the
+//                       grid size.
+//   * k_reduce_rows  -- inner == 1 with many rows: one warp per row.
+//   * k_reduce_cols  -- inner > 1: lanes own 16-byte column vectors (loads
+//                       coalesced along inner), the CTA's warps split k into
+//                       contiguous slices, slices combine in warp order.
+// Accumulation is binary32 (binary16 inputs widen exactly); max/min use an
+// order-preserving integer key so the result is exact and order-free
+// (IEEE 754-2019 maximum/minimum: -0 < +0, NaN wins as 0x7fffffff).
+// mean = sum * (1.0f / (float)k), a reciprocal multiply like
+// Reduction.cpp:347-356; the reciprocal is rounded on the host.
+#include "qsml_internal.cuh"
+
+#include <climits>
+
+namespace qsml {
+namespace {
+
+constexpr int kRT = 256;             // threads of the segment kernel
+constexpr int kSegIters = 8;         // 16-byte packs per thread per chunk
+constexpr int kMaxSegments = 16384;  // ticket counters kept in scratch
+constexpr size_t kCounterBytes = kMaxSegments * sizeof(unsigned);
+
+template <typename T> struct alignas(16) Pack {
+    static constexpr int N = 16 / sizeof(T);
+    T v[N];
+};
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+__device__ __forceinline__ void from_f(float v, float* o) { *o = v; }
+__device__ __forceinline__ void from_f(float v, __half* o) { *o = __float2half_rn(v); }
+
+// Order-preserving key of a binary32: signed-integer order of the keys is
+// the IEEE total order of the values (so -0 < +0).
+__device__ __forceinline__ int fkey(float x) {
+    int b = __float_as_int(x);
+    return b ^ ((b >> 31) & 0x7fffffff);
+}
+__device__ __forceinline__ float unkey(int k) { return __int_as_float(k ^ ((k >> 31) & 0x7fffffff)); }
+__device__ __forceinline__ bool is_nan(float x) { return (__float_as_int(x) & 0x7fffffff) > 0x7f800000; }
+
+template <int OP> struct Red;
+template <> struct Red<QSML_RED_SUM> {
+    using V = float;
+    static __device__ __forceinline__ V ident() { return 0.0f; }
+    static __device__ __forceinline__ V lift(float x) { return x; }
+    static __device__ __forceinline__ V comb(V a, V b) { return __fadd_rn(a, b); }
+    static __device__ __forceinline__ float fin(V a, float) { return a; }
+    static __device__ __forceinline__ V shfl(V v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+};
+template <> struct Red<QSML_RED_MEAN> : Red<QSML_RED_SUM> {
+    static __device__ __forceinline__ float fin(V a, float scale) { return __fmul_rn(a, scale); }
+};
+template <> struct Red<QSML_RED_MAX> {
+    using V = int;
+    static __device__ __forceinline__ V ident() { return fkey(-INFINITY); }
+    static __device__ __forceinline__ V lift(float x) { return is_nan(x) ? INT_MAX : fkey(x); }
+    static __device__ __forceinline__ V comb(V a, V b) { return max(a, b); }
+    static __device__ __forceinline__ float fin(V a, float) { return unkey(a); }  // INT_MAX -> 0x7fffffff
+    static __device__ __forceinline__ V shfl(V v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+};
+template <> struct Red<QSML_RED_MIN> {
+    using V = int;
+    static __device__ __forceinline__ V ident() { return fkey(INFINITY); }
+    static __device__ __forceinline__ V lift(float x) { return is_nan(x) ? INT_MIN : fkey(x); }
+    static __device__ __forceinline__ V comb(V a, V b) { return min(a, b); }
+    static __device__ __forceinline__ float fin(V a, float) {
+        return a == INT_MIN ? __int_as_float(0x7fffffff) : unkey(a);
+    }
+    static __device__ __forceinline__ V shfl(V v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+};
+
+// Butterfly: every lane ends with the same bits (each step combines the same
+// two operands on both partner lanes, and the ops are commutative).
+template <int OP>
+__device__ __forceinline__ typename Red<OP>::V warp_reduce(typename Red<OP>::V v) {
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) v = Red<OP>::comb(v, Red<OP>::shfl(v, m));
+    return v;
+}
+
+// Block of kRT threads; result valid in every thread.
+template <int OP>
+__device__ __forceinline__ typename Red<OP>::V block_reduce(typename Red<OP>::V v) {
+    using R = Red<OP>;
+    __shared__ typename R::V sh[kRT / 32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    v = warp_reduce<OP>(v);
+    __syncthreads();  // sh may still be read by a previous call
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    typename R::V t = lane < kRT / 32 ? sh[lane] : R::ident();
+    return warp_reduce<OP>(t);
+}
+
+// ---------------------------------------------------------------------------
+// Segment kernel: x = [nseg rows, len] contiguous; one partial per chunk.
+// ---------------------------------------------------------------------------
+template <typename T, typename OT, int OP, bool VEC>
+__global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int64_t nseg, int64_t len,
+                                                    int64_t chunk, int64_t cps, OT* __restrict__ out,
+                                                    float scale, unsigned* __restrict__ counters,
+                                                    typename Red<OP>::V* __restrict__ partials) {
+    using R = Red<OP>;
+    using V = typename R::V;
+    constexpr int PV = Pack<T>::N;
+    __shared__ bool s_last;
+    const int t = threadIdx.x;
+    const int64_t total = nseg * cps;
+    for (int64_t c = blockIdx.x; c < total; c += gridDim.x) {
+        const int64_t s = c / cps, ci = c - s * cps;
+        const int64_t lo = ci * chunk;
+        const int64_t hi = lo + chunk < len ? lo + chunk : len;
+        const T* row = x + s * len;
+        V acc = R::ident();
+        if (VEC && hi - lo == chunk) {
+            const Pack<T>* p = reinterpret_cast<const Pack<T>*>(row + lo);
+            Pack<T> r[kSegIters];
+#pragma unroll
+            for (int i = 0; i < kSegIters; ++i) r[i] = p[i * kRT + t];
+#pragma unroll
+            for (int i = 0; i < kSegIters; ++i)
+#pragma unroll
+                for (int e = 0; e < PV; ++e) acc = R::comb(acc, R::lift(to_f(r[i].v[e])));
+        } else {
+            for (int64_t j = lo + t; j < hi; j += kRT) acc = R::comb(acc, R::lift(to_f(row[j])));
+        }
+        acc = block_reduce<OP>(acc);
+        if (t == 0) {
+            partials[c] = acc;
+            __threadfence();
+            unsigned ticket = atomicAdd(&counters[s], 1u);
+            s_last = ticket == static_cast<unsigned>(cps - 1);
+        }
+        __syncthreads();
+        if (s_last) {
+            // This CTA completed row s: combine its partials in chunk order.
+            __threadfence();
+            V a = R::ident();
+            for (int64_t j = t; j < cps; j += kRT) a = R::comb(a, __ldcg(&partials[s * cps + j]));
+            a = block_reduce<OP>(a);
+            if (t == 0) {
+                from_f(R::fin(a, scale), &out[s]);
+                counters[s] = 0;  // ready for the next launch on this stream
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Row kernel: one warp per row of `len` contiguous elements.
+// ---------------------------------------------------------------------------
+template <typename T, typename OT, int OP, bool VEC>
+__global__ void __launch_bounds__(256) k_reduce_rows(const T* __restrict__ x, int64_t rows, int64_t len,
+                                                     OT* __restrict__ out, float scale) {
+    using R = Red<OP>;
+    using V = typename R::V;
+    constexpr int PV = Pack<T>::N;
+    constexpr int U = 4;
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const T* row = x + r * len;
+        V acc = R::ident();
+        if (VEC) {
+            const Pack<T>* p = reinterpret_cast<const Pack<T>*>(row);
+            const int64_t np = len / PV;
+            int64_t i = lane;
+            for (; i + (U - 1) * 32 < np; i += U * 32) {
+                Pack<T> v[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) v[u] = p[i + u * 32];
+#pragma unroll
+                for (int u = 0; u < U; ++u)
+#pragma unroll
+                    for (int e = 0; e < PV; ++e) acc = R::comb(acc, R::lift(to_f(v[u].v[e])));
+            }
+            for (; i < np; i += 32) {
+                Pack<T> v = p[i];
+#pragma unroll
+                for (int e = 0; e < PV; ++e) acc = R::comb(acc, R::lift(to_f(v.v[e])));
+            }
+        } else {
+            for (int64_t j = lane; j < len; j += 32) acc = R::comb(acc, R::lift(to_f(row[j])));
+        }
+        acc = warp_reduce<OP>(acc);
+        if (lane == 0) from_f(R::fin(acc, scale), &out[r]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Column kernel: out[o, i] = reduce_k x[o, k, i]; block (32, W).
+// ---------------------------------------------------------------------------
+template <typename T, typename OT, int OP, bool VEC>
+__global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k, int64_t inner,
+                              int64_t tiles_per_o, OT* __restrict__ out, float scale) {
+    using R = Red<OP>;
+    using V = typename R::V;
+    constexpr int PV = VEC ? Pack<T>::N : 1;
+    constexpr int U = 8;
+    extern __shared__ unsigned char smem_raw[];
+    V* red = reinterpret_cast<V*>(smem_raw);
+    const int lane = threadIdx.x, w = threadIdx.y, W = blockDim.y;
+    const int64_t tile = blockIdx.x;
+    const int64_t o = tile / tiles_per_o;
+    const int64_t c0 = (tile - o * tiles_per_o) * (32 * PV) + static_cast<int64_t>(lane) * PV;
+    const int64_t kper = (k + W - 1) / W;
+    const int64_t k0 = w * kper;
+    const int64_t k1 = k0 + kper < k ? k0 + kper : k;
+    V acc[PV];
+#pragma unroll
+    for (int e = 0; e < PV; ++e) acc[e] = R::ident();
+    if (o < outer && c0 < inner) {
+        const T* base = x + (o * k) * inner + c0;
+        int64_t kk = k0;
+        if (VEC) {
+            for (; kk + U <= k1; kk += U) {
+                Pack<T> v[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) v[u] = *reinterpret_cast<const Pack<T>*>(base + (kk + u) * inner);
+#pragma unroll
+                for (int u = 0; u < U; ++u)
+#pragma unroll
+                    for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v[u].v[e])));
+            }
+            for (; kk < k1; ++kk) {
+                Pack<T> v = *reinterpret_cast<const Pack<T>*>(base + kk * inner);
+#pragma unroll
+                for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v.v[e])));
+            }
+        } else {
+            for (; kk + U <= k1; kk += U) {
+                T v[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) v[u] = base[(kk + u) * inner];
+#pragma unroll
+                for (int u = 0; u < U; ++u) acc[0] = R::comb(acc[0], R::lift(to_f(v[u])));
+            }
+            for (; kk < k1; ++kk) acc[0] = R::comb(acc[0], R::lift(to_f(base[kk * inner])));
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < PV; ++e) red[(w * 32 + lane) * PV + e] = acc[e];
+    __syncthreads();
+    // Combine the W slices in slice order, one output column per thread.
+    const int tid = w * 32 + lane;
+    for (int col = tid; col < 32 * PV; col += 32 * W) {
+        V a = red[col];
+        for (int ww = 1; ww < W; ++ww) a = R::comb(a, red[ww * 32 * PV + col]);
+        const int64_t ci = (tile - o * tiles_per_o) * (32 * PV) + col;
+        if (o < outer && ci < inner) from_f(R::fin(a, scale), &out[o * inner + ci]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host dispatch
+// ---------------------------------------------------------------------------
+template <typename T, typename OT, int OP>
+qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int64_t inner, OT* out) {
+    using V = typename Red<OP>::V;
+    constexpr int PV = Pack<T>::N;
+    const float scale = 1.0f / static_cast<float>(k);
+    const bool x_al = aligned16(x);
+    if (inner == 1 && (outer == 1 || (outer < 592 && k >= 8192))) {
+        // Segment kernel.
+        if (outer > kMaxSegments) return set_error(ctx, QSML_E_UNSUPPORTED, "too many segments");
+        const bool vec = x_al && (k * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+        const int64_t chunk = static_cast<int64_t>(kRT) * kSegIters * (vec ? PV : 1);
+        const int64_t cps = (k + chunk - 1) / chunk;
+        const int64_t total = outer * cps;
+        void* scratch = nullptr;
+        QSML_TRY_STATUS(get_scratch(ctx, kCounterBytes + static_cast<size_t>(total) * sizeof(V), &scratch));
+        unsigned* counters = static_cast<unsigned*>(scratch);
+        V* partials = reinterpret_cast<V*>(static_cast<char*>(scratch) + kCounterBytes);
+        int64_t grid = static_cast<int64_t>(ctx->num_sms) * 8;
+        if (grid > total) grid = total;
+        if (vec)
+            k_reduce_seg<T, OT, OP, true><<<static_cast<unsigned>(grid), kRT, 0, ctx->stream>>>(
+                x, outer, k, chunk, cps, out, scale, counters, partials);
+        else
+            k_reduce_seg<T, OT, OP, false><<<static_cast<unsigned>(grid), kRT, 0, ctx->stream>>>(
+                x, outer, k, chunk, cps, out, scale, counters, partials);
+        return after_launch(ctx, "k_reduce_seg");
+    }
+    if (inner == 1) {
+        const bool vec = x_al && (k * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+        int64_t grid = (outer + 7) / 8;  // 8 warps per CTA
+        int64_t cap = static_cast<int64_t>(ctx->num_sms) * 32;
+        if (grid > cap) grid = cap;
+        if (vec)
+            k_reduce_rows<T, OT, OP, true><<<static_cast<unsigned>(grid), 256, 0, ctx->stream>>>(x, outer, k, out, scale);
+        else
+            k_reduce_rows<T, OT, OP, false><<<static_cast<unsigned>(grid), 256, 0, ctx->stream>>>(x, outer, k, out, scale);
+        return after_launch(ctx, "k_reduce_rows");
+    }
+    const bool vec = x_al && (inner * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+    const int pv = vec ? PV : 1;
+    const int64_t tiles_per_o = (inner + 32 * pv - 1) / (32 * pv);
+    const int64_t tiles = tiles_per_o * outer;
+    int64_t W = (8192 + tiles - 1) / tiles;
+    if (W > 16) W = 16;
+    if (W > k) W = k;
+    if (W < 1) W = 1;
+    dim3 block(32, static_cast<unsigned>(W));
+    size_t smem = static_cast<size_t>(W) * 32 * pv * sizeof(V);
+    if (tiles > INT32_MAX) return set_error(ctx, QSML_E_UNSUPPORTED, "reduction too large");
+    if (vec)
+        k_reduce_cols<T, OT, OP, true><<<static_cast<unsigned>(tiles), block, smem, ctx->stream>>>(
+            x, outer, k, inner, tiles_per_o, out, scale);
+    else
+        k_reduce_cols<T, OT, OP, false><<<static_cast<unsigned>(tiles), block, smem, ctx->stream>>>(
+            x, outer, k, inner, tiles_per_o, out, scale);
+    return after_launch(ctx, "k_reduce_cols");
+}
+
+template <typename T, typename OT>
+qsml_status_t reduce_op(Context* ctx, int op, const T* x, int64_t outer, int64_t k, int64_t inner, OT* out) {
+    switch (op) {
+        case QSML_RED_SUM: return run_reduce<T, OT, QSML_RED_SUM>(ctx, x, outer, k, inner, out);
+        case QSML_RED_MEAN: return run_reduce<T, OT, QSML_RED_MEAN>(ctx, x, outer, k, inner, out);
+        case QSML_RED_MAX: return run_reduce<T, OT, QSML_RED_MAX>(ctx, x, outer, k, inner, out);
+        case QSML_RED_MIN: return run_reduce<T, OT, QSML_RED_MIN>(ctx, x, outer, k, inner, out);
+    }
+    return set_error(ctx, QSML_E_INVALID, "qsml_reduce: unknown op");
+}
+
+template <typename T>
+__global__ void k_fill_value(T* p, T v, int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        p[i] = v;
+}
+
+}  // namespace
+}  // namespace qsml
+
+using namespace qsml;
+
+extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_tdesc* a, int32_t axis,
+                                     int32_t keepdims, const qsml_tdesc* out) {
+    QSML_CTX(handle);
+    QSML_TRY_STATUS(check_desc(C_, a, "a"));
+    QSML_TRY_STATUS(check_desc(C_, out, "out"));
+    if (op < QSML_RED_SUM || op > QSML_RED_MIN) return set_error(C_, QSML_E_INVALID, "qsml_reduce: unknown op");
+    if (a->dtype != QSML_F32 && a->dtype != QSML_F16)
+        return set_error(C_, QSML_E_DTYPE, "qsml_reduce: input must be F32 or F16");
+    if (out->dtype != a->dtype && out->dtype != QSML_F32)
+        return set_error(C_, QSML_E_DTYPE, "qsml_reduce: out dtype must equal the input's or be F32");
+    if (!is_contiguous(a))
+        return set_error(C_, QSML_E_UNSUPPORTED, "qsml_reduce: input must be contiguous (materialise it with qsml_gather)");
+    if (!is_contiguous(out)) return set_error(C_, QSML_E_SHAPE, "qsml_reduce: out must be contiguous");
+
+    int64_t outer = 1, k = 1, inner = 1;
+    int64_t expect[QSML_MAX_DIMS];
+    int en = 0;
+    if (axis == QSML_AXIS_ALL) {
+        k = numel(a);
+        if (numel(out) != 1) return set_error(C_, QSML_E_SHAPE, "qsml_reduce: full reduction needs a 1-element out");
+    } else {
+        int ax = axis < 0 ? axis + a->ndim : axis;
+        if (ax < 0 || ax >= a->ndim) return set_error(C_, QSML_E_SHAPE, "qsml_reduce: invalid axis");
+        for (int i = 0; i < ax; ++i) outer *= a->shape[i];
+        k = a->shape[ax];
+        for (int i = ax + 1; i < a->ndim; ++i) inner *= a->shape[i];
+        for (int i = 0; i < a->ndim; ++i) {
+            if (i == ax) {
+                if (keepdims) expect[en++] = 1;
+            } else {
+                expect[en++] = a->shape[i];
+            }
+        }
+        // The reference returns shape [1] when every dim is reduced away
+        // (Reduction.cpp:297-305).
+        bool ok = true;
+        if (en == 0) {
+            ok = numel(out) == 1 && out->ndim <= 1;
+        } else {
+            ok = out->ndim == en;
+            for (int i = 0; ok && i < en; ++i) ok = out->shape[i] == expect[i];
+        }
+        if (!ok) return set_error(C_, QSML_E_SHAPE, "qsml_reduce: out shape does not match the reduced shape");
+    }
+    const int64_t nout = outer * inner;
+    if (nout == 0) return QSML_OK;
+    if (k == 0) {
+        if (op == QSML_RED_MAX || op == QSML_RED_MIN)
+            return set_error(C_, QSML_E_SHAPE, "qsml_reduce: max/min of an empty axis");
+        // sum = 0; mean = 0 * (1/0) = NaN, like the reference's arithmetic.
+        float v = 0.0f;
+        if (op != QSML_RED_SUM) {
+            const uint32_t nan_bits = 0x7fffffffu;
+            std::memcpy(&v, &nan_bits, 4);
+        }
+        int64_t blocks = (nout + 255) / 256;
+        if (blocks > 4096) blocks = 4096;
+        if (out->dtype == QSML_F32)
+            k_fill_value<float><<<static_cast<unsigned>(blocks), 256, 0, C_->stream>>>(static_cast<float*>(out->data), v, nout);
+        else
+            k_fill_value<__half><<<static_cast<unsigned>(blocks), 256, 0, C_->stream>>>(static_cast<__half*>(out->data),
+                                                                                         __float2half_rn(v), nout);
+        return after_launch(C_, "k_fill_value");
+    }
+    if (a->dtype == QSML_F32)
+        return reduce_op<float, float>(C_, op, static_cast<const float*>(a->data), outer, k, inner,
+                                       static_cast<float*>(out->data));
+    if (out->dtype == QSML_F16)
+        return reduce_op<__half, __half>(C_, op, static_cast<const __half*>(a->data), outer, k, inner,
+                                         static_cast<__half*>(out->data));
+    return reduce_op<__half, float>(C_, op, static_cast<const __half*>(a->data), outer, k, inner,
+                                    static_cast<float*>(out->data));
+}

@@ -1,0 +1,115 @@
+"""GPU matmul (through the C ABI).
+
+fp32 (QSML_MM_FP32_FFMA): the kernel keeps the reference's per-output fma
+chain in k order, so small cases are bit-identical to the oracle's chain;
+at 8192^3 sampled entries are checked against binary64 dot products with
+max|err| / max|ref| <= 1e-4.
+fp16 inputs, fp32 accumulate: max|err| / max|ref| <= 1e-2 against binary64
+products of the same fp16 inputs (observed errors are far smaller).
+"""
+import numpy as np
+import pytest
+
+from helpers import assert_bits_equal, d, dev, empty, host
+from quasarml_b200 import abi, datagen
+
+pytestmark = pytest.mark.gpu
+
+
+def mm(ctx, a, b, out_dtype=np.float32, precision=abi.MM_AUTO):
+    ta, tb = dev(a), dev(b)
+    shape = a.shape[:-1] + (b.shape[-1],)
+    c = empty(shape, out_dtype)
+    ctx.matmul(d(ta), d(tb), d(c), precision)
+    return host(c)
+
+
+@pytest.mark.parametrize("mkn", [(1, 1, 1), (2, 3, 4), (129, 65, 257), (256, 256, 256), (300, 1000, 70),
+                                 (64, 8, 128), (5, 300, 3)])
+def test_fp32_bitexact_small(ctx, orc, mkn):
+    M, K, N = mkn
+    a = datagen.uniform(41, (M, K), -1, 1)
+    b = datagen.uniform(42, (K, N), -1, 1)
+    assert_bits_equal(mm(ctx, a, b, precision=abi.MM_FP32_FFMA), orc.matmul_fma(a, b), str(mkn))
+
+
+def test_reference_known_answer(ctx):
+    """_test_qsml_functionality.cpp:135-143: ones[2,3] @ ones[3,4] = 3."""
+    c = mm(ctx, np.ones((2, 3), np.float32), np.ones((3, 4), np.float32))
+    assert c.shape == (2, 4) and np.all(c == 3.0)
+
+
+def _sample_check(C, A, B, tol, n=256, seed=0):
+    rng = np.random.default_rng(seed)
+    ii = rng.integers(0, A.shape[-2], n)
+    jj = rng.integers(0, B.shape[-1], n)
+    ref = np.einsum("ik,ki->i", A[ii].astype(np.float64), B[:, jj].astype(np.float64))
+    got = C[ii, jj].astype(np.float64)
+    err = np.max(np.abs(got - ref)) / np.max(np.abs(ref))
+    assert err <= tol, err
+
+
+def test_fp32_8192(ctx):
+    s = 1.0 / np.sqrt(8192.0)
+    A = datagen.uniform(datagen.SEEDS["mm_A"], (8192, 8192), -s, s)
+    B = datagen.uniform(datagen.SEEDS["mm_B"], (8192, 8192), -s, s)
+    C = mm(ctx, A, B, precision=abi.MM_FP32_FFMA)
+    _sample_check(C, A, B, 1e-4)
+
+
+def test_fp16_8192(ctx):
+    s = 1.0 / np.sqrt(8192.0)
+    A = datagen.uniform(datagen.SEEDS["mm_A"], (8192, 8192), -s, s).astype(np.float16)
+    B = datagen.uniform(datagen.SEEDS["mm_B"], (8192, 8192), -s, s).astype(np.float16)
+    C = mm(ctx, A, B, precision=abi.MM_FP16_F32ACC)
+    _sample_check(C, A, B, 1e-2)
+    _sample_check(C, A, B, 1e-4, seed=1)  # fp32 accumulation keeps it far tighter
+
+
+def test_batched(ctx, orc):
+    s = 1.0 / np.sqrt(1024.0)
+    A = datagen.uniform(datagen.SEEDS["mm_Ab"], (32, 2048, 1024), -s, s)
+    B = datagen.uniform(datagen.SEEDS["mm_Bb"], (32, 1024, 2048), -s, s)
+    C = mm(ctx, A, B, precision=abi.MM_FP32_FFMA)
+    for bi in (0, 13, 31):
+        _sample_check(C[bi], A[bi], B[bi], 1e-4, n=64, seed=bi)
+    Ch = mm(ctx, A.astype(np.float16), B.astype(np.float16), precision=abi.MM_FP16_F32ACC)
+    for bi in (0, 31):
+        _sample_check(Ch[bi], A[bi].astype(np.float16), B[bi].astype(np.float16), 1e-2, n=64, seed=bi)
+    # small batched case, bit-exact per batch entry
+    a = datagen.uniform(43, (3, 33, 17), -1, 1)
+    b = datagen.uniform(44, (3, 17, 9), -1, 1)
+    assert_bits_equal(mm(ctx, a, b), orc.matmul_fma(a, b), "batched small")
+
+
+@pytest.mark.parametrize("mkn", [(128, 64, 128), (256, 512, 384), (100, 72, 200), (1, 64, 64), (512, 1024, 256)])
+@pytest.mark.parametrize("out", [np.float32, np.float16])
+def test_fp16_small(ctx, orc, mkn, out):
+    M, K, N = mkn
+    a = datagen.uniform(45, (M, K), -1, 1).astype(np.float16)
+    b = datagen.uniform(46, (K, N), -1, 1).astype(np.float16)
+    c = mm(ctx, a, b, out_dtype=out, precision=abi.MM_FP16_F32ACC).astype(np.float64)
+    ref = orc.matmul_f64(a, b)
+    err = np.max(np.abs(c - ref)) / np.max(np.abs(ref))
+    assert err <= (1e-5 if out == np.float32 else 1e-3), err
+
+
+def test_shared_b_batch_stride_zero(ctx, orc):
+    a = datagen.uniform(47, (4, 16, 8), -1, 1)
+    b = datagen.uniform(48, (8, 12), -1, 1)
+    ta, tb = dev(a), dev(b)
+    bview = abi.make_desc(tb.data_ptr(), abi.F32, (4, 8, 12), (0, 12, 1))
+    c = empty((4, 16, 12), np.float32)
+    ctx.matmul(d(ta), bview, d(c))
+    ref = orc.matmul_fma(a, np.broadcast_to(b, (4, 8, 12)).copy())
+    assert_bits_equal(host(c), ref, "stride-0 B")
+
+
+def test_errors(ctx):
+    with pytest.raises(abi.QsmlError) as e:
+        mm(ctx, np.ones((2, 3), np.float32), np.ones((4, 5), np.float32))
+    assert e.value.status == abi.E_SHAPE
+    with pytest.raises(abi.QsmlError) as e:
+        ctx.matmul(d(dev(np.ones((2, 3), np.float32))), d(dev(np.ones((3, 2), np.float16))),
+                   d(empty((2, 2), np.float32)))
+    assert e.value.status == abi.E_DTYPE

@@ -1,0 +1,137 @@
+"""GPU parity of the reductions (through the C ABI) against the oracle.
+
+Tolerances: sum/mean |gpu - exact| <= 1e-5 * sum|x| (binary64 "exact" sum of
+the same inputs; sum|x| is the scale of any summation's rounding error), plus
+one output rounding when the output is binary16.  max/min are order-free and
+bit-exact.  Results must also be bit-identical run to run.
+"""
+import numpy as np
+import pytest
+
+from helpers import d, dev, empty, host
+from quasarml_b200 import abi, datagen
+
+pytestmark = pytest.mark.gpu
+
+OPS = {"sum": abi.RED_SUM, "mean": abi.RED_MEAN, "max": abi.RED_MAX, "min": abi.RED_MIN}
+
+
+def gpu_reduce(ctx, op, t, axis, keepdims=False, out_dtype=None):
+    shape = abi.reduced_shape(tuple(t.shape), axis, keepdims)
+    import torch
+    odt = out_dtype or t.dtype
+    out = torch.empty(shape, dtype=odt, device="cuda")
+    ctx.reduce(op, d(t), abi.AXIS_ALL if axis is None else axis, keepdims, d(out))
+    return host(out)
+
+
+def check(orc, name, x_np, axis, g, out_is_half):
+    o32, o64, ab = orc.reduce(OPS[name], x_np, axis)
+    g = g.astype(np.float64).reshape(o64.shape)
+    if name in ("max", "min"):
+        ref = o32.astype(np.float16) if out_is_half else o32
+        assert np.array_equal(g, ref.astype(np.float64)), name
+        return
+    tol = 1e-5 * ab + 1e-30
+    if out_is_half:
+        tol = tol + np.abs(o64) * 2.0 ** -11
+    err = np.abs(g - o64)
+    worst = float(np.max(err / tol))
+    assert worst <= 1.0, f"{name} axis={axis}: error {worst:.3g} x tolerance"
+
+
+@pytest.fixture(scope="module")
+def x3():
+    return datagen.normal(datagen.SEEDS["red_X"], (64, 512, 1024), 0.0, 1.0)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16"])
+@pytest.mark.parametrize("axis", [None, 0, 1, 2])
+def test_workload_64x512x1024(ctx, orc, x3, dtype, axis):
+    """X[64,512,1024] ~ N(0,1): sum/mean/max/min over each axis and all."""
+    x = x3 if dtype == "f32" else x3.astype(np.float16)
+    t = dev(x)
+    for name, op in OPS.items():
+        g = gpu_reduce(ctx, op, t, axis)
+        check(orc, name, x, axis, g, dtype == "f16")
+        g2 = gpu_reduce(ctx, op, t, axis)
+        assert np.array_equal(g.view(np.uint8), g2.view(np.uint8)), "not deterministic"
+
+
+def test_f16_input_f32_output(ctx, orc, x3):
+    import torch
+    x = x3[:8].astype(np.float16)
+    t = dev(x)
+    for axis in (None, 1, 2):
+        for name, op in OPS.items():
+            g = gpu_reduce(ctx, op, t, axis, out_dtype=torch.float32)
+            check(orc, name, x, axis, g, False)
+
+
+ODD = [((10,), None), ((10,), 0), ((4, 100003), 1), ((4, 100003), -1), ((33, 1001), 1), ((7, 13, 5), 1),
+       ((7, 13, 5), 0), ((7, 13, 5), 2), ((1, 33), 0), ((5,), None), ((3, 70000), None), ((2, 3, 4, 5), 2),
+       ((300, 8192), 1), ((8192, 3), 0), ((1, 1 << 20), 1), ((1000, 17), 1)]
+
+
+@pytest.mark.parametrize("shape,axis", ODD)
+@pytest.mark.parametrize("dtype", [np.float32, np.float16])
+def test_odd_shapes(ctx, orc, shape, axis, dtype):
+    x = datagen.normal(21, shape, 0.3, 1.5).astype(dtype)
+    t = dev(x)
+    for name, op in OPS.items():
+        check(orc, name, x, axis, gpu_reduce(ctx, op, t, axis), dtype == np.float16)
+
+
+def test_keepdims_and_shapes(ctx):
+    x = dev(np.ones((4, 5, 6), np.float32))
+    assert gpu_reduce(ctx, abi.RED_SUM, x, 1, keepdims=True).shape == (4, 1, 6)
+    assert gpu_reduce(ctx, abi.RED_SUM, x, -1).shape == (4, 5)
+    assert np.all(gpu_reduce(ctx, abi.RED_SUM, x, 2) == 6.0)
+    y = dev(np.arange(1, 11, dtype=np.float32))
+    # Reduction.cpp:297-305: reducing the only axis gives shape [1]
+    assert gpu_reduce(ctx, abi.RED_MEAN, y, 0).shape == (1,)
+    assert gpu_reduce(ctx, abi.RED_MEAN, y, 0)[0] == np.float32(5.5)
+    with pytest.raises(abi.QsmlError) as e:
+        ctx.reduce(abi.RED_SUM, d(x), 3, False, d(empty((4, 5), np.float32)))
+    assert e.value.status == abi.E_SHAPE
+
+
+def test_reference_known_answers(ctx):
+    """_test_comprehensive.cpp:170-191: sum/mean/max/min of 1..10."""
+    y = dev(np.arange(1, 11, dtype=np.float32))
+    for op, want in ((abi.RED_SUM, 55.0), (abi.RED_MEAN, 5.5), (abi.RED_MAX, 10.0), (abi.RED_MIN, 1.0)):
+        assert abs(float(gpu_reduce(ctx, op, y, None)[0]) - want) < 1e-3
+
+
+def test_nan_and_signed_zero(ctx):
+    x = np.zeros(100000, np.float32)
+    x[::2] = -0.0
+    t = dev(x)
+    assert not np.signbit(gpu_reduce(ctx, abi.RED_MAX, t, None)[0])
+    assert np.signbit(gpu_reduce(ctx, abi.RED_MIN, t, None)[0])
+    x = datagen.normal(5, (3, 50000), 0, 1)
+    x[1, 777] = np.nan
+    t = dev(x)
+    for op in OPS.values():
+        r = gpu_reduce(ctx, op, t, 1)
+        assert np.isnan(r[1]) and not np.isnan(r[0]) and not np.isnan(r[2])
+    for op in (abi.RED_MAX, abi.RED_MIN):
+        r = gpu_reduce(ctx, op, t, None)
+        assert r.view(np.uint32)[0] == 0x7FFFFFFF  # canonical NaN
+    inf = dev(np.float32([-np.inf, -np.inf, -np.inf]))
+    assert gpu_reduce(ctx, abi.RED_MAX, inf, None)[0] == -np.inf
+
+
+def test_empty_axis(ctx):
+    x = empty((3, 0), np.float32)
+    assert np.all(gpu_reduce(ctx, abi.RED_SUM, x, 1) == 0)
+    assert np.all(np.isnan(gpu_reduce(ctx, abi.RED_MEAN, x, 1)))
+    with pytest.raises(abi.QsmlError):
+        gpu_reduce(ctx, abi.RED_MAX, x, 1)
+
+
+def test_non_contiguous_input_rejected(ctx):
+    x = dev(np.ones((8, 8), np.float32)).t()
+    with pytest.raises(abi.QsmlError) as e:
+        gpu_reduce(ctx, abi.RED_SUM, x, 0)
+    assert e.value.status == abi.E_UNSUPPORTED
