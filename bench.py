@@ -160,12 +160,25 @@ class Dist:
 # ---------------------------------------------------------------------------
 # Workloads
 # ---------------------------------------------------------------------------
+class Workload:
+    """A step = compute() (the kernel calls, captured once in a CUDA graph)
+    followed by exchange() (collectives between ranks, issued eagerly)."""
+    calls = []
+
+    def exchange(self):
+        pass
+
+    def step(self):
+        self.compute()
+        self.exchange()
+
+
 def _t(x):
     import torch
     return torch.from_numpy(np.ascontiguousarray(x)).cuda()
 
 
-class ReduceWorkload:
+class ReduceWorkload(Workload):
     """sum/mean/max/min over axis 0, 1, 2, all of X[64,512,1024], fp32 + fp16."""
     name = "reductions X[64,512,1024] fp32 and fp16: sum/mean/max/min over axis 0, 1, 2 and all"
     SHAPE = (64, 512, 1024)
@@ -226,23 +239,26 @@ class ReduceWorkload:
         self.h2d_bytes = sum(x.numel() * 4 for x in self.x32) + sum(x.numel() * 2 for x in self.x16)
         self.d2h_bytes = sum(c[6].numel() * c[6].element_size() for c in self.calls)
 
-    def step(self, events=None):
+    def compute(self, calls=None):
         ctx = self.ctx
-        for i, (op, xd, axis, od, fam, nb, out) in enumerate(self.calls):
-            if events is not None:
-                events[i][0].record()
+        for (op, xd, axis, od, fam, nb, out) in (self.calls if calls is None else calls):
             ctx.reduce(op, xd, axis, False, od)
-            if events is not None:
-                events[i][1].record()
-        if self.dist.pg:
-            dist = self.dist.pg
-            for (dt, grp), buf in self.flat.items():
-                op = {"sum": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN}[grp]
-                dist.all_reduce(buf, op=op)
-            # means were summed over ranks: divide by the number of ranks
-            for (op, xd, axis, od, fam, nb, out) in self.calls:
-                if op == self.abi.RED_MEAN and axis in (self.abi.AXIS_ALL, 0):
-                    ctx.binary_scalar(self.abi.OP_MUL, od, 1.0 / self.dist.world, od)
+
+    def exchange(self):
+        if not self.dist.pg:
+            return
+        dist = self.dist.pg
+        for (dt, grp), buf in self.flat.items():
+            op = {"sum": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN}[grp]
+            dist.all_reduce(buf, op=op)
+        # means were summed over ranks: divide by the number of ranks
+        for (op, xd, axis, od, fam, nb, out) in self.calls:
+            if op == self.abi.RED_MEAN and axis in (self.abi.AXIS_ALL, 0):
+                self.ctx.binary_scalar(self.abi.OP_MUL, od, 1.0 / self.dist.world, od)
+
+    def step(self):
+        self.compute()
+        self.exchange()
 
     # End-to-end: host -> device copies of X, the reductions, results back.
     def e2e_setup(self):
@@ -263,7 +279,7 @@ class ReduceWorkload:
             ctx.d2h(h.data_ptr(), out.data_ptr(), out.numel() * out.element_size(), sync=False)
 
 
-class ChainWorkload:
+class ChainWorkload(Workload):
     """relu(pow((A+B)*B - A, 2) / D), A[4096,4096], B[1,4096], D[4096,1]."""
     name = "elementwise chain relu(pow((A+B)*B - A, 2.0) / D), A[4096,4096], B[1,4096], D[4096,1] fp32"
 
@@ -291,9 +307,9 @@ class ChainWorkload:
         self.units_per_step = sum(c[5] for c in self.calls)
         self.unit = "GB/s"
 
-    def step(self, events=None):
+    def compute(self, calls=None):
         ctx = self.ctx
-        for kind, op, a, b, out, _ in self.calls:
+        for kind, op, a, b, out, _ in (self.calls if calls is None else calls):
             if kind == "bin":
                 ctx.binary(op, a, b, out)
             elif kind == "scal":
@@ -302,7 +318,7 @@ class ChainWorkload:
                 ctx.unary(op, a, out)
 
 
-class GatherWorkload:
+class GatherWorkload(Workload):
     name = "strided gather X[5::3, 1::2] and X.T[::4, :] of X[8192,8192] int32 and fp32"
 
     def __init__(self, ctx, dist: Dist):
@@ -323,12 +339,12 @@ class GatherWorkload:
         self.units_per_step = sum(c[2] for c in self.calls)
         self.unit = "GB/s"
 
-    def step(self, events=None):
-        for v, o, _ in self.calls:
+    def compute(self, calls=None):
+        for v, o, _ in (self.calls if calls is None else calls):
             self.ctx.gather(v, o)
 
 
-class LayerNormWorkload:
+class LayerNormWorkload(Workload):
     name = "layer norm X[16384,4096] fp32 and fp16, gamma/beta fp32, eps 1e-5"
 
     def __init__(self, ctx, dist: Dist):
@@ -347,12 +363,12 @@ class LayerNormWorkload:
         self.units_per_step = sum(c[4] for c in self.calls)
         self.unit = "GB/s"
 
-    def step(self, events=None):
-        for x, g, b, y, _ in self.calls:
+    def compute(self, calls=None):
+        for x, g, b, y, _ in (self.calls if calls is None else calls):
             self.ctx.layer_norm(x, g, b, 1e-5, y)
 
 
-class MatmulWorkload:
+class MatmulWorkload(Workload):
     def __init__(self, ctx, dist: Dist, dtype: str, batched: bool):
         import torch
         from quasarml_b200 import abi, datagen
@@ -381,83 +397,125 @@ class MatmulWorkload:
         self.units_per_step = self.flops
         self.unit = "TFLOP/s"
 
-    def step(self, events=None):
+    def compute(self, calls=None):
         self.ctx.matmul(self.a, self.b, self.c, self.prec)
 
 
 # ---------------------------------------------------------------------------
 # Timing
 # ---------------------------------------------------------------------------
-def time_steps(wl, dist: Dist, steps: int, warmup: int, per_call_events: bool = False, sampler=None):
+def capture(fn, stream):
+    """Captures fn() (which enqueues on `stream`) into a CUDA graph."""
     import torch
-    for _ in range(warmup):
-        wl.step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    ev = None
-    if per_call_events:
-        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in wl.calls] for _ in range(steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches0 = wl.ctx.launch_count()
-    if sampler:
-        sampler.__enter__()
-    start.record()
-    for s in range(steps):
-        wl.step(ev[s] if ev else None)
-    end.record()
-    torch.cuda.synchronize()
-    if sampler:
-        sampler.__exit__()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    return g
+
+
+def time_steps(wl, dist: Dist, stream, steps: int, warmup: int, sampler=None, use_graph=True):
+    """Times `steps` steps on `stream` with CUDA events; returns the max over
+    ranks (ms), the kernel launches counted by the library and the graph."""
+    import torch
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            wl.step()
+        torch.cuda.synchronize()
+        g = capture(wl.compute, stream) if use_graph else None
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        per_step = None
+        if g is not None:
+            # launches per step: the library counts each launch it enqueues
+            l0 = wl.ctx.launch_count()
+            wl.compute()
+            per_step = wl.ctx.launch_count() - l0
+            torch.cuda.synchronize()
+        launches0 = wl.ctx.launch_count()
+        if sampler:
+            sampler.__enter__()
+        start.record(stream)
+        for _ in range(steps):
+            if g is not None:
+                g.replay()
+                wl.exchange()
+            else:
+                wl.step()
+        end.record(stream)
+        torch.cuda.synchronize()
+        if sampler:
+            sampler.__exit__()
     launches = wl.ctx.launch_count() - launches0
+    if g is not None:
+        launches += per_step * steps
     ms = start.elapsed_time(end)
     dist.barrier()
-    ms_max = dist.max(ms)
-    per_call = None
-    if ev:
-        per_call = [[a.elapsed_time(b) for (a, b) in row] for row in ev]
-    return ms_max, launches, per_call
+    return dist.max(ms), launches, g
 
 
-def time_e2e(wl, dist: Dist, steps: int, warmup: int):
+def family_times(wl, stream, reps: int = 5):
+    """Average device duration of one launch of each kernel family: the
+    family's calls of one step captured alone in a CUDA graph and replayed."""
     import torch
-    wl.e2e_setup()
-    for _ in range(warmup):
-        wl.e2e_step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps):
-        wl.e2e_step()
-    end.record()
-    torch.cuda.synchronize()
+    fams = {}
+    for c in wl.calls:
+        fams.setdefault(c[4], []).append(c)
+    out = {}
+    with torch.cuda.stream(stream):
+        for fam, calls in fams.items():
+            g = capture(lambda: wl.compute(calls), stream)
+            g.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(reps):
+                g.replay()
+            b.record(stream)
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / reps
+            out[fam] = {"launches": len(calls), "ms": ms, "bytes": sum(c[5] for c in calls)}
+            del g
+    return out
+
+
+def time_e2e(wl, dist: Dist, stream, steps: int, warmup: int):
+    import torch
+    with torch.cuda.stream(stream):
+        wl.e2e_setup()
+        for _ in range(warmup):
+            wl.e2e_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(steps):
+            wl.e2e_step()
+        end.record(stream)
+        torch.cuda.synchronize()
     return dist.max(start.elapsed_time(end))
 
 
-def roofline_from_calls(wl, per_call, hbm_peak, peak_kind):
-    fam_t, fam_b, fam_n = {}, {}, {}
-    for row in per_call:
-        for (call, ms) in zip(wl.calls, row):
-            fam, nb = call[4], call[5]
-            fam_t[fam] = fam_t.get(fam, 0.0) + ms
-            fam_b[fam] = fam_b.get(fam, 0.0) + nb
-            fam_n[fam] = fam_n.get(fam, 0) + 1
-    dom = max(fam_t, key=fam_t.get)
-    total = sum(fam_t.values())
-    achieved = fam_b[dom] / (fam_t[dom] / 1e3) / 1e9
+def roofline_from_families(fam, hbm_peak, peak_kind):
+    total = sum(f["ms"] for f in fam.values())
+    dom = max(fam, key=lambda k: fam[k]["ms"])
+    f = fam[dom]
+    per_launch_ms = f["ms"] / f["launches"]
+    achieved = f["bytes"] / (f["ms"] / 1e3) / 1e9
     traffic = ncu_traffic().get(dom)
     return {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,
-            "traffic": traffic, "algorithmic_bytes_per_launch": round(fam_b[dom] / fam_n[dom]),
-            "avg_launch_us": round(fam_t[dom] / fam_n[dom] * 1e3, 2),
-            "share_of_step": round(fam_t[dom] / total, 3),
-            "families": {f: {"share": round(fam_t[f] / total, 3),
-                             "gbs": round(fam_b[f] / (fam_t[f] / 1e3) / 1e9, 1),
-                             "frac": round(fam_b[f] / (fam_t[f] / 1e3) / 1e9 / hbm_peak, 4),
-                             "launches": fam_n[f]} for f in fam_t}}
+            "traffic": traffic, "algorithmic_bytes_per_launch": round(f["bytes"] / f["launches"]),
+            "avg_launch_us": round(per_launch_ms * 1e3, 2),
+            "share_of_step": round(f["ms"] / total, 3),
+            "timing": "CUDA events around replays of a graph holding one step's launches of this kernel",
+            "families": {k: {"share": round(v["ms"] / total, 3),
+                             "gbs": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1),
+                             "frac": round(v["bytes"] / (v["ms"] / 1e3) / 1e9 / hbm_peak, 4),
+                             "avg_launch_us": round(v["ms"] / v["launches"] * 1e3, 2),
+                             "launches": v["launches"]} for k, v in fam.items()}}
 
 
 # ---------------------------------------------------------------------------
@@ -564,7 +622,10 @@ def main():
     from quasarml_b200 import abi
     torch.cuda.set_device(dist.local)
     dist.init("nccl")
-    ctx = abi.Context(dist.local)
+    # All library work goes to one non-default stream so it can be captured.
+    stream = torch.cuda.Stream()
+    ctx = abi.Context(dist.local, use_torch_stream=False)
+    ctx.set_stream(stream.cuda_stream)
     hbm, tf_burst, tf_sus, peak_kind = peaks()
 
     wl = {"reduce": lambda: ReduceWorkload(ctx, dist), "chain": lambda: ChainWorkload(ctx, dist),
@@ -573,14 +634,10 @@ def main():
           "matmul_f32": lambda: MatmulWorkload(ctx, dist, "f32", False)}[args.workload]()
 
     sampler = ClockSampler(dist.local)
-    ms, launches, per_call = time_steps(wl, dist, args.steps, args.warmup,
-                                        per_call_events=hasattr(wl, "calls") and args.workload == "reduce",
-                                        sampler=sampler)
+    ms, launches, graph = time_steps(wl, dist, stream, args.steps, args.warmup, sampler=sampler)
+    del graph
     units = wl.units_per_step * args.steps * dist.world
-    if wl.unit == "GB/s":
-        value = units / (ms / 1e3) / 1e9
-    else:
-        value = units / (ms / 1e3) / 1e12
+    value = units / (ms / 1e3) / (1e9 if wl.unit == "GB/s" else 1e12)
 
     line = {"metric": METRIC, "value": round(value, 2), "unit": wl.unit, "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
@@ -590,13 +647,15 @@ def main():
             "config": {"workload": wl.name, "parallelism": f"dp{dist.world}",
                        "l2": "inputs larger than L2: 8 distinct X per dtype per step (1.5 GB)"
                        if args.workload == "reduce" else "inputs larger than L2",
-                       "calls_per_step": len(getattr(wl, "calls", [])) or 1},
+                       "calls_per_step": len(getattr(wl, "calls", [])) or 1,
+                       "launch": "each step's kernel calls replayed from one CUDA graph; "
+                                 "NCCL all-reduces (N>1) issued eagerly after it"},
             "gpu_launches": launches, "clocks": sampler.summary()}
-    if per_call:
-        line["roofline"] = roofline_from_calls(wl, per_call, hbm, peak_kind)
+    if args.workload == "reduce":
+        line["roofline"] = roofline_from_families(family_times(wl, stream), hbm, peak_kind)
     if hasattr(wl, "e2e_step"):
         e_steps = max(2, min(args.steps, 5))
-        ems = time_e2e(wl, dist, e_steps, 1)
+        ems = time_e2e(wl, dist, stream, e_steps, 1)
         ev = wl.units_per_step * e_steps * dist.world / (ems / 1e3) / 1e9
         line["e2e"] = {"value": round(ev, 2), "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes,
                        "d2h_bytes_per_step": wl.d2h_bytes, "ms_per_step": round(ems / e_steps, 3),
@@ -614,13 +673,15 @@ def main():
                             ("batched_matmul_f16", lambda: MatmulWorkload(ctx, dist, "f16", True), 5)):
             try:
                 w = mk()
-                ms_x, l_x, _ = time_steps(w, dist, st, 3)
+                ms_x, l_x, g = time_steps(w, dist, stream, st, 3)
+                del g
                 v = w.units_per_step * st / (ms_x / 1e3) / (1e9 if w.unit == "GB/s" else 1e12)
                 peak = hbm if w.unit == "GB/s" else tf_burst
                 extras[key] = {"workload": w.name, "value": round(v, 2), "unit": w.unit,
                                "frac_of_peak": round(v / peak, 4), "peak": peak,
                                "ms_per_step": round(ms_x / st, 3), "launches_per_step": l_x // st}
                 del w
+                torch.cuda.synchronize()
                 torch.cuda.empty_cache()
             except Exception as e:  # report, do not hide
                 extras[key] = {"error": repr(e)[:300]}

@@ -128,10 +128,12 @@ QSML_API qsml_status_t qsml_init(int32_t device, qsml_ctx** ctx);
  * Device::~Device (QuasarML/src/Core/Device.cpp:19-23). */
 QSML_API qsml_status_t qsml_destroy(qsml_ctx* ctx);
 
-/* Makes the context enqueue on `stream` (a cudaStream_t; NULL restores the
- * context's own stream).  Pending work on the previous stream is waited for
- * first, so cached blocks stay stream-ordered.  No reference counterpart
- * (the reference owns one Vulkan queue per device). */
+/* Makes the context enqueue on `stream`, a cudaStream_t used as given: NULL
+ * is the CUDA legacy default stream (stream 0).  The context's own stream
+ * is what qsml_get_stream returns on a fresh context.  Pending work on the
+ * previous stream is waited for first, so cached blocks stay
+ * stream-ordered.  No reference counterpart (the reference owns one Vulkan
+ * queue per device). */
 QSML_API qsml_status_t qsml_set_stream(qsml_ctx* ctx, void* stream);
 QSML_API qsml_status_t qsml_get_stream(qsml_ctx* ctx, void** stream);
 

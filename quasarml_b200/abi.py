@@ -180,6 +180,8 @@ class Context:
             pass
 
     def set_stream(self, stream_ptr: int) -> None:
+        """Enqueue on this cudaStream_t (0 = the legacy default stream, which is
+        what torch reports for its default stream)."""
         self.check(self.lib.qsml_set_stream(self.h, ctypes.c_void_p(int(stream_ptr)) if stream_ptr else None))
 
     def stream(self) -> int:

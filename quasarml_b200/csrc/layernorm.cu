@@ -2,11 +2,12 @@
 // with the biased (population) variance.  The reference snapshot has no
 // layer norm; this is a new op of the same API family.
 //
-// k_layer_norm_reg: one CTA per row, the row held in registers (16-byte
-// loads), so x is read from HBM exactly once and y written once.  Each
+// k_layer_norm_reg: persistent CTAs, one row at a time held in registers
+// (16-byte loads) with the next row already in flight, so x is read from HBM
+// exactly once and y written once; gamma/beta stay in registers.  Each
 // thread's values give a local (mean, M2); warps merge them with Chan's
-// pairwise update (equal counts, written symmetrically so partner lanes
-// hold identical bits), then the warps' results merge in warp order.
+// pairwise update (equal counts, written symmetrically so partner lanes hold
+// identical bits), then the warps' results merge the same way.
 // k_layer_norm_generic: any width or alignment, Welford over global memory
 // (reads x twice).
 #include "qsml_internal.cuh"
@@ -32,27 +33,70 @@ __device__ __forceinline__ void chan_equal(float& mean, float& m2, float mo, flo
     m2 = __fadd_rn(__fadd_rn(m2, m2o), __fmul_rn(dd, __fmul_rn(n, 0.5f)));
 }
 
+// PV consecutive gamma/beta values as binary32, with 16-byte loads.
+template <typename GT, int PV>
+__device__ __forceinline__ void load_params(const GT* p, float* out) {
+    if constexpr (sizeof(GT) == 4) {
+#pragma unroll
+        for (int i = 0; i < PV; i += 4) {
+            float4 v = *reinterpret_cast<const float4*>(p + i);
+            out[i] = v.x; out[i + 1] = v.y; out[i + 2] = v.z; out[i + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < PV; i += 8) {
+            Pack<__half> v = *reinterpret_cast<const Pack<__half>*>(p + i);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) out[i + e] = __half2float(v.v[e]);
+        }
+    }
+}
+
+// Persistent CTAs: gamma/beta of the thread's columns stay in registers and
+// the next row's x is loaded before the current row is reduced, so each CTA
+// always has a row in flight.
 template <typename T, typename GT, int NV>
-__global__ void k_layer_norm_reg(const T* __restrict__ x, const GT* __restrict__ gamma, const GT* __restrict__ beta,
-                                 T* __restrict__ y, int64_t rows, int cols, float eps) {
+__global__ void __launch_bounds__(256) k_layer_norm_reg(const T* __restrict__ x, const GT* __restrict__ gamma,
+                                                        const GT* __restrict__ beta, T* __restrict__ y,
+                                                        int64_t rows, int cols, float eps) {
     constexpr int PV = Pack<T>::N;
     constexpr int E = NV * PV;  // elements per thread
-    __shared__ float s_mean[32], s_m2[32];
+    __shared__ float s_mean[32], s_m2[32], s_stat[2];
     const int t = threadIdx.x, lane = t & 31, w = t >> 5, nw = blockDim.x >> 5;
-    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int th = blockDim.x;
+    const bool pow2 = (nw & (nw - 1)) == 0;
+    float g[E], b[E];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c0 = (t + i * th) * PV;
+        load_params<GT, PV>(gamma + c0, g + i * PV);
+        load_params<GT, PV>(beta + c0, b + i * PV);
+    }
+    Pack<T> cur[NV], nxt[NV];
+    int64_t row = blockIdx.x;
+    if (row < rows) {
         const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + row * cols);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) cur[i] = xr[t + i * th];
+    }
+    for (; row < rows; row += gridDim.x) {
+        const int64_t nrow = row + gridDim.x;
+        if (nrow < rows) {
+            const Pack<T>* xn = reinterpret_cast<const Pack<T>*>(x + nrow * cols);
+#pragma unroll
+            for (int i = 0; i < NV; ++i) nxt[i] = xn[t + i * th];
+        }
         float v[E];
 #pragma unroll
-        for (int i = 0; i < NV; ++i) {
-            Pack<T> p = xr[t + i * blockDim.x];
+        for (int i = 0; i < NV; ++i)
 #pragma unroll
-            for (int e = 0; e < PV; ++e) v[i * PV + e] = to_f(p.v[e]);
-        }
-        // Thread-local statistics (two passes over registers).
+            for (int e = 0; e < PV; ++e) v[i * PV + e] = to_f(cur[i].v[e]);
+        // Thread-local statistics (two passes over registers; E is a power
+        // of two, so the multiply by 1/E is exact).
         float s = 0.0f;
 #pragma unroll
         for (int i = 0; i < E; ++i) s = __fadd_rn(s, v[i]);
-        float mean = __fdiv_rn(s, static_cast<float>(E));
+        float mean = __fmul_rn(s, 1.0f / static_cast<float>(E));
         float m2 = 0.0f;
 #pragma unroll
         for (int i = 0; i < E; ++i) {
@@ -68,37 +112,59 @@ __global__ void k_layer_norm_reg(const T* __restrict__ x, const GT* __restrict__
             chan_equal(mean, m2, mo, m2o, n);
             n = __fmul_rn(n, 2.0f);
         }
-        __syncthreads();  // previous row's readers are done with s_mean/s_m2
         if (lane == 0) {
             s_mean[w] = mean;
             s_m2[w] = m2;
         }
         __syncthreads();
-        // Merge warps in order 0..nw-1 (general Chan update, equal counts).
-        float gm = s_mean[0], gm2 = s_m2[0], gn = n;
-        for (int j = 1; j < nw; ++j) {
-            float mb = s_mean[j], m2b = s_m2[j];
-            float tot = __fadd_rn(gn, n);
-            float d = __fsub_rn(mb, gm);
-            gm = __fadd_rn(gm, __fmul_rn(d, __fdiv_rn(n, tot)));
-            gm2 = __fadd_rn(__fadd_rn(gm2, m2b), __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(gn, n), tot)));
-            gn = tot;
+        if (w == 0) {
+            float gm = lane < nw ? s_mean[lane] : 0.0f, gm2 = lane < nw ? s_m2[lane] : 0.0f;
+            if (pow2) {
+                // equal counts again: butterfly inside aligned groups of nw lanes
+                float gn = n;
+                for (int m = 1; m < nw; m <<= 1) {
+                    float mo = __shfl_xor_sync(0xffffffffu, gm, m);
+                    float m2o = __shfl_xor_sync(0xffffffffu, gm2, m);
+                    chan_equal(gm, gm2, mo, m2o, gn);
+                    gn = __fmul_rn(gn, 2.0f);
+                }
+            } else if (lane == 0) {
+                float gn = n;
+                for (int j = 1; j < nw; ++j) {
+                    float tot = __fadd_rn(gn, n);
+                    float d = __fsub_rn(s_mean[j], gm);
+                    gm = __fadd_rn(gm, __fmul_rn(d, __fdiv_rn(n, tot)));
+                    gm2 = __fadd_rn(__fadd_rn(gm2, s_m2[j]),
+                                    __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(gn, n), tot)));
+                    gn = tot;
+                }
+            }
+            if (lane == 0) {
+                s_stat[0] = gm;
+                s_stat[1] = gm2;
+            }
         }
-        const float var = __fdiv_rn(gm2, static_cast<float>(cols));
+        __syncthreads();
+        const float gm = s_stat[0];
+        const float var = __fdiv_rn(s_stat[1], static_cast<float>(cols));
         const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
         Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
-            const int c0 = (t + i * blockDim.x) * PV;
             Pack<T> o;
 #pragma unroll
             for (int e = 0; e < PV; ++e) {
-                float g = to_f(gamma[c0 + e]), b = to_f(beta[c0 + e]);
-                float z = __fmul_rn(__fsub_rn(v[i * PV + e], gm), rstd);
-                o.v[e] = from_f_tag(__fmaf_rn(z, g, b), static_cast<T*>(nullptr));
+                const int k = i * PV + e;
+                float z = __fmul_rn(__fsub_rn(v[k], gm), rstd);
+                o.v[e] = from_f_tag(__fmaf_rn(z, g[k], b[k]), static_cast<T*>(nullptr));
             }
-            yr[t + i * blockDim.x] = o;
+            yr[t + i * th] = o;
         }
+#pragma unroll
+        for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
+        // s_mean/s_m2/s_stat are rewritten next row only after every thread
+        // has passed this barrier.
+        __syncthreads();
     }
 }
 
@@ -159,17 +225,42 @@ __global__ void __launch_bounds__(256) k_layer_norm_generic(const T* __restrict_
     }
 }
 
+template <typename T, typename GT, int NV>
+qsml_status_t launch_reg(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int cols,
+                         float eps, unsigned th) {
+    // Resident CTAs per SM for this block size, queried once per kernel
+    // variant and block size (so later calls, graph capture included, make
+    // no runtime query).
+    static std::mutex mu;
+    static std::map<unsigned, int> per_sm_cache;
+    int per_sm = 0;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = per_sm_cache.find(th);
+        if (it == per_sm_cache.end()) {
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_layer_norm_reg<T, GT, NV>, static_cast<int>(th), 0);
+            if (per_sm < 1) per_sm = 1;
+            per_sm_cache[th] = per_sm;
+        } else {
+            per_sm = it->second;
+        }
+    }
+    int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
+    if (grid > rows) grid = rows;
+    k_layer_norm_reg<T, GT, NV><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, g, b, y, rows, cols, eps);
+    return after_launch(ctx, "k_layer_norm_reg");
+}
+
 template <typename T, typename GT>
 qsml_status_t run_ln(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int64_t cols, float eps) {
     constexpr int PV = Pack<T>::N;
-    int64_t grid = rows < 65535 * 16 ? rows : 65535 * 16;
-    if (cols % PV == 0 && aligned16(x) && aligned16(y) && cols <= INT32_MAX) {
+    if (cols % PV == 0 && aligned16(x) && aligned16(y) && aligned16(g) && aligned16(b) && cols <= INT32_MAX) {
         const int64_t packs = cols / PV;
         int nv = 0;
         for (int cand : {1, 2, 4, 8}) {
             if (packs % cand) continue;
             int64_t th = packs / cand;
-            if (th % 32 == 0 && th <= 512) {
+            if (th % 32 == 0 && th <= 256) {
                 nv = cand;
                 break;
             }
@@ -178,14 +269,14 @@ qsml_status_t run_ln(Context* ctx, const T* x, const GT* g, const GT* b, T* y, i
             const unsigned th = static_cast<unsigned>(packs / nv);
             const int c = static_cast<int>(cols);
             switch (nv) {
-                case 1: k_layer_norm_reg<T, GT, 1><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, g, b, y, rows, c, eps); break;
-                case 2: k_layer_norm_reg<T, GT, 2><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, g, b, y, rows, c, eps); break;
-                case 4: k_layer_norm_reg<T, GT, 4><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, g, b, y, rows, c, eps); break;
-                default: k_layer_norm_reg<T, GT, 8><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, g, b, y, rows, c, eps); break;
+                case 1: return launch_reg<T, GT, 1>(ctx, x, g, b, y, rows, c, eps, th);
+                case 2: return launch_reg<T, GT, 2>(ctx, x, g, b, y, rows, c, eps, th);
+                case 4: return launch_reg<T, GT, 4>(ctx, x, g, b, y, rows, c, eps, th);
+                default: return launch_reg<T, GT, 8>(ctx, x, g, b, y, rows, c, eps, th);
             }
-            return after_launch(ctx, "k_layer_norm_reg");
         }
     }
+    int64_t grid = rows < 65535 * 16 ? rows : 65535 * 16;
     k_layer_norm_generic<T, GT><<<static_cast<unsigned>(grid), 256, 0, ctx->stream>>>(x, g, b, y, rows, cols, eps);
     return after_launch(ctx, "k_layer_norm_generic");
 }

@@ -9,13 +9,13 @@
 // Here the input is viewed as [outer, k, inner] (Reduction.cpp:310-312) and
 // one of three kernels runs, chosen from the shape alone:
 //   * k_reduce_seg   -- inner == 1 with few long rows, including the full
-//                       reduction (one row).  Each row is cut into fixed
-//                       chunks; a chunk is reduced by one CTA in a fixed
-//                       order and its partial stored; the CTA that completes
-//                       the last chunk of a row (atomic ticket per row)
-//                       combines that row's partials in chunk order.  One
-//                       launch, deterministic for a given shape whatever the
-//                       grid size.
+//                       reduction (one row).  Each row is cut into a number
+//                       of contiguous slices fixed by the shape; a slice is
+//                       reduced by one CTA in a fixed order and its partial
+//                       stored; the CTA that takes the last ticket of a row
+//                       (atomic counter per row) combines that row's
+//                       partials in slice order.  One launch, deterministic
+//                       for a given shape whatever the grid size.
 //   * k_reduce_rows  -- inner == 1 with many rows: one warp per row.
 //   * k_reduce_cols  -- inner > 1: lanes own 16-byte column vectors (loads
 //                       coalesced along inner), the CTA's warps split k into
@@ -33,7 +33,9 @@ namespace qsml {
 namespace {
 
 constexpr int kRT = 256;             // threads of the segment kernel
-constexpr int kSegIters = 8;         // 16-byte packs per thread per chunk
+constexpr int kSegIters = 8;         // 16-byte loads in flight per thread
+constexpr int64_t kSegSlots = 1184;  // slices per launch (148 SMs x 8 CTAs), a constant
+constexpr int64_t kSegMinSlice = 4096;  // elements: short rows use fewer slices
 constexpr int kMaxSegments = 16384;  // ticket counters kept in scratch
 constexpr size_t kCounterBytes = kMaxSegments * sizeof(unsigned);
 
@@ -111,50 +113,66 @@ __device__ __forceinline__ typename Red<OP>::V block_reduce(typename Red<OP>::V 
 }
 
 // ---------------------------------------------------------------------------
-// Segment kernel: x = [nseg rows, len] contiguous; one partial per chunk.
+// Segment kernel: x = [nseg rows, len] contiguous.  Each row is split into
+// P contiguous slices (P depends on the shape only); work unit (s, j) reduces
+// slice j of row s with thread-strided 16-byte loads, kSegIters in flight per
+// thread, in a fixed order, then one block reduction gives partial (s, j).
+// The unit that takes the row's last ticket combines its P partials in slice
+// order.  The result depends on the shape alone, not on the grid size.
 // ---------------------------------------------------------------------------
 template <typename T, typename OT, int OP, bool VEC>
 __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int64_t nseg, int64_t len,
-                                                    int64_t chunk, int64_t cps, OT* __restrict__ out,
-                                                    float scale, unsigned* __restrict__ counters,
+                                                    int64_t P, OT* __restrict__ out, float scale,
+                                                    unsigned* __restrict__ counters,
                                                     typename Red<OP>::V* __restrict__ partials) {
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
     __shared__ bool s_last;
     const int t = threadIdx.x;
-    const int64_t total = nseg * cps;
-    for (int64_t c = blockIdx.x; c < total; c += gridDim.x) {
-        const int64_t s = c / cps, ci = c - s * cps;
-        const int64_t lo = ci * chunk;
-        const int64_t hi = lo + chunk < len ? lo + chunk : len;
+    const int64_t units = nseg * P;
+    for (int64_t w = blockIdx.x; w < units; w += gridDim.x) {
+        const int64_t s = w / P, j = w - s * P;
         const T* row = x + s * len;
         V acc = R::ident();
-        if (VEC && hi - lo == chunk) {
-            const Pack<T>* p = reinterpret_cast<const Pack<T>*>(row + lo);
-            Pack<T> r[kSegIters];
+        if (VEC) {
+            const int64_t npk = len / PV;
+            const int64_t lo = j * npk / P, hi = (j + 1) * npk / P;
+            const Pack<T>* p = reinterpret_cast<const Pack<T>*>(row);
+            int64_t q = lo + t;
+            for (; q + (kSegIters - 1) * kRT < hi; q += kSegIters * kRT) {
+                Pack<T> r[kSegIters];
 #pragma unroll
-            for (int i = 0; i < kSegIters; ++i) r[i] = p[i * kRT + t];
+                for (int i = 0; i < kSegIters; ++i) r[i] = p[q + i * kRT];
 #pragma unroll
-            for (int i = 0; i < kSegIters; ++i)
+                for (int i = 0; i < kSegIters; ++i)
 #pragma unroll
-                for (int e = 0; e < PV; ++e) acc = R::comb(acc, R::lift(to_f(r[i].v[e])));
+                    for (int e = 0; e < PV; ++e) acc = R::comb(acc, R::lift(to_f(r[i].v[e])));
+            }
+            for (; q < hi; q += kRT) {
+                Pack<T> r = p[q];
+#pragma unroll
+                for (int e = 0; e < PV; ++e) acc = R::comb(acc, R::lift(to_f(r.v[e])));
+            }
+            // elements past the last whole pack belong to the last slice
+            if (j == P - 1 && t < len - npk * PV) acc = R::comb(acc, R::lift(to_f(row[npk * PV + t])));
         } else {
-            for (int64_t j = lo + t; j < hi; j += kRT) acc = R::comb(acc, R::lift(to_f(row[j])));
+            const int64_t lo = j * len / P, hi = (j + 1) * len / P;
+            for (int64_t q = lo + t; q < hi; q += kRT) acc = R::comb(acc, R::lift(to_f(row[q])));
         }
         acc = block_reduce<OP>(acc);
         if (t == 0) {
-            partials[c] = acc;
+            partials[w] = acc;
             __threadfence();
             unsigned ticket = atomicAdd(&counters[s], 1u);
-            s_last = ticket == static_cast<unsigned>(cps - 1);
+            s_last = ticket == static_cast<unsigned>(P - 1);
         }
         __syncthreads();
         if (s_last) {
-            // This CTA completed row s: combine its partials in chunk order.
+            // This unit completed row s: combine its partials in slice order.
             __threadfence();
             V a = R::ident();
-            for (int64_t j = t; j < cps; j += kRT) a = R::comb(a, __ldcg(&partials[s * cps + j]));
+            for (int64_t i = t; i < P; i += kRT) a = R::comb(a, __ldcg(&partials[s * P + i]));
             a = block_reduce<OP>(a);
             if (t == 0) {
                 from_f(R::fin(a, scale), &out[s]);
@@ -282,22 +300,26 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
     if (inner == 1 && (outer == 1 || (outer < 592 && k >= 8192))) {
         // Segment kernel.
         if (outer > kMaxSegments) return set_error(ctx, QSML_E_UNSUPPORTED, "too many segments");
-        const bool vec = x_al && (k * static_cast<int64_t>(sizeof(T))) % 16 == 0;
-        const int64_t chunk = static_cast<int64_t>(kRT) * kSegIters * (vec ? PV : 1);
-        const int64_t cps = (k + chunk - 1) / chunk;
-        const int64_t total = outer * cps;
+        // One row may end in a partial pack (handled in-kernel); several rows
+        // need every row start 16-byte aligned.
+        const bool vec = x_al && (outer == 1 || (k * static_cast<int64_t>(sizeof(T))) % 16 == 0);
+        int64_t P = kSegSlots / outer;
+        const int64_t by_size = (k + kSegMinSlice - 1) / kSegMinSlice;
+        if (P > by_size) P = by_size;
+        if (P < 1) P = 1;
+        const int64_t units = outer * P;
         void* scratch = nullptr;
-        QSML_TRY_STATUS(get_scratch(ctx, kCounterBytes + static_cast<size_t>(total) * sizeof(V), &scratch));
+        QSML_TRY_STATUS(get_scratch(ctx, kCounterBytes + static_cast<size_t>(units) * sizeof(V), &scratch));
         unsigned* counters = static_cast<unsigned*>(scratch);
         V* partials = reinterpret_cast<V*>(static_cast<char*>(scratch) + kCounterBytes);
         int64_t grid = static_cast<int64_t>(ctx->num_sms) * 8;
-        if (grid > total) grid = total;
+        if (grid > units) grid = units;
         if (vec)
             k_reduce_seg<T, OT, OP, true><<<static_cast<unsigned>(grid), kRT, 0, ctx->stream>>>(
-                x, outer, k, chunk, cps, out, scale, counters, partials);
+                x, outer, k, P, out, scale, counters, partials);
         else
             k_reduce_seg<T, OT, OP, false><<<static_cast<unsigned>(grid), kRT, 0, ctx->stream>>>(
-                x, outer, k, chunk, cps, out, scale, counters, partials);
+                x, outer, k, P, out, scale, counters, partials);
         return after_launch(ctx, "k_reduce_seg");
     }
     if (inner == 1) {

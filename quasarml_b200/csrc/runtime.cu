@@ -264,7 +264,10 @@ qsml_status_t qsml_destroy(qsml_ctx* handle) {
 
 qsml_status_t qsml_set_stream(qsml_ctx* handle, void* stream) {
     QSML_CTX(handle);
-    cudaStream_t s = stream ? reinterpret_cast<cudaStream_t>(stream) : C_->own_stream;
+    // NULL is the CUDA legacy default stream (what a framework reports as
+    // stream 0); the context's own stream is available from qsml_get_stream
+    // on a fresh context.
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (s == C_->stream) return QSML_OK;
     QSML_TRY_STATUS(qsml::check_cuda(C_, cudaStreamSynchronize(C_->stream), "qsml_set_stream"));
     C_->stream = s;
