@@ -597,6 +597,56 @@ def run_reference(args, dist: Dist):
     print(json.dumps(line), flush=True)
 
 
+def run_single(which: str, reps: int = 3):
+    """One kernel of the workloads, `reps` launches on full-size inputs (for
+    ncu: the launch to capture is then the 2nd or 3rd)."""
+    import torch
+    from quasarml_b200 import abi, datagen
+    torch.cuda.set_device(0)
+    ctx = abi.Context(0)
+    d = abi.desc_of
+    if which.startswith("reduce"):
+        x = _t(datagen.normal(datagen.SEEDS["red_X"], (64, 512, 1024), 0.0, 1.0))
+        if which.endswith("f16"):
+            x = x.half()
+        axis = {"reduce_all": None, "reduce_all_f16": None, "reduce_axis0": 0, "reduce_axis1": 1,
+                "reduce_axis2": 2}[which]
+        out = torch.empty(abi.reduced_shape(tuple(x.shape), axis, False), dtype=x.dtype, device="cuda")
+        for _ in range(reps):
+            ctx.reduce(abi.RED_SUM, d(x), abi.AXIS_ALL if axis is None else axis, False, d(out))
+    elif which == "chain_add":
+        A = _t(datagen.uniform(1, (4096, 4096), -1, 1))
+        B = _t(datagen.uniform(2, (1, 4096), -1, 1))
+        out = torch.empty_like(A)
+        for _ in range(reps):
+            ctx.binary(abi.OP_ADD, d(A), d(B), d(out))
+    elif which.startswith("gather"):
+        X = _t(datagen.iota_i32((8192, 8192)))
+        if which == "gather_t":
+            v, out = abi.make_desc(X.data_ptr(), abi.I32, (2048, 8192), (4, 8192)), torch.empty((2048, 8192), dtype=torch.int32, device="cuda")
+        else:
+            v = abi.make_desc(X.data_ptr() + (5 * 8192 + 1) * 4, abi.I32, (2729, 4096), (3 * 8192, 2))
+            out = torch.empty((2729, 4096), dtype=torch.int32, device="cuda")
+        for _ in range(reps):
+            ctx.gather(v, d(out))
+    elif which == "layernorm":
+        X = _t(datagen.normal(10, (16384, 4096), 0.5, 2.0))
+        g = _t(datagen.normal(11, (4096,), 1.0, 0.1))
+        b = _t(datagen.normal(12, (4096,), 0.0, 0.1))
+        Y = torch.empty_like(X)
+        for _ in range(reps):
+            ctx.layer_norm(d(X), d(g), d(b), 1e-5, d(Y))
+    elif which == "matmul_f16":
+        s = 1.0 / np.sqrt(8192.0)
+        A = _t(datagen.uniform(6, (8192, 8192), -s, s)).half()
+        B = _t(datagen.uniform(7, (8192, 8192), -s, s)).half()
+        C = torch.empty((8192, 8192), device="cuda")
+        for _ in range(reps):
+            ctx.matmul(d(A), d(B), d(C), abi.MM_FP16_F32ACC)
+    torch.cuda.synchronize()
+    ctx.close()
+
+
 # ---------------------------------------------------------------------------
 # Main
 # ---------------------------------------------------------------------------
@@ -610,8 +660,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="reduce",
                     choices=["reduce", "chain", "gather", "layernorm", "matmul_f16", "matmul_f32"])
+    ap.add_argument("--single", default=None,
+                    choices=["reduce_all", "reduce_axis0", "reduce_axis1", "reduce_axis2", "reduce_all_f16",
+                             "chain_add", "gather_t", "gather_s", "layernorm", "matmul_f16"],
+                    help="run one kernel of the workloads a few times and exit (profiling aid, prints nothing)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+
+    if args.single:
+        run_single(args.single)
+        return
 
     dist = Dist()
     if args.impl == "reference":

@@ -84,6 +84,7 @@ inline int64_t numel(const qsml_tdesc* d) {
 }
 
 inline bool is_contiguous(const qsml_tdesc* d) {
+    if (numel(d) == 0) return true;  // no element is addressed
     int64_t s = 1;
     for (int i = d->ndim - 1; i >= 0; --i) {
         if (d->shape[i] != 1 && d->stride[i] != s) return false;
