@@ -137,8 +137,10 @@ QSML_API qsml_status_t qsml_destroy(qsml_ctx* ctx);
 QSML_API qsml_status_t qsml_set_stream(qsml_ctx* ctx, void* stream);
 QSML_API qsml_status_t qsml_get_stream(qsml_ctx* ctx, void** stream);
 
-/* Blocks until all work enqueued on the context has finished.  Replaces
- * Device::synchronize / flush_pending (QuasarML/src/Core/Device.cpp:96-102,
+/* Blocks until all work enqueued on the context has finished, then reports
+ * QSML_E_TIMEOUT (and clears it) if a kernel gave up a bounded device-side
+ * wait since the previous call.  Replaces Device::synchronize /
+ * flush_pending (QuasarML/src/Core/Device.cpp:96-102,
  * QuasarML/src/Backend/Vulkan/VulkanBackend.cpp:613-658). */
 QSML_API qsml_status_t qsml_synchronize(qsml_ctx* ctx);
 

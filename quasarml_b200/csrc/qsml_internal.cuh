@@ -53,6 +53,9 @@ struct Context {
     // ticket counter.  Grown on demand, zero-initialised once.
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
+    // Device word where kernels with bounded waits report QSML_E_TIMEOUT;
+    // qsml_synchronize reads and clears it.
+    int* status = nullptr;
     uint64_t launches = 0;
     std::mutex err_mu;
     std::string last_error;

@@ -10,7 +10,7 @@
 // one of three kernels runs, chosen from the shape alone:
 //   * k_reduce_seg   -- inner == 1 with few long rows, including the full
 //                       reduction (one row).  Each row is cut into a number
-//                       of contiguous slices fixed by the shape; a slice is
+//                       of interleaved slices fixed by the shape; a slice is
 //                       reduced by one CTA in a fixed order and its partial
 //                       stored; the CTA that takes the last ticket of a row
 //                       (atomic counter per row) combines that row's
@@ -20,9 +20,9 @@
 //   * k_reduce_cols  -- inner > 1: lanes own 16-byte column vectors (loads
 //                       coalesced along inner), the CTA's warps split k into
 //                       contiguous slices, slices combine in warp order.
-// Accumulation is binary32 (binary16 inputs widen exactly); max/min use an
-// order-preserving integer key so the result is exact and order-free
-// (IEEE 754-2019 maximum/minimum: -0 < +0, NaN wins as 0x7fffffff).
+// Accumulation is binary32 (binary16 inputs widen exactly); max/min use PTX
+// max.NaN/min.NaN, so the result is exact and order-free (IEEE 754-2019
+// maximum/minimum: -0 < +0, NaN wins as 0x7fffffff).
 // mean = sum * (1.0f / (float)k), a reciprocal multiply like
 // Reduction.cpp:347-356; the reciprocal is rounded on the host.
 #include "qsml_internal.cuh"
@@ -49,15 +49,6 @@ __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 __device__ __forceinline__ void from_f(float v, float* o) { *o = v; }
 __device__ __forceinline__ void from_f(float v, __half* o) { *o = __float2half_rn(v); }
 
-// Order-preserving key of a binary32: signed-integer order of the keys is
-// the IEEE total order of the values (so -0 < +0).
-__device__ __forceinline__ int fkey(float x) {
-    int b = __float_as_int(x);
-    return b ^ ((b >> 31) & 0x7fffffff);
-}
-__device__ __forceinline__ float unkey(int k) { return __int_as_float(k ^ ((k >> 31) & 0x7fffffff)); }
-__device__ __forceinline__ bool is_nan(float x) { return (__float_as_int(x) & 0x7fffffff) > 0x7f800000; }
-
 template <int OP> struct Red;
 template <> struct Red<QSML_RED_SUM> {
     using V = float;
@@ -70,22 +61,34 @@ template <> struct Red<QSML_RED_SUM> {
 template <> struct Red<QSML_RED_MEAN> : Red<QSML_RED_SUM> {
     static __device__ __forceinline__ float fin(V a, float scale) { return __fmul_rn(a, scale); }
 };
+// max/min: PTX max.NaN / min.NaN return the canonical NaN 0x7fffffff when
+// either operand is NaN and order -0 below +0, i.e. IEEE 754-2019
+// maximum/minimum in one instruction; the result is independent of the
+// combine order.
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float min_nan(float a, float b) {
+    float r;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
 template <> struct Red<QSML_RED_MAX> {
-    using V = int;
-    static __device__ __forceinline__ V ident() { return fkey(-INFINITY); }
-    static __device__ __forceinline__ V lift(float x) { return is_nan(x) ? INT_MAX : fkey(x); }
-    static __device__ __forceinline__ V comb(V a, V b) { return max(a, b); }
-    static __device__ __forceinline__ float fin(V a, float) { return unkey(a); }  // INT_MAX -> 0x7fffffff
+    using V = float;
+    static __device__ __forceinline__ V ident() { return -INFINITY; }
+    static __device__ __forceinline__ V lift(float x) { return x; }
+    static __device__ __forceinline__ V comb(V a, V b) { return max_nan(a, b); }
+    static __device__ __forceinline__ float fin(V a, float) { return a; }
     static __device__ __forceinline__ V shfl(V v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
 };
 template <> struct Red<QSML_RED_MIN> {
-    using V = int;
-    static __device__ __forceinline__ V ident() { return fkey(INFINITY); }
-    static __device__ __forceinline__ V lift(float x) { return is_nan(x) ? INT_MIN : fkey(x); }
-    static __device__ __forceinline__ V comb(V a, V b) { return min(a, b); }
-    static __device__ __forceinline__ float fin(V a, float) {
-        return a == INT_MIN ? __int_as_float(0x7fffffff) : unkey(a);
-    }
+    using V = float;
+    static __device__ __forceinline__ V ident() { return INFINITY; }
+    static __device__ __forceinline__ V lift(float x) { return x; }
+    static __device__ __forceinline__ V comb(V a, V b) { return min_nan(a, b); }
+    static __device__ __forceinline__ float fin(V a, float) { return a; }
     static __device__ __forceinline__ V shfl(V v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
 };
 
@@ -114,8 +117,8 @@ __device__ __forceinline__ typename Red<OP>::V block_reduce(typename Red<OP>::V 
 
 // ---------------------------------------------------------------------------
 // Segment kernel: x = [nseg rows, len] contiguous.  Each row is split into
-// P contiguous slices (P depends on the shape only); work unit (s, j) reduces
-// slice j of row s with thread-strided 16-byte loads, kSegIters in flight per
+// P interleaved slices (P depends on the shape only); work unit (s, j)
+// reduces slice j of row s with 16-byte loads, kSegIters in flight per
 // thread, in a fixed order, then one block reduction gives partial (s, j).
 // The unit that takes the row's last ticket combines its P partials in slice
 // order.  The result depends on the shape alone, not on the grid size.
@@ -135,21 +138,24 @@ __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int
         const int64_t s = w / P, j = w - s * P;
         const T* row = x + s * len;
         V acc = R::ident();
+        // Slice j of a row is the interleaved set of 256-thread blocks
+        // j, j + P, j + 2P, ...: at any moment the P units of a row stream
+        // through one contiguous region, which keeps DRAM pages hot.
+        const int64_t stride = P * kRT;
         if (VEC) {
             const int64_t npk = len / PV;
-            const int64_t lo = j * npk / P, hi = (j + 1) * npk / P;
             const Pack<T>* p = reinterpret_cast<const Pack<T>*>(row);
-            int64_t q = lo + t;
-            for (; q + (kSegIters - 1) * kRT < hi; q += kSegIters * kRT) {
+            int64_t q = j * kRT + t;
+            for (; q + (kSegIters - 1) * stride < npk; q += kSegIters * stride) {
                 Pack<T> r[kSegIters];
 #pragma unroll
-                for (int i = 0; i < kSegIters; ++i) r[i] = p[q + i * kRT];
+                for (int i = 0; i < kSegIters; ++i) r[i] = p[q + i * stride];
 #pragma unroll
                 for (int i = 0; i < kSegIters; ++i)
 #pragma unroll
                     for (int e = 0; e < PV; ++e) acc = R::comb(acc, R::lift(to_f(r[i].v[e])));
             }
-            for (; q < hi; q += kRT) {
+            for (; q < npk; q += stride) {
                 Pack<T> r = p[q];
 #pragma unroll
                 for (int e = 0; e < PV; ++e) acc = R::comb(acc, R::lift(to_f(r.v[e])));
@@ -157,8 +163,7 @@ __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int
             // elements past the last whole pack belong to the last slice
             if (j == P - 1 && t < len - npk * PV) acc = R::comb(acc, R::lift(to_f(row[npk * PV + t])));
         } else {
-            const int64_t lo = j * len / P, hi = (j + 1) * len / P;
-            for (int64_t q = lo + t; q < hi; q += kRT) acc = R::comb(acc, R::lift(to_f(row[q])));
+            for (int64_t q = j * kRT + t; q < len; q += stride) acc = R::comb(acc, R::lift(to_f(row[q])));
         }
         acc = block_reduce<OP>(acc);
         if (t == 0) {
@@ -449,3 +454,4 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
     return reduce_op<__half, float>(C_, op, static_cast<const __half*>(a->data), outer, k, inner,
                                     static_cast<float*>(out->data));
 }
+

@@ -246,6 +246,15 @@ qsml_status_t qsml_init(int32_t device, qsml_ctx** out) {
         return qsml::set_error(nullptr, QSML_E_CUDA, std::string("cudaStreamCreate: ") + cudaGetErrorString(e));
     }
     ctx->stream = ctx->own_stream;
+    if ((e = cudaMalloc(&ctx->status, 256)) != cudaSuccess ||
+        (e = cudaMemsetAsync(ctx->status, 0, 256, ctx->own_stream)) != cudaSuccess ||
+        (e = cudaStreamSynchronize(ctx->own_stream)) != cudaSuccess) {
+        cudaGetLastError();
+        if (ctx->status) cudaFree(ctx->status);
+        cudaStreamDestroy(ctx->own_stream);
+        delete ctx;
+        return qsml::set_error(nullptr, QSML_E_CUDA, std::string("qsml_init: status word: ") + cudaGetErrorString(e));
+    }
     ctx->allocator = new qsml::CachingAllocator(device);
     *out = reinterpret_cast<qsml_ctx*>(ctx);
     return QSML_OK;
@@ -257,6 +266,7 @@ qsml_status_t qsml_destroy(qsml_ctx* handle) {
     if (C_->stream != C_->own_stream) cudaStreamSynchronize(C_->own_stream);
     delete C_->allocator;
     if (C_->scratch) cudaFree(C_->scratch);
+    if (C_->status) cudaFree(C_->status);
     cudaStreamDestroy(C_->own_stream);
     delete C_;
     return QSML_OK;
@@ -283,7 +293,17 @@ qsml_status_t qsml_get_stream(qsml_ctx* handle, void** stream) {
 
 qsml_status_t qsml_synchronize(qsml_ctx* handle) {
     QSML_CTX(handle);
-    return qsml::check_cuda(C_, cudaStreamSynchronize(C_->stream), "qsml_synchronize");
+    QSML_TRY_STATUS(qsml::check_cuda(C_, cudaStreamSynchronize(C_->stream), "qsml_synchronize"));
+    // A kernel whose bounded device-side wait expired left a code here.
+    int code = 0;
+    QSML_TRY_STATUS(qsml::check_cuda(C_, cudaMemcpy(&code, C_->status, sizeof(int), cudaMemcpyDeviceToHost),
+                                     "qsml_synchronize status"));
+    if (code != 0) {
+        cudaMemset(C_->status, 0, sizeof(int));
+        return qsml::set_error(C_, code, "a kernel's bounded device-side wait expired (status " +
+                                             std::to_string(code) + ")");
+    }
+    return QSML_OK;
 }
 
 const char* qsml_last_error(qsml_ctx* handle) {
