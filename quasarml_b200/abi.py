@@ -81,6 +81,7 @@ _SIGS = {
     "qsml_gather": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc)]),
     "qsml_layer_norm": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_float, _P(TDesc)]),
     "qsml_matmul": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_int32]),
+    "qsml_reduce_noalloc": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_int32, _c.c_int32, _P(TDesc)]),
     "qsml_launch_count": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64)]),
     "qsml_cpu_fallback_count": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64)]),
     "qsml_allocator_stats": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64), _P(_c.c_uint64),

@@ -455,3 +455,162 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
                                     static_cast<float*>(out->data));
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory when they reduce: code that
+// enqueues work while a stream is being captured into a CUDA graph (where
+// cudaMalloc is not allowed), latency-critical serving paths that must not
+// block on the driver's allocator, and host frameworks whose allocator
+// already owns every byte of HBM.  qsml_reduce_noalloc gives them the
+// segment reduction with its scratch (ticket counters + partials) in the
+// fixed device array below instead of the context's scratch buffer, and it
+// needs no qsml_ctx at all -- only the caller's stream.
+//
+// The array is a file-scope __device__ object: every GPU that loads this
+// library holds its kNoAllocScratchBytes until the process exits.  In host
+// code its name is only a stand-in, so its device address is looked up with
+// cudaGetSymbolAddress once per device (first call on that device, with the
+// device current) and passed to the kernel.  All calls share the array and it
+// keeps the last call's contents, so the counters are cleared before every
+// launch; calls whose work overlaps on the GPU (different streams, or
+// concurrent devices sharing nothing but a stream) race on it.
+// ---------------------------------------------------------------------------
+namespace qsml {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 10;         // 64 KiB per device
+constexpr int64_t kNoAllocMaxRows = 64;                           // ticket counters
+constexpr size_t kNoAllocCounterBytes = 256;                      // 64 x u32
+constexpr int64_t kNoAllocMaxUnits =
+    static_cast<int64_t>((kNoAllocScratchBytes - kNoAllocCounterBytes) / 4);  // 4-byte partials
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+std::map<int, void*> g_noalloc_addr;  // device -> device address of g_noalloc_scratch
+
+qsml_status_t noalloc_scratch(void** ptr) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(nullptr, QSML_E_CUDA, std::string("qsml_reduce_noalloc: cudaGetDevice: ") +
+                                                   cudaGetErrorString(e));
+    }
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    auto it = g_noalloc_addr.find(dev);
+    if (it != g_noalloc_addr.end()) {
+        *ptr = it->second;
+        return QSML_OK;
+    }
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+        cudaGetLastError();
+        return set_error(nullptr, QSML_E_CUDA, std::string("qsml_reduce_noalloc: cudaGetSymbolAddress: ") +
+                                                   cudaGetErrorString(e));
+    }
+    g_noalloc_addr[dev] = p;
+    *ptr = p;
+    return QSML_OK;
+}
+
+template <typename T, typename OT, int OP>
+qsml_status_t run_noalloc(cudaStream_t stream, const T* x, int64_t rows, int64_t k, OT* out, void* scratch) {
+    using V = typename Red<OP>::V;
+    static_assert(sizeof(V) == 4, "partials are 4 bytes");
+    const float scale = 1.0f / static_cast<float>(k);
+    const bool vec = aligned16(x) && (rows == 1 || (k * static_cast<int64_t>(sizeof(T))) % 16 == 0);
+    // Same slicing rule as the context path, so both give identical bits.
+    int64_t P = kSegSlots / rows;
+    const int64_t by_size = (k + kSegMinSlice - 1) / kSegMinSlice;
+    if (P > by_size) P = by_size;
+    if (P < 1) P = 1;
+    const int64_t units = rows * P;
+    if (units > kNoAllocMaxUnits)
+        return set_error(nullptr, QSML_E_UNSUPPORTED, "qsml_reduce_noalloc: needs more partials than its fixed scratch holds");
+    unsigned* counters = static_cast<unsigned*>(scratch);
+    V* partials = reinterpret_cast<V*>(static_cast<char*>(scratch) + kNoAllocCounterBytes);
+    cudaError_t e = cudaMemsetAsync(counters, 0, static_cast<size_t>(rows) * sizeof(unsigned), stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(nullptr, QSML_E_CUDA, std::string("qsml_reduce_noalloc: counter clear: ") + cudaGetErrorString(e));
+    }
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int64_t grid = static_cast<int64_t>(sms) * 8;
+    if (grid > units) grid = units;
+    if (vec)
+        k_reduce_seg<T, OT, OP, true><<<static_cast<unsigned>(grid), kRT, 0, stream>>>(x, rows, k, P, out, scale,
+                                                                                        counters, partials);
+    else
+        k_reduce_seg<T, OT, OP, false><<<static_cast<unsigned>(grid), kRT, 0, stream>>>(x, rows, k, P, out, scale,
+                                                                                         counters, partials);
+    e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return set_error(nullptr, QSML_E_CUDA, std::string("qsml_reduce_noalloc: launch: ") + cudaGetErrorString(e));
+    return QSML_OK;
+}
+
+template <typename T, typename OT>
+qsml_status_t noalloc_op(cudaStream_t s, int op, const T* x, int64_t rows, int64_t k, OT* out, void* scratch) {
+    switch (op) {
+        case QSML_RED_SUM: return run_noalloc<T, OT, QSML_RED_SUM>(s, x, rows, k, out, scratch);
+        case QSML_RED_MEAN: return run_noalloc<T, OT, QSML_RED_MEAN>(s, x, rows, k, out, scratch);
+        case QSML_RED_MAX: return run_noalloc<T, OT, QSML_RED_MAX>(s, x, rows, k, out, scratch);
+        case QSML_RED_MIN: return run_noalloc<T, OT, QSML_RED_MIN>(s, x, rows, k, out, scratch);
+    }
+    return set_error(nullptr, QSML_E_INVALID, "qsml_reduce_noalloc: unknown op");
+}
+
+}  // namespace
+}  // namespace qsml
+
+extern "C" qsml_status_t qsml_reduce_noalloc(void* stream, int32_t op, const qsml_tdesc* a, int32_t axis,
+                                             int32_t keepdims, const qsml_tdesc* out) {
+    QSML_TRY_STATUS(check_desc(nullptr, a, "a"));
+    QSML_TRY_STATUS(check_desc(nullptr, out, "out"));
+    if (op < QSML_RED_SUM || op > QSML_RED_MIN) return set_error(nullptr, QSML_E_INVALID, "qsml_reduce_noalloc: unknown op");
+    if (a->dtype != QSML_F32 && a->dtype != QSML_F16)
+        return set_error(nullptr, QSML_E_DTYPE, "qsml_reduce_noalloc: input must be F32 or F16");
+    if (out->dtype != a->dtype && out->dtype != QSML_F32)
+        return set_error(nullptr, QSML_E_DTYPE, "qsml_reduce_noalloc: out dtype must equal the input's or be F32");
+    if (!is_contiguous(a) || !is_contiguous(out))
+        return set_error(nullptr, QSML_E_UNSUPPORTED, "qsml_reduce_noalloc: a and out must be contiguous");
+    // Only reductions whose reduced elements are contiguous: all elements, or
+    // an axis with nothing but unit dims after it.
+    int64_t rows = 1, k = numel(a);
+    if (axis != QSML_AXIS_ALL) {
+        const int ax = axis < 0 ? axis + a->ndim : axis;
+        if (ax < 0 || ax >= a->ndim) return set_error(nullptr, QSML_E_SHAPE, "qsml_reduce_noalloc: invalid axis");
+        for (int i = ax + 1; i < a->ndim; ++i)
+            if (a->shape[i] != 1)
+                return set_error(nullptr, QSML_E_UNSUPPORTED,
+                                 "qsml_reduce_noalloc: only all-element or last-axis reductions are supported");
+        k = a->shape[ax];
+        rows = k == 0 ? numel(out) : numel(a) / k;
+        int64_t expect = 1;
+        for (int i = 0; i < a->ndim; ++i)
+            if (i != ax) expect *= a->shape[i];
+        if (numel(out) != expect) return set_error(nullptr, QSML_E_SHAPE, "qsml_reduce_noalloc: out has the wrong size");
+        (void)keepdims;
+    } else if (numel(out) != 1) {
+        return set_error(nullptr, QSML_E_SHAPE, "qsml_reduce_noalloc: full reduction needs a 1-element out");
+    }
+    if (k == 0 || rows == 0) return set_error(nullptr, QSML_E_SHAPE, "qsml_reduce_noalloc: empty reduction");
+    if (rows > kNoAllocMaxRows)
+        return set_error(nullptr, QSML_E_UNSUPPORTED, "qsml_reduce_noalloc: at most 64 rows (its fixed scratch holds 64 counters)");
+    void* scratch = nullptr;
+    QSML_TRY_STATUS(noalloc_scratch(&scratch));
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (a->dtype == QSML_F32)
+        return noalloc_op<float, float>(s, op, static_cast<const float*>(a->data), rows, k,
+                                        static_cast<float*>(out->data), scratch);
+    if (out->dtype == QSML_F16)
+        return noalloc_op<__half, __half>(s, op, static_cast<const __half*>(a->data), rows, k,
+                                          static_cast<__half*>(out->data), scratch);
+    return noalloc_op<__half, float>(s, op, static_cast<const __half*>(a->data), rows, k,
+                                     static_cast<float*>(out->data), scratch);
+}
