@@ -4,7 +4,7 @@
  * libqsml_cuda.so replaces QuasarML's Vulkan backend (the abstract Backend of
  * QuasarML/src/Backend/BackendInterface.h:43-85 with its VulkanBackend
  * implementation) together with the per-op GLSL generation of
- * QuasarML/src/Ops/*.cpp.  The C++ QuasarML layer (Tensor, Device, Ops::*,
+ * the op files under QuasarML/src/Ops.  The C++ QuasarML layer (Tensor, Device, Ops::*,
  * qsml::) calls these entry points; any other host language can bind them
  * directly (plain pointers, sizes and POD descriptors, no C++ types).
  *
@@ -100,6 +100,7 @@ typedef struct qsml_ctx qsml_ctx;
 #define QSML_RED_MEAN 1
 #define QSML_RED_MAX 2
 #define QSML_RED_MIN 3
+#define QSML_RED_PROD 4
 #define QSML_AXIS_ALL (-1000)
 
 /* Matmul precisions (qsml_matmul). */
@@ -203,7 +204,7 @@ QSML_API qsml_status_t qsml_binary_scalar(qsml_ctx* ctx, int32_t op, const qsml_
 QSML_API qsml_status_t qsml_unary(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a,
                                   const qsml_tdesc* out);
 
-/* Sum / mean / max / min over one axis (negative counts from the end) or
+/* Sum / mean / max / min / prod over one axis (negative counts from the end) or
  * over all elements (axis = QSML_AXIS_ALL).  out has the reduced shape
  * (keepdims keeps the axis as 1; the full reduction gives shape [1]) and the
  * input's dtype; F16 input accumulates in fp32.  mean = sum * (1.0f/(float)n).
@@ -215,7 +216,10 @@ QSML_API qsml_status_t qsml_reduce(qsml_ctx* ctx, int32_t op, const qsml_tdesc* 
                                    int32_t axis, int32_t keepdims, const qsml_tdesc* out);
 
 /* Materialises a strided view (any strides, including 0 and negative) into
- * the contiguous `out` of the same shape and dtype, bit-exactly.  Replaces
+ * `out` of the same shape and dtype, bit-exactly.  `out` is normally
+ * contiguous (the fast paths); a strided `out` (a slice of a larger tensor,
+ * as concat/stack/broadcast_to need) is also accepted and must not overlap
+ * itself or `src`.  Replaces
  * Ops::copy (QuasarML/src/Ops/Manipulation.cpp:171-184), Ops::slice's host
  * round trip (QuasarML/src/Ops/Manipulation.cpp:146-161) and the
  * materialising transpose (QuasarML/src/Ops/LinAlg.cpp:329-351). */

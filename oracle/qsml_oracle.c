@@ -342,12 +342,14 @@ void orc_relu_f16_n(const uint16_t* x, int64_t n, uint16_t* out) {
             double a64 = 0.0, aabs = 0.0;                                       \
             if (op == ORC_MAX) a32 = -INFINITY;                                 \
             else if (op == ORC_MIN) a32 = INFINITY;                             \
+            else if (op == ORC_PROD) { a32 = 1.0f; a64 = 1.0; }                 \
             else a32 = 0.0f;                                                    \
             const int64_t base = o * k * inner + i;                             \
             for (int64_t kk = 0; kk < k; ++kk) {                                \
                 float v = LOAD(base + kk * inner);                              \
                 if (op == ORC_MAX) a32 = orc_max_f32(a32, v);                   \
                 else if (op == ORC_MIN) a32 = orc_min_f32(a32, v);              \
+                else if (op == ORC_PROD) { a32 = a32 * v; a64 *= (double)v; }   \
                 else { a32 = a32 + v; a64 += (double)v; aabs += fabs((double)v); } \
             }                                                                   \
             int64_t j = o * inner + i;                                          \
@@ -357,6 +359,7 @@ void orc_relu_f16_n(const uint16_t* x, int64_t n, uint16_t* out) {
                 aabs = aabs / (double)k;                                        \
             }                                                                   \
             if (op == ORC_MAX || op == ORC_MIN) { a64 = (double)a32; aabs = fabs(a64); } \
+            if (op == ORC_PROD) aabs = fabs(a64);                               \
             if (out32) out32[j] = a32;                                          \
             if (out64) out64[j] = a64;                                          \
             if (absum) absum[j] = aabs;                                         \
@@ -555,12 +558,14 @@ void orc_set_num_threads(int n) {
 static inline float comb(int op, float a, float v) {
     if (op == ORC_MAX) return orc_max_f32(a, v);
     if (op == ORC_MIN) return orc_min_f32(a, v);
+    if (op == ORC_PROD) return a * v;
     return a + v;
 }
 
 static inline float ident(int op) {
     if (op == ORC_MAX) return -INFINITY;
     if (op == ORC_MIN) return INFINITY;
+    if (op == ORC_PROD) return 1.0f;
     return 0.0f;
 }
 

@@ -33,7 +33,7 @@ extern "C" {
 
 /* Operation codes shared with include/qsml_cuda.h. */
 enum { ORC_ADD = 0, ORC_SUB = 1, ORC_MUL = 2, ORC_DIV = 3, ORC_POW = 4 };
-enum { ORC_SUM = 0, ORC_MEAN = 1, ORC_MAX = 2, ORC_MIN = 3 };
+enum { ORC_SUM = 0, ORC_MEAN = 1, ORC_MAX = 2, ORC_MIN = 3, ORC_PROD = 4 };
 
 /* Element conversions (IEEE binary16 <-> binary32, round-to-nearest-even). */
 float    orc_half_to_float(uint16_t h);

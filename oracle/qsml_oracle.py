@@ -16,7 +16,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libqsml_oracle.so")
 
 ADD, SUB, MUL, DIV, POW = range(5)
-SUM, MEAN, MAX, MIN = range(4)
+SUM, MEAN, MAX, MIN, PROD = range(5)
 
 _lib = None
 _P = ctypes.c_void_p

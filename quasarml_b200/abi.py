@@ -26,7 +26,7 @@ MAX_DIMS = 8
 OP_ADD, OP_SUB, OP_MUL, OP_DIV, OP_POW = range(5)
 (UN_RELU, UN_NEG, UN_ABS, UN_SQRT, UN_EXP, UN_LOG, UN_SIN, UN_COS, UN_TANH,
  UN_SIGMOID, UN_GELU) = range(11)
-RED_SUM, RED_MEAN, RED_MAX, RED_MIN = range(4)
+RED_SUM, RED_MEAN, RED_MAX, RED_MIN, RED_PROD = range(5)
 AXIS_ALL = -1000
 MM_AUTO, MM_FP32_FFMA, MM_FP32_3XTF32, MM_FP16_F32ACC = range(4)
 

@@ -1,0 +1,55 @@
+// A CUDA device as QuasarML sees it (QuasarML/src/Core/Device.h): owns a
+// qsml_ctx (stream + caching allocator) of libqsml_cuda.so in place of the
+// Vulkan backend.  GLSL kernel creation (create_kernel / get_kernel) has no
+// counterpart: every op is a precompiled sm_100a kernel.
+#pragma once
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../Common/Types.h"
+
+struct qsml_ctx;
+
+namespace QuasarML {
+
+class Tensor;
+
+class QS_API Device {
+public:
+    Device(const std::string& name, u32 device_index = 0);
+    ~Device();
+    Device(const Device&) = delete;
+    Device& operator=(const Device&) = delete;
+
+    bool is_valid() const { return _ctx != nullptr; }
+    u32 device_index() const { return _device_index; }
+    const std::string& name() const { return _name; }
+    qsml_ctx* ctx() const { return _ctx; }
+
+    std::shared_ptr<Tensor> create_tensor(const std::vector<u32>& shape, DataType dtype = DataType::F32,
+                                          bool host_visible = false);
+
+    // Work is enqueued in order on one stream, so a batch needs no
+    // bracketing; these keep the reference's interface.
+    void begin_batch();
+    void end_batch();
+    void flush_pending();
+    void synchronize();
+    void wait_idle();
+
+    // Throws std::runtime_error with the library's message if st != 0.
+    void check(int st) const;
+    // Tensors hold this to learn whether the device still exists.
+    std::weak_ptr<int> alive_token() const { return _alive; }
+
+private:
+    qsml_ctx* _ctx = nullptr;
+    std::shared_ptr<int> _alive;
+    std::string _name;
+    u32 _device_index = 0;
+    bool _in_batch = false;
+};
+
+}  // namespace QuasarML

@@ -184,6 +184,42 @@ __global__ void __launch_bounds__(kGT) k_gather_generic(const T* __restrict__ sr
     }
 }
 
+// Strided destination (a slice of a larger tensor, e.g. concat/stack): both
+// sides decomposed per element.
+struct CopyPlan {
+    int nd;
+    int64_t shape[kMaxDims];
+    int64_t ss[kMaxDims];  // source strides
+    int64_t ds[kMaxDims];  // destination strides
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kGT) k_copy_strided(const T* __restrict__ src, T* __restrict__ dst, CopyPlan p,
+                                                      int64_t n) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kGT + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * kGT) {
+        int64_t rem = i, so = 0, dof = 0;
+        for (int d = p.nd - 1; d >= 0; --d) {
+            int64_t c = rem % p.shape[d];
+            rem /= p.shape[d];
+            so += c * p.ss[d];
+            dof += c * p.ds[d];
+        }
+        dst[dof] = src[so];
+    }
+}
+
+template <int ES>
+qsml_status_t copy_strided_typed(Context* ctx, const CopyPlan& p, const void* src, void* dst, int64_t n) {
+    using T = typename EType<ES>::T;
+    int64_t blocks = (n + kGT - 1) / kGT;
+    int64_t cap = static_cast<int64_t>(ctx->num_sms) * 16;
+    if (blocks > cap) blocks = cap;
+    k_copy_strided<T><<<static_cast<unsigned>(blocks), kGT, 0, ctx->stream>>>(static_cast<const T*>(src),
+                                                                                static_cast<T*>(dst), p, n);
+    return after_launch(ctx, "k_copy_strided");
+}
+
 template <int ES>
 qsml_status_t gather_typed(Context* ctx, const GPlan& p, const void* srcv, void* dstv, int64_t n) {
     using T = typename EType<ES>::T;
@@ -253,10 +289,26 @@ extern "C" qsml_status_t qsml_gather(qsml_ctx* handle, const qsml_tdesc* src, co
     if (src->ndim != out->ndim) return set_error(C_, QSML_E_SHAPE, "qsml_gather: rank mismatch");
     for (int d = 0; d < src->ndim; ++d)
         if (src->shape[d] != out->shape[d]) return set_error(C_, QSML_E_SHAPE, "qsml_gather: shape mismatch");
-    if (!is_contiguous(out)) return set_error(C_, QSML_E_SHAPE, "qsml_gather: out must be contiguous");
     const int64_t n = numel(src);
     if (n == 0) return QSML_OK;
     const int es = dtype_size(src->dtype);
+    if (!is_contiguous(out)) {
+        // Strided destination: an element-wise copy between two views.
+        CopyPlan cp;
+        cp.nd = src->ndim;
+        for (int d = 0; d < src->ndim; ++d) {
+            cp.shape[d] = src->shape[d];
+            cp.ss[d] = src->stride[d];
+            cp.ds[d] = out->stride[d];
+        }
+        switch (es) {
+            case 1: return copy_strided_typed<1>(C_, cp, src->data, out->data, n);
+            case 2: return copy_strided_typed<2>(C_, cp, src->data, out->data, n);
+            case 4: return copy_strided_typed<4>(C_, cp, src->data, out->data, n);
+            case 8: return copy_strided_typed<8>(C_, cp, src->data, out->data, n);
+        }
+        return set_error(C_, QSML_E_DTYPE, "qsml_gather: unsupported element size");
+    }
 
     GPlan p;
     int nd = 0;

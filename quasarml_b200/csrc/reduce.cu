@@ -92,6 +92,16 @@ template <> struct Red<QSML_RED_MIN> {
     static __device__ __forceinline__ V shfl(V v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
 };
 
+// prod (Reduction.cpp:190-211: `shared_data[tid] *= ...`, identity 1).
+template <> struct Red<QSML_RED_PROD> {
+    using V = float;
+    static __device__ __forceinline__ V ident() { return 1.0f; }
+    static __device__ __forceinline__ V lift(float x) { return x; }
+    static __device__ __forceinline__ V comb(V a, V b) { return __fmul_rn(a, b); }
+    static __device__ __forceinline__ float fin(V a, float) { return a; }
+    static __device__ __forceinline__ V shfl(V v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
+};
+
 // Butterfly: every lane ends with the same bits (each step combines the same
 // two operands on both partner lanes, and the ops are commutative).
 template <int OP>
@@ -365,6 +375,7 @@ qsml_status_t reduce_op(Context* ctx, int op, const T* x, int64_t outer, int64_t
         case QSML_RED_MEAN: return run_reduce<T, OT, QSML_RED_MEAN>(ctx, x, outer, k, inner, out);
         case QSML_RED_MAX: return run_reduce<T, OT, QSML_RED_MAX>(ctx, x, outer, k, inner, out);
         case QSML_RED_MIN: return run_reduce<T, OT, QSML_RED_MIN>(ctx, x, outer, k, inner, out);
+        case QSML_RED_PROD: return run_reduce<T, OT, QSML_RED_PROD>(ctx, x, outer, k, inner, out);
     }
     return set_error(ctx, QSML_E_INVALID, "qsml_reduce: unknown op");
 }
@@ -386,7 +397,7 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
     QSML_CTX(handle);
     QSML_TRY_STATUS(check_desc(C_, a, "a"));
     QSML_TRY_STATUS(check_desc(C_, out, "out"));
-    if (op < QSML_RED_SUM || op > QSML_RED_MIN) return set_error(C_, QSML_E_INVALID, "qsml_reduce: unknown op");
+    if (op < QSML_RED_SUM || op > QSML_RED_PROD) return set_error(C_, QSML_E_INVALID, "qsml_reduce: unknown op");
     if (a->dtype != QSML_F32 && a->dtype != QSML_F16)
         return set_error(C_, QSML_E_DTYPE, "qsml_reduce: input must be F32 or F16");
     if (out->dtype != a->dtype && out->dtype != QSML_F32)
@@ -430,9 +441,9 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
     if (k == 0) {
         if (op == QSML_RED_MAX || op == QSML_RED_MIN)
             return set_error(C_, QSML_E_SHAPE, "qsml_reduce: max/min of an empty axis");
-        // sum = 0; mean = 0 * (1/0) = NaN, like the reference's arithmetic.
-        float v = 0.0f;
-        if (op != QSML_RED_SUM) {
+        // sum = 0, prod = 1; mean = 0 * (1/0) = NaN, like the reference's arithmetic.
+        float v = op == QSML_RED_PROD ? 1.0f : 0.0f;
+        if (op == QSML_RED_MEAN) {
             const uint32_t nan_bits = 0x7fffffffu;
             std::memcpy(&v, &nan_bits, 4);
         }

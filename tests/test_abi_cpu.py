@@ -30,7 +30,7 @@ def test_header_constants_match_binding():
         assert defs["QSML_OP_" + name] == getattr(abi, "OP_" + name)
     for name in ("RELU", "NEG", "ABS", "SQRT", "EXP", "LOG", "SIN", "COS", "TANH", "SIGMOID", "GELU"):
         assert defs["QSML_UN_" + name] == getattr(abi, "UN_" + name)
-    for name in ("SUM", "MEAN", "MAX", "MIN"):
+    for name in ("SUM", "MEAN", "MAX", "MIN", "PROD"):
         assert defs["QSML_RED_" + name] == getattr(abi, "RED_" + name)
     assert defs["QSML_AXIS_ALL"] == abi.AXIS_ALL
     for name in ("OK", "E_INVALID", "E_SHAPE", "E_DTYPE", "E_OOM", "E_CUDA", "E_NCCL", "E_TIMEOUT",

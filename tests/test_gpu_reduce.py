@@ -144,3 +144,14 @@ def test_non_contiguous_input_rejected(ctx):
     with pytest.raises(abi.QsmlError) as e:
         gpu_reduce(ctx, abi.RED_SUM, x, 0)
     assert e.value.status == abi.E_UNSUPPORTED
+
+
+@pytest.mark.parametrize("shape,axis", [((1000,), None), ((7, 300), 1), ((5, 40, 3), 1), ((3, 100000), 1)])
+def test_prod(ctx, orc, shape, axis):
+    """prod (Reduction.cpp:190-211 in the reference): |err| <= n * 2^-24 * |exact|
+    (the worst-case bound of n binary32 roundings)."""
+    x = datagen.uniform(61, shape, 0.999, 1.001)
+    g = gpu_reduce(ctx, abi.RED_PROD, dev(x), axis).astype(np.float64)
+    _, o64, _ = orc.reduce(orc.PROD, x, axis)
+    n = x.size if axis is None else x.shape[axis]
+    assert np.all(np.abs(g.reshape(o64.shape) - o64) <= n * 2.0 ** -24 * np.abs(o64))

@@ -195,3 +195,13 @@ def test_matmul_fma_chain(orc):
     bb = rng.uniform(-1, 1, (3, 6, 2)).astype(np.float32)
     cb = orc.matmul_f64(ab, bb)
     assert np.allclose(cb, np.einsum("bij,bjk->bik", ab.astype(np.float64), bb.astype(np.float64)))
+
+
+def test_prod_reference_order(orc):
+    """prod accumulates in k order like the reference's prod shader tree
+    restated serially (Reduction.cpp:190-211), binary64 as the truth."""
+    x = np.float32([1.5, -2.0, 0.5, 4.0, 1.25])
+    o32, o64, _ = orc.reduce(orc.PROD, x)
+    assert o32 == np.float32(-7.5) and o64 == -7.5
+    y = np.arange(1, 11, dtype=np.float32).reshape(2, 5)
+    assert np.array_equal(orc.reduce(orc.PROD, y, axis=1)[0], np.float32([120, 30240]))
