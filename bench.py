@@ -52,7 +52,9 @@ def peaks():
 
 
 def ncu_traffic():
-    """Per-launch DRAM bytes from the committed ncu summary (kernel -> bytes)."""
+    """DRAM-traffic / algorithmic-bytes ratio of each kernel's committed ncu
+    capture (profiles/ncu_traffic.txt: kernel, dram bytes, algorithmic bytes of
+    the captured launch)."""
     p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
     out = {}
     if os.path.exists(p):
@@ -61,8 +63,8 @@ def ncu_traffic():
             if not line or line.startswith("#"):
                 continue
             parts = line.split()
-            if len(parts) >= 2:
-                out[parts[0]] = float(parts[1])
+            if len(parts) >= 3:
+                out[parts[0]] = float(parts[1]) / float(parts[2])
     return out
 
 
@@ -185,14 +187,14 @@ class ReduceWorkload(Workload):
 
     def __init__(self, ctx, dist: Dist, batch: int = 8):
         import torch
-        from quasarml_b200 import abi, datagen
+        from quasarml_b200 import abi, datagen, sharding
         self.ctx, self.dist, self.batch, self.abi = ctx, dist, batch, abi
         n = int(np.prod(self.SHAPE))
         self.x32, self.x16 = [], []
         host = np.empty(self.SHAPE, np.float32)
         for b in range(batch):
             datagen.normal(datagen.SEEDS["red_X"], self.SHAPE, 0.0, 1.0,
-                           offset=(b * dist.world + dist.rank) * n, out=host)
+                           offset=sharding.shard_offset(b, dist.world, dist.rank, n), out=host)
             t = _t(host)
             self.x32.append(t)
             self.x16.append(t.half())
@@ -214,8 +216,8 @@ class ReduceWorkload(Workload):
                     oshape = abi.reduced_shape(self.SHAPE, axis, False)
                     on = int(np.prod(oshape))
                     for op in self.ops:
-                        grp = {abi.RED_SUM: "sum", abi.RED_MEAN: "sum", abi.RED_MAX: "max", abi.RED_MIN: "min"}[op]
-                        exch = axis in (None, 0)
+                        grp = sharding.collective(op)
+                        exch = sharding.needs_exchange(axis)
                         plan.append((b, axis, op, oshape, on, grp, exch))
                         if exch:
                             sizes[grp] += on
@@ -235,7 +237,9 @@ class ReduceWorkload(Workload):
                 self.bytes_per_step += nbytes
         self.units_per_step = self.bytes_per_step
         self.unit = "GB/s"
-        self.mean_views = []
+        # descriptors of the exchanged mean outputs, rescaled after the all-reduce
+        self.mean_views = [c[3] for c in self.calls
+                           if c[0] == abi.RED_MEAN and sharding.needs_exchange(c[2])]
         self.h2d_bytes = sum(x.numel() * 4 for x in self.x32) + sum(x.numel() * 2 for x in self.x16)
         self.d2h_bytes = sum(c[6].numel() * c[6].element_size() for c in self.calls)
 
@@ -247,14 +251,10 @@ class ReduceWorkload(Workload):
     def exchange(self):
         if not self.dist.pg:
             return
-        dist = self.dist.pg
-        for (dt, grp), buf in self.flat.items():
-            op = {"sum": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN}[grp]
-            dist.all_reduce(buf, op=op)
-        # means were summed over ranks: divide by the number of ranks
-        for (op, xd, axis, od, fam, nb, out) in self.calls:
-            if op == self.abi.RED_MEAN and axis in (self.abi.AXIS_ALL, 0):
-                self.ctx.binary_scalar(self.abi.OP_MUL, od, 1.0 / self.dist.world, od)
+        from quasarml_b200 import sharding
+        abi, ctx = self.abi, self.ctx
+        sharding.exchange(self.dist.pg, self.flat, self.mean_views, self.dist.world,
+                          scale_fn=lambda od, f: ctx.binary_scalar(abi.OP_MUL, od, f, od))
 
     def step(self):
         self.compute()
@@ -504,10 +504,15 @@ def roofline_from_families(fam, hbm_peak, peak_kind):
     f = fam[dom]
     per_launch_ms = f["ms"] / f["launches"]
     achieved = f["bytes"] / (f["ms"] / 1e3) / 1e9
-    traffic = ncu_traffic().get(dom)
+    ratio = ncu_traffic().get(dom)
+    # DRAM bytes per launch: the captured launch's traffic/algorithmic ratio
+    # (profiles/) applied to this family's average algorithmic bytes per launch.
+    traffic = round(ratio * f["bytes"] / f["launches"]) if ratio else None
     return {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,
-            "traffic": traffic, "algorithmic_bytes_per_launch": round(f["bytes"] / f["launches"]),
+            "traffic": traffic, "traffic_source": "ncu capture in profiles/, scaled by bytes processed"
+            if ratio else None,
+            "algorithmic_bytes_per_launch": round(f["bytes"] / f["launches"]),
             "avg_launch_us": round(per_launch_ms * 1e3, 2),
             "share_of_step": round(f["ms"] / total, 3),
             "timing": "CUDA events around replays of a graph holding one step's launches of this kernel",
@@ -670,6 +675,11 @@ def main():
     if args.single:
         run_single(args.single)
         return
+
+    # Ranks share the host: split its cores between the input generators.
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and "OMP_NUM_THREADS" not in os.environ:
+        local = int(os.environ.get("LOCAL_WORLD_SIZE", os.environ.get("WORLD_SIZE", "1")))
+        os.environ["OMP_NUM_THREADS"] = str(max(1, (os.cpu_count() or 1) // local))
 
     dist = Dist()
     if args.impl == "reference":
