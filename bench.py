@@ -209,14 +209,14 @@ class ReduceWorkload(Workload):
         for dt, xs in (("f32", self.x32), ("f16", self.x16)):
             tdt = torch.float32 if dt == "f32" else torch.float16
             es = 4 if dt == "f32" else 2
-            sizes = {"sum": 0, "max": 0, "min": 0}
+            sizes = {"sum": 0, "mean": 0, "max": 0, "min": 0}
             plan = []
             for b in range(batch):
                 for axis in self.axes:
                     oshape = abi.reduced_shape(self.SHAPE, axis, False)
                     on = int(np.prod(oshape))
                     for op in self.ops:
-                        grp = sharding.collective(op)
+                        grp = sharding.group(op)
                         exch = sharding.needs_exchange(axis)
                         plan.append((b, axis, op, oshape, on, grp, exch))
                         if exch:
@@ -237,9 +237,7 @@ class ReduceWorkload(Workload):
                 self.bytes_per_step += nbytes
         self.units_per_step = self.bytes_per_step
         self.unit = "GB/s"
-        # descriptors of the exchanged mean outputs, rescaled after the all-reduce
-        self.mean_views = [c[3] for c in self.calls
-                           if c[0] == abi.RED_MEAN and sharding.needs_exchange(c[2])]
+        self.flat_desc = {k: abi.desc_of(v) for k, v in self.flat.items()}
         self.h2d_bytes = sum(x.numel() * 4 for x in self.x32) + sum(x.numel() * 2 for x in self.x16)
         self.d2h_bytes = sum(c[6].numel() * c[6].element_size() for c in self.calls)
 
@@ -253,8 +251,9 @@ class ReduceWorkload(Workload):
             return
         from quasarml_b200 import sharding
         abi, ctx = self.abi, self.ctx
-        sharding.exchange(self.dist.pg, self.flat, self.mean_views, self.dist.world,
-                          scale_fn=lambda od, f: ctx.binary_scalar(abi.OP_MUL, od, f, od))
+        sharding.exchange(self.dist.pg, self.flat, self.dist.world,
+                          scale_fn=lambda key, f: ctx.binary_scalar(abi.OP_MUL, self.flat_desc[key], f,
+                                                                     self.flat_desc[key]))
 
     def step(self):
         self.compute()

@@ -6,11 +6,14 @@ A global tensor X[N*64, 512, 1024] is split along axis 0; rank r holds rows
 
 * axis 1 / axis 2: each rank's output is its own slice of the global output,
   no exchange;
-* axis 0 / all elements: partial outputs are all-reduced -- sum and max/min
-  with the matching reduction; mean as the all-reduced sum of per-rank means
+* axis 0 / all elements: partial outputs are all-reduced -- sums and max/min
+  with the matching reduction; means as the all-reduced sum of per-rank means
   times 1/world (every shard has the same size).
 
-The same plan drives bench.py (NCCL over NVLink) and the CPU test with gloo.
+Exchanged outputs live in one flat buffer per (dtype, group), group one of
+"sum", "mean", "max", "min", so a step issues one all-reduce per buffer and
+one rescale per mean buffer.  The same plan drives bench.py (NCCL over
+NVLink) and the CPU test with gloo.
 """
 from __future__ import annotations
 
@@ -27,27 +30,24 @@ def needs_exchange(axis) -> bool:
     return axis is None or axis == 0 or axis == -1000
 
 
-def collective(op: int) -> str:
-    """The all-reduce that combines per-rank partials of reduction `op`."""
-    return {SUM: "sum", MEAN: "sum", MAX: "max", MIN: "min"}[op]
+def group(op: int) -> str:
+    """Flat-buffer group of reduction `op`'s exchanged outputs."""
+    return {SUM: "sum", MEAN: "mean", MAX: "max", MIN: "min"}[op]
 
 
-def post_scale(op: int, world: int) -> float:
-    """Factor applied after the all-reduce (mean of equal-size shards)."""
-    return 1.0 / world if op == MEAN else 1.0
-
-
-def exchange(dist, buffers_by_collective: dict, scale_views=(), world: int = 1, scale_fn=None) -> None:
-    """All-reduces each flat buffer with its collective, then rescales the
-    mean views.  `dist` is torch.distributed; `scale_fn(view, factor)` scales
-    in place (the GPU path passes a qsml_binary_scalar call)."""
-    ops = {"sum": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN}
-    for key, buf in buffers_by_collective.items():
-        grp = key[-1] if isinstance(key, tuple) else key
-        dist.all_reduce(buf, op=ops[grp])
+def exchange(dist, buffers: dict, world: int, scale_fn=None) -> None:
+    """All-reduces every flat buffer (keys end in the group name), then scales
+    the mean buffers by 1/world.  `dist` is torch.distributed; `scale_fn(key,
+    factor)` rescales a buffer in place (the GPU path issues one
+    qsml_binary_scalar per buffer); without it the tensor's mul_ is used."""
+    ops = {"sum": dist.ReduceOp.SUM, "mean": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX,
+           "min": dist.ReduceOp.MIN}
+    for key, buf in buffers.items():
+        dist.all_reduce(buf, op=ops[key[-1] if isinstance(key, tuple) else key])
     if world > 1:
-        for v in scale_views:
-            if scale_fn is None:
-                v.mul_(1.0 / world)
-            else:
-                scale_fn(v, 1.0 / world)
+        for key, buf in buffers.items():
+            if (key[-1] if isinstance(key, tuple) else key) == "mean":
+                if scale_fn is None:
+                    buf.mul_(1.0 / world)
+                else:
+                    scale_fn(key, 1.0 / world)

@@ -39,26 +39,25 @@ def _rank(rank, port, q):
         n = int(np.prod(SHARD))
         x = datagen.normal(4, SHARD, 0.0, 1.0, offset=sharding.shard_offset(0, WORLD, rank, n))
         results = {}
-        flat = {"sum": [], "max": [], "min": []}
+        flat = {"sum": [], "mean": [], "max": [], "min": []}
         for axis in (None, 0, 1, 2):
             for op in (sharding.SUM, sharding.MEAN, sharding.MAX, sharding.MIN):
                 o32 = orc.reduce(op, x, axis)[0].astype(np.float32).reshape(-1)
                 t = torch.from_numpy(o32.copy())
                 results[(axis, op)] = t
                 if sharding.needs_exchange(axis):
-                    flat[sharding.collective(op)].append(t)
-        # flat buffers per collective, as the benchmark lays them out
+                    flat[sharding.group(op)].append(t)
+        # flat buffers per group, as the benchmark lays them out
         bufs, views = {}, []
         for grp, ts in flat.items():
             buf = torch.cat(ts)
-            bufs[grp] = buf
+            bufs[("f32", grp)] = buf
             off = 0
             for t in ts:
                 results_key = next(k for k, v in results.items() if v is t)
                 views.append((results_key, buf, off, t.numel()))
                 off += t.numel()
-        means = [buf[off:off + cnt] for (k, buf, off, cnt) in views if k[1] == sharding.MEAN]
-        sharding.exchange(dist, bufs, means, WORLD)
+        sharding.exchange(dist, bufs, WORLD)
         for (k, buf, off, cnt) in views:
             results[k] = buf[off:off + cnt].clone()
         # gather everything on rank 0 for the comparison
