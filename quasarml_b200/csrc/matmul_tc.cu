@@ -13,8 +13,9 @@
 //     warp 0 (one lane) issues the TMA loads, warp 1 (one lane) issues the
 //     MMAs and commits each stage back to the producer;
 //   * two 256-column fp32 accumulators in TMEM (512 columns allocated): the
-//     4 epilogue warps drain one (tcgen05.ld 32x32b -> registers -> global)
-//     while the MMA warp fills the other;
+//     4 epilogue warps drain one (tcgen05.ld 32x32b -> registers ->
+//     swizzled shared-memory staging -> TMA bulk-tensor store, clipped at the
+//     matrix edges by the hardware) while the MMA warp fills the other;
 //   * persistent CTAs (one per SM) walk the tiles in groups of 16 M-tiles so
 //     concurrently running tiles share A and B panels in L2;
 //   * every wait is bounded: on expiry the CTA records QSML_E_TIMEOUT in the
@@ -37,7 +38,10 @@ constexpr int TMEM_COLS = 512;                    // 2 accumulators x 256 fp32 c
 constexpr int GROUP_M = 16;
 constexpr int NUM_THREADS = 192;                  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr long long WAIT_CYCLES = 2000000000LL;   // ~1 s at 2 GHz
-constexpr size_t SMEM_BYTES = size_t(STAGES) * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int C_BOX_BYTES = 32 * 128;              // epilogue staging: 32 rows x 128 bytes
+constexpr int C_STAGE_BYTES = 4 * 2 * C_BOX_BYTES;  // 4 epilogue warps x 2 buffers = 32 KiB
+constexpr size_t SMEM_BYTES =
+    size_t(STAGES) * STAGE_BYTES + C_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
 // Instruction descriptor: D f32, A/B f16, A K-major, B MN-major, N=256, M=128.
 constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
@@ -154,22 +158,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 template <bool OUT_F16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    k_gemm_tc_f16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* Cv, int M,
-                  int N, int K, TileMap tm, long long sC, int a_batched, int b_batched, int* status) {
+    k_gemm_tc_f16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                  const __grid_constant__ CUtensorMap tmC, int M, int N, int K, TileMap tm, int a_batched,
+                  int b_batched, int* status) {
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;  // swizzled tiles need 1024-byte alignment
     unsigned char* gbase = smem_raw + (base - raw);
     const uint32_t sA = base;
     const uint32_t sB = base + STAGES * A_STAGE_BYTES;
-    const uint32_t bars = base + STAGES * STAGE_BYTES;
+    const uint32_t sC_stage = base + STAGES * STAGE_BYTES;  // 1024-aligned: the swizzle needs it
+    const uint32_t bars = sC_stage + C_STAGE_BYTES;
     // barrier layout: full[STAGES], empty[STAGES], tfull[2], tempty[2], drain
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
     auto tfull_bar = [&](int a) { return bars + 8u * (2 * STAGES + a); };
     auto tempty_bar = [&](int a) { return bars + 8u * (2 * STAGES + 2 + a); };
     const uint32_t drain_bar = bars + 8u * (2 * STAGES + 4);
-    unsigned char* gmisc = gbase + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 5);
+    unsigned char* gmisc = gbase + STAGES * STAGE_BYTES + C_STAGE_BYTES + 8 * (2 * STAGES + 5);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gmisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gmisc + 4);
 
@@ -302,38 +308,54 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tc_fence_after();
             int b, mt, nt;
             tm.decode(t, b, mt, nt);
-            const int row = mt * BM + quarter * 32 + lane;
+            const int row0 = mt * BM + quarter * 32;  // first of this warp's 32 rows
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            for (int c0 = 0; c0 < BN; c0 += 32) {
-                uint32_t r[32];
-                tmem_ld32(taddr + c0, r);
-                const int col = nt * BN + c0;
-                if (row < M && col < N) {
-                    if (OUT_F16) {
-                        __half* C = static_cast<__half*>(Cv) + b * sC + static_cast<long long>(row) * N + col;
-                        if (col + 32 <= N) {
+            // Each chunk is 32 rows x 128 bytes (32 fp32 or 64 fp16 columns):
+            // lane = row; the row goes to a staging buffer in the 128-byte
+            // swizzle the C tensor map expects, then one TMA store writes the
+            // box (clipped at the matrix edges by the hardware).
+            constexpr int CHUNK_COLS = OUT_F16 ? 64 : 32;
+            for (int c0 = 0; c0 < BN; c0 += CHUNK_COLS) {
+                // Past the last column nothing is stored; stopping here also
+                // keeps "one bulk group per buffer use" true, which the
+                // wait_group.read accounting below relies on.
+                if (nt * BN + c0 >= N) break;
+                uint32_t words[32];  // the row's 128 bytes
+                if (OUT_F16) {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(taddr + c0, r0);
+                    tmem_ld32(taddr + c0 + 32, r1);
 #pragma unroll
-                            for (int i = 0; i < 32; i += 8) {
-                                __align__(16) __half h[8];
-#pragma unroll
-                                for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(__uint_as_float(r[i + e]));
-                                *reinterpret_cast<uint4*>(C + i) = *reinterpret_cast<uint4*>(h);
-                            }
-                        } else {
-                            for (int i = 0; i < 32 && col + i < N; ++i) C[i] = __float2half_rn(__uint_as_float(r[i]));
-                        }
-                    } else {
-                        float* C = static_cast<float*>(Cv) + b * sC + static_cast<long long>(row) * N + col;
-                        if (col + 32 <= N) {
-#pragma unroll
-                            for (int i = 0; i < 32; i += 4)
-                                *reinterpret_cast<float4*>(C + i) =
-                                    make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
-                                                __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-                        } else {
-                            for (int i = 0; i < 32 && col + i < N; ++i) C[i] = __uint_as_float(r[i]);
-                        }
+                    for (int i = 0; i < 16; ++i) {
+                        __half2 h = __floats2half2_rn(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+                        words[i] = *reinterpret_cast<uint32_t*>(&h);
+                        __half2 g = __floats2half2_rn(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+                        words[16 + i] = *reinterpret_cast<uint32_t*>(&g);
                     }
+                } else {
+                    tmem_ld32(taddr + c0, words);
+                }
+                const int buf = (c0 / CHUNK_COLS) & 1;
+                const uint32_t stage = sC_stage + static_cast<uint32_t>((quarter * 2 + buf) * C_BOX_BYTES);
+                // the store issued from this buffer two chunks ago has read it
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t a = stage + lane * 128 + ((j ^ (lane & 7)) << 4);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(words[4 * j]),
+                                 "r"(words[4 * j + 1]), "r"(words[4 * j + 2]), "r"(words[4 * j + 3])
+                                 : "memory");
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                const int col = nt * BN + c0;
+                if (lane == 0 && row0 < M && col < N) {
+                    asm volatile(
+                        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                        ::"l"(reinterpret_cast<uint64_t>(&tmC)), "r"(col), "r"(row0), "r"(b), "r"(stage)
+                        : "memory");
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 }
             }
             tc_fence_before();
@@ -344,6 +366,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 acc_phase ^= 1u;
             }
         }
+        // every TMA store has finished before the CTA can exit
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
@@ -374,14 +399,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 3-D fp16 tensor map: dims {inner, outer, batch}, 128-byte swizzle.
 bool make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t batch, uint64_t row_bytes,
-              uint64_t batch_bytes, uint32_t box_inner, uint32_t box_outer) {
+              uint64_t batch_bytes, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[3] = {inner, outer, batch};
     cuuint64_t strides[2] = {row_bytes, batch_bytes};
     cuuint32_t box[3] = {box_inner, box_outer, 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+    CUresult r = fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
@@ -399,9 +425,14 @@ qsml_status_t matmul_tc_f16(Context* ctx, const MatmulArgs& g, bool out_f16) {
     if (!ctx->status) return QSML_E_UNSUPPORTED;
     const uint64_t a_batch = g.sA ? static_cast<uint64_t>(g.batch) : 1;
     const uint64_t b_batch = g.sB ? static_cast<uint64_t>(g.batch) : 1;
-    CUtensorMap tmA, tmB;
+    CUtensorMap tmA, tmB, tmC;
+    // C: 128-byte wide boxes of 32 rows (32 fp32 or 64 fp16 columns), written
+    // by the epilogue from swizzled shared-memory staging.
+    const uint64_t c_es = out_f16 ? 2 : 4;
     if (!make_map(&tmA, g.A, g.K, g.M, a_batch, g.lda * 2, (g.sA ? g.sA : g.lda * g.M) * 2, BK, BM) ||
-        !make_map(&tmB, g.B, g.N, g.K, b_batch, g.ldb * 2, (g.sB ? g.sB : g.ldb * g.K) * 2, 64, BK))
+        !make_map(&tmB, g.B, g.N, g.K, b_batch, g.ldb * 2, (g.sB ? g.sB : g.ldb * g.K) * 2, 64, BK) ||
+        !make_map(&tmC, g.C, g.N, g.M, g.batch, g.N * c_es, g.M * g.N * c_es, static_cast<uint32_t>(128 / c_es), 32,
+                  out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
         return QSML_E_UNSUPPORTED;
     // The dynamic shared-memory opt-in is per device; set it once each.
     static std::mutex attr_mu;
@@ -428,11 +459,11 @@ qsml_status_t matmul_tc_f16(Context* ctx, const MatmulArgs& g, bool out_f16) {
     int grid = static_cast<int>(total < ctx->num_sms ? total : ctx->num_sms);
     if (out_f16)
         k_gemm_tc_f16<true><<<grid, NUM_THREADS, SMEM_BYTES, ctx->stream>>>(
-            tmA, tmB, g.C, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), tm, g.sC,
+            tmA, tmB, tmC, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), tm,
             g.sA ? 1 : 0, g.sB ? 1 : 0, ctx->status);
     else
         k_gemm_tc_f16<false><<<grid, NUM_THREADS, SMEM_BYTES, ctx->stream>>>(
-            tmA, tmB, g.C, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), tm, g.sC,
+            tmA, tmB, tmC, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), tm,
             g.sA ? 1 : 0, g.sB ? 1 : 0, ctx->status);
     return after_launch(ctx, "k_gemm_tc_f16");
 }
