@@ -368,7 +368,7 @@ class LayerNormWorkload(Workload):
 
 
 class MatmulWorkload(Workload):
-    def __init__(self, ctx, dist: Dist, dtype: str, batched: bool):
+    def __init__(self, ctx, dist: Dist, dtype: str, batched: bool, fp32_precision: str = "3xtf32"):
         import torch
         from quasarml_b200 import abi, datagen
         self.ctx, self.abi = ctx, abi
@@ -390,7 +390,8 @@ class MatmulWorkload(Workload):
             A, B = A.half(), B.half()
             self.prec = abi.MM_FP16_F32ACC
         else:
-            self.prec = abi.MM_FP32_FFMA
+            self.prec = abi.MM_FP32_3XTF32 if fp32_precision == "3xtf32" else abi.MM_FP32_FFMA
+            self.name += f" ({fp32_precision})"
         self.keep = [A, B, C]
         self.a, self.b, self.c = abi.desc_of(A), abi.desc_of(B), abi.desc_of(C)
         self.units_per_step = self.flops
@@ -736,8 +737,10 @@ def main():
                             ("gather", lambda: GatherWorkload(ctx, dist), 20),
                             ("layernorm", lambda: LayerNormWorkload(ctx, dist), 20),
                             ("matmul_f16_8192", lambda: MatmulWorkload(ctx, dist, "f16", False), 5),
-                            ("matmul_f32_8192", lambda: MatmulWorkload(ctx, dist, "f32", False), 3),
-                            ("batched_matmul_f16", lambda: MatmulWorkload(ctx, dist, "f16", True), 5)):
+                            ("matmul_f32_8192_3xtf32", lambda: MatmulWorkload(ctx, dist, "f32", False), 5),
+                            ("matmul_f32_8192_ffma", lambda: MatmulWorkload(ctx, dist, "f32", False, "ffma"), 3),
+                            ("batched_matmul_f16", lambda: MatmulWorkload(ctx, dist, "f16", True), 5),
+                            ("batched_matmul_f32_3xtf32", lambda: MatmulWorkload(ctx, dist, "f32", True), 5)):
             try:
                 w = mk()
                 ms_x, l_x, g = time_steps(w, dist, stream, st, 3)

@@ -62,8 +62,13 @@ extern "C" qsml_status_t qsml_matmul(qsml_ctx* handle, const qsml_tdesc* a, cons
     if (a->dtype == QSML_F32) {
         if (c->dtype != QSML_F32) return set_error(C_, QSML_E_DTYPE, "qsml_matmul: F32 inputs need an F32 C");
         if (precision == QSML_MM_AUTO || precision == QSML_MM_FP32_FFMA) return matmul_simt<float, float>(C_, g);
-        if (precision == QSML_MM_FP32_3XTF32)
-            return set_error(C_, QSML_E_UNSUPPORTED, "qsml_matmul: 3xTF32 is not built into this library");
+        if (precision == QSML_MM_FP32_3XTF32) {
+            qsml_status_t st = matmul_tc_3xtf32(C_, g);
+            if (st == QSML_E_UNSUPPORTED)
+                return set_error(C_, st, "qsml_matmul: 3xTF32 needs dense A and B, K % 4 == 0, N % 8 == 0 and "
+                                         "16-byte aligned operands");
+            return st;
+        }
         return set_error(C_, QSML_E_INVALID, "qsml_matmul: precision does not apply to F32 inputs");
     }
     if (a->dtype == QSML_F16) {

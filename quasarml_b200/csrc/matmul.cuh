@@ -22,4 +22,9 @@ qsml_status_t matmul_simt(Context* ctx, const MatmulArgs& g);
 // is outside what the kernel takes, so the caller can pick another path.
 qsml_status_t matmul_tc_f16(Context* ctx, const MatmulArgs& g, bool out_f16);
 
+// fp32 inputs as three tf32 tensor-core products (Ahi*Bhi + Ahi*Blo +
+// Alo*Bhi) with fp32 accumulation; A and B must be dense.  Same
+// QSML_E_UNSUPPORTED convention as matmul_tc_f16.
+qsml_status_t matmul_tc_3xtf32(Context* ctx, const MatmulArgs& g);
+
 }  // namespace qsml

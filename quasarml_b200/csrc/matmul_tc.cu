@@ -1,21 +1,27 @@
-// Tensor-core matmul for fp16 inputs with fp32 accumulation on sm_100a:
-// tcgen05.mma with the accumulator in tensor memory (TMEM), operands staged in
-// shared memory by TMA (cp.async.bulk.tensor, no multicast).
+// Tensor-core matmul on sm_100a: tcgen05.mma with the accumulator in tensor
+// memory (TMEM), operands staged in shared memory by TMA (cp.async.bulk.tensor,
+// no multicast), results written by TMA bulk-tensor stores.
 //
 // Reference: Ops::matmul (Ops/LinAlg.cpp:221-271) runs a SIMT shader with
 // 16x16 workgroups and 4x4 register blocks; Ops::batch_matmul
-// (LinAlg.cpp:273-290) is broken.  Here:
-//   * C tile 128 x 256 per CTA, k-blocks of 64; one tcgen05.mma
-//     (M=128, N=256, K=16, cta_group::1) per 16-wide k slice;
+// (LinAlg.cpp:273-290) is broken.  Two configurations share one kernel:
+//   * CfgF16  -- fp16 A/B, fp32 accumulate: C tile 128 x 256, k-blocks of 64,
+//                one tcgen05.mma (kind::f16, M=128, N=256, K=16) per 16-wide
+//                k slice, 4-stage ring;
+//   * Cfg3xTF32 -- fp32 A/B as three tf32 products (A = Ahi + Alo,
+//                B = Bhi + Blo; Ahi*Bhi + Ahi*Blo + Alo*Bhi, the Alo*Blo term
+//                is below fp32 resolution), C tile 128 x 128, k-blocks of 32,
+//                three kind::tf32 MMAs (K=8) per 8-wide k slice, 3-stage ring.
+// Common structure:
 //   * A [M,K] row-major is K-major in shared memory, B [K,N] row-major is
-//     MN-major (N contiguous); both use the 128-byte swizzle TMA writes;
-//   * 4-stage ring of shared-memory buffers with full/empty mbarriers:
-//     warp 0 (one lane) issues the TMA loads, warp 1 (one lane) issues the
-//     MMAs and commits each stage back to the producer;
-//   * two 256-column fp32 accumulators in TMEM (512 columns allocated): the
-//     4 epilogue warps drain one (tcgen05.ld 32x32b -> registers ->
-//     swizzled shared-memory staging -> TMA bulk-tensor store, clipped at the
-//     matrix edges by the hardware) while the MMA warp fills the other;
+//     MN-major (N contiguous); both use a 128-byte swizzle written by TMA
+//     (16-byte units, except MN-major tf32 B, which needs 32-byte units);
+//   * full/empty mbarriers per stage: warp 0 (one lane) issues the TMA loads,
+//     warp 1 (one lane) issues the MMAs and commits each stage back;
+//   * two fp32 accumulators in TMEM: the 4 epilogue warps drain one
+//     (tcgen05.ld 32x32b -> registers -> swizzled shared-memory staging ->
+//     TMA bulk-tensor store, clipped at the matrix edges by the hardware)
+//     while the MMA warp fills the other;
 //   * persistent CTAs (one per SM) walk the tiles in groups of 16 M-tiles so
 //     concurrently running tiles share A and B panels in L2;
 //   * every wait is bounded: on expiry the CTA records QSML_E_TIMEOUT in the
@@ -29,23 +35,60 @@
 namespace qsml {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_STAGE_BYTES = BM * BK * 2;        // 16 KiB
-constexpr int B_STAGE_BYTES = BK * BN * 2;        // 32 KiB
-constexpr int B_BOX_BYTES = BK * 64 * 2;          // one 64-column TMA box: 8 KiB
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
-constexpr int TMEM_COLS = 512;                    // 2 accumulators x 256 fp32 columns
+constexpr int BM = 128;
 constexpr int GROUP_M = 16;
-constexpr int NUM_THREADS = 192;                  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr long long WAIT_CYCLES = 2000000000LL;   // ~1 s at 2 GHz
-constexpr int C_BOX_BYTES = 32 * 128;              // epilogue staging: 32 rows x 128 bytes
+constexpr int NUM_THREADS = 192;                    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr long long WAIT_CYCLES = 2000000000LL;     // ~1 s at 2 GHz
+constexpr int C_BOX_BYTES = 32 * 128;               // epilogue staging: 32 rows x 128 bytes
 constexpr int C_STAGE_BYTES = 4 * 2 * C_BOX_BYTES;  // 4 epilogue warps x 2 buffers = 32 KiB
-constexpr size_t SMEM_BYTES =
-    size_t(STAGES) * STAGE_BYTES + C_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
-// Instruction descriptor: D f32, A/B f16, A K-major, B MN-major, N=256, M=128.
-constexpr uint32_t IDESC = (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
-                           (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+// Instruction descriptor: D f32, A/B format, A K-major, B MN-major, N, M=128.
+constexpr uint32_t make_idesc(uint32_t ab_format, int n) {
+    return (1u << 4) | (ab_format << 7) | (ab_format << 10) | (0u << 15) | (1u << 16) |
+           (uint32_t(n >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+}
+
+// Shared-memory descriptor layout types (bits 61-63 of the descriptor).
+constexpr uint32_t DESC_SW128 = 2;         // 16-byte units swizzled across 8 rows of 128 bytes
+constexpr uint32_t DESC_SW128_BASE32 = 1;  // 32-byte units swizzled across 4 rows of 128 bytes
+
+// B is MN-major.  For 16-bit types it uses the ordinary 128-byte swizzle
+// (8-row atoms, k groups 1024 bytes apart); MN-major 32-bit (tf32) operands
+// only accept the 128-byte swizzle with 32-byte units, whose atoms are 4
+// rows, so k groups of 4 rows are 512 bytes apart.  TMA writes the matching
+// pattern with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
+struct CfgF16 {
+    static constexpr bool TF32 = false;
+    static constexpr int BN = 256, BK = 64, STAGES = 4, ESIZE = 2;
+    static constexpr int NA = 1, NB = 1;            // A and B tiles per stage
+    static constexpr int MMA_K = 16;
+    static constexpr uint32_t IDESC = make_idesc(0 /*f16*/, BN);
+    static constexpr uint32_t B_DESC_LAYOUT = DESC_SW128, B_SBO = 1024;
+    static constexpr CUtensorMapSwizzle B_SWIZZLE = CU_TENSOR_MAP_SWIZZLE_128B;
+};
+
+struct Cfg3xTF32 {
+    static constexpr bool TF32 = true;
+    static constexpr int BN = 128, BK = 32, STAGES = 3, ESIZE = 4;
+    static constexpr int NA = 2, NB = 2;            // hi and lo parts of A and of B
+    static constexpr int MMA_K = 8;
+    static constexpr uint32_t IDESC = make_idesc(2 /*tf32*/, BN);
+    static constexpr uint32_t B_DESC_LAYOUT = DESC_SW128_BASE32, B_SBO = 512;
+    static constexpr CUtensorMapSwizzle B_SWIZZLE = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+};
+
+template <class Cfg> struct Layout {
+    static constexpr int ROW_ELEMS = 128 / Cfg::ESIZE;             // one 128-byte swizzle row
+    static constexpr int A_TILE = BM * Cfg::BK * Cfg::ESIZE;       // K-major: BM rows of 128 B
+    static constexpr int B_BOX = Cfg::BK * 128;                    // MN-major: BK rows of 128 B
+    static constexpr int B_BOXES = Cfg::BN / ROW_ELEMS;
+    static constexpr int B_TILE = B_BOXES * B_BOX;
+    static constexpr int STAGE = Cfg::NA * A_TILE + Cfg::NB * B_TILE;
+    static constexpr int TMEM_COLS = 2 * Cfg::BN;                  // double-buffered accumulator
+    static constexpr size_t SMEM = size_t(Cfg::STAGES) * STAGE + C_STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
+    static_assert(Cfg::BK * Cfg::ESIZE == 128, "one k-block is one 128-byte swizzle row of A");
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
 
 struct TileMap {
     int tiles_m, tiles_n, batch;
@@ -114,24 +157,35 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+// Shared-memory matrix descriptor (sm_100 version field) for a swizzled layout.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout = DESC_SW128) {
     uint64_t d = 0;
     d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
     d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
     d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
     d |= static_cast<uint64_t>(1) << 46;  // descriptor version for tcgen05
-    d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+    d |= static_cast<uint64_t>(layout) << 61;
     return d;
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accumulate)
-        : "memory");
+template <class Cfg>
+__device__ __forceinline__ void mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    if constexpr (Cfg::TF32) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+            ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(Cfg::IDESC), "r"(accumulate)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+            ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(Cfg::IDESC), "r"(accumulate)
+            : "memory");
+    }
 }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
@@ -156,18 +210,26 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <bool OUT_F16>
+// Operand maps: tmA[0..NA), tmB[0..NB) (hi then lo for 3xTF32).
+struct OperandMaps {
+    CUtensorMap a[2];
+    CUtensorMap b[2];
+};
+
+template <class Cfg, bool OUT_F16>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    k_gemm_tc_f16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                  const __grid_constant__ CUtensorMap tmC, int M, int N, int K, TileMap tm, int a_batched,
-                  int b_batched, int* status) {
+    k_gemm_tc(const __grid_constant__ OperandMaps ops, const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
+              TileMap tm, int a_batched, int b_batched, int* status) {
+    using L = Layout<Cfg>;
+    constexpr int BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;  // swizzled tiles need 1024-byte alignment
     unsigned char* gbase = smem_raw + (base - raw);
-    const uint32_t sA = base;
-    const uint32_t sB = base + STAGES * A_STAGE_BYTES;
-    const uint32_t sC_stage = base + STAGES * STAGE_BYTES;  // 1024-aligned: the swizzle needs it
+    // stage s: A tiles [NA], then B tiles [NB]
+    auto a_tile = [&](int s, int i) { return base + s * L::STAGE + i * L::A_TILE; };
+    auto b_tile = [&](int s, int i) { return base + s * L::STAGE + Cfg::NA * L::A_TILE + i * L::B_TILE; };
+    const uint32_t sC_stage = base + STAGES * L::STAGE;  // 1024-aligned: the swizzle needs it
     const uint32_t bars = sC_stage + C_STAGE_BYTES;
     // barrier layout: full[STAGES], empty[STAGES], tfull[2], tempty[2], drain
     auto full_bar = [&](int s) { return bars + 8u * s; };
@@ -175,7 +237,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     auto tfull_bar = [&](int a) { return bars + 8u * (2 * STAGES + a); };
     auto tempty_bar = [&](int a) { return bars + 8u * (2 * STAGES + 2 + a); };
     const uint32_t drain_bar = bars + 8u * (2 * STAGES + 4);
-    unsigned char* gmisc = gbase + STAGES * STAGE_BYTES + C_STAGE_BYTES + 8 * (2 * STAGES + 5);
+    unsigned char* gmisc = gbase + STAGES * L::STAGE + C_STAGE_BYTES + 8 * (2 * STAGES + 5);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gmisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gmisc + 4);
 
@@ -196,7 +258,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TMEM_COLS)
+                     "r"(L::TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -225,12 +287,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(full_bar(stage), STAGE_BYTES);
-                    tma_load_3d(sA + stage * A_STAGE_BYTES, &tmA, full_bar(stage), kb * BK, mt * BM, ab);
+                    mbar_expect_tx(full_bar(stage), L::STAGE);
 #pragma unroll
-                    for (int j = 0; j < BN / 64; ++j)
-                        tma_load_3d(sB + stage * B_STAGE_BYTES + j * B_BOX_BYTES, &tmB, full_bar(stage),
-                                    nt * BN + j * 64, kb * BK, bb);
+                    for (int i = 0; i < Cfg::NA; ++i)
+                        tma_load_3d(a_tile(stage, i), &ops.a[i], full_bar(stage), kb * BK, mt * BM, ab);
+#pragma unroll
+                    for (int i = 0; i < Cfg::NB; ++i)
+#pragma unroll
+                        for (int j = 0; j < L::B_BOXES; ++j)
+                            tma_load_3d(b_tile(stage, i) + j * L::B_BOX, &ops.b[i], full_bar(stage),
+                                        nt * BN + j * L::ROW_ELEMS, kb * BK, bb);
                     issued[stage] = static_cast<int>(phase);
                     if (++stage == STAGES) {
                         stage = 0;
@@ -264,15 +330,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = sA + stage * A_STAGE_BYTES;
-                    const uint32_t b0 = sB + stage * B_STAGE_BYTES;
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) {
-                        // A: K-major, advance 16 fp16 = 32 bytes inside the 128-byte swizzle row.
-                        const uint64_t ad = smem_desc(a0 + k * 32, 16, 1024);
-                        // B: MN-major, advance 16 k-rows of 128 bytes; 64-column chunks are 8 KiB apart.
-                        const uint64_t bd = smem_desc(b0 + k * 16 * 128, B_BOX_BYTES, 1024);
-                        mma_f16(d_tmem, ad, bd, (kb > 0 || k > 0) ? 1u : 0u);
+                    for (int k = 0; k < BK / Cfg::MMA_K; ++k) {
+                        // A: K-major, a k slice is 32 bytes inside the 128-byte swizzle row.
+                        // B: MN-major, a k slice is MMA_K rows of 128 bytes; the
+                        //    128-byte column chunks are one TMA box (B_BOX bytes) apart.
+                        const uint32_t ak = static_cast<uint32_t>(k * 32);
+                        const uint32_t bk = static_cast<uint32_t>(k * Cfg::MMA_K * 128);
+                        const uint32_t acc_in = (kb > 0 || k > 0) ? 1u : 0u;
+                        auto bdesc = [&](int part) {
+                            return smem_desc(b_tile(stage, part) + bk, L::B_BOX, Cfg::B_SBO, Cfg::B_DESC_LAYOUT);
+                        };
+                        if constexpr (Cfg::TF32) {
+                            // hi*hi + hi*lo + lo*hi
+                            mma<Cfg>(d_tmem, smem_desc(a_tile(stage, 0) + ak, 16, 1024), bdesc(0), acc_in);
+                            mma<Cfg>(d_tmem, smem_desc(a_tile(stage, 0) + ak, 16, 1024), bdesc(1), 1u);
+                            mma<Cfg>(d_tmem, smem_desc(a_tile(stage, 1) + ak, 16, 1024), bdesc(0), 1u);
+                        } else {
+                            mma<Cfg>(d_tmem, smem_desc(a_tile(stage, 0) + ak, 16, 1024), bdesc(0), acc_in);
+                        }
                     }
                     mma_commit(empty_bar(stage));  // stage free once these MMAs have read it
                     if (++stage == STAGES) {
@@ -309,7 +385,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int b, mt, nt;
             tm.decode(t, b, mt, nt);
             const int row0 = mt * BM + quarter * 32;  // first of this warp's 32 rows
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+            const uint32_t taddr =
+                tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
             // Each chunk is 32 rows x 128 bytes (32 fp32 or 64 fp16 columns):
             // lane = row; the row goes to a staging buffer in the 128-byte
             // swizzle the C tensor map expects, then one TMA store writes the
@@ -375,8 +452,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (*abort_flag && threadIdx.x == 0) atomicExch(status, QSML_E_TIMEOUT);
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(L::TMEM_COLS)
                      : "memory");
+    }
+}
+
+// fp32 -> (hi, lo) for 3xTF32: hi is x rounded to tf32 (cvt.rna, low 13 bits
+// zero), lo = x - hi exactly, itself rounded to tf32 (its own error is below
+// 2^-22 |x|).
+__global__ void __launch_bounds__(256) k_split_tf32(const float4* __restrict__ x, float4* __restrict__ hi,
+                                                    float4* __restrict__ lo, int64_t n4) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * 256) {
+        float4 v = x[i], h, l;
+        float* pv = &v.x;
+        float* ph = &h.x;
+        float* pl = &l.x;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            uint32_t hb, lb;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hb) : "f"(pv[e]));
+            ph[e] = __uint_as_float(hb);
+            const float r = __fsub_rn(pv[e], ph[e]);
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lb) : "f"(r));
+            pl[e] = __uint_as_float(lb);
+        }
+        hi[i] = h;
+        lo[i] = l;
     }
 }
 
@@ -397,75 +499,133 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 3-D fp16 tensor map: dims {inner, outer, batch}, 128-byte swizzle.
+// 3-D tensor map: dims {inner, outer, batch}, 128-byte swizzle (16- or 32-byte units).
 bool make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t batch, uint64_t row_bytes,
-              uint64_t batch_bytes, uint32_t box_inner, uint32_t box_outer,
-              CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16) {
+              uint64_t batch_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapDataType dt,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[3] = {inner, outer, batch};
     cuuint64_t strides[2] = {row_bytes, batch_bytes};
     cuuint32_t box[3] = {box_inner, box_outer, 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = fn(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
+}
+
+// Opt in to the kernel's dynamic shared memory once per device.
+template <class Cfg, bool OUT_F16>
+qsml_status_t set_smem_attr(Context* ctx) {
+    static std::mutex mu;
+    static uint64_t done = 0;
+    std::lock_guard<std::mutex> lk(mu);
+    const uint64_t bit = uint64_t(1) << (ctx->device & 63);
+    if (done & bit) return QSML_OK;
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<Cfg, OUT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(Layout<Cfg>::SMEM));
+    if (e != cudaSuccess) return check_cuda(ctx, e, "matmul: shared-memory attribute");
+    done |= bit;
+    return QSML_OK;
+}
+
+// Operand pointers per part (hi/lo for 3xTF32) with their batch strides.
+struct Operands {
+    const void* a[2];
+    const void* b[2];
+    int64_t lda, ldb, sA, sB;
+};
+
+template <class Cfg, bool OUT_F16>
+qsml_status_t launch_tc(Context* ctx, const MatmulArgs& g, const Operands& o) {
+    constexpr CUtensorMapDataType in_t =
+        Cfg::TF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    constexpr uint64_t es = Cfg::ESIZE;
+    const uint64_t a_batch = o.sA ? static_cast<uint64_t>(g.batch) : 1;
+    const uint64_t b_batch = o.sB ? static_cast<uint64_t>(g.batch) : 1;
+    OperandMaps maps;
+    for (int i = 0; i < Cfg::NA; ++i)
+        if (!make_map(&maps.a[i], o.a[i], g.K, g.M, a_batch, o.lda * es, (o.sA ? o.sA : o.lda * g.M) * es,
+                      Layout<Cfg>::ROW_ELEMS, BM, in_t))
+            return QSML_E_UNSUPPORTED;
+    for (int i = 0; i < Cfg::NB; ++i)
+        if (!make_map(&maps.b[i], o.b[i], g.N, g.K, b_batch, o.ldb * es, (o.sB ? o.sB : o.ldb * g.K) * es,
+                      Layout<Cfg>::ROW_ELEMS, Cfg::BK, in_t, Cfg::B_SWIZZLE))
+            return QSML_E_UNSUPPORTED;
+    for (int i = Cfg::NA; i < 2; ++i) maps.a[i] = maps.a[0];
+    for (int i = Cfg::NB; i < 2; ++i) maps.b[i] = maps.b[0];
+    // C: 128-byte wide boxes of 32 rows (32 fp32 or 64 fp16 columns).
+    CUtensorMap tmC;
+    const uint64_t c_es = OUT_F16 ? 2 : 4;
+    if (!make_map(&tmC, g.C, g.N, g.M, g.batch, g.N * c_es, g.M * g.N * c_es, static_cast<uint32_t>(128 / c_es), 32,
+                  OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
+        return QSML_E_UNSUPPORTED;
+    QSML_TRY_STATUS((set_smem_attr<Cfg, OUT_F16>(ctx)));
+    TileMap tm;
+    tm.tiles_m = static_cast<int>((g.M + BM - 1) / BM);
+    tm.tiles_n = static_cast<int>((g.N + Cfg::BN - 1) / Cfg::BN);
+    tm.batch = static_cast<int>(g.batch);
+    const int64_t total = static_cast<int64_t>(tm.tiles_m) * tm.tiles_n * tm.batch;
+    const int grid = static_cast<int>(total < ctx->num_sms ? total : ctx->num_sms);
+    k_gemm_tc<Cfg, OUT_F16><<<grid, NUM_THREADS, Layout<Cfg>::SMEM, ctx->stream>>>(
+        maps, tmC, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), tm, o.sA ? 1 : 0,
+        o.sB ? 1 : 0, ctx->status);
+    return after_launch(ctx, Cfg::TF32 ? "k_gemm_tc<3xtf32>" : "k_gemm_tc<f16>");
+}
+
+// What the kernels take: 16-byte aligned operands and row strides (TMA), N a
+// multiple of 8 (128-byte output boxes stay inside rows of whole 16-byte units).
+bool tc_shape_ok(const MatmulArgs& g, int es) {
+    const int64_t q = 16 / es;
+    return g.K % q == 0 && g.N % 8 == 0 && g.lda % q == 0 && g.ldb % q == 0 && g.sA % q == 0 && g.sB % q == 0 &&
+           aligned16(g.A) && aligned16(g.B) && aligned16(g.C) && g.M > 0 && g.N > 0 && g.K > 0;
 }
 
 }  // namespace
 
 qsml_status_t matmul_tc_f16(Context* ctx, const MatmulArgs& g, bool out_f16) {
-    // What the kernel takes: 16-byte aligned operands and row strides (TMA),
-    // N a multiple of 8 (vector stores), and a status word for timeouts.
-    const bool shapes_ok = g.K % 8 == 0 && g.N % 8 == 0 && g.lda % 8 == 0 && g.ldb % 8 == 0 && g.sA % 8 == 0 &&
-                           g.sB % 8 == 0 && aligned16(g.A) && aligned16(g.B) && aligned16(g.C) && g.M > 0 &&
-                           g.N > 0 && g.K > 0;
-    if (!shapes_ok) return QSML_E_UNSUPPORTED;
-    if (!ctx->status) return QSML_E_UNSUPPORTED;
-    const uint64_t a_batch = g.sA ? static_cast<uint64_t>(g.batch) : 1;
-    const uint64_t b_batch = g.sB ? static_cast<uint64_t>(g.batch) : 1;
-    CUtensorMap tmA, tmB, tmC;
-    // C: 128-byte wide boxes of 32 rows (32 fp32 or 64 fp16 columns), written
-    // by the epilogue from swizzled shared-memory staging.
-    const uint64_t c_es = out_f16 ? 2 : 4;
-    if (!make_map(&tmA, g.A, g.K, g.M, a_batch, g.lda * 2, (g.sA ? g.sA : g.lda * g.M) * 2, BK, BM) ||
-        !make_map(&tmB, g.B, g.N, g.K, b_batch, g.ldb * 2, (g.sB ? g.sB : g.ldb * g.K) * 2, 64, BK) ||
-        !make_map(&tmC, g.C, g.N, g.M, g.batch, g.N * c_es, g.M * g.N * c_es, static_cast<uint32_t>(128 / c_es), 32,
-                  out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
-        return QSML_E_UNSUPPORTED;
-    // The dynamic shared-memory opt-in is per device; set it once each.
-    static std::mutex attr_mu;
-    static uint64_t attr_done[2] = {0, 0};
-    {
-        std::lock_guard<std::mutex> lk(attr_mu);
-        const uint64_t bit = uint64_t(1) << (ctx->device & 63);
-        if (!(attr_done[out_f16] & bit)) {
-            cudaError_t e = out_f16 ? cudaFuncSetAttribute(k_gemm_tc_f16<true>,
-                                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                           static_cast<int>(SMEM_BYTES))
-                                    : cudaFuncSetAttribute(k_gemm_tc_f16<false>,
-                                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                           static_cast<int>(SMEM_BYTES));
-            if (e != cudaSuccess) return check_cuda(ctx, e, "matmul: shared-memory attribute");
-            attr_done[out_f16] |= bit;
+    if (!tc_shape_ok(g, 2) || !ctx->status) return QSML_E_UNSUPPORTED;
+    Operands o{{g.A, g.A}, {g.B, g.B}, g.lda, g.ldb, g.sA, g.sB};
+    return out_f16 ? launch_tc<CfgF16, true>(ctx, g, o) : launch_tc<CfgF16, false>(ctx, g, o);
+}
+
+qsml_status_t matmul_tc_3xtf32(Context* ctx, const MatmulArgs& g) {
+    if (!tc_shape_ok(g, 4) || !ctx->status) return QSML_E_UNSUPPORTED;
+    // Split A and B into contiguous hi/lo copies (scratch from the caching
+    // allocator, returned to it after the launch: reuse is stream-ordered).
+    const int64_t a_elems = (g.sA ? g.batch : 1) * g.M * g.K;
+    const int64_t b_elems = (g.sB ? g.batch : 1) * g.K * g.N;
+    const bool a_dense = g.lda == g.K && (!g.sA || g.sA == g.M * g.K);
+    const bool b_dense = g.ldb == g.N && (!g.sB || g.sB == g.K * g.N);
+    if (!a_dense || !b_dense) return QSML_E_UNSUPPORTED;
+    void* buf[4] = {nullptr, nullptr, nullptr, nullptr};
+    std::string err;
+    const size_t sizes[4] = {static_cast<size_t>(a_elems) * 4, static_cast<size_t>(a_elems) * 4,
+                             static_cast<size_t>(b_elems) * 4, static_cast<size_t>(b_elems) * 4};
+    for (int i = 0; i < 4; ++i) {
+        qsml_status_t st = ctx->allocator->alloc(sizes[i], &buf[i], &err);
+        if (st != QSML_OK) {
+            for (int j = 0; j < i; ++j) ctx->allocator->free(buf[j], &err);
+            return set_error(ctx, st, err);
         }
     }
-    TileMap tm;
-    tm.tiles_m = static_cast<int>((g.M + BM - 1) / BM);
-    tm.tiles_n = static_cast<int>((g.N + BN - 1) / BN);
-    tm.batch = static_cast<int>(g.batch);
-    const int64_t total = static_cast<int64_t>(tm.tiles_m) * tm.tiles_n * tm.batch;
-    int grid = static_cast<int>(total < ctx->num_sms ? total : ctx->num_sms);
-    if (out_f16)
-        k_gemm_tc_f16<true><<<grid, NUM_THREADS, SMEM_BYTES, ctx->stream>>>(
-            tmA, tmB, tmC, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), tm,
-            g.sA ? 1 : 0, g.sB ? 1 : 0, ctx->status);
-    else
-        k_gemm_tc_f16<false><<<grid, NUM_THREADS, SMEM_BYTES, ctx->stream>>>(
-            tmA, tmB, tmC, static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(g.K), tm,
-            g.sA ? 1 : 0, g.sB ? 1 : 0, ctx->status);
-    return after_launch(ctx, "k_gemm_tc_f16");
+    auto split = [&](const void* src, void* hi, void* lo, int64_t n) {
+        const int64_t n4 = n / 4;  // K % 4 == 0 and N % 8 == 0, so n is a multiple of 4
+        int64_t blocks = (n4 + 255) / 256;
+        if (blocks > int64_t(ctx->num_sms) * 16) blocks = int64_t(ctx->num_sms) * 16;
+        k_split_tf32<<<static_cast<unsigned>(blocks), 256, 0, ctx->stream>>>(
+            static_cast<const float4*>(src), static_cast<float4*>(hi), static_cast<float4*>(lo), n4);
+        return after_launch(ctx, "k_split_tf32");
+    };
+    qsml_status_t st = split(g.A, buf[0], buf[1], a_elems);
+    if (st == QSML_OK) st = split(g.B, buf[2], buf[3], b_elems);
+    if (st == QSML_OK) {
+        Operands o{{buf[0], buf[1]}, {buf[2], buf[3]}, g.K, g.N, g.sA ? g.M * g.K : 0, g.sB ? g.K * g.N : 0};
+        st = launch_tc<Cfg3xTF32, false>(ctx, g, o);
+        if (st == QSML_E_UNSUPPORTED) st = set_error(ctx, QSML_E_CUDA, "matmul 3xTF32: tensor map creation failed");
+    }
+    for (int i = 0; i < 4; ++i) ctx->allocator->free(buf[i], &err);
+    return st;
 }
 
 }  // namespace qsml

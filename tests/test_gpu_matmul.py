@@ -113,3 +113,37 @@ def test_errors(ctx):
         ctx.matmul(d(dev(np.ones((2, 3), np.float32))), d(dev(np.ones((3, 2), np.float16))),
                    d(empty((2, 2), np.float32)))
     assert e.value.status == abi.E_DTYPE
+
+
+@pytest.mark.parametrize("mkn", [(128, 64, 128), (256, 512, 384), (100, 72, 200), (1, 64, 64), (512, 1024, 256),
+                                 (300, 1000, 72)])
+def test_fp32_3xtf32_small(ctx, orc, mkn):
+    """fp32 via three tf32 tensor-core products: max|err| / max|ref| <= 1e-4
+    against binary64 (observed errors are near fp32 rounding)."""
+    M, K, N = mkn
+    a = datagen.uniform(49, (M, K), -1, 1)
+    b = datagen.uniform(50, (K, N), -1, 1)
+    c = mm(ctx, a, b, precision=abi.MM_FP32_3XTF32).astype(np.float64)
+    ref = orc.matmul_f64(a, b)
+    err = np.max(np.abs(c - ref)) / np.max(np.abs(ref))
+    assert err <= 1e-4, err
+    assert err <= 1e-5, err  # far tighter than the fp32 bar in practice
+
+
+def test_fp32_3xtf32_8192_and_batched(ctx):
+    s = 1.0 / np.sqrt(8192.0)
+    A = datagen.uniform(datagen.SEEDS["mm_A"], (8192, 8192), -s, s)
+    B = datagen.uniform(datagen.SEEDS["mm_B"], (8192, 8192), -s, s)
+    _sample_check(mm(ctx, A, B, precision=abi.MM_FP32_3XTF32), A, B, 1e-4)
+    s = 1.0 / np.sqrt(1024.0)
+    Ab = datagen.uniform(datagen.SEEDS["mm_Ab"], (32, 2048, 1024), -s, s)
+    Bb = datagen.uniform(datagen.SEEDS["mm_Bb"], (32, 1024, 2048), -s, s)
+    Cb = mm(ctx, Ab, Bb, precision=abi.MM_FP32_3XTF32)
+    for bi in (0, 17, 31):
+        _sample_check(Cb[bi], Ab[bi], Bb[bi], 1e-4, n=64, seed=bi)
+
+
+def test_fp32_3xtf32_rejects_unsupported_shapes(ctx):
+    with pytest.raises(abi.QsmlError) as e:
+        mm(ctx, np.ones((4, 33), np.float32), np.ones((33, 8), np.float32), precision=abi.MM_FP32_3XTF32)
+    assert e.value.status == abi.E_UNSUPPORTED
