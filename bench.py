@@ -20,8 +20,8 @@ roofline  : the dominant kernel family of the step, its algorithmic bytes per
             bandwidth (MEASURED_PEAKS.json).
 cpu_baseline / --impl reference : the oracle's CPU restatement of the same
             reductions (OpenMP over all host cores) on a bounded sample.
-other_workloads (N=1): the elementwise chain, strided gathers, layer norm and
-            matmul configurations, each timed the same way.
+other_workloads (N=1): the elementwise chain, strided gathers, layer norm,
+            argmax/argmin and matmul configurations, each timed the same way.
 """
 from __future__ import annotations
 
@@ -341,6 +341,35 @@ class GatherWorkload(Workload):
     def compute(self, calls=None):
         for v, o, _ in (self.calls if calls is None else calls):
             self.ctx.gather(v, o)
+
+
+class ArgReduceWorkload(Workload):
+    name = "argmax/argmin X[64,512,1024] fp32 and fp16 over axis 0, 1, 2 and all, I32 indices"
+    SHAPE = (64, 512, 1024)
+
+    def __init__(self, ctx, dist: Dist):
+        import torch
+        from quasarml_b200 import abi, datagen
+        self.ctx = ctx
+        n = int(np.prod(self.SHAPE))
+        X = _t(datagen.normal(datagen.SEEDS["red_X"], self.SHAPE, 0.0, 1.0, offset=dist.rank * n))
+        Xh = X.half()
+        self.keep = [X, Xh]
+        self.calls = []
+        for x, es in ((X, 4), (Xh, 2)):
+            for axis in (None, 0, 1, 2):
+                oshape = abi.reduced_shape(self.SHAPE, axis, False)
+                out = torch.empty(oshape, dtype=torch.int32, device="cuda")
+                self.keep.append(out)
+                for op in (abi.ARG_MAX, abi.ARG_MIN):
+                    self.calls.append((op, abi.desc_of(x), abi.AXIS_ALL if axis is None else axis,
+                                       abi.desc_of(out), n * es + out.numel() * 4))
+        self.units_per_step = sum(c[4] for c in self.calls)
+        self.unit = "GB/s"
+
+    def compute(self, calls=None):
+        for op, x, axis, o, _ in (self.calls if calls is None else calls):
+            self.ctx.arg_reduce(op, x, axis, False, o)
 
 
 class LayerNormWorkload(Workload):
@@ -736,6 +765,7 @@ def main():
         for key, mk, st in (("elementwise_chain", lambda: ChainWorkload(ctx, dist), 10),
                             ("gather", lambda: GatherWorkload(ctx, dist), 20),
                             ("layernorm", lambda: LayerNormWorkload(ctx, dist), 20),
+                            ("argmax_argmin", lambda: ArgReduceWorkload(ctx, dist), 20),
                             ("matmul_f16_8192", lambda: MatmulWorkload(ctx, dist, "f16", False), 5),
                             ("matmul_f32_8192_3xtf32", lambda: MatmulWorkload(ctx, dist, "f32", False), 5),
                             ("matmul_f32_8192_ffma", lambda: MatmulWorkload(ctx, dist, "f32", False, "ffma"), 3),

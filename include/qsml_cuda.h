@@ -103,6 +103,10 @@ typedef struct qsml_ctx qsml_ctx;
 #define QSML_RED_PROD 4
 #define QSML_AXIS_ALL (-1000)
 
+/* arg-reduction ops (qsml_arg_reduce) */
+#define QSML_ARG_MAX 0
+#define QSML_ARG_MIN 1
+
 /* Matmul precisions (qsml_matmul). */
 #define QSML_MM_AUTO 0          /* F32 inputs -> FP32_FFMA, F16 -> FP16_F32ACC */
 #define QSML_MM_FP32_FFMA 1     /* fp32 CUDA-core fma, k ascending             */
@@ -214,6 +218,19 @@ QSML_API qsml_status_t qsml_unary(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a
  * (QuasarML/src/Ops/Reduction.cpp:285-382), whose axis max/min are stubs. */
 QSML_API qsml_status_t qsml_reduce(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a,
                                    int32_t axis, int32_t keepdims, const qsml_tdesc* out);
+
+/* Index of the largest (QSML_ARG_MAX) or smallest (QSML_ARG_MIN) element
+ * over one axis (negative counts from the end) or over all elements (axis =
+ * QSML_AXIS_ALL, an index into the flattened tensor).  Any input dtype,
+ * contiguous; out is I32 or U32 with the reduced shape (keepdims as in
+ * qsml_reduce).  Ties give the first index; values compare numerically
+ * (-0 == +0) and a NaN counts as beyond every number, so the first NaN wins
+ * (NumPy's argmax/argmin).  The reduced axis must be non-empty and shorter
+ * than 2^31 (I32 out) or 2^32 - 1 (U32 out).  Replaces Ops::argmax/argmin
+ * (QuasarML/src/Ops/Reduction.cpp:388-396), stubs there that ignore the axis
+ * and return the max/min value. */
+QSML_API qsml_status_t qsml_arg_reduce(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a,
+                                       int32_t axis, int32_t keepdims, const qsml_tdesc* out);
 
 /* Materialises a strided view (any strides, including 0 and negative) into
  * `out` of the same shape and dtype, bit-exactly.  `out` is normally

@@ -381,6 +381,50 @@ void orc_reduce_f16(int op, const uint16_t* x, int64_t outer, int64_t k, int64_t
 }
 
 /* ------------------------------------------------------------------------ */
+/* argmax / argmin                                                            */
+/* ------------------------------------------------------------------------ */
+
+/* The reference's argmax/argmin (Ops/Reduction.cpp:388-396) ignore the axis
+ * and return max/min values, not indices.  This restates what the names
+ * promise, with NumPy's argmax/argmin conventions: scan k in ascending
+ * order, keep the first strictly better value; a NaN beats every number and
+ * the first NaN is kept.  Values are read as double (exact for every
+ * QSML dtype). */
+static inline double arg_load(int dtype, const void* x, int64_t i) {
+    switch (dtype) {
+        case 0: return ((const float*)x)[i];
+        case 1: return h2f(((const uint16_t*)x)[i]);
+        case 2: return ((const int32_t*)x)[i];
+        case 3: return ((const int16_t*)x)[i];
+        case 4: return ((const int8_t*)x)[i];
+        case 5: return ((const uint32_t*)x)[i];
+        case 6: return ((const uint16_t*)x)[i];
+        default: return ((const uint8_t*)x)[i];
+    }
+}
+
+void orc_argreduce(int op, int dtype, const void* x, int64_t outer, int64_t k, int64_t inner, int64_t* out) {
+    if (dtype == 1) h2f_table_init();
+#pragma omp parallel for schedule(static)
+    for (int64_t o = 0; o < outer; ++o) {
+        for (int64_t i = 0; i < inner; ++i) {
+            const int64_t base = o * k * inner + i;
+            double best = arg_load(dtype, x, base);
+            int64_t bi = 0;
+            for (int64_t j = 1; j < k && best == best; ++j) {
+                const double v = arg_load(dtype, x, base + j * inner);
+                const int better = v != v || (op == 0 ? v > best : v < best);
+                if (better) {
+                    best = v;
+                    bi = j;
+                }
+            }
+            out[o * inner + i] = bi;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Strided gather                                                             */
 /* ------------------------------------------------------------------------ */
 

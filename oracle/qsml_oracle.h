@@ -90,6 +90,13 @@ void orc_reduce_f32(int op, const float* x, int64_t outer, int64_t k, int64_t in
 void orc_reduce_f16(int op, const uint16_t* x, int64_t outer, int64_t k, int64_t inner,
                     float* out32, double* out64, double* absum);
 
+/* argmax (op 0) / argmin (op 1) of x viewed as [outer, k, inner] over the
+ * middle axis, k >= 1; dtype is a QSML_* code (F32 .. U8).  out[o*inner+i]
+ * is the first index of the largest (smallest) value; values compare
+ * numerically (-0 == +0) and a NaN counts as larger (smaller) than every
+ * number, so the first NaN wins. */
+void orc_argreduce(int op, int dtype, const void* x, int64_t outer, int64_t k, int64_t inner, int64_t* out);
+
 /* Strided gather: copies the view (base, ndim, shape, strides in elements,
  * possibly negative) of esize-byte elements into contiguous out. */
 void orc_gather(const void* base, int esize, int ndim, const int64_t* shape,

@@ -53,6 +53,7 @@ def _load():
         "orc_unary_f32": (ctypes.c_int, [ctypes.c_int, _P, _I64, _P]),
         "orc_reduce_f32": (None, [ctypes.c_int, _P, _I64, _I64, _I64, _P, _P, _P]),
         "orc_reduce_f16": (None, [ctypes.c_int, _P, _I64, _I64, _I64, _P, _P, _P]),
+        "orc_argreduce": (None, [ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P]),
         "orc_gather": (None, [_P, ctypes.c_int, ctypes.c_int, _P, _P, _P]),
         "orc_layer_norm_f32": (None, [_P, _P, _P, _I64, _I64, ctypes.c_float, _P]),
         "orc_layer_norm_f16": (None, [_P, _P, _P, _I64, _I64, ctypes.c_float, _P]),
@@ -165,6 +166,31 @@ def reduce(op: int, x: np.ndarray, axis=None):
     fn = L.orc_reduce_f32 if x.dtype == np.float32 else L.orc_reduce_f16
     fn(op, _ptr(x), outer, k, inner, _ptr(o32), _ptr(o64), _ptr(ab))
     return o32.reshape(oshape), o64.reshape(oshape), ab.reshape(oshape)
+
+
+ARGMAX, ARGMIN = 0, 1
+_QSML_DTYPE = {np.dtype(np.float32): 0, np.dtype(np.float16): 1, np.dtype(np.int32): 2, np.dtype(np.int16): 3,
+               np.dtype(np.int8): 4, np.dtype(np.uint32): 5, np.dtype(np.uint16): 6, np.dtype(np.uint8): 7}
+
+
+def argreduce(op: int, x: np.ndarray, axis=None) -> np.ndarray:
+    """Index (int64) of the first max (op ARGMAX) or min (ARGMIN) over `axis`
+    (None = the flattened array); NaN beats every number."""
+    L = _load()
+    x = np.ascontiguousarray(x)
+    if axis is None:
+        outer, k, inner, oshape = 1, x.size, 1, ()
+    else:
+        ax = axis + x.ndim if axis < 0 else axis
+        outer = int(np.prod(x.shape[:ax], dtype=np.int64))
+        k = x.shape[ax]
+        inner = int(np.prod(x.shape[ax + 1:], dtype=np.int64))
+        oshape = tuple(d for i, d in enumerate(x.shape) if i != ax)
+    if k == 0:
+        raise ValueError("argreduce of an empty axis")
+    out = np.empty(outer * inner, dtype=np.int64)
+    L.orc_argreduce(op, _QSML_DTYPE[x.dtype], _ptr(x), outer, k, inner, _ptr(out))
+    return out.reshape(oshape)
 
 
 def gather(base: np.ndarray, offset: int, shape, strides) -> np.ndarray:

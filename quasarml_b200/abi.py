@@ -28,6 +28,7 @@ OP_ADD, OP_SUB, OP_MUL, OP_DIV, OP_POW = range(5)
  UN_SIGMOID, UN_GELU) = range(11)
 RED_SUM, RED_MEAN, RED_MAX, RED_MIN, RED_PROD = range(5)
 AXIS_ALL = -1000
+ARG_MAX, ARG_MIN = 0, 1
 MM_AUTO, MM_FP32_FFMA, MM_FP32_3XTF32, MM_FP16_F32ACC = range(4)
 
 DTYPE_SIZE = {F32: 4, F16: 2, I32: 4, I16: 2, I8: 1, U32: 4, U16: 2, U8: 1}
@@ -78,6 +79,7 @@ _SIGS = {
     "qsml_binary_scalar": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_float, _P(TDesc)]),
     "qsml_unary": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _P(TDesc)]),
     "qsml_reduce": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_int32, _c.c_int32, _P(TDesc)]),
+    "qsml_arg_reduce": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_int32, _c.c_int32, _P(TDesc)]),
     "qsml_gather": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc)]),
     "qsml_layer_norm": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_float, _P(TDesc)]),
     "qsml_matmul": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_int32]),
@@ -240,6 +242,10 @@ class Context:
 
     def reduce(self, op: int, a: TDesc, axis: int, keepdims: bool, out: TDesc) -> None:
         self.check(self.lib.qsml_reduce(self.h, op, ctypes.byref(a), int(axis), int(bool(keepdims)), ctypes.byref(out)))
+
+    def arg_reduce(self, op: int, a: TDesc, axis: int, keepdims: bool, out: TDesc) -> None:
+        self.check(self.lib.qsml_arg_reduce(self.h, op, ctypes.byref(a), int(axis), int(bool(keepdims)),
+                                            ctypes.byref(out)))
 
     def gather(self, src: TDesc, out: TDesc) -> None:
         self.check(self.lib.qsml_gather(self.h, ctypes.byref(src), ctypes.byref(out)))

@@ -145,6 +145,8 @@ inline TensorPtr max(TensorPtr x, i32 axis, bool keepdims = false) { return Quas
 inline TensorPtr min(TensorPtr x) { return QuasarML::Ops::min(device(), x); }
 inline TensorPtr min(TensorPtr x, i32 axis, bool keepdims = false) { return QuasarML::Ops::min(device(), x, axis, keepdims); }
 inline TensorPtr prod(TensorPtr x) { return QuasarML::Ops::prod(device(), x); }
+inline TensorPtr argmax(TensorPtr x, i32 axis = -1) { return QuasarML::Ops::argmax(device(), x, axis); }
+inline TensorPtr argmin(TensorPtr x, i32 axis = -1) { return QuasarML::Ops::argmin(device(), x, axis); }
 
 inline TensorPtr matmul(TensorPtr a, TensorPtr b) { return QuasarML::Ops::matmul(device(), a, b); }
 inline TensorPtr matmul(TensorPtr a, TensorPtr b, DataType out_dtype) { return QuasarML::Ops::matmul(device(), a, b, out_dtype); }

@@ -153,15 +153,22 @@ TP min(Device& d, TP a) { return reduce_all(d, QSML_RED_MIN, a); }
 TP min(Device& d, TP a, i32 axis, bool keepdims) { return reduce_axis(d, QSML_RED_MIN, a, axis, keepdims); }
 TP prod(Device& d, TP a) { return reduce_all(d, QSML_RED_PROD, a); }
 
-// The reference's argmax/argmin return max/min values, not indices
-// (Ops/Reduction.cpp:384-396); rather than reproduce that, they report that
-// this backend does not provide them.
-TP argmax(Device&, TP, i32) {
-    throw std::runtime_error("argmax is not provided by the B200 backend");
+// The reference's argmax/argmin (Ops/Reduction.cpp:388-396) ignore the axis
+// and return max/min values.  These return I32 indices over `axis` (the axis
+// is dropped from the shape): the first index of the largest (smallest)
+// value, a NaN counting as beyond every number.
+TP arg_reduce(Device& device, int op, const TP& a, i32 axis) {
+    QS_ASSERT(a, "null tensor");
+    axis = norm_axis(axis, a->rank());
+    QS_ASSERT(a->dim(axis) > 0, "argmax/argmin of an empty axis");
+    auto x = a->contiguous();
+    auto out = device.create_tensor(reduced_shape(a->shape(), axis, false), DataType::I32);
+    qsml_tdesc dx = x->desc(), dout = out->desc();
+    device.check(qsml_arg_reduce(device.ctx(), op, &dx, axis, 0, &dout));
+    return out;
 }
-TP argmin(Device&, TP, i32) {
-    throw std::runtime_error("argmin is not provided by the B200 backend");
-}
+TP argmax(Device& d, TP a, i32 axis) { return arg_reduce(d, QSML_ARG_MAX, a, axis); }
+TP argmin(Device& d, TP a, i32 axis) { return arg_reduce(d, QSML_ARG_MIN, a, axis); }
 
 // ---- linear algebra ---------------------------------------------------------
 TP matmul(Device& d, TP a, TP b) { return matmul(d, a, b, a->dtype()); }

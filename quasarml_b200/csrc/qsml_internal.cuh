@@ -101,6 +101,15 @@ qsml_status_t check_desc(Context* ctx, const qsml_tdesc* d, const char* name);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// A reduction of `a` over `axis` (QSML_AXIS_ALL = every element) viewed as
+// [outer, k, inner] (Ops/Reduction.cpp:310-312).  Checks that `out` has the
+// reduced shape: the axis dropped, or kept as 1 with keepdims, and shape [1]
+// (or a 1-element rank <= 1 tensor) when nothing is left, like
+// Reduction.cpp:297-305.  `what` prefixes the error message.
+qsml_status_t plan_reduction(Context* ctx, const qsml_tdesc* a, int32_t axis, int32_t keepdims,
+                             const qsml_tdesc* out, const char* what, int64_t* outer, int64_t* k,
+                             int64_t* inner);
+
 constexpr int kMaxDims = QSML_MAX_DIMS;
 
 }  // namespace qsml

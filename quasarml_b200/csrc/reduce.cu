@@ -407,35 +407,7 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
     if (!is_contiguous(out)) return set_error(C_, QSML_E_SHAPE, "qsml_reduce: out must be contiguous");
 
     int64_t outer = 1, k = 1, inner = 1;
-    int64_t expect[QSML_MAX_DIMS];
-    int en = 0;
-    if (axis == QSML_AXIS_ALL) {
-        k = numel(a);
-        if (numel(out) != 1) return set_error(C_, QSML_E_SHAPE, "qsml_reduce: full reduction needs a 1-element out");
-    } else {
-        int ax = axis < 0 ? axis + a->ndim : axis;
-        if (ax < 0 || ax >= a->ndim) return set_error(C_, QSML_E_SHAPE, "qsml_reduce: invalid axis");
-        for (int i = 0; i < ax; ++i) outer *= a->shape[i];
-        k = a->shape[ax];
-        for (int i = ax + 1; i < a->ndim; ++i) inner *= a->shape[i];
-        for (int i = 0; i < a->ndim; ++i) {
-            if (i == ax) {
-                if (keepdims) expect[en++] = 1;
-            } else {
-                expect[en++] = a->shape[i];
-            }
-        }
-        // The reference returns shape [1] when every dim is reduced away
-        // (Reduction.cpp:297-305).
-        bool ok = true;
-        if (en == 0) {
-            ok = numel(out) == 1 && out->ndim <= 1;
-        } else {
-            ok = out->ndim == en;
-            for (int i = 0; ok && i < en; ++i) ok = out->shape[i] == expect[i];
-        }
-        if (!ok) return set_error(C_, QSML_E_SHAPE, "qsml_reduce: out shape does not match the reduced shape");
-    }
+    QSML_TRY_STATUS(plan_reduction(C_, a, axis, keepdims, out, "qsml_reduce", &outer, &k, &inner));
     const int64_t nout = outer * inner;
     if (nout == 0) return QSML_OK;
     if (k == 0) {

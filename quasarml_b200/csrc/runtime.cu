@@ -54,6 +54,43 @@ qsml_status_t check_desc(Context* ctx, const qsml_tdesc* d, const char* name) {
     return QSML_OK;
 }
 
+qsml_status_t plan_reduction(Context* ctx, const qsml_tdesc* a, int32_t axis, int32_t keepdims,
+                             const qsml_tdesc* out, const char* what, int64_t* outer, int64_t* k,
+                             int64_t* inner) {
+    *outer = 1;
+    *k = 1;
+    *inner = 1;
+    if (axis == QSML_AXIS_ALL) {
+        *k = numel(a);
+        if (numel(out) != 1)
+            return set_error(ctx, QSML_E_SHAPE, std::string(what) + ": full reduction needs a 1-element out");
+        return QSML_OK;
+    }
+    const int ax = axis < 0 ? axis + a->ndim : axis;
+    if (ax < 0 || ax >= a->ndim) return set_error(ctx, QSML_E_SHAPE, std::string(what) + ": invalid axis");
+    int64_t expect[kMaxDims];
+    int en = 0;
+    for (int i = 0; i < a->ndim; ++i) {
+        if (i < ax) *outer *= a->shape[i];
+        if (i > ax) *inner *= a->shape[i];
+        if (i == ax) {
+            *k = a->shape[i];
+            if (keepdims) expect[en++] = 1;
+        } else {
+            expect[en++] = a->shape[i];
+        }
+    }
+    bool ok = true;
+    if (en == 0) {
+        ok = numel(out) == 1 && out->ndim <= 1;
+    } else {
+        ok = out->ndim == en;
+        for (int i = 0; ok && i < en; ++i) ok = out->shape[i] == expect[i];
+    }
+    if (!ok) return set_error(ctx, QSML_E_SHAPE, std::string(what) + ": out shape does not match the reduced shape");
+    return QSML_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Caching allocator
 // ---------------------------------------------------------------------------

@@ -152,6 +152,16 @@ static void test_axis_reductions() {
     auto sv = get(s1);
     check("sum axis 1", sv[0] == 13 && sv[1] == 14);
     check("mean axis 0", get(qsml::mean(A, 0))[1] == 7.0f);
+    // argmax/argmin give I32 indices (the reference's return values)
+    auto am = qsml::argmax(A);  // last axis
+    vector<int32_t> ai(am->numel());
+    am->download(ai.data(), ai.size() * sizeof(int32_t));
+    check("argmax dtype/shape", am->dtype() == QuasarML::DataType::I32 && am->rank() == 1 && am->dim(0) == 2);
+    check("argmax axis -1", ai[0] == 1 && ai[1] == 0);
+    auto an = qsml::argmin(A, 0);
+    vector<int32_t> ni(an->numel());
+    an->download(ni.data(), ni.size() * sizeof(int32_t));
+    check("argmin axis 0", ni.size() == 3 && ni[0] == 0 && ni[1] == 1 && ni[2] == 1);
 }
 
 static void test_views_and_gathers() {

@@ -205,3 +205,22 @@ def test_prod_reference_order(orc):
     assert o32 == np.float32(-7.5) and o64 == -7.5
     y = np.arange(1, 11, dtype=np.float32).reshape(2, 5)
     assert np.array_equal(orc.reduce(orc.PROD, y, axis=1)[0], np.float32([120, 30240]))
+
+
+def test_argreduce_matches_numpy(orc):
+    """argmax/argmin: the reference's are stubs returning values
+    (Reduction.cpp:388-396); the oracle restates NumPy's index semantics,
+    checked here against NumPy itself, NaN and ties included."""
+    rng = np.random.default_rng(3)
+    for dt in (np.float32, np.float16, np.int32, np.int16, np.int8, np.uint32, np.uint16, np.uint8):
+        x = rng.integers(0, 20, (7, 9, 11)).astype(dt)
+        for ax in (None, 0, 1, 2, -1):
+            assert np.array_equal(orc.argreduce(orc.ARGMAX, x, ax), np.argmax(x, axis=ax)), (dt, ax)
+            assert np.array_equal(orc.argreduce(orc.ARGMIN, x, ax), np.argmin(x, axis=ax)), (dt, ax)
+    y = np.float32([1, np.nan, 3, np.nan, -0.0, 0.0])
+    assert orc.argreduce(orc.ARGMAX, y) == np.argmax(y) == 1
+    assert orc.argreduce(orc.ARGMIN, y) == np.argmin(y) == 1
+    z = np.float32([0.0, -0.0, 5.0, -0.0])
+    assert orc.argreduce(orc.ARGMIN, z) == np.argmin(z) == 0
+    with pytest.raises(ValueError):
+        orc.argreduce(orc.ARGMAX, np.zeros((3, 0), np.float32), 1)
