@@ -20,8 +20,9 @@ roofline  : the dominant kernel family of the step, its algorithmic bytes per
             bandwidth (MEASURED_PEAKS.json).
 cpu_baseline / --impl reference : the oracle's CPU restatement of the same
             reductions (OpenMP over all host cores) on a bounded sample.
-other_workloads (N=1): the elementwise chain, strided gathers, layer norm,
-            argmax/argmin and matmul configurations, each timed the same way.
+other_workloads (N=1): the elementwise chain (op by op and fused), strided
+            gathers, layer norm, argmax/argmin and matmul configurations, each
+            timed the same way.
 """
 from __future__ import annotations
 
@@ -315,6 +316,40 @@ class ChainWorkload(Workload):
                 ctx.binary_scalar(op, a, b, out)
             else:
                 ctx.unary(op, a, out)
+
+
+class FusedChainWorkload(Workload):
+    """The same chain as ChainWorkload in one qsml_elementwise_fused call per
+    set; algorithmic bytes = read A, B, D once + write the result."""
+    name = ("elementwise chain relu(pow((A+B)*B - A, 2.0) / D) fused into one kernel, A[4096,4096], B[1,4096], "
+            "D[4096,1] fp32")
+
+    def __init__(self, ctx, dist: Dist, batch: int = 4):
+        import torch
+        from quasarml_b200 import abi, datagen
+        self.ctx = ctx
+        N = 4096 * 4096
+        e = abi.Expr()
+        a, b, dd = e.input(0), e.input(1), e.input(2)
+        t = e.binary(abi.OP_SUB, e.binary(abi.OP_MUL, e.binary(abi.OP_ADD, a, b), b), a)
+        e.unary(abi.UN_RELU, e.binary(abi.OP_DIV, e.binary(abi.OP_POW, t, e.const(2.0)), dd))
+        self.nodes = (abi.FuseNode * len(e.nodes))(*[abi.FuseNode(*n) for n in e.nodes])
+        self.keep, self.calls = [], []
+        d = abi.desc_of
+        for bi in range(batch):
+            off = (bi * dist.world + dist.rank)
+            A = _t(datagen.uniform(datagen.SEEDS["ew_A"], (4096, 4096), -1, 1, offset=off * N))
+            B = _t(datagen.uniform(datagen.SEEDS["ew_B"], (1, 4096), -1, 1))
+            D = _t(datagen.uniform(datagen.SEEDS["ew_D"], (4096, 1), 0.5, 2, offset=off * 4096))
+            out = torch.empty((4096, 4096), device="cuda")
+            self.keep += [A, B, D, out]
+            self.calls.append(([d(A), d(B), d(D)], d(out), 2 * N * 4 + 2 * 4096 * 4))
+        self.units_per_step = sum(c[2] for c in self.calls)
+        self.unit = "GB/s"
+
+    def compute(self, calls=None):
+        for ins, out, _ in (self.calls if calls is None else calls):
+            self.ctx.elementwise_fused(self.nodes, ins, out)
 
 
 class GatherWorkload(Workload):
@@ -654,6 +689,16 @@ def run_single(which: str, reps: int = 3):
         out = torch.empty_like(A)
         for _ in range(reps):
             ctx.binary(abi.OP_ADD, d(A), d(B), d(out))
+    elif which == "chain_fused":
+        wl = FusedChainWorkload(ctx, Dist(), batch=1)
+        for _ in range(reps):
+            wl.compute()
+    elif which.startswith("argmax"):
+        x = _t(datagen.normal(datagen.SEEDS["red_X"], (64, 512, 1024), 0.0, 1.0))
+        axis = None if which == "argmax_all" else 1
+        out = torch.empty(abi.reduced_shape(tuple(x.shape), axis, False), dtype=torch.int32, device="cuda")
+        for _ in range(reps):
+            ctx.arg_reduce(abi.ARG_MAX, d(x), abi.AXIS_ALL if axis is None else axis, False, d(out))
     elif which.startswith("gather"):
         X = _t(datagen.iota_i32((8192, 8192)))
         if which == "gather_t":
@@ -696,7 +741,8 @@ def main():
                     choices=["reduce", "chain", "gather", "layernorm", "matmul_f16", "matmul_f32"])
     ap.add_argument("--single", default=None,
                     choices=["reduce_all", "reduce_axis0", "reduce_axis1", "reduce_axis2", "reduce_all_f16",
-                             "chain_add", "gather_t", "gather_s", "layernorm", "matmul_f16"],
+                             "chain_add", "chain_fused", "gather_t", "gather_s", "layernorm", "matmul_f16",
+                             "argmax_all", "argmax_axis1"],
                     help="run one kernel of the workloads a few times and exit (profiling aid, prints nothing)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -763,6 +809,7 @@ def main():
         del wl
         torch.cuda.empty_cache()
         for key, mk, st in (("elementwise_chain", lambda: ChainWorkload(ctx, dist), 10),
+                            ("elementwise_chain_fused", lambda: FusedChainWorkload(ctx, dist), 20),
                             ("gather", lambda: GatherWorkload(ctx, dist), 20),
                             ("layernorm", lambda: LayerNormWorkload(ctx, dist), 20),
                             ("argmax_argmin", lambda: ArgReduceWorkload(ctx, dist), 20),

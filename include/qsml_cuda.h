@@ -232,6 +232,61 @@ QSML_API qsml_status_t qsml_reduce(qsml_ctx* ctx, int32_t op, const qsml_tdesc* 
 QSML_API qsml_status_t qsml_arg_reduce(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a,
                                        int32_t axis, int32_t keepdims, const qsml_tdesc* out);
 
+/* Fused elementwise expression: out = the value of the last node, computed
+ * per element in one kernel that reads every input once and writes only out.
+ * Nodes form a DAG in topological order (operands are earlier nodes):
+ *   QSML_FUSE_INPUT   inputs[code]
+ *   QSML_FUSE_CONST   the binary32 `value`
+ *   QSML_FUSE_BINARY  QSML_OP_<code>(node a, node b)
+ *   QSML_FUSE_UNARY   QSML_UN_<code>(node a)
+ * Inputs broadcast to out's shape (NumPy rules; out must be exactly their
+ * broadcast shape) and share out's dtype, F32 or F16.  Every node computes
+ * what qsml_binary / qsml_unary computes for that element and rounds to the
+ * dtype, and a CONST operand acts like qsml_binary_scalar's `s` (used as
+ * binary32), so the result is bit-identical to the unfused sequence of calls.
+ * At most QSML_FUSE_MAX_NODES nodes and QSML_FUSE_MAX_INPUTS inputs; very
+ * deep or heavily shared expressions may exceed the kernel's program limits
+ * (48 instructions after expanding shared nodes, 16 distinct constants, 3
+ * temporaries) and return QSML_E_UNSUPPORTED.  The reference has no fusion
+ * (README.md:78 lists it as not done): each of its ops is a dispatch that
+ * writes a full intermediate (QuasarML/src/Ops/Elementwise.cpp:139-417). */
+#define QSML_FUSE_INPUT 0
+#define QSML_FUSE_CONST 1
+#define QSML_FUSE_BINARY 2
+#define QSML_FUSE_UNARY 3
+#define QSML_FUSE_MAX_NODES 64
+#define QSML_FUSE_MAX_INPUTS 6
+
+typedef struct {
+    int32_t kind;   /* QSML_FUSE_*                                   */
+    int32_t code;   /* input index, QSML_OP_* or QSML_UN_*            */
+    int32_t a, b;   /* operand node indices (b: binary nodes only)    */
+    float value;    /* QSML_FUSE_CONST                                */
+} qsml_fuse_node;
+
+QSML_API qsml_status_t qsml_elementwise_fused(qsml_ctx* ctx, const qsml_fuse_node* nodes, int32_t n_nodes,
+                                              const qsml_tdesc* inputs, int32_t n_inputs,
+                                              const qsml_tdesc* out);
+
+/* Which kernel runs a fused expression.  AUTO (the default): a kernel
+ * generated for the expression and compiled at run time with NVRTC (first
+ * use of each expression / dtype / layout class; cached per device) when the
+ * collapsed layout is at most 2-D with every input contiguous or broadcast
+ * along the inner dim, else the precompiled interpreter kernel.  INTERP:
+ * always the interpreter.  JIT: the compiled kernel or QSML_E_UNSUPPORTED.
+ * All paths give bit-identical results.  The reference compiles a generated
+ * shader per op at run time (QuasarML/src/Ops/ShaderGen.cpp,
+ * Backend/Vulkan/VulkanBackend.cpp:44-80). */
+#define QSML_FUSE_MODE_AUTO 0
+#define QSML_FUSE_MODE_INTERP 1
+#define QSML_FUSE_MODE_JIT 2
+QSML_API qsml_status_t qsml_set_fuse_mode(qsml_ctx* ctx, int32_t mode);
+
+/* Fused launches on this context by kernel kind, and the number of
+ * expression kernels compiled so far in the process. */
+QSML_API qsml_status_t qsml_fuse_stats(qsml_ctx* ctx, uint64_t* jit_launches, uint64_t* interp_launches,
+                                       uint64_t* jit_kernels);
+
 /* Materialises a strided view (any strides, including 0 and negative) into
  * `out` of the same shape and dtype, bit-exactly.  `out` is normally
  * contiguous (the fast paths); a strided `out` (a slice of a larger tensor,

@@ -47,6 +47,50 @@ class TDesc(ctypes.Structure):
     ]
 
 
+FUSE_INPUT, FUSE_CONST, FUSE_BINARY, FUSE_UNARY = range(4)
+FUSE_MODE_AUTO, FUSE_MODE_INTERP, FUSE_MODE_JIT = range(3)
+FUSE_MAX_NODES, FUSE_MAX_INPUTS = 64, 6
+
+
+class FuseNode(ctypes.Structure):
+    """One node of a qsml_elementwise_fused expression."""
+    _fields_ = [
+        ("kind", ctypes.c_int32),
+        ("code", ctypes.c_int32),
+        ("a", ctypes.c_int32),
+        ("b", ctypes.c_int32),
+        ("value", ctypes.c_float),
+    ]
+
+
+class Expr:
+    """Builds a qsml_elementwise_fused node list:
+
+        e = Expr(); A, B = e.input(0), e.input(1)
+        root = e.unary(UN_RELU, e.binary(OP_ADD, A, e.const(2.0)))
+        ctx.elementwise_fused(e.nodes, [dA, dB], dOut)   # root = last node
+    """
+
+    def __init__(self):
+        self.nodes = []
+
+    def _add(self, kind, code=0, a=0, b=0, value=0.0) -> int:
+        self.nodes.append((kind, code, a, b, value))
+        return len(self.nodes) - 1
+
+    def input(self, j: int) -> int:
+        return self._add(FUSE_INPUT, j)
+
+    def const(self, v: float) -> int:
+        return self._add(FUSE_CONST, value=float(v))
+
+    def binary(self, op: int, a: int, b: int) -> int:
+        return self._add(FUSE_BINARY, op, a, b)
+
+    def unary(self, op: int, a: int) -> int:
+        return self._add(FUSE_UNARY, op, a)
+
+
 class QsmlError(RuntimeError):
     def __init__(self, status: int, message: str):
         super().__init__(f"{STATUS_NAME.get(status, status)}: {message}")
@@ -80,6 +124,10 @@ _SIGS = {
     "qsml_unary": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _P(TDesc)]),
     "qsml_reduce": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_int32, _c.c_int32, _P(TDesc)]),
     "qsml_arg_reduce": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_int32, _c.c_int32, _P(TDesc)]),
+    "qsml_elementwise_fused": (_c.c_int32, [_c.c_void_p, _P(FuseNode), _c.c_int32, _P(TDesc), _c.c_int32,
+                                            _P(TDesc)]),
+    "qsml_set_fuse_mode": (_c.c_int32, [_c.c_void_p, _c.c_int32]),
+    "qsml_fuse_stats": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64), _P(_c.c_uint64), _P(_c.c_uint64)]),
     "qsml_gather": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc)]),
     "qsml_layer_norm": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_float, _P(TDesc)]),
     "qsml_matmul": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_int32]),
@@ -246,6 +294,28 @@ class Context:
     def arg_reduce(self, op: int, a: TDesc, axis: int, keepdims: bool, out: TDesc) -> None:
         self.check(self.lib.qsml_arg_reduce(self.h, op, ctypes.byref(a), int(axis), int(bool(keepdims)),
                                             ctypes.byref(out)))
+
+    def elementwise_fused(self, nodes, inputs: Sequence[TDesc], out: TDesc) -> None:
+        """nodes: FuseNode array or (kind, code, a, b, value) tuples; the
+        last node is the result."""
+        if not isinstance(nodes, ctypes.Array):
+            arr = (FuseNode * max(len(nodes), 1))()
+            for i, n in enumerate(nodes):
+                arr[i] = FuseNode(*n)
+            n_nodes = len(nodes)
+        else:
+            arr, n_nodes = nodes, len(nodes)
+        ins = (TDesc * max(len(inputs), 1))(*inputs)
+        self.check(self.lib.qsml_elementwise_fused(self.h, arr, n_nodes, ins, len(inputs), ctypes.byref(out)))
+
+    def set_fuse_mode(self, mode: int) -> None:
+        self.check(self.lib.qsml_set_fuse_mode(self.h, int(mode)))
+
+    def fuse_stats(self) -> tuple:
+        """(runtime-compiled launches, interpreter launches, kernels compiled)."""
+        j, i, k = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        self.check(self.lib.qsml_fuse_stats(self.h, ctypes.byref(j), ctypes.byref(i), ctypes.byref(k)))
+        return j.value, i.value, k.value
 
     def gather(self, src: TDesc, out: TDesc) -> None:
         self.check(self.lib.qsml_gather(self.h, ctypes.byref(src), ctypes.byref(out)))

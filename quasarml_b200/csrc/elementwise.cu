@@ -15,127 +15,19 @@
 //   * k_ew_generic: any strides (one element per thread), always correct.
 // Arithmetic is IEEE binary32 with explicit round-to-nearest intrinsics, so
 // no multiply-add contraction can happen (bit-exact with the oracle).
-#include "qsml_internal.cuh"
+#include "ew_common.cuh"
 
 namespace qsml {
 namespace {
+
+using namespace ew;
 
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
 
 // ---------------------------------------------------------------------------
-// Element types: storage type T, compute type C.
+// Plan: collapsed output shape and per-operand element strides (ew_common.cuh).
 // ---------------------------------------------------------------------------
-template <typename T> struct Elem;
-template <> struct Elem<float> {
-    using C = float;
-    static __device__ __forceinline__ float ld(float v) { return v; }
-    static __device__ __forceinline__ float st(float v) { return v; }
-};
-template <> struct Elem<__half> {
-    using C = float;
-    static __device__ __forceinline__ float ld(__half v) { return __half2float(v); }
-    static __device__ __forceinline__ __half st(float v) { return __float2half_rn(v); }
-};
-template <> struct Elem<int32_t> {
-    using C = int32_t;
-    static __device__ __forceinline__ int32_t ld(int32_t v) { return v; }
-    static __device__ __forceinline__ int32_t st(int32_t v) { return v; }
-};
-
-template <typename T> struct alignas(16) Pack {
-    static constexpr int N = 16 / sizeof(T);
-    T v[N];
-};
-
-// ---------------------------------------------------------------------------
-// Operators
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ float pow_f32(float x, float y) {
-    // Exponent 2 is the single correctly rounded product; any other exponent
-    // goes through binary64 pow (error far below 1 binary32 ulp) rounded once.
-    if (y == 2.0f) return __fmul_rn(x, x);
-    return __double2float_rn(pow(static_cast<double>(x), static_cast<double>(y)));
-}
-
-template <int OP> struct BinOp {
-    __device__ __forceinline__ float operator()(float a, float b) const {
-        if (OP == QSML_OP_ADD) return __fadd_rn(a, b);
-        if (OP == QSML_OP_SUB) return __fsub_rn(a, b);
-        if (OP == QSML_OP_MUL) return __fmul_rn(a, b);
-        if (OP == QSML_OP_DIV) return __fdiv_rn(a, b);
-        return pow_f32(a, b);
-    }
-    __device__ __forceinline__ int32_t operator()(int32_t a, int32_t b) const {
-        uint32_t ua = static_cast<uint32_t>(a), ub = static_cast<uint32_t>(b);
-        if (OP == QSML_OP_ADD) return static_cast<int32_t>(ua + ub);
-        if (OP == QSML_OP_SUB) return static_cast<int32_t>(ua - ub);
-        if (OP == QSML_OP_MUL) return static_cast<int32_t>(ua * ub);
-        if (OP == QSML_OP_DIV) {
-            if (b == 0) return 0;
-            if (a == INT32_MIN && b == -1) return INT32_MIN;
-            return a / b;
-        }
-        return 0;
-    }
-};
-
-// Scalar right operand held by value.
-template <int OP> struct ScalarOp {
-    float s;
-    __device__ __forceinline__ float operator()(float a) const { return BinOp<OP>()(a, s); }
-    __device__ __forceinline__ int32_t operator()(int32_t a) const {
-        return BinOp<OP>()(a, static_cast<int32_t>(s));
-    }
-};
-
-template <int OP> struct UnOp {
-    __device__ __forceinline__ float operator()(float x) const {
-        switch (OP) {
-            case QSML_UN_RELU: return (x != x) ? x : (x > 0.0f ? x : 0.0f);
-            case QSML_UN_NEG: return -x;
-            case QSML_UN_ABS: return fabsf(x);
-            case QSML_UN_SQRT: return __fsqrt_rn(x);
-            case QSML_UN_EXP: return expf(x);
-            case QSML_UN_LOG: return logf(x);
-            case QSML_UN_SIN: return sinf(x);
-            case QSML_UN_COS: return cosf(x);
-            case QSML_UN_TANH: return tanhf(x);
-            case QSML_UN_SIGMOID:
-                // Ops/Elementwise.cpp:77: 1 / (1 + exp(-x))
-                return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
-            case QSML_UN_GELU: {
-                // Ops/Elementwise.cpp:93, evaluated left to right:
-                // 0.5*x*(1 + tanh(0.7978845608*(x + 0.044715*x*x*x)))
-                float c = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
-                float t = tanhf(__fmul_rn(0.7978845608f, __fadd_rn(x, c)));
-                return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, t));
-            }
-        }
-        return x;
-    }
-    __device__ __forceinline__ int32_t operator()(int32_t x) const {
-        switch (OP) {
-            case QSML_UN_RELU: return x > 0 ? x : 0;
-            case QSML_UN_NEG: return static_cast<int32_t>(0u - static_cast<uint32_t>(x));
-            case QSML_UN_ABS: return x < 0 ? static_cast<int32_t>(0u - static_cast<uint32_t>(x)) : x;
-        }
-        return x;
-    }
-};
-
-// relu on binary16 keeps NaN payloads and maps every non-positive to +0,
-// exactly like the binary32 rule (conversion is exact both ways).
-
-// ---------------------------------------------------------------------------
-// Plan: collapsed output shape and per-operand element strides.
-// ---------------------------------------------------------------------------
-struct EwPlan {
-    int nd;
-    int64_t shape[kMaxDims];
-    int64_t st[2][kMaxDims];  // input strides (0 = broadcast)
-};
-
 template <typename T, int NIN> struct Ptrs {
     const T* in[2];
     T* out;
@@ -145,20 +37,6 @@ template <typename C, int NIN, typename Op>
 __device__ __forceinline__ C apply(const Op& op, C a, C b) {
     if constexpr (NIN == 2) return op(a, b);
     else return op(a);
-}
-
-// Offset of the first element of collapsed row `row` for input j.
-template <typename IDX>
-__device__ __forceinline__ int64_t row_offset(const EwPlan& p, int j, IDX row) {
-    int64_t off = 0;
-    for (int d = p.nd - 2; d >= 1; --d) {
-        IDX e = static_cast<IDX>(p.shape[d]);
-        IDX c = row % e;
-        row /= e;
-        off += static_cast<int64_t>(c) * p.st[j][d];
-    }
-    if (p.nd >= 2) off += static_cast<int64_t>(row) * p.st[j][0];
-    return off;
 }
 
 // Row kernel: out is [R, Cn] with Cn % VEC == 0; each input's inner stride is
@@ -296,65 +174,6 @@ __global__ void __launch_bounds__(kThreads) k_ew_generic(Ptrs<T, NIN> P, EwPlan 
 // ---------------------------------------------------------------------------
 // Host planning
 // ---------------------------------------------------------------------------
-
-// Aligns each input's shape/strides to out's dims (NumPy broadcasting) and
-// collapses.  Returns QSML_OK or a shape error.
-qsml_status_t make_plan(Context* ctx, const qsml_tdesc* out, const qsml_tdesc* const* ins, int nin, EwPlan* p) {
-    const int nd = out->ndim;
-    int64_t shape[kMaxDims];
-    int64_t st[2][kMaxDims];
-    for (int d = 0; d < nd; ++d) shape[d] = out->shape[d];
-    for (int j = 0; j < nin; ++j) {
-        const qsml_tdesc* a = ins[j];
-        if (a->ndim > nd) return set_error(ctx, QSML_E_SHAPE, "input has more dims than the output");
-        for (int d = 0; d < nd; ++d) {
-            int ad = a->ndim - nd + d;
-            if (ad < 0) { st[j][d] = 0; continue; }
-            if (a->shape[ad] == out->shape[d]) st[j][d] = out->shape[d] == 1 ? 0 : a->stride[ad];
-            else if (a->shape[ad] == 1) st[j][d] = 0;
-            else return set_error(ctx, QSML_E_SHAPE, "operand shape does not broadcast to the output shape");
-        }
-    }
-    // Output shape must be exactly the broadcast of the inputs: every out
-    // extent > 1 must come from some input.
-    for (int d = 0; d < nd; ++d) {
-        if (out->shape[d] == 1) continue;
-        bool from_input = false;
-        for (int j = 0; j < nin; ++j) {
-            int ad = ins[j]->ndim - nd + d;
-            if (ad >= 0 && ins[j]->shape[ad] == out->shape[d]) from_input = true;
-        }
-        if (!from_input) return set_error(ctx, QSML_E_SHAPE, "output shape is not the broadcast shape of the inputs");
-    }
-    // Drop size-1 dims, then merge dims contiguous for every operand
-    // (out is contiguous, so only the inputs decide).
-    int n = 0;
-    for (int d = 0; d < nd; ++d) {
-        if (shape[d] == 1) continue;
-        if (n > 0) {
-            bool merge = true;
-            for (int j = 0; j < nin; ++j)
-                if (p->st[j][n - 1] != st[j][d] * shape[d]) merge = false;
-            if (merge) {
-                p->shape[n - 1] *= shape[d];
-                for (int j = 0; j < nin; ++j) p->st[j][n - 1] = st[j][d];
-                continue;
-            }
-        }
-        p->shape[n] = shape[d];
-        for (int j = 0; j < nin; ++j) p->st[j][n] = st[j][d];
-        ++n;
-    }
-    if (n == 0) {
-        p->shape[0] = 1;
-        for (int j = 0; j < 2; ++j) p->st[j][0] = 0;
-        n = 1;
-    }
-    for (int j = nin; j < 2; ++j)
-        for (int d = 0; d < n; ++d) p->st[j][d] = 0;
-    p->nd = n;
-    return QSML_OK;
-}
 
 template <typename T, int NIN, typename Op>
 qsml_status_t launch_ew(Context* ctx, const EwPlan& p, const qsml_tdesc* const* ins, const qsml_tdesc* out, Op op) {

@@ -57,6 +57,9 @@ struct Context {
     // qsml_synchronize reads and clears it.
     int* status = nullptr;
     uint64_t launches = 0;
+    // Fused elementwise expressions: QSML_FUSE_MODE_* and which kernel ran.
+    int fuse_mode = 0;
+    uint64_t fuse_jit_launches = 0, fuse_interp_launches = 0;
     std::mutex err_mu;
     std::string last_error;
 };
