@@ -31,8 +31,15 @@ public:
     std::shared_ptr<Tensor> create_tensor(const std::vector<u32>& shape, DataType dtype = DataType::F32,
                                           bool host_visible = false);
 
-    // Work is enqueued in order on one stream, so a batch needs no
-    // bracketing; these keep the reference's interface.
+    // Elementwise fusion: while on (set_fusion(true), or between begin_batch
+    // and end_batch) elementwise ops on F32/F16 tensors return deferred
+    // results that evaluate as one fused kernel on first access.
+    void set_fusion(bool on);
+    bool fusion() const { return _fusion; }
+    bool defer_elementwise() const { return _fusion || _in_batch; }
+
+    // Work is enqueued in order on one stream; a batch additionally defers
+    // and fuses elementwise ops (see set_fusion).
     void begin_batch();
     void end_batch();
     void flush_pending();
@@ -50,6 +57,7 @@ private:
     std::string _name;
     u32 _device_index = 0;
     bool _in_batch = false;
+    bool _fusion = false;
 };
 
 }  // namespace QuasarML

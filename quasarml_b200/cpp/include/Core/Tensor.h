@@ -6,11 +6,19 @@
 //    apart and contiguous() materialises one with a device gather;
 //  * refcounted storage: a view keeps its parent's buffer alive (the
 //    reference's views hold a raw handle with owns_buffer = false,
-//    Core/Tensor.cpp:128-136, and dangle when the parent dies).
+//    Core/Tensor.cpp:128-136, and dangle when the parent dies);
+//  * deferred elementwise results: with fusion on (Device::set_fusion, or
+//    inside begin_batch / end_batch) an elementwise op returns a tensor that
+//    holds the expression over its materialised inputs instead of memory.
+//    The first access to its data evaluates the whole expression in one
+//    fused kernel (qsml_elementwise_fused); writes into a buffer first
+//    evaluate the deferred tensors that read it, so results equal eager
+//    execution.
 #pragma once
 
 #include <functional>
 #include <memory>
+#include <mutex>
 #include <numeric>
 #include <string>
 #include <vector>
@@ -21,6 +29,7 @@
 namespace QuasarML {
 
 class Device;
+class Tensor;
 
 // A device allocation from the context's caching allocator.
 struct QS_API Storage {
@@ -32,6 +41,17 @@ struct QS_API Storage {
     void* ptr = nullptr;
     u64 bytes = 0;
     std::weak_ptr<int> alive;  // expires when the device (and its allocator) is gone
+    // Deferred tensors whose expression reads this buffer; evaluated before
+    // the buffer is written.
+    std::mutex readers_mu;
+    std::vector<std::weak_ptr<Tensor>> readers;
+};
+
+// A deferred elementwise expression: qsml_elementwise_fused's node list over
+// materialised input tensors (the last node is the value).
+struct LazyExpr {
+    std::vector<qsml_fuse_node> nodes;
+    std::vector<std::shared_ptr<Tensor>> inputs;
 };
 
 class QS_API Tensor : public std::enable_shared_from_this<Tensor> {
@@ -40,6 +60,9 @@ public:
     // View over existing storage (element strides and element offset).
     Tensor(std::shared_ptr<Storage> storage, const std::vector<u32>& shape, const std::vector<u64>& strides,
            u64 element_offset, DataType dtype);
+    // Deferred result of an elementwise expression (see the file comment);
+    // register_reads() must follow once the tensor is owned by a shared_ptr.
+    Tensor(Device* device, const std::vector<u32>& shape, DataType dtype, std::shared_ptr<LazyExpr> expr);
     ~Tensor() = default;
     Tensor(const Tensor&) = delete;
     Tensor& operator=(const Tensor&) = delete;
@@ -67,7 +90,7 @@ public:
     std::shared_ptr<Tensor> view(const std::vector<u32>& new_shape) const;
     std::shared_ptr<Tensor> flatten() const;
 
-    bool is_valid() const { return _storage != nullptr; }
+    bool is_valid() const { return _storage != nullptr || _lazy != nullptr; }
     bool is_shape_compatible(const Tensor& other) const { return _shape == other._shape; }
     bool is_broadcastable(const std::vector<u32>& target) const;
 
@@ -82,18 +105,29 @@ public:
     std::shared_ptr<Tensor> contiguous() const;  // *this if contiguous, else a gathered copy
     std::shared_ptr<Tensor> strided_view(const std::vector<u32>& shape, const std::vector<u64>& strides,
                                          u64 element_offset) const;
-    const std::shared_ptr<Storage>& storage() const { return _storage; }
+    const std::shared_ptr<Storage>& storage() const;
     void* data() const;            // device address of element [0, ..., 0]
     qsml_tdesc desc() const;       // descriptor for the C ABI
 
+    // Deferred results.
+    bool is_lazy() const { return _lazy != nullptr; }
+    const std::shared_ptr<LazyExpr>& lazy_expr() const { return _lazy; }
+    void materialize() const;      // evaluates a deferred result (no-op otherwise)
+    void register_reads();         // records this deferred tensor on its inputs' buffers
+
 private:
-    std::shared_ptr<Storage> _storage;
+    mutable std::shared_ptr<Storage> _storage;
+    mutable std::shared_ptr<LazyExpr> _lazy;
+    Device* _device = nullptr;
     std::vector<u32> _shape;
     std::vector<u64> _strides;
     u64 _offset = 0;
     DataType _dtype = DataType::F32;
     u64 _numel = 0;
     void compute_numel();
+    // Evaluates deferred tensors that read this tensor's buffer (and this
+    // tensor itself if deferred) before it is written.
+    void prepare_write();
 };
 
 inline u64 compute_numel(const std::vector<u32>& shape) {

@@ -175,6 +175,10 @@ inline TensorPtr copy(TensorPtr x) { return QuasarML::Ops::copy(device(), x); }
 inline TensorPtr contiguous(TensorPtr x) { return QuasarML::Ops::contiguous(device(), x); }
 
 // Ops that ran on the host instead of the GPU: always 0 in this backend.
+// Elementwise fusion (deferred results evaluated as one kernel on access).
+inline void set_fusion(bool on) { device().set_fusion(on); }
+inline bool fusion_enabled() { return device().fusion(); }
+
 inline u64 cpu_fallback_count() {
     uint64_t n = 0;
     device().check(qsml_cpu_fallback_count(device().ctx(), &n));

@@ -86,7 +86,7 @@ std::vector<u64> contiguous_strides(const std::vector<u32>& shape) {
 }
 
 Tensor::Tensor(Device* device, const std::vector<u32>& shape, DataType dtype, bool)
-    : _shape(shape), _dtype(dtype) {
+    : _device(device), _shape(shape), _dtype(dtype) {
     // Core/Tensor.cpp:70-73 of the reference: a shape is non-empty with positive dims.
     QS_ASSERT(!shape.empty(), "Shape cannot be empty");
     for (u32 d : shape) QS_ASSERT(d > 0, "Dimension must be positive");
@@ -99,7 +99,70 @@ Tensor::Tensor(std::shared_ptr<Storage> storage, const std::vector<u32>& shape, 
                u64 element_offset, DataType dtype)
     : _storage(std::move(storage)), _shape(shape), _strides(strides), _offset(element_offset), _dtype(dtype) {
     QS_ASSERT(_shape.size() == _strides.size(), "shape and strides differ in rank");
+    _device = _storage ? _storage->device : nullptr;
     compute_numel();
+}
+
+Tensor::Tensor(Device* device, const std::vector<u32>& shape, DataType dtype, std::shared_ptr<LazyExpr> expr)
+    : _lazy(std::move(expr)), _device(device), _shape(shape), _dtype(dtype) {
+    QS_ASSERT(device && device->is_valid(), "Tensor needs a valid device");
+    QS_ASSERT(!shape.empty(), "Shape cannot be empty");
+    compute_numel();
+    _strides = contiguous_strides(shape);
+}
+
+void Tensor::register_reads() {
+    if (!_lazy) return;
+    std::weak_ptr<Tensor> self = weak_from_this();
+    for (const auto& in : _lazy->inputs) {
+        const auto& st = in->storage();
+        std::lock_guard<std::mutex> lk(st->readers_mu);
+        if (st->readers.size() >= 64) {  // drop readers that are gone
+            std::vector<std::weak_ptr<Tensor>> live;
+            for (auto& w : st->readers)
+                if (!w.expired()) live.push_back(w);
+            st->readers.swap(live);
+        }
+        st->readers.push_back(self);
+    }
+}
+
+void Tensor::materialize() const {
+    if (!_lazy) return;
+    std::shared_ptr<LazyExpr> e = _lazy;
+    auto st = std::make_shared<Storage>(_device, _numel * element_size());
+    std::vector<qsml_tdesc> ins(e->inputs.size());
+    for (size_t j = 0; j < ins.size(); ++j) ins[j] = e->inputs[j]->desc();
+    qsml_tdesc out;
+    std::memset(&out, 0, sizeof(out));
+    out.data = st->ptr;
+    out.dtype = static_cast<int32_t>(_dtype);
+    out.ndim = static_cast<int32_t>(_shape.size());
+    for (size_t i = 0; i < _shape.size(); ++i) {
+        out.shape[i] = _shape[i];
+        out.stride[i] = static_cast<int64_t>(_strides[i]);
+    }
+    _device->check(qsml_elementwise_fused(_device->ctx(), e->nodes.data(), static_cast<int32_t>(e->nodes.size()),
+                                          ins.data(), static_cast<int32_t>(ins.size()), &out));
+    _storage = st;
+    _lazy.reset();
+}
+
+void Tensor::prepare_write() {
+    materialize();
+    std::vector<std::shared_ptr<Tensor>> pending;
+    {
+        std::lock_guard<std::mutex> lk(_storage->readers_mu);
+        for (auto& w : _storage->readers)
+            if (auto t = w.lock()) pending.push_back(t);
+        _storage->readers.clear();
+    }
+    for (auto& t : pending) t->materialize();
+}
+
+const std::shared_ptr<Storage>& Tensor::storage() const {
+    materialize();
+    return _storage;
 }
 
 void Tensor::compute_numel() {
@@ -112,9 +175,12 @@ u32 Tensor::dim(u32 i) const {
     return _shape[i];
 }
 
-Device* Tensor::device() const { return _storage ? _storage->device : nullptr; }
+Device* Tensor::device() const { return _device; }
 
-void* Tensor::data() const { return static_cast<char*>(_storage->ptr) + _offset * element_size(); }
+void* Tensor::data() const {
+    materialize();
+    return static_cast<char*>(_storage->ptr) + _offset * element_size();
+}
 
 qsml_tdesc Tensor::desc() const {
     qsml_tdesc d;
@@ -131,6 +197,7 @@ qsml_tdesc Tensor::desc() const {
 }
 
 bool Tensor::is_contiguous() const {
+    if (_lazy) return true;  // evaluates into a contiguous buffer
     u64 s = 1;
     for (int i = static_cast<int>(_shape.size()) - 1; i >= 0; --i) {
         if (_shape[i] != 1 && _strides[i] != s) return false;
@@ -140,6 +207,7 @@ bool Tensor::is_contiguous() const {
 }
 
 std::shared_ptr<Tensor> Tensor::contiguous() const {
+    materialize();
     if (is_contiguous()) return std::const_pointer_cast<Tensor>(shared_from_this());
     auto out = device()->create_tensor(_shape, _dtype);
     qsml_tdesc s = desc(), o = out->desc();
@@ -149,6 +217,7 @@ std::shared_ptr<Tensor> Tensor::contiguous() const {
 
 std::shared_ptr<Tensor> Tensor::strided_view(const std::vector<u32>& shape, const std::vector<u64>& strides,
                                              u64 element_offset) const {
+    materialize();
     return std::make_shared<Tensor>(_storage, shape, strides, element_offset, _dtype);
 }
 
@@ -156,6 +225,7 @@ void Tensor::upload(const void* data) { upload(data, size_bytes(), 0); }
 
 void Tensor::upload(const void* src, u64 size, u64 offset) {
     QS_ASSERT(is_valid(), "Tensor not valid");
+    prepare_write();
     QS_ASSERT(is_contiguous(), "upload into a non-contiguous view");
     QS_ASSERT(offset + size <= size_bytes(), "upload beyond the tensor");
     device()->check(qsml_h2d(device()->ctx(), static_cast<char*>(this->data()) + offset, src, size));
@@ -172,6 +242,7 @@ void Tensor::download(void* dst, u64 size, u64 offset) const {
 
 void Tensor::fill(const void* value) {
     QS_ASSERT(is_valid(), "Tensor not valid");
+    prepare_write();
     if (is_contiguous()) {
         device()->check(qsml_fill(device()->ctx(), data(), value, static_cast<int32_t>(element_size()),
                                   static_cast<int64_t>(_numel)));
@@ -189,6 +260,8 @@ void Tensor::zero() {
 
 void Tensor::copy_from(const Tensor& src) {
     QS_ASSERT(size_bytes() == src.size_bytes(), "Size mismatch");
+    src.materialize();
+    prepare_write();
     QS_ASSERT(src.dtype() == _dtype || (is_contiguous() && src.is_contiguous()), "Type mismatch");
     if (src.shape() == _shape) {
         qsml_tdesc s = src.desc(), o = desc();
@@ -203,6 +276,7 @@ void Tensor::copy_from(const Tensor& src) {
 
 Tensor& Tensor::reshape(const std::vector<u32>& new_shape) {
     QS_ASSERT(QuasarML::compute_numel(new_shape) == _numel, "Element count mismatch in reshape");
+    prepare_write();  // deferred readers of this tensor see its old shape
     QS_ASSERT(is_contiguous(), "reshape of a non-contiguous view (use contiguous() first)");
     _shape = new_shape;
     _strides = contiguous_strides(new_shape);
@@ -211,6 +285,7 @@ Tensor& Tensor::reshape(const std::vector<u32>& new_shape) {
 
 std::shared_ptr<Tensor> Tensor::view(const std::vector<u32>& new_shape) const {
     QS_ASSERT(QuasarML::compute_numel(new_shape) == _numel, "Element count mismatch in view");
+    materialize();
     QS_ASSERT(is_contiguous(), "view of a non-contiguous tensor (use contiguous() first)");
     return strided_view(new_shape, contiguous_strides(new_shape), _offset);
 }
@@ -274,6 +349,8 @@ void Device::check(int st) const {
 std::shared_ptr<Tensor> Device::create_tensor(const std::vector<u32>& shape, DataType dtype, bool host_visible) {
     return std::make_shared<Tensor>(this, shape, dtype, host_visible);
 }
+
+void Device::set_fusion(bool on) { _fusion = on; }
 
 void Device::begin_batch() {
     QS_ASSERT(!_in_batch, "Already in batch");

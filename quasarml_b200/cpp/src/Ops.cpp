@@ -37,9 +37,91 @@ std::vector<u32> broadcast_shape(const std::vector<u32>& a, const std::vector<u3
     return out;
 }
 
+// ---- deferred (fused) elementwise ops ---------------------------------------
+// An operand is spliced into the new expression: a deferred tensor brings its
+// nodes (its inputs merged into the new input list), a materialised one
+// becomes an input node.  An expression that would exceed the fused entry
+// point's limits evaluates its largest deferred operand first.
+class ExprBuilder {
+public:
+    ExprBuilder() : e_(std::make_shared<LazyExpr>()) {}
+
+    int operand(const TP& t) {
+        if (!t->is_lazy()) return add({QSML_FUSE_INPUT, input_index(t), 0, 0, 0.0f});
+        const LazyExpr& src = *t->lazy_expr();
+        std::vector<int> remap(src.inputs.size());
+        for (size_t j = 0; j < src.inputs.size(); ++j) remap[j] = input_index(src.inputs[j]);
+        const int base = static_cast<int>(e_->nodes.size());
+        for (qsml_fuse_node n : src.nodes) {
+            if (n.kind == QSML_FUSE_INPUT) n.code = remap[n.code];
+            if (n.kind == QSML_FUSE_BINARY || n.kind == QSML_FUSE_UNARY) n.a += base;
+            if (n.kind == QSML_FUSE_BINARY) n.b += base;
+            e_->nodes.push_back(n);
+        }
+        return static_cast<int>(e_->nodes.size()) - 1;
+    }
+    int constant(f32 v) { return add({QSML_FUSE_CONST, 0, 0, 0, v}); }
+    int binary(int op, int a, int b) { return add({QSML_FUSE_BINARY, op, a, b, 0.0f}); }
+    int unary(int op, int a) { return add({QSML_FUSE_UNARY, op, a, 0, 0.0f}); }
+
+    bool fits() const {
+        return e_->nodes.size() <= QSML_FUSE_MAX_NODES && e_->inputs.size() <= QSML_FUSE_MAX_INPUTS;
+    }
+    std::shared_ptr<LazyExpr> expr() const { return e_; }
+
+private:
+    int add(qsml_fuse_node n) {
+        e_->nodes.push_back(n);
+        return static_cast<int>(e_->nodes.size()) - 1;
+    }
+    int input_index(const TP& t) {
+        for (size_t j = 0; j < e_->inputs.size(); ++j)
+            if (e_->inputs[j] == t) return static_cast<int>(j);
+        e_->inputs.push_back(t);
+        return static_cast<int>(e_->inputs.size()) - 1;
+    }
+    std::shared_ptr<LazyExpr> e_;
+};
+
+bool deferrable(const Device& device, const TP& t) {
+    return device.defer_elementwise() && (t->dtype() == DataType::F32 || t->dtype() == DataType::F16);
+}
+
+TP make_deferred(Device& device, const std::vector<u32>& shape, DataType dtype, const std::shared_ptr<LazyExpr>& e) {
+    auto out = std::make_shared<Tensor>(&device, shape, dtype, e);
+    out->register_reads();
+    return out;
+}
+
+// Builds `build(builder, operand node indices...)`; if the result does not
+// fit, evaluates the deferred operands (largest first) and retries.
+template <typename Build>
+std::shared_ptr<LazyExpr> build_expr(std::vector<TP> ops, Build build) {
+    for (;;) {
+        ExprBuilder b;
+        std::vector<int> idx;
+        for (const auto& t : ops) idx.push_back(b.operand(t));
+        build(b, idx);
+        if (b.fits()) return b.expr();
+        size_t big = 0, best = 0;
+        for (size_t i = 0; i < ops.size(); ++i)
+            if (ops[i]->is_lazy() && ops[i]->lazy_expr()->nodes.size() >= best) {
+                best = ops[i]->lazy_expr()->nodes.size();
+                big = i;
+            }
+        QS_ASSERT(ops[big]->is_lazy(), "fused expression limits exceeded");
+        ops[big]->materialize();
+    }
+}
+
 TP binary(Device& device, int op, const TP& a, const TP& b) {
     QS_ASSERT(a && b, "null tensor");
     QS_ASSERT(a->dtype() == b->dtype(), "Type mismatch");
+    if (deferrable(device, a)) {
+        auto shape = broadcast_shape(a->shape(), b->shape());
+        auto e = build_expr({a, b}, [op](ExprBuilder& bl, const std::vector<int>& i) { bl.binary(op, i[0], i[1]); });
+        return make_deferred(device, shape, a->dtype(), e);
+    }
     auto out = device.create_tensor(broadcast_shape(a->shape(), b->shape()), a->dtype());
     qsml_tdesc da = a->desc(), db = b->desc(), dout = out->desc();
     device.check(qsml_binary(device.ctx(), op, &da, &db, &dout));
@@ -48,6 +130,12 @@ TP binary(Device& device, int op, const TP& a, const TP& b) {
 
 TP scalar_op(Device& device, int op, const TP& a, f32 s) {
     QS_ASSERT(a, "null tensor");
+    if (deferrable(device, a)) {
+        auto e = build_expr({a}, [op, s](ExprBuilder& bl, const std::vector<int>& i) {
+            bl.binary(op, i[0], bl.constant(s));
+        });
+        return make_deferred(device, a->shape(), a->dtype(), e);
+    }
     auto out = device.create_tensor(a->shape(), a->dtype());
     qsml_tdesc da = a->desc(), dout = out->desc();
     device.check(qsml_binary_scalar(device.ctx(), op, &da, s, &dout));
@@ -56,6 +144,10 @@ TP scalar_op(Device& device, int op, const TP& a, f32 s) {
 
 TP unary(Device& device, int op, const TP& a) {
     QS_ASSERT(a, "null tensor");
+    if (deferrable(device, a)) {
+        auto e = build_expr({a}, [op](ExprBuilder& bl, const std::vector<int>& i) { bl.unary(op, i[0]); });
+        return make_deferred(device, a->shape(), a->dtype(), e);
+    }
     auto out = device.create_tensor(a->shape(), a->dtype());
     qsml_tdesc da = a->desc(), dout = out->desc();
     device.check(qsml_unary(device.ctx(), op, &da, &dout));

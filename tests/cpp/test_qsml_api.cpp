@@ -2,8 +2,9 @@
 // reference's unit tests check it (a pass/fail counter, nonzero exit on any
 // failure): the known answers of unit-tests/src/_test_comprehensive.cpp,
 // _test_qsml_functionality.cpp and _test_minimal.cpp, then the ops this
-// backend adds (broadcasting, pow, axis max/min, strided slices, layer norm,
-// batched and fp16 matmul, concat/stack) and the error convention.
+// backend adds (broadcasting, pow, axis max/min, argmax/argmin, strided
+// slices, layer norm, batched and fp16 matmul, concat/stack, deferred fused
+// elementwise results) and the error convention.
 #include <QuasarML.h>
 
 #include <cmath>
@@ -152,7 +153,7 @@ static void test_axis_reductions() {
     auto sv = get(s1);
     check("sum axis 1", sv[0] == 13 && sv[1] == 14);
     check("mean axis 0", get(qsml::mean(A, 0))[1] == 7.0f);
-    // argmax/argmin give I32 indices (the reference's return values)
+    // argmax/argmin give I32 indices (the reference's stubs return max/min values)
     auto am = qsml::argmax(A);  // last axis
     vector<int32_t> ai(am->numel());
     am->download(ai.data(), ai.size() * sizeof(int32_t));
@@ -258,6 +259,72 @@ static void test_layer_norm_and_matmul() {
     check("fp16 tensor-core matmul within 1e-2 of fp32", err / ref < 1e-2);
 }
 
+static uint64_t launches() {
+    uint64_t n = 0;
+    qsml::device().check(qsml_launch_count(qsml::device().ctx(), &n));
+    return n;
+}
+
+static bool same_bits(const vector<float>& a, const vector<float>& b) {
+    return a.size() == b.size() && std::memcmp(a.data(), b.data(), a.size() * sizeof(float)) == 0;
+}
+
+// Deferred elementwise results (set_fusion / begin_batch): one fused launch,
+// bit-identical to eager execution, writes after deferred reads, long chains.
+static void test_fusion() {
+    const qsml::u32 R = 64, C = 256;
+    vector<float> a(R * C), b(C), dv(R);
+    uint32_t x = 12345u;
+    auto rnd = [&](float lo, float hi) {
+        x = x * 1664525u + 1013904223u;
+        return lo + (hi - lo) * static_cast<float>(x >> 8) / 16777216.0f;
+    };
+    for (auto& v : a) v = rnd(-1, 1);
+    for (auto& v : b) v = rnd(-1, 1);
+    for (auto& v : dv) v = rnd(0.5f, 2.0f);
+    auto A = qsml::from_data(a.data(), {R, C});
+    auto B = qsml::from_data(b.data(), {1, C});
+    auto D = qsml::from_data(dv.data(), {R, 1});
+    auto chain = [&]() {
+        return qsml::relu(qsml::div(qsml::pow(qsml::sub(qsml::mul(qsml::add(A, B), B), A), 2.0f), D));
+    };
+    auto eager = get(chain());
+    qsml::set_fusion(true);
+    const uint64_t l0 = launches();
+    auto T = chain();
+    check("fusion: result deferred", T->is_lazy() && launches() == l0);
+    auto fused = get(T);
+    check("fusion: one launch for the chain", launches() - l0 == 1);
+    check("fusion: bit-identical to eager", same_bits(eager, fused));
+
+    // a write into an input evaluates the deferred readers first
+    qsml::set_fusion(false);
+    auto ref_sum = get(qsml::add(A, B));
+    qsml::set_fusion(true);
+    auto U = qsml::add(A, B);
+    vector<float> zeros(R * C, 0.0f);
+    A->upload(zeros.data());
+    check("fusion: deferred read before a write sees old data", same_bits(get(U), ref_sum));
+    A->upload(a.data());
+
+    // a chain longer than one fused kernel takes splits itself
+    qsml::TensorPtr L = A;
+    for (int i = 0; i < 100; ++i) L = qsml::add_scalar(L, 0.25f);
+    auto long_fused = get(L);
+    qsml::set_fusion(false);
+    qsml::TensorPtr E = A;
+    for (int i = 0; i < 100; ++i) E = qsml::add_scalar(E, 0.25f);
+    check("fusion: 100-op chain equals eager", same_bits(long_fused, get(E)));
+
+    // the reference's batch bracket defers too
+    qsml::device().begin_batch();
+    auto Tb = chain();
+    qsml::device().end_batch();
+    check("batch: deferred inside begin/end_batch", Tb->is_lazy());
+    check("batch: bit-identical to eager", same_bits(get(Tb), eager));
+    check("fusion off again", !qsml::fusion_enabled());
+}
+
 static void test_errors_and_counters() {
     bool threw = false;
     try {
@@ -291,6 +358,7 @@ int main() {
         test_axis_reductions();
         test_views_and_gathers();
         test_layer_norm_and_matmul();
+        test_fusion();
         test_errors_and_counters();
     } catch (const std::exception& e) {
         std::cout << "EXCEPTION: " << e.what() << "\n";
