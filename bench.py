@@ -722,6 +722,13 @@ def run_single(which: str, reps: int = 3):
         C = torch.empty((8192, 8192), device="cuda")
         for _ in range(reps):
             ctx.matmul(d(A), d(B), d(C), abi.MM_FP16_F32ACC)
+    elif which == "matmul_3xtf32":
+        s = 1.0 / np.sqrt(8192.0)
+        A = _t(datagen.uniform(6, (8192, 8192), -s, s))
+        B = _t(datagen.uniform(7, (8192, 8192), -s, s))
+        C = torch.empty((8192, 8192), device="cuda")
+        for _ in range(reps):
+            ctx.matmul(d(A), d(B), d(C), abi.MM_FP32_3XTF32)
     torch.cuda.synchronize()
     ctx.close()
 
@@ -742,7 +749,7 @@ def main():
     ap.add_argument("--single", default=None,
                     choices=["reduce_all", "reduce_axis0", "reduce_axis1", "reduce_axis2", "reduce_all_f16",
                              "chain_add", "chain_fused", "gather_t", "gather_s", "layernorm", "matmul_f16",
-                             "argmax_all", "argmax_axis1"],
+                             "matmul_3xtf32", "argmax_all", "argmax_axis1"],
                     help="run one kernel of the workloads a few times and exit (profiling aid, prints nothing)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
