@@ -8,7 +8,8 @@ batch of 8 distinct X per dtype (1.5 GB of input, so no input is L2-resident
 when it is read again), i.e. 256 reduction calls.  Under torchrun each rank
 holds its own [64,512,1024] shards of a [64N,512,1024] tensor (weak scaling);
 axis-0 and full reductions combine their per-rank partials with NCCL
-all-reduces (torch.distributed), axis-1/2 results need no exchange.
+all-reduces (torch.distributed) that run while the axis-1/2 reductions, which
+need no exchange, compute (two CUDA graphs per step, collectives between).
 
 value     : algorithmic bytes (each input read once, each output written once)
             of all ranks / max-over-ranks device time, inputs resident in HBM.
@@ -248,17 +249,42 @@ class ReduceWorkload(Workload):
             ctx.reduce(op, xd, axis, False, od)
 
     def exchange(self):
+        self.exchange_finish(self.exchange_start())
+
+    # Overlapped step: the exchanged reductions (axis 0 and full) first, their
+    # all-reduces started, the local ones (axes 1, 2) while NCCL runs, then
+    # the wait and the mean rescale.
+    @property
+    def calls_x(self):
+        return [c for c in self.calls if c[2] in (0, self.abi.AXIS_ALL)]
+
+    @property
+    def calls_l(self):
+        return [c for c in self.calls if c[2] not in (0, self.abi.AXIS_ALL)]
+
+    def exchange_start(self):
+        if not self.dist.pg:
+            return []
+        from quasarml_b200 import sharding
+        return sharding.exchange_start(self.dist.pg, self.flat)
+
+    def exchange_finish(self, works):
         if not self.dist.pg:
             return
         from quasarml_b200 import sharding
         abi, ctx = self.abi, self.ctx
-        sharding.exchange(self.dist.pg, self.flat, self.dist.world,
-                          scale_fn=lambda key, f: ctx.binary_scalar(abi.OP_MUL, self.flat_desc[key], f,
-                                                                     self.flat_desc[key]))
+        sharding.exchange_finish(works, self.flat, self.dist.world,
+                                 scale_fn=lambda key, f: ctx.binary_scalar(abi.OP_MUL, self.flat_desc[key], f,
+                                                                            self.flat_desc[key]))
 
     def step(self):
-        self.compute()
-        self.exchange()
+        if not self.dist.pg:
+            self.compute()
+            return
+        self.compute(self.calls_x)
+        works = self.exchange_start()
+        self.compute(self.calls_l)
+        self.exchange_finish(works)
 
     # End-to-end: host -> device copies of X, the reductions, results back.
     def e2e_setup(self):
@@ -485,7 +511,16 @@ def time_steps(wl, dist: Dist, stream, steps: int, warmup: int, sampler=None, us
         for _ in range(warmup):
             wl.step()
         torch.cuda.synchronize()
-        g = capture(wl.compute, stream) if use_graph else None
+        # Workloads with an exchange and a split step (ReduceWorkload) replay
+        # two graphs with the collectives started between them.
+        split = use_graph and dist.pg is not None and hasattr(wl, "exchange_start")
+        g = None
+        if split:
+            gx = capture(lambda: wl.compute(wl.calls_x), stream)
+            gl = capture(lambda: wl.compute(wl.calls_l), stream)
+            g = (gx, gl)
+        elif use_graph:
+            g = capture(wl.compute, stream)
         torch.cuda.synchronize()
         dist.barrier()
         torch.cuda.synchronize()
@@ -502,7 +537,12 @@ def time_steps(wl, dist: Dist, stream, steps: int, warmup: int, sampler=None, us
             sampler.__enter__()
         start.record(stream)
         for _ in range(steps):
-            if g is not None:
+            if split:
+                g[0].replay()
+                works = wl.exchange_start()
+                g[1].replay()
+                wl.exchange_finish(works)
+            elif g is not None:
                 g.replay()
                 wl.exchange()
             else:
@@ -798,8 +838,9 @@ def main():
                        "l2": "inputs larger than L2: 8 distinct X per dtype per step (1.5 GB)"
                        if args.workload == "reduce" else "inputs larger than L2",
                        "calls_per_step": len(getattr(wl, "calls", [])) or 1,
-                       "launch": "each step's kernel calls replayed from one CUDA graph; "
-                                 "NCCL all-reduces (N>1) issued eagerly after it"},
+                       "launch": "each step's kernel calls replayed from one CUDA graph (N=1); for N>1 two "
+                                 "graphs, the exchanged reductions then the local ones, with the NCCL "
+                                 "all-reduces started between them and waited for after"},
             "gpu_launches": launches, "clocks": sampler.summary()}
     if args.workload == "reduce":
         line["roofline"] = roofline_from_families(family_times(wl, stream), hbm, peak_kind)

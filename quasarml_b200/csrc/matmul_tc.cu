@@ -1,6 +1,6 @@
 // Tensor-core matmul on sm_100a: tcgen05.mma with the accumulator in tensor
 // memory (TMEM), operands staged in shared memory by TMA (cp.async.bulk.tensor,
-// no multicast), results written by TMA bulk-tensor stores.
+// every CTA loading its own tiles), results written by TMA bulk-tensor stores.
 //
 // Reference: Ops::matmul (Ops/LinAlg.cpp:221-271) runs a SIMT shader with
 // 16x16 workgroups and 4x4 register blocks; Ops::batch_matmul

@@ -35,19 +35,36 @@ def group(op: int) -> str:
     return {SUM: "sum", MEAN: "mean", MAX: "max", MIN: "min"}[op]
 
 
-def exchange(dist, buffers: dict, world: int, scale_fn=None) -> None:
-    """All-reduces every flat buffer (keys end in the group name), then scales
-    the mean buffers by 1/world.  `dist` is torch.distributed; `scale_fn(key,
-    factor)` rescales a buffer in place (the GPU path issues one
-    qsml_binary_scalar per buffer); without it the tensor's mul_ is used."""
+def _group_of(key) -> str:
+    return key[-1] if isinstance(key, tuple) else key
+
+
+def exchange_start(dist, buffers: dict) -> list:
+    """Starts the all-reduce of every flat buffer (keys end in the group name)
+    and returns the work handles.  With NCCL the collectives run on NCCL's
+    stream after the work already enqueued on the current stream, so kernels
+    enqueued next overlap them."""
     ops = {"sum": dist.ReduceOp.SUM, "mean": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX,
            "min": dist.ReduceOp.MIN}
-    for key, buf in buffers.items():
-        dist.all_reduce(buf, op=ops[key[-1] if isinstance(key, tuple) else key])
+    return [dist.all_reduce(buf, op=ops[_group_of(key)], async_op=True) for key, buf in buffers.items()]
+
+
+def exchange_finish(works: list, buffers: dict, world: int, scale_fn=None) -> None:
+    """Waits for the all-reduces (the current stream waits; the host does not
+    block with NCCL), then scales the mean buffers by 1/world.  `scale_fn(key,
+    factor)` rescales a buffer in place (the GPU path issues one
+    qsml_binary_scalar per buffer); without it the tensor's mul_ is used."""
+    for w in works:
+        w.wait()
     if world > 1:
         for key, buf in buffers.items():
-            if (key[-1] if isinstance(key, tuple) else key) == "mean":
+            if _group_of(key) == "mean":
                 if scale_fn is None:
                     buf.mul_(1.0 / world)
                 else:
                     scale_fn(key, 1.0 / world)
+
+
+def exchange(dist, buffers: dict, world: int, scale_fn=None) -> None:
+    """exchange_start + exchange_finish."""
+    exchange_finish(exchange_start(dist, buffers), buffers, world, scale_fn)
