@@ -22,8 +22,8 @@ roofline  : the dominant kernel family of the step, its algorithmic bytes per
 cpu_baseline / --impl reference : the oracle's CPU restatement of the same
             reductions (OpenMP over all host cores) on a bounded sample.
 other_workloads (N=1): the elementwise chain (op by op and fused), strided
-            gathers, layer norm, argmax/argmin and matmul configurations, each
-            timed the same way.
+            gathers, layer norm, softmax, argmax/argmin and matmul
+            configurations, each timed the same way.
 """
 from __future__ import annotations
 
@@ -457,6 +457,28 @@ class LayerNormWorkload(Workload):
             self.ctx.layer_norm(x, g, b, 1e-5, y)
 
 
+class SoftmaxWorkload(Workload):
+    name = "softmax over the last axis of X[16384,4096] fp32 and fp16"
+
+    def __init__(self, ctx, dist: Dist):
+        import torch
+        from quasarml_b200 import abi, datagen
+        self.ctx = ctx
+        n = 16384 * 4096
+        X = _t(datagen.normal(datagen.SEEDS["ln_X"], (16384, 4096), 0.5, 2.0, offset=dist.rank * n))
+        Xh = X.half()
+        Y, Yh = torch.empty_like(X), torch.empty_like(Xh)
+        self.keep = [X, Xh, Y, Yh]
+        d = abi.desc_of
+        self.calls = [(d(X), d(Y), 2 * n * 4), (d(Xh), d(Yh), 2 * n * 2)]
+        self.units_per_step = sum(c[2] for c in self.calls)
+        self.unit = "GB/s"
+
+    def compute(self, calls=None):
+        for x, y, _ in (self.calls if calls is None else calls):
+            self.ctx.softmax(x, -1, y)
+
+
 class MatmulWorkload(Workload):
     def __init__(self, ctx, dist: Dist, dtype: str, batched: bool, fp32_precision: str = "3xtf32"):
         import torch
@@ -861,6 +883,7 @@ def main():
                             ("gather", lambda: GatherWorkload(ctx, dist), 20),
                             ("layernorm", lambda: LayerNormWorkload(ctx, dist), 20),
                             ("argmax_argmin", lambda: ArgReduceWorkload(ctx, dist), 20),
+                            ("softmax", lambda: SoftmaxWorkload(ctx, dist), 20),
                             ("matmul_f16_8192", lambda: MatmulWorkload(ctx, dist, "f16", False), 5),
                             ("matmul_f32_8192_3xtf32", lambda: MatmulWorkload(ctx, dist, "f32", False), 5),
                             ("matmul_f32_8192_ffma", lambda: MatmulWorkload(ctx, dist, "f32", False, "ffma"), 3),

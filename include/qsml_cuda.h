@@ -297,6 +297,14 @@ QSML_API qsml_status_t qsml_fuse_stats(qsml_ctx* ctx, uint64_t* jit_launches, ui
  * materialising transpose (QuasarML/src/Ops/LinAlg.cpp:329-351). */
 QSML_API qsml_status_t qsml_gather(qsml_ctx* ctx, const qsml_tdesc* src, const qsml_tdesc* out);
 
+/* y = exp(x - max) / sum(exp(x - max)) over one axis (negative counts from
+ * the end); x and y F32 or F16 with the same contiguous shape, binary32
+ * arithmetic (max, subtract, expf, sum, one division per element).  A NaN in a
+ * slice makes that slice NaN.  Replaces Ops::softmax
+ * (QuasarML/src/Ops/Elementwise.cpp:395-417, shader :98-135), whose indexing
+ * is right for the last axis only. */
+QSML_API qsml_status_t qsml_softmax(qsml_ctx* ctx, const qsml_tdesc* x, int32_t axis, const qsml_tdesc* y);
+
 /* y = (x - mean) / sqrt(var + eps) * gamma + beta over the last dim (biased
  * variance).  x/y F32 or F16; gamma/beta F32 or the dtype of x, shape
  * [last dim].  No reference counterpart (layer norm is absent from the

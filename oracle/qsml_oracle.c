@@ -425,6 +425,41 @@ void orc_argreduce(int op, int dtype, const void* x, int64_t outer, int64_t k, i
 }
 
 /* ------------------------------------------------------------------------ */
+/* Softmax                                                                    */
+/* ------------------------------------------------------------------------ */
+
+/* The reference's shader (Ops/Elementwise.cpp:98-135): row max, sum of
+ * exp(x - max), then exp(x - max) / sum; here in binary64 over any axis. */
+void orc_softmax(const void* x, int f16, int64_t outer, int64_t k, int64_t inner, double* out) {
+    if (f16) h2f_table_init();
+#pragma omp parallel for schedule(static)
+    for (int64_t o = 0; o < outer; ++o) {
+        for (int64_t i = 0; i < inner; ++i) {
+            const int64_t base = o * k * inner + i;
+            double m = -INFINITY;
+            int nan = 0;
+            for (int64_t j = 0; j < k; ++j) {
+                const int64_t q = base + j * inner;
+                const double v = f16 ? (double)h2f(((const uint16_t*)x)[q]) : (double)((const float*)x)[q];
+                if (v != v) nan = 1;
+                if (v > m) m = v;
+            }
+            double s = 0.0;
+            for (int64_t j = 0; j < k; ++j) {
+                const int64_t q = base + j * inner;
+                const double v = f16 ? (double)h2f(((const uint16_t*)x)[q]) : (double)((const float*)x)[q];
+                s += exp(v - m);
+            }
+            for (int64_t j = 0; j < k; ++j) {
+                const int64_t q = base + j * inner;
+                const double v = f16 ? (double)h2f(((const uint16_t*)x)[q]) : (double)((const float*)x)[q];
+                out[q] = nan ? NAN : exp(v - m) / s;
+            }
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Strided gather                                                             */
 /* ------------------------------------------------------------------------ */
 

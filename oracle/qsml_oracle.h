@@ -16,9 +16,10 @@
  * shaderc and spdlog are absent and no graphics stack exists), so the oracle
  * is pinned only by the known-answer vectors of the reference's own unit
  * tests (unit-tests/src/_test_comprehensive.cpp, _test_qsml_functionality.cpp,
- * _test_minimal.cpp).  Broadcasting, pow, axis min/max, strided slicing,
- * layer norm, fp16 and batched matmul have no reference implementation or
- * test: for those ops the oracle restates NumPy semantics and is
+ * _test_minimal.cpp).  Broadcasting, pow, axis min/max, argmax/argmin,
+ * softmax values, strided slicing, layer norm, fp16 and batched matmul have
+ * no reference implementation or test of their values: for those ops the
+ * oracle restates NumPy semantics (or the reference shader's formula) and is
  * "parity unpinned".
  */
 #ifndef QSML_ORACLE_H
@@ -96,6 +97,12 @@ void orc_reduce_f16(int op, const uint16_t* x, int64_t outer, int64_t k, int64_t
  * numerically (-0 == +0) and a NaN counts as larger (smaller) than every
  * number, so the first NaN wins. */
 void orc_argreduce(int op, int dtype, const void* x, int64_t outer, int64_t k, int64_t inner, int64_t* out);
+
+/* Softmax of x viewed as [outer, k, inner] over the middle axis, in binary64:
+ * m = max (any NaN -> NaN), e = exp(x - m), out = e / sum(e)
+ * (Ops/Elementwise.cpp:98-135 restated for any axis).  x is binary32 or
+ * binary16 (f16 != 0). */
+void orc_softmax(const void* x, int f16, int64_t outer, int64_t k, int64_t inner, double* out);
 
 /* Strided gather: copies the view (base, ndim, shape, strides in elements,
  * possibly negative) of esize-byte elements into contiguous out. */

@@ -54,6 +54,7 @@ def _load():
         "orc_reduce_f32": (None, [ctypes.c_int, _P, _I64, _I64, _I64, _P, _P, _P]),
         "orc_reduce_f16": (None, [ctypes.c_int, _P, _I64, _I64, _I64, _P, _P, _P]),
         "orc_argreduce": (None, [ctypes.c_int, ctypes.c_int, _P, _I64, _I64, _I64, _P]),
+        "orc_softmax": (None, [_P, ctypes.c_int, _I64, _I64, _I64, _P]),
         "orc_gather": (None, [_P, ctypes.c_int, ctypes.c_int, _P, _P, _P]),
         "orc_layer_norm_f32": (None, [_P, _P, _P, _I64, _I64, ctypes.c_float, _P]),
         "orc_layer_norm_f16": (None, [_P, _P, _P, _I64, _I64, ctypes.c_float, _P]),
@@ -191,6 +192,18 @@ def argreduce(op: int, x: np.ndarray, axis=None) -> np.ndarray:
     out = np.empty(outer * inner, dtype=np.int64)
     L.orc_argreduce(op, _QSML_DTYPE[x.dtype], _ptr(x), outer, k, inner, _ptr(out))
     return out.reshape(oshape)
+
+
+def softmax(x: np.ndarray, axis: int = -1) -> np.ndarray:
+    """binary64 softmax over `axis` of a float32 / float16 array."""
+    x = np.ascontiguousarray(x)
+    ax = axis + x.ndim if axis < 0 else axis
+    outer = int(np.prod(x.shape[:ax], dtype=np.int64))
+    k = x.shape[ax]
+    inner = int(np.prod(x.shape[ax + 1:], dtype=np.int64))
+    out = np.empty(x.shape, dtype=np.float64)
+    _load().orc_softmax(_ptr(x), 1 if x.dtype == np.float16 else 0, outer, k, inner, _ptr(out))
+    return out
 
 
 def gather(base: np.ndarray, offset: int, shape, strides) -> np.ndarray:

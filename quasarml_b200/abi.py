@@ -129,6 +129,7 @@ _SIGS = {
     "qsml_set_fuse_mode": (_c.c_int32, [_c.c_void_p, _c.c_int32]),
     "qsml_fuse_stats": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64), _P(_c.c_uint64), _P(_c.c_uint64)]),
     "qsml_gather": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc)]),
+    "qsml_softmax": (_c.c_int32, [_c.c_void_p, _P(TDesc), _c.c_int32, _P(TDesc)]),
     "qsml_layer_norm": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_float, _P(TDesc)]),
     "qsml_matmul": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_int32]),
     "qsml_reduce_noalloc": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_int32, _c.c_int32, _P(TDesc)]),
@@ -319,6 +320,9 @@ class Context:
 
     def gather(self, src: TDesc, out: TDesc) -> None:
         self.check(self.lib.qsml_gather(self.h, ctypes.byref(src), ctypes.byref(out)))
+
+    def softmax(self, x: TDesc, axis: int, y: TDesc) -> None:
+        self.check(self.lib.qsml_softmax(self.h, ctypes.byref(x), int(axis), ctypes.byref(y)))
 
     def layer_norm(self, x: TDesc, g: TDesc, b: TDesc, eps: float, y: TDesc) -> None:
         self.check(self.lib.qsml_layer_norm(self.h, ctypes.byref(x), ctypes.byref(g), ctypes.byref(b),

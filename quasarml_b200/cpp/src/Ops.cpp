@@ -224,14 +224,16 @@ TP relu(Device& d, TP a) { return unary(d, QSML_UN_RELU, a); }
 TP sigmoid(Device& d, TP a) { return unary(d, QSML_UN_SIGMOID, a); }
 TP gelu(Device& d, TP a) { return unary(d, QSML_UN_GELU, a); }
 
-// Ops/Elementwise.cpp:98-135 computes softmax over the last axis as
-// exp(x - max) / sum(exp(x - max)); here over any axis, from the same parts.
+// Ops/Elementwise.cpp:395-417: exp(x - max) / sum(exp(x - max)) over `axis`
+// (any axis here), one kernel.
 TP softmax(Device& d, TP a, i32 axis) {
+    QS_ASSERT(a, "null tensor");
     axis = norm_axis(axis, a->rank());
-    auto m = max(d, a, axis, true);
-    auto e = exp(d, subtract(d, a, m));
-    auto s = sum(d, e, axis, true);
-    return divide(d, e, s);
+    auto x = a->contiguous();
+    auto out = d.create_tensor(a->shape(), a->dtype());
+    qsml_tdesc dx = x->desc(), dout = out->desc();
+    d.check(qsml_softmax(d.ctx(), &dx, axis, &dout));
+    return out;
 }
 
 // ---- reductions -------------------------------------------------------------

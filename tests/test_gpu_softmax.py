@@ -1,0 +1,75 @@
+"""GPU softmax (qsml_softmax) against the oracle's binary64 softmax.
+
+Bar: |gpu - ref| <= 1e-5 * ref + 1e-30 for F32 output (max, expf with a few
+ulp, a binary32 sum and one division per element), <= 1e-3 * ref + 1e-7 for
+F16 output; every slice sums to 1 within 1e-5 (F32).  Shapes reach the
+register-resident row kernel, the three-pass row kernel (odd and very long
+rows) and the column kernel (axis before the last).
+"""
+import numpy as np
+import pytest
+
+from helpers import d, dev, empty, host
+from quasarml_b200 import abi, datagen
+
+pytestmark = pytest.mark.gpu
+
+CASES = [
+    ((16384, 4096), -1),   # register rows, 256 threads x 4 packs
+    ((2048, 1024), 1),     # register rows
+    ((333, 160), -1),      # 160 = 40 packs: not a whole warp of packs -> generic rows
+    ((100, 77), -1),       # odd width -> generic rows
+    ((3, 50000), -1),      # long rows -> generic rows
+    ((64, 512, 1024), 1),  # column kernel
+    ((64, 512, 32), 0),    # column kernel, outer 1
+    ((7,), 0),             # 1-D
+]
+
+
+def run(ctx, x, axis):
+    tx = dev(x)
+    y = empty(x.shape, x.dtype)
+    ctx.softmax(d(tx), axis, d(y))
+    return host(y)
+
+
+@pytest.mark.parametrize("case", range(len(CASES)))
+@pytest.mark.parametrize("dtype", [np.float32, np.float16])
+def test_matches_oracle(ctx, orc, case, dtype):
+    shape, axis = CASES[case]
+    if np.prod(shape) > 20_000_000 and dtype == np.float16 and case != 0:
+        pytest.skip("large fp16 shape covered by case 0")
+    x = datagen.normal(datagen.SEEDS["ln_X"] + case, shape, 0.5, 2.0).astype(dtype)
+    got = run(ctx, x, axis).astype(np.float64)
+    ref = orc.softmax(x, axis)
+    rtol, atol = (1e-5, 1e-30) if dtype == np.float32 else (1e-3, 1e-7)
+    err = np.abs(got - ref) - rtol * ref
+    assert np.max(err) <= atol, (shape, axis, float(np.max(err)))
+    if dtype == np.float32:
+        assert np.max(np.abs(got.sum(axis=axis) - 1.0)) <= 1e-5
+
+
+def test_special_values(ctx, orc):
+    x = np.array([[0.0, 1.0, 2.0, 3.0], [1.0, np.nan, 0.0, 0.0], [5.0, 5.0, 5.0, 5.0],
+                  [-np.inf, 0.0, -np.inf, 0.0], [88.0, 89.0, -100.0, 90.0]], np.float32)
+    got = run(ctx, x, -1)
+    assert np.all(np.isnan(got[1]))
+    assert np.all(got[2] == np.float32(0.25))
+    assert got[3][0] == 0.0 and got[3][2] == 0.0 and got[3][1] == np.float32(0.5)
+    ref = orc.softmax(x, -1)
+    ok = ~np.isnan(ref)
+    # exp(-190) underflows binary32 to 0 (binary64: 2e-83), hence the tiny floor
+    assert np.allclose(got[ok], ref[ok], rtol=1e-5, atol=1e-30)
+
+
+def test_deterministic_and_errors(ctx):
+    x = datagen.normal(3, (512, 4096), 0.0, 1.0)
+    a, b = run(ctx, x, -1), run(ctx, x, -1)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    tx = dev(x)
+    with pytest.raises(abi.QsmlError) as e:
+        ctx.softmax(d(tx), 2, d(empty(x.shape, np.float32)))
+    assert e.value.status == abi.E_SHAPE
+    with pytest.raises(abi.QsmlError) as e:
+        ctx.softmax(d(tx), -1, d(empty(x.shape, np.float16)))
+    assert e.value.status == abi.E_DTYPE
