@@ -770,8 +770,10 @@ def run_single(which: str, reps: int = 3):
             out = torch.empty((2729, 4096), dtype=torch.int32, device="cuda")
         for _ in range(reps):
             ctx.gather(v, d(out))
-    elif which == "layernorm":
+    elif which in ("layernorm", "layernorm_f16"):
         X = _t(datagen.normal(10, (16384, 4096), 0.5, 2.0))
+        if which == "layernorm_f16":
+            X = X.half()
         g = _t(datagen.normal(11, (4096,), 1.0, 0.1))
         b = _t(datagen.normal(12, (4096,), 0.0, 0.1))
         Y = torch.empty_like(X)
@@ -784,6 +786,13 @@ def run_single(which: str, reps: int = 3):
         C = torch.empty((8192, 8192), device="cuda")
         for _ in range(reps):
             ctx.matmul(d(A), d(B), d(C), abi.MM_FP16_F32ACC)
+    elif which in ("softmax", "softmax_f16"):
+        X = _t(datagen.normal(10, (16384, 4096), 0.5, 2.0))
+        if which == "softmax_f16":
+            X = X.half()
+        Y = torch.empty_like(X)
+        for _ in range(reps):
+            ctx.softmax(d(X), -1, d(Y))
     elif which == "matmul_3xtf32":
         s = 1.0 / np.sqrt(8192.0)
         A = _t(datagen.uniform(6, (8192, 8192), -s, s))
@@ -811,7 +820,8 @@ def main():
     ap.add_argument("--single", default=None,
                     choices=["reduce_all", "reduce_axis0", "reduce_axis1", "reduce_axis2", "reduce_all_f16",
                              "chain_add", "chain_fused", "gather_t", "gather_s", "layernorm", "matmul_f16",
-                             "matmul_3xtf32", "argmax_all", "argmax_axis1"],
+                             "matmul_3xtf32", "argmax_all", "argmax_axis1", "softmax", "softmax_f16",
+                             "layernorm_f16"],
                     help="run one kernel of the workloads a few times and exit (profiling aid, prints nothing)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

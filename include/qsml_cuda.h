@@ -299,7 +299,8 @@ QSML_API qsml_status_t qsml_gather(qsml_ctx* ctx, const qsml_tdesc* src, const q
 
 /* y = exp(x - max) / sum(exp(x - max)) over one axis (negative counts from
  * the end); x and y F32 or F16 with the same contiguous shape, binary32
- * arithmetic (max, subtract, expf, sum, one division per element).  A NaN in a
+ * arithmetic (max, subtract, expf, sum, then multiply by the correctly
+ * rounded reciprocal of the sum).  A NaN in a
  * slice makes that slice NaN.  Replaces Ops::softmax
  * (QuasarML/src/Ops/Elementwise.cpp:395-417, shader :98-135), whose indexing
  * is right for the last axis only. */

@@ -3,8 +3,8 @@
 // layer norm; this is a new op of the same API family.
 //
 // k_layer_norm_reg: persistent CTAs, one row at a time held in registers
-// (16-byte loads) with the next row already in flight, so x is read from HBM
-// exactly once and y written once; gamma/beta stay in registers.  Each
+// (16-byte loads) with the next two rows already in flight, so x is read from HBM
+// exactly once and y written once; gamma/beta stay in shared memory.  Each
 // thread's values give a local (mean, M2); warps merge them with Chan's
 // pairwise update (equal counts, written symmetrically so partner lanes hold
 // identical bits), then the warps' results merge the same way.
@@ -52,43 +52,52 @@ __device__ __forceinline__ void load_params(const GT* p, float* out) {
     }
 }
 
-// Persistent CTAs: gamma/beta of the thread's columns stay in registers and
-// the next row's x is loaded before the current row is reduced, so each CTA
-// always has a row in flight.
-// At most 256 threads per CTA, so no variant's registers are capped below
-// its need.
-template <int NV> constexpr int ln_max_threads() { return 256; }
-
+// Persistent CTAs; the next two rows' x are loaded before the current row is
+// reduced, so each CTA always has a row in flight.  gamma/beta (as binary32)
+// sit in dynamic shared memory, each thread holding exactly the columns it
+// reads, so they need no barrier and no registers.  Per-warp statistics go to
+// slots double-buffered by row parity; after one barrier every warp merges
+// all slots itself (identical bits in every warp), so a row costs one
+// barrier: row r+2 rewrites row r's slots only after every thread has passed
+// row r+1's barrier, i.e. after it read row r's slots.
 template <typename T, typename GT, int NV>
-__global__ void __launch_bounds__(ln_max_threads<NV>()) k_layer_norm_reg(const T* __restrict__ x, const GT* __restrict__ gamma,
+__global__ void __launch_bounds__(256) k_layer_norm_reg(const T* __restrict__ x, const GT* __restrict__ gamma,
                                                         const GT* __restrict__ beta, T* __restrict__ y,
                                                         int64_t rows, int cols, float eps) {
     constexpr int PV = Pack<T>::N;
     constexpr int E = NV * PV;  // elements per thread
-    __shared__ float s_mean[32], s_m2[32], s_stat[2];
+    extern __shared__ float4 ln_smem[];
+    float* sg = reinterpret_cast<float*>(ln_smem);
+    float* sb = sg + cols;
+    __shared__ float s_mean[2][8], s_m2[2][8];
     const int t = threadIdx.x, lane = t & 31, w = t >> 5, nw = blockDim.x >> 5;
     const int th = blockDim.x;
     const bool pow2 = (nw & (nw - 1)) == 0;
-    float g[E], b[E];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         const int c0 = (t + i * th) * PV;
-        load_params<GT, PV>(gamma + c0, g + i * PV);
-        load_params<GT, PV>(beta + c0, b + i * PV);
+        load_params<GT, PV>(gamma + c0, sg + c0);
+        load_params<GT, PV>(beta + c0, sb + c0);
     }
-    Pack<T> cur[NV], nxt[NV];
+    // Two rows in flight beyond the one being reduced (cur <- nxt <- nxt2).
+    Pack<T> cur[NV], nxt[NV], nxt2[NV];
     int64_t row = blockIdx.x;
     if (row < rows) {
         const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + row * cols);
 #pragma unroll
         for (int i = 0; i < NV; ++i) cur[i] = xr[t + i * th];
     }
-    for (; row < rows; row += gridDim.x) {
-        const int64_t nrow = row + gridDim.x;
+    if (row + gridDim.x < rows) {
+        const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + (row + gridDim.x) * cols);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) nxt[i] = xr[t + i * th];
+    }
+    for (int parity = 0; row < rows; row += gridDim.x, parity ^= 1) {
+        const int64_t nrow = row + 2 * static_cast<int64_t>(gridDim.x);
         if (nrow < rows) {
             const Pack<T>* xn = reinterpret_cast<const Pack<T>*>(x + nrow * cols);
 #pragma unroll
-            for (int i = 0; i < NV; ++i) nxt[i] = xn[t + i * th];
+            for (int i = 0; i < NV; ++i) nxt2[i] = xn[t + i * th];
         }
         float v[E];
 #pragma unroll
@@ -117,58 +126,61 @@ __global__ void __launch_bounds__(ln_max_threads<NV>()) k_layer_norm_reg(const T
             n = __fmul_rn(n, 2.0f);
         }
         if (lane == 0) {
-            s_mean[w] = mean;
-            s_m2[w] = m2;
+            s_mean[parity][w] = mean;
+            s_m2[parity][w] = m2;
         }
         __syncthreads();
-        if (w == 0) {
-            float gm = lane < nw ? s_mean[lane] : 0.0f, gm2 = lane < nw ? s_m2[lane] : 0.0f;
-            if (pow2) {
-                // equal counts again: butterfly inside aligned groups of nw lanes
-                float gn = n;
-                for (int m = 1; m < nw; m <<= 1) {
-                    float mo = __shfl_xor_sync(0xffffffffu, gm, m);
-                    float m2o = __shfl_xor_sync(0xffffffffu, gm2, m);
-                    chan_equal(gm, gm2, mo, m2o, gn);
-                    gn = __fmul_rn(gn, 2.0f);
-                }
-            } else if (lane == 0) {
-                float gn = n;
-                for (int j = 1; j < nw; ++j) {
-                    float tot = __fadd_rn(gn, n);
-                    float d = __fsub_rn(s_mean[j], gm);
-                    gm = __fadd_rn(gm, __fmul_rn(d, __fdiv_rn(n, tot)));
-                    gm2 = __fadd_rn(__fadd_rn(gm2, s_m2[j]),
-                                    __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(gn, n), tot)));
-                    gn = tot;
-                }
+        // Every warp merges the nw warp results the same way.
+        float gm = lane < nw ? s_mean[parity][lane] : 0.0f, gm2 = lane < nw ? s_m2[parity][lane] : 0.0f;
+        if (pow2) {
+            // equal counts again: butterfly inside aligned groups of nw lanes
+            float gn = n;
+            for (int m = 1; m < nw; m <<= 1) {
+                float mo = __shfl_xor_sync(0xffffffffu, gm, m);
+                float m2o = __shfl_xor_sync(0xffffffffu, gm2, m);
+                chan_equal(gm, gm2, mo, m2o, gn);
+                gn = __fmul_rn(gn, 2.0f);
             }
-            if (lane == 0) {
-                s_stat[0] = gm;
-                s_stat[1] = gm2;
+        } else if (lane == 0) {
+            float gn = n;
+            for (int j = 1; j < nw; ++j) {
+                float tot = __fadd_rn(gn, n);
+                float d = __fsub_rn(s_mean[parity][j], gm);
+                gm = __fadd_rn(gm, __fmul_rn(d, __fdiv_rn(n, tot)));
+                gm2 = __fadd_rn(__fadd_rn(gm2, s_m2[parity][j]),
+                                __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(gn, n), tot)));
+                gn = tot;
             }
         }
-        __syncthreads();
-        const float gm = s_stat[0];
-        const float var = __fdiv_rn(s_stat[1], static_cast<float>(cols));
+        gm = __shfl_sync(0xffffffffu, gm, 0);
+        gm2 = __shfl_sync(0xffffffffu, gm2, 0);
+        const float var = __fdiv_rn(gm2, static_cast<float>(cols));
         const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
         Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
+            const int c0 = (t + i * th) * PV;
+            float g[PV], b[PV];
+#pragma unroll
+            for (int e = 0; e < PV; e += 4) {
+                const float4 gv = *reinterpret_cast<const float4*>(sg + c0 + e);
+                const float4 bv = *reinterpret_cast<const float4*>(sb + c0 + e);
+                g[e] = gv.x; g[e + 1] = gv.y; g[e + 2] = gv.z; g[e + 3] = gv.w;
+                b[e] = bv.x; b[e + 1] = bv.y; b[e + 2] = bv.z; b[e + 3] = bv.w;
+            }
             Pack<T> o;
 #pragma unroll
             for (int e = 0; e < PV; ++e) {
-                const int k = i * PV + e;
-                float z = __fmul_rn(__fsub_rn(v[k], gm), rstd);
-                o.v[e] = from_f_tag(__fmaf_rn(z, g[k], b[k]), static_cast<T*>(nullptr));
+                float z = __fmul_rn(__fsub_rn(v[i * PV + e], gm), rstd);
+                o.v[e] = from_f_tag(__fmaf_rn(z, g[e], b[e]), static_cast<T*>(nullptr));
             }
             yr[t + i * th] = o;
         }
 #pragma unroll
-        for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
-        // s_mean/s_m2/s_stat are rewritten next row only after every thread
-        // has passed this barrier.
-        __syncthreads();
+        for (int i = 0; i < NV; ++i) {
+            cur[i] = nxt[i];
+            nxt[i] = nxt2[i];
+        }
     }
 }
 
@@ -232,26 +244,37 @@ __global__ void __launch_bounds__(256) k_layer_norm_generic(const T* __restrict_
 template <typename T, typename GT, int NV>
 qsml_status_t launch_reg(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int cols,
                          float eps, unsigned th) {
-    // Resident CTAs per SM for this block size, queried once per kernel
-    // variant and block size (so later calls, graph capture included, make
-    // no runtime query).
+    // gamma and beta as binary32 in dynamic shared memory: 8 bytes per column,
+    // at most 128 KiB (fp16 rows of 256 threads x 8 packs x 8 = 16384 columns).
+    const size_t smem = static_cast<size_t>(cols) * 2 * sizeof(float);
+    // Resident CTAs per SM for this block size and width, queried once per
+    // kernel variant (later calls, graph capture included, make no runtime
+    // query); the attribute for more than 48 KiB is set at the same time.
     static std::mutex mu;
-    static std::map<unsigned, int> per_sm_cache;
+    static std::map<std::pair<unsigned, int>, int> per_sm_cache;
     int per_sm = 0;
     {
         std::lock_guard<std::mutex> lk(mu);
-        auto it = per_sm_cache.find(th);
+        auto key = std::make_pair(th, cols);
+        auto it = per_sm_cache.find(key);
         if (it == per_sm_cache.end()) {
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_layer_norm_reg<T, GT, NV>, static_cast<int>(th), 0);
+            if (smem > 48 * 1024)
+                QSML_TRY_STATUS(check_cuda(ctx,
+                                           cudaFuncSetAttribute(k_layer_norm_reg<T, GT, NV>,
+                                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                                static_cast<int>(smem)),
+                                           "layer norm: shared-memory attribute"));
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_layer_norm_reg<T, GT, NV>, static_cast<int>(th),
+                                                          smem);
             if (per_sm < 1) per_sm = 1;
-            per_sm_cache[th] = per_sm;
+            per_sm_cache[key] = per_sm;
         } else {
             per_sm = it->second;
         }
     }
     int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
     if (grid > rows) grid = rows;
-    k_layer_norm_reg<T, GT, NV><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, g, b, y, rows, cols, eps);
+    k_layer_norm_reg<T, GT, NV><<<static_cast<unsigned>(grid), th, smem, ctx->stream>>>(x, g, b, y, rows, cols, eps);
     return after_launch(ctx, "k_layer_norm_reg");
 }
 

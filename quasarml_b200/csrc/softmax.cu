@@ -5,9 +5,11 @@
 // the row max, another for the sum of exp(x - max), then
 // out = exp(x - max) / sum.  Its indexing (offset = row * axis_size) is right
 // for the last axis only.  Here the same arithmetic (max, subtract, expf,
-// binary32 sum, one division per element) runs over any axis:
+// binary32 sum; the division as a correctly rounded reciprocal per slice and
+// one multiply per element, within 1.5 ulp of the quotient -- GLSL's `/` is
+// not correctly rounded either) runs over any axis:
 //   * k_softmax_rows -- last axis, row held in registers (16-byte loads):
-//     persistent CTAs with the next row in flight, so x is read once and y
+//     persistent CTAs with the next two rows in flight, so x is read once and y
 //     written once;
 //   * k_softmax_rows_generic -- last axis, any width: one CTA per row, three
 //     passes over global memory (max, sum, write);
@@ -36,9 +38,13 @@ __device__ __forceinline__ float max_nan(float a, float b) {
     return r;
 }
 
-// Block-wide max and sum of kBlock/32 warps: xor butterflies inside warps
-// (both partners hold identical bits), then warp 0 combines the warp results
-// in warp order.  `sh` holds 33 floats.
+// Block-wide max or sum: xor butterflies inside warps (both partners hold
+// identical bits), one slot per warp in `sh`, one barrier, then every thread
+// combines the slots in warp order (the same bits everywhere).  Callers use a
+// separate `sh` for the max and for the sum of a row: the max slots of row
+// r+1 are written only after every thread passed row r's sum barrier (so
+// after it read row r's max), and the sum slots of row r+1 only after row
+// r+1's max barrier (so after every thread read row r's sum).
 template <bool MAX>
 __device__ __forceinline__ float block_combine(float v, float* sh) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -49,15 +55,9 @@ __device__ __forceinline__ float block_combine(float v, float* sh) {
     }
     if (lane == 0) sh[w] = v;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float a = sh[0];
-        for (int j = 1; j < nw; ++j) a = MAX ? max_nan(a, sh[j]) : __fadd_rn(a, sh[j]);
-        sh[32] = a;
-    }
-    __syncthreads();
-    const float r = sh[32];
-    __syncthreads();  // sh is reused by the next call
-    return r;
+    float a = sh[0];
+    for (int j = 1; j < nw; ++j) a = MAX ? max_nan(a, sh[j]) : __fadd_rn(a, sh[j]);
+    return a;
 }
 
 template <typename T, int NV>
@@ -65,21 +65,27 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const T* __restrict__ x, T
                                                       int cols) {
     constexpr int PV = Pack<T>::N;
     constexpr int E = NV * PV;
-    __shared__ float sh[33];
+    __shared__ float sh_max[8], sh_sum[8];
     const int t = threadIdx.x, th = blockDim.x;
-    Pack<T> cur[NV], nxt[NV];
+    // Two rows in flight beyond the one being reduced (cur <- nxt <- nxt2).
+    Pack<T> cur[NV], nxt[NV], nxt2[NV];
     int64_t row = blockIdx.x;
     if (row < rows) {
         const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + row * cols);
 #pragma unroll
         for (int i = 0; i < NV; ++i) cur[i] = xr[t + i * th];
     }
+    if (row + gridDim.x < rows) {
+        const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + (row + gridDim.x) * cols);
+#pragma unroll
+        for (int i = 0; i < NV; ++i) nxt[i] = xr[t + i * th];
+    }
     for (; row < rows; row += gridDim.x) {
-        const int64_t nrow = row + gridDim.x;
+        const int64_t nrow = row + 2 * static_cast<int64_t>(gridDim.x);
         if (nrow < rows) {
             const Pack<T>* xn = reinterpret_cast<const Pack<T>*>(x + nrow * cols);
 #pragma unroll
-            for (int i = 0; i < NV; ++i) nxt[i] = xn[t + i * th];
+            for (int i = 0; i < NV; ++i) nxt2[i] = xn[t + i * th];
         }
         float v[E];
 #pragma unroll
@@ -89,42 +95,47 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const T* __restrict__ x, T
         float m = -INFINITY;
 #pragma unroll
         for (int k = 0; k < E; ++k) m = max_nan(m, v[k]);
-        m = block_combine<true>(m, sh);
+        m = block_combine<true>(m, sh_max);
         float s = 0.0f;
 #pragma unroll
         for (int k = 0; k < E; ++k) {
             v[k] = expf(__fsub_rn(v[k], m));
             s = __fadd_rn(s, v[k]);
         }
-        s = block_combine<false>(s, sh);
+        s = block_combine<false>(s, sh_sum);
+        const float inv = __frcp_rn(s);
         Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
             Pack<T> o;
 #pragma unroll
-            for (int e = 0; e < PV; ++e) from_f(__fdiv_rn(v[i * PV + e], s), &o.v[e]);
+            for (int e = 0; e < PV; ++e) from_f(__fmul_rn(v[i * PV + e], inv), &o.v[e]);
             yr[t + i * th] = o;
         }
 #pragma unroll
-        for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
+        for (int i = 0; i < NV; ++i) {
+            cur[i] = nxt[i];
+            nxt[i] = nxt2[i];
+        }
     }
 }
 
 template <typename T>
 __global__ void __launch_bounds__(256) k_softmax_rows_generic(const T* __restrict__ x, T* __restrict__ y,
                                                               int64_t rows, int64_t cols) {
-    __shared__ float sh[33];
+    __shared__ float sh_max[8], sh_sum[8];
     for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const T* xr = x + row * cols;
         float m = -INFINITY;
         for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) m = max_nan(m, to_f(xr[c]));
-        m = block_combine<true>(m, sh);
+        m = block_combine<true>(m, sh_max);
         float s = 0.0f;
         for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) s = __fadd_rn(s, expf(__fsub_rn(to_f(xr[c]), m)));
-        s = block_combine<false>(s, sh);
+        s = block_combine<false>(s, sh_sum);
+        const float inv = __frcp_rn(s);
         T* yr = y + row * cols;
         for (int64_t c = threadIdx.x; c < cols; c += blockDim.x)
-            from_f(__fdiv_rn(expf(__fsub_rn(to_f(xr[c]), m)), s), &yr[c]);
+            from_f(__fmul_rn(expf(__fsub_rn(to_f(xr[c]), m)), inv), &yr[c]);
     }
 }
 
@@ -143,7 +154,8 @@ __global__ void __launch_bounds__(256) k_softmax_cols(const T* __restrict__ x, T
         for (int64_t j = 0; j < k; ++j) m = max_nan(m, to_f(xc[j * inner]));
         float s = 0.0f;
         for (int64_t j = 0; j < k; ++j) s = __fadd_rn(s, expf(__fsub_rn(to_f(xc[j * inner]), m)));
-        for (int64_t j = 0; j < k; ++j) from_f(__fdiv_rn(expf(__fsub_rn(to_f(xc[j * inner]), m)), s), &yc[j * inner]);
+        const float inv = __frcp_rn(s);
+        for (int64_t j = 0; j < k; ++j) from_f(__fmul_rn(expf(__fsub_rn(to_f(xc[j * inner]), m)), inv), &yc[j * inner]);
     }
 }
 
