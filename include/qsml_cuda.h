@@ -322,6 +322,38 @@ QSML_API qsml_status_t qsml_layer_norm(qsml_ctx* ctx, const qsml_tdesc* x, const
 QSML_API qsml_status_t qsml_matmul(qsml_ctx* ctx, const qsml_tdesc* a, const qsml_tdesc* b,
                                    const qsml_tdesc* c, int32_t precision);
 
+/* ---- Multi-GPU groups (NCCL) ------------------------------------------------
+ * The reference is single-GPU; sharded execution combines per-GPU partial
+ * results with an in-place all-reduce.  Two ways to form a group:
+ *   one process per GPU   -- one rank calls qsml_group_unique_id, the host
+ *                            shares the bytes, every rank calls
+ *                            qsml_group_init_rank with its context;
+ *   one process, n GPUs   -- qsml_group_init_all over n contexts (rank i =
+ *                            ctxs[i]); collectives for several of them from
+ *                            one thread go between qsml_group_start and
+ *                            qsml_group_end.
+ * Collectives run on the rank's context stream, in order with its kernels.
+ * Every wait on NCCL is bounded by QSML_NCCL_TIMEOUT_MS (default 60000): a
+ * rank that never joins, or a collective that makes no progress, returns
+ * QSML_E_TIMEOUT; qsml_group_destroy then aborts the communicators. */
+#define QSML_UNIQUE_ID_BYTES 128
+typedef struct qsml_group qsml_group;
+
+QSML_API qsml_status_t qsml_group_unique_id(uint8_t* id /* QSML_UNIQUE_ID_BYTES */);
+QSML_API qsml_status_t qsml_group_init_rank(qsml_ctx* ctx, const uint8_t* id, int32_t nranks, int32_t rank,
+                                            qsml_group** group);
+QSML_API qsml_status_t qsml_group_init_all(qsml_ctx* const* ctxs, int32_t n, qsml_group** group);
+QSML_API qsml_status_t qsml_group_size(qsml_group* group, int32_t* nranks, int32_t* local_ranks);
+QSML_API qsml_status_t qsml_group_start(void);
+QSML_API qsml_status_t qsml_group_end(void);
+/* In-place all-reduce of `count` elements at buf (device memory of local rank
+ * `local`'s context; 0 for init_rank groups): op QSML_RED_SUM, MEAN (the sum
+ * divided by the number of ranks), MAX, MIN or PROD; dtype F32, F16, I32,
+ * U32, I8 or U8. */
+QSML_API qsml_status_t qsml_allreduce(qsml_group* group, int32_t local, void* buf, int64_t count, int32_t dtype,
+                                      int32_t op);
+QSML_API qsml_status_t qsml_group_destroy(qsml_group* group);
+
 /* Allocation-free sum / mean / max / min over all elements (axis =
  * QSML_AXIS_ALL) or over an axis followed only by unit dims, for callers that
  * cannot allocate device memory at that point: work enqueued while a stream

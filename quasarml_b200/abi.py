@@ -128,6 +128,14 @@ _SIGS = {
                                             _P(TDesc)]),
     "qsml_set_fuse_mode": (_c.c_int32, [_c.c_void_p, _c.c_int32]),
     "qsml_fuse_stats": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64), _P(_c.c_uint64), _P(_c.c_uint64)]),
+    "qsml_group_unique_id": (_c.c_int32, [_c.c_void_p]),
+    "qsml_group_init_rank": (_c.c_int32, [_c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _P(_c.c_void_p)]),
+    "qsml_group_init_all": (_c.c_int32, [_P(_c.c_void_p), _c.c_int32, _P(_c.c_void_p)]),
+    "qsml_group_size": (_c.c_int32, [_c.c_void_p, _P(_c.c_int32), _P(_c.c_int32)]),
+    "qsml_group_start": (_c.c_int32, []),
+    "qsml_group_end": (_c.c_int32, []),
+    "qsml_allreduce": (_c.c_int32, [_c.c_void_p, _c.c_int32, _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_int32]),
+    "qsml_group_destroy": (_c.c_int32, [_c.c_void_p]),
     "qsml_gather": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc)]),
     "qsml_softmax": (_c.c_int32, [_c.c_void_p, _P(TDesc), _c.c_int32, _P(TDesc)]),
     "qsml_layer_norm": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_float, _P(TDesc)]),
@@ -157,6 +165,66 @@ def load() -> ctypes.CDLL:
         fn.argtypes = args
     _lib = lib
     return lib
+
+
+UNIQUE_ID_BYTES = 128
+
+
+def _check_global(st: int) -> None:
+    if st != OK:
+        raise QsmlError(st, load().qsml_last_error(None).decode())
+
+
+def group_unique_id() -> bytes:
+    """A new NCCL unique id (one rank makes it, every rank of the group uses it)."""
+    buf = (ctypes.c_uint8 * UNIQUE_ID_BYTES)()
+    _check_global(load().qsml_group_unique_id(buf))
+    return bytes(buf)
+
+
+class Group:
+    """A qsml_group: init_rank(ctx, uid, nranks, rank) for one process per
+    GPU, or init_all([ctx, ...]) for one process driving several GPUs."""
+
+    def __init__(self, handle, ctxs):
+        self.h, self.ctxs = handle, list(ctxs)
+
+    @classmethod
+    def init_rank(cls, ctx, uid: bytes, nranks: int, rank: int) -> "Group":
+        h = ctypes.c_void_p()
+        buf = (ctypes.c_uint8 * UNIQUE_ID_BYTES).from_buffer_copy(uid)
+        ctx.check(ctx.lib.qsml_group_init_rank(ctx.h, buf, int(nranks), int(rank), ctypes.byref(h)))
+        return cls(h, [ctx])
+
+    @classmethod
+    def init_all(cls, ctxs) -> "Group":
+        h = ctypes.c_void_p()
+        arr = (ctypes.c_void_p * len(ctxs))(*[c.h.value for c in ctxs])
+        _check_global(load().qsml_group_init_all(arr, len(ctxs), ctypes.byref(h)))
+        return cls(h, ctxs)
+
+    def size(self) -> tuple:
+        n, loc = ctypes.c_int32(), ctypes.c_int32()
+        _check_global(load().qsml_group_size(self.h, ctypes.byref(n), ctypes.byref(loc)))
+        return n.value, loc.value
+
+    def allreduce(self, local: int, ptr: int, count: int, dtype: int, op: int) -> None:
+        st = load().qsml_allreduce(self.h, int(local), ctypes.c_void_p(ptr), int(count), int(dtype), int(op))
+        if st != OK:
+            raise QsmlError(st, load().qsml_last_error(self.ctxs[local].h).decode())
+
+    def destroy(self) -> None:
+        if self.h:
+            _check_global(load().qsml_group_destroy(self.h))
+            self.h = None
+
+
+def group_start() -> None:
+    _check_global(load().qsml_group_start())
+
+
+def group_end() -> None:
+    _check_global(load().qsml_group_end())
 
 
 def declared_functions() -> list:

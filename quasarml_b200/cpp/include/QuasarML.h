@@ -16,6 +16,7 @@
 #include "Core/Device.h"
 #include "Core/DeviceManager.h"
 #include "Core/Tensor.h"
+#include "Ops/Distributed.h"
 #include "Ops/Elementwise.h"
 #include "Ops/LinAlg.h"
 #include "Ops/Manipulation.h"
@@ -175,6 +176,13 @@ inline TensorPtr copy(TensorPtr x) { return QuasarML::Ops::copy(device(), x); }
 inline TensorPtr contiguous(TensorPtr x) { return QuasarML::Ops::contiguous(device(), x); }
 
 // Ops that ran on the host instead of the GPU: always 0 in this backend.
+// Multi-GPU: in-place all-reduce of one tensor per device (this process
+// drives all of them).
+using QuasarML::ReduceOp;
+inline void all_reduce(const std::vector<TensorPtr>& per_device, ReduceOp op = ReduceOp::Sum) {
+    QuasarML::Ops::all_reduce(per_device, op);
+}
+
 // Elementwise fusion (deferred results evaluated as one kernel on access).
 inline void set_fusion(bool on) { device().set_fusion(on); }
 inline bool fusion_enabled() { return device().fusion(); }

@@ -11,6 +11,7 @@
 #include "Core/Device.h"
 #include "Core/DeviceManager.h"
 #include "Core/Tensor.h"
+#include "Ops/Distributed.h"
 
 namespace QuasarML {
 
@@ -411,6 +412,7 @@ void DeviceManager::set_default(u32 device_id) {
 }
 
 void DeviceManager::shutdown() {
+    Ops::release_device_groups();  // groups hold the devices' contexts
     std::lock_guard<std::mutex> lock(_mutex);
     if (_shutdown) return;
     _shutdown = true;

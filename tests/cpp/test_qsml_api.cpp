@@ -325,6 +325,28 @@ static void test_fusion() {
     check("fusion off again", !qsml::fusion_enabled());
 }
 
+// All-reduce across the devices of this process (identity with one GPU).
+static void test_all_reduce() {
+    const qsml::u32 n = qsml::device_count() >= 2 ? 2 : 1;
+    std::vector<qsml::TensorPtr> parts;
+    for (qsml::u32 i = 0; i < n; ++i) {
+        vector<float> v(1024, static_cast<float>(i + 1));
+        auto t = qsml::device(i).create_tensor({1024});
+        t->upload(v.data());
+        parts.push_back(t);
+    }
+    qsml::all_reduce(parts, qsml::ReduceOp::Sum);
+    const float want = n == 2 ? 3.0f : 1.0f;
+    bool ok = true;
+    for (auto& t : parts) {
+        auto v = get(t);
+        ok &= v[0] == want && v[1023] == want;
+    }
+    check("all_reduce sum across devices", ok);
+    qsml::all_reduce(parts, qsml::ReduceOp::Max);
+    check("all_reduce max", get(parts[0])[5] == want);
+}
+
 static void test_errors_and_counters() {
     bool threw = false;
     try {
@@ -359,6 +381,7 @@ int main() {
         test_views_and_gathers();
         test_layer_norm_and_matmul();
         test_fusion();
+        test_all_reduce();
         test_errors_and_counters();
     } catch (const std::exception& e) {
         std::cout << "EXCEPTION: " << e.what() << "\n";
