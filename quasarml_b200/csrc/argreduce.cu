@@ -209,7 +209,18 @@ __global__ void __launch_bounds__(256) k_arg_rows(const T* __restrict__ x, int64
         if (VEC) {
             const APack<T>* p = reinterpret_cast<const APack<T>*>(row);
             const int64_t np = len / PV;
-            for (int64_t i = lane; i < np; i += 32) {
+            constexpr int U = 4;
+            int64_t i = lane;
+            for (; i + (U - 1) * 32 < np; i += U * 32) {
+                APack<T> v[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) v[u] = p[i + u * 32];
+#pragma unroll
+                for (int u = 0; u < U; ++u)
+#pragma unroll
+                    for (int e = 0; e < PV; ++e) b.see(cval(v[u].v[e]), static_cast<uint32_t>((i + u * 32) * PV + e));
+            }
+            for (; i < np; i += 32) {
                 APack<T> v = p[i];
 #pragma unroll
                 for (int e = 0; e < PV; ++e) b.see(cval(v.v[e]), static_cast<uint32_t>(i * PV + e));
@@ -242,14 +253,33 @@ __global__ void k_arg_cols(const T* __restrict__ x, int64_t outer, int64_t k, in
     Best<OP, C> b[PV];
     if (o < outer && c0 < inner) {
         const T* base = x + (o * k) * inner + c0;
+        // U rows of loads in flight before they are consumed in k order.
+        constexpr int U = 8;
+        int64_t kk = k0;
         if (VEC) {
-            for (int64_t kk = k0; kk < k1; ++kk) {
+            for (; kk + U <= k1; kk += U) {
+                APack<T> v[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) v[u] = *reinterpret_cast<const APack<T>*>(base + (kk + u) * inner);
+#pragma unroll
+                for (int u = 0; u < U; ++u)
+#pragma unroll
+                    for (int e = 0; e < PV; ++e) b[e].see(cval(v[u].v[e]), static_cast<uint32_t>(kk + u));
+            }
+            for (; kk < k1; ++kk) {
                 APack<T> v = *reinterpret_cast<const APack<T>*>(base + kk * inner);
 #pragma unroll
                 for (int e = 0; e < PV; ++e) b[e].see(cval(v.v[e]), static_cast<uint32_t>(kk));
             }
         } else {
-            for (int64_t kk = k0; kk < k1; ++kk) b[0].see(cval(base[kk * inner]), static_cast<uint32_t>(kk));
+            for (; kk + U <= k1; kk += U) {
+                T v[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) v[u] = base[(kk + u) * inner];
+#pragma unroll
+                for (int u = 0; u < U; ++u) b[0].see(cval(v[u]), static_cast<uint32_t>(kk + u));
+            }
+            for (; kk < k1; ++kk) b[0].see(cval(base[kk * inner]), static_cast<uint32_t>(kk));
         }
     }
 #pragma unroll

@@ -143,7 +143,7 @@ std::string generate(const qsml_fuse_node* nodes, int n, const JitInput* ins, in
     if (half) s << kHalfHelpers;
     s << "extern \"C\" __global__ void __launch_bounds__(" << kJitThreads << ") qsml_fused_kernel(";
     for (int j = 0; j < nin; ++j) s << "const " << T << "* __restrict__ p" << j << ", long long r" << j << ", ";
-    s << T << "* __restrict__ out, unsigned items, unsigned cpr) {\n";
+    s << T << "* __restrict__ out, unsigned items, unsigned cpr, unsigned magic, unsigned sh1, unsigned sh2) {\n";
     s << "  const int V = " << V << ", U = " << U << ";\n";
     s << "  const unsigned base = blockIdx.x * (" << kJitThreads << "u * U) + threadIdx.x;\n";
     for (int j = 0; j < nin; ++j) s << "  float x" << j << "[U * V];\n";
@@ -151,7 +151,9 @@ std::string generate(const qsml_fuse_node* nodes, int n, const JitInput* ins, in
     s << "#pragma unroll\n  for (int u = 0; u < U; ++u) {\n";
     s << "    const unsigned it = base + u * " << kJitThreads << "u;\n";
     s << "    ok[u] = it < items;\n    its[u] = it;\n";
-    s << "    const unsigned row = ok[u] ? it / cpr : 0u;\n    const unsigned cv = it - row * cpr;\n";
+    // row = it / cpr by multiply-high (Granlund-Montgomery, exact for 32-bit it)
+    s << "    const unsigned t1 = __umulhi(magic, it);\n";
+    s << "    const unsigned row = ok[u] ? (t1 + ((it - t1) >> sh1)) >> sh2 : 0u;\n    const unsigned cv = it - row * cpr;\n";
     for (int j = 0; j < nin; ++j) {
         if (ins[j].vec) {
             s << "    { const uint4 w = ok[u] ? *reinterpret_cast<const uint4*>(p" << j << " + (long long)row * r" << j
@@ -288,6 +290,13 @@ qsml_status_t fused_jit(Context* ctx, const qsml_fuse_node* nodes, int n_nodes, 
     std::vector<const void*> ptrs(nin);
     std::vector<long long> strides(nin);
     unsigned items32 = static_cast<unsigned>(items), cpr32 = static_cast<unsigned>(cpr);
+    // Division by cpr as (t1 + ((n - t1) >> sh1)) >> sh2, t1 = mulhi(magic, n)
+    // (Granlund & Montgomery 1994, unsigned division by invariant integers):
+    // l = ceil(log2 cpr), magic = floor(2^32 (2^l - cpr) / cpr) + 1.
+    unsigned l = 0;
+    while ((uint64_t(1) << l) < cpr32) ++l;
+    unsigned magic = static_cast<unsigned>(((uint64_t(1) << 32) * ((uint64_t(1) << l) - cpr32)) / cpr32 + 1);
+    unsigned sh1 = l < 1 ? l : 1, sh2 = l > 1 ? l - 1 : 0;
     void* outp = out;
     for (int j = 0; j < nin; ++j) {
         ptrs[j] = ins[j].ptr;
@@ -300,6 +309,9 @@ qsml_status_t fused_jit(Context* ctx, const qsml_fuse_node* nodes, int n_nodes, 
     args.push_back(&outp);
     args.push_back(&items32);
     args.push_back(&cpr32);
+    args.push_back(&magic);
+    args.push_back(&sh1);
+    args.push_back(&sh2);
     const int per_block = kJitThreads * (kJitElems / (half ? 8 : 4));
     const int64_t blocks = (items + per_block - 1) / per_block;
     const CUresult lr = r.launch(fn, static_cast<unsigned>(blocks), 1, 1, kJitThreads, 1, 1, 0,
