@@ -793,6 +793,13 @@ def run_single(which: str, reps: int = 3):
         Y = torch.empty_like(X)
         for _ in range(reps):
             ctx.softmax(d(X), -1, d(Y))
+    elif which == "bmm_f16":
+        s = 1.0 / np.sqrt(1024.0)
+        A = _t(datagen.uniform(9, (32, 2048, 1024), -s, s)).half()
+        B = _t(datagen.uniform(8, (32, 1024, 2048), -s, s)).half()
+        C = torch.empty((32, 2048, 2048), device="cuda")
+        for _ in range(reps):
+            ctx.matmul(d(A), d(B), d(C), abi.MM_FP16_F32ACC)
     elif which == "matmul_3xtf32":
         s = 1.0 / np.sqrt(8192.0)
         A = _t(datagen.uniform(6, (8192, 8192), -s, s))
@@ -820,7 +827,7 @@ def main():
     ap.add_argument("--single", default=None,
                     choices=["reduce_all", "reduce_axis0", "reduce_axis1", "reduce_axis2", "reduce_all_f16",
                              "chain_add", "chain_fused", "gather_t", "gather_s", "layernorm", "matmul_f16",
-                             "matmul_3xtf32", "argmax_all", "argmax_axis1", "softmax", "softmax_f16",
+                             "matmul_3xtf32", "bmm_f16", "argmax_all", "argmax_axis1", "softmax", "softmax_f16",
                              "layernorm_f16"],
                     help="run one kernel of the workloads a few times and exit (profiling aid, prints nothing)")
     args = ap.parse_args()
