@@ -165,8 +165,12 @@ QSML_API qsml_status_t qsml_free(qsml_ctx* ctx, void* ptr);
 QSML_API qsml_status_t qsml_empty_cache(qsml_ctx* ctx);
 
 /* Host<->device copies on the context stream.  qsml_h2d is asynchronous for
- * pinned host memory; qsml_d2h waits for the copy before returning.
- * Replace Backend::upload_buffer / download_buffer / copy_buffer
+ * pinned host memory; from pageable memory it returns once the source may be
+ * reused (copies of 8 MiB and more are staged through the context's pinned
+ * buffers by several host threads, the DMAs stay ordered on the stream).
+ * qsml_d2h waits for the data before returning (pageable destinations of
+ * 8 MiB and more are staged the same way).  Replace Backend::upload_buffer /
+ * download_buffer / copy_buffer
  * (QuasarML/src/Backend/Vulkan/VulkanBackend.cpp:327-373). */
 QSML_API qsml_status_t qsml_h2d(qsml_ctx* ctx, void* dst, const void* src, size_t bytes);
 QSML_API qsml_status_t qsml_d2h(qsml_ctx* ctx, void* dst, const void* src, size_t bytes);

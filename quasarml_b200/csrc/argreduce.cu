@@ -29,6 +29,7 @@ constexpr int64_t kArgSlots = 1184;       // slices per launch (148 SMs x 8 CTAs
 constexpr int64_t kArgMinSlice = 4096;    // elements: short rows use fewer slices
 constexpr int kArgMaxSegments = 16384;    // ticket counters at the start of scratch
 constexpr size_t kArgCounterBytes = kArgMaxSegments * sizeof(unsigned);
+static_assert(kArgCounterBytes == kScratchCounterBytes, "counters fill the reserved scratch region");
 constexpr uint32_t kNone = 0xFFFFFFFFu;   // per-thread "no element yet"
 
 template <typename T> struct alignas(16) APack {

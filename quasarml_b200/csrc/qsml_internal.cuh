@@ -41,6 +41,8 @@ private:
     uint64_t malloc_calls_ = 0;
 };
 
+struct Staging;  // pinned staging buffers for pageable copies (transfer.cu)
+
 // Per-device execution context: what a reference Device owned through its
 // Backend (queue, allocator, kernel cache), on CUDA.
 struct Context {
@@ -60,6 +62,7 @@ struct Context {
     // Fused elementwise expressions: QSML_FUSE_MODE_* and which kernel ran.
     int fuse_mode = 0;
     uint64_t fuse_jit_launches = 0, fuse_interp_launches = 0;
+    Staging* staging = nullptr;
     std::mutex err_mu;
     std::string last_error;
 };
@@ -70,8 +73,19 @@ qsml_status_t check_cuda(Context* ctx, cudaError_t e, const char* what);
 // Checks the launch that was just enqueued and counts it.
 qsml_status_t after_launch(Context* ctx, const char* kernel);
 
-// Scratch of at least `bytes` (the first 256 bytes hold zeroed counters).
+// Scratch of at least `bytes`.  Its first kScratchCounterBytes hold the
+// reductions' ticket counters, which every kernel that uses them leaves at
+// zero; other users place their data after that region.
+constexpr size_t kScratchCounterBytes = size_t(64) << 10;
 qsml_status_t get_scratch(Context* ctx, size_t bytes, void** ptr);
+
+// Host <-> device copies (transfer.cu): pageable host memory of 8 MiB and
+// more goes through pinned staging with multi-threaded host copies.
+// copy_h2d returns once the source may be reused; copy_d2h once the data is
+// in dst.
+qsml_status_t copy_h2d(Context* ctx, void* dst, const void* src, size_t bytes);
+qsml_status_t copy_d2h(Context* ctx, void* dst, const void* src, size_t bytes);
+void staging_free(Context* ctx);
 
 // Descriptor helpers ---------------------------------------------------------
 inline int dtype_size(int32_t dt) {

@@ -38,6 +38,7 @@ constexpr int64_t kSegSlots = 1184;  // slices per launch (148 SMs x 8 CTAs), a 
 constexpr int64_t kSegMinSlice = 4096;  // elements: short rows use fewer slices
 constexpr int kMaxSegments = 16384;  // ticket counters kept in scratch
 constexpr size_t kCounterBytes = kMaxSegments * sizeof(unsigned);
+static_assert(kCounterBytes == kScratchCounterBytes, "counters fill the reserved scratch region");
 
 template <typename T> struct alignas(16) Pack {
     static constexpr int N = 16 / sizeof(T);

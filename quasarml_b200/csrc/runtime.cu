@@ -301,6 +301,7 @@ qsml_status_t qsml_destroy(qsml_ctx* handle) {
     QSML_CTX(handle);
     cudaStreamSynchronize(C_->stream);
     if (C_->stream != C_->own_stream) cudaStreamSynchronize(C_->own_stream);
+    qsml::staging_free(C_);
     delete C_->allocator;
     if (C_->scratch) cudaFree(C_->scratch);
     if (C_->status) cudaFree(C_->status);
@@ -378,7 +379,7 @@ qsml_status_t qsml_h2d(qsml_ctx* handle, void* dst, const void* src, size_t byte
     QSML_CTX(handle);
     if (bytes == 0) return QSML_OK;
     if (!dst || !src) return qsml::set_error(C_, QSML_E_INVALID, "qsml_h2d: null pointer");
-    return qsml::check_cuda(C_, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, C_->stream), "qsml_h2d");
+    return qsml::copy_h2d(C_, dst, src, bytes);
 }
 
 qsml_status_t qsml_d2h_async(qsml_ctx* handle, void* dst, const void* src, size_t bytes) {
@@ -389,9 +390,10 @@ qsml_status_t qsml_d2h_async(qsml_ctx* handle, void* dst, const void* src, size_
 }
 
 qsml_status_t qsml_d2h(qsml_ctx* handle, void* dst, const void* src, size_t bytes) {
-    QSML_TRY_STATUS(qsml_d2h_async(handle, dst, src, bytes));
-    Context* C_ = reinterpret_cast<Context*>(handle);
-    return qsml::check_cuda(C_, cudaStreamSynchronize(C_->stream), "qsml_d2h sync");
+    QSML_CTX(handle);
+    if (bytes == 0) return QSML_OK;
+    if (!dst || !src) return qsml::set_error(C_, QSML_E_INVALID, "qsml_d2h: null pointer");
+    return qsml::copy_d2h(C_, dst, src, bytes);
 }
 
 qsml_status_t qsml_d2d(qsml_ctx* handle, void* dst, const void* src, size_t bytes) {

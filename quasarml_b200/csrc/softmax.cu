@@ -13,6 +13,8 @@
 //     written once;
 //   * k_softmax_rows_generic -- last axis, any width: one CTA per row, three
 //     passes over global memory (max, sum, write);
+//   * k_softmax_long_{max,sum,out} -- last axis, fewer rows than SMs and long
+//     rows: slices of each row over many CTAs, three launches;
 //   * k_softmax_cols -- inner dims after the axis: one thread per column of
 //     the [outer, k, inner] view, three passes over k.
 // The max is IEEE 754-2019 maximum (a NaN in the row makes the row NaN), and
@@ -159,6 +161,99 @@ __global__ void __launch_bounds__(256) k_softmax_cols(const T* __restrict__ x, T
     }
 }
 
+// ---------------------------------------------------------------------------
+// Long rows (few rows, many elements): each row is cut into P slices, one CTA
+// per (row, slice), in three launches -- slice maxima; slice sums of
+// exp(x - m) with every CTA combining the row's maxima itself in slice order;
+// then y = exp(x - m) * (1 / s) with m and s recombined the same way.  The
+// combine orders depend on the shape only, so results are deterministic.
+// ---------------------------------------------------------------------------
+constexpr int kLongThreads = 256;
+
+template <typename T>
+__device__ __forceinline__ void slice_bounds(int64_t cols, int64_t P, int64_t j, int64_t* c0, int64_t* c1) {
+    const int64_t per = (cols + P - 1) / P;
+    *c0 = j * per;
+    *c1 = *c0 + per < cols ? *c0 + per : cols;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kLongThreads) k_softmax_long_max(const T* __restrict__ x, int64_t rows,
+                                                                   int64_t cols, int64_t P, float* __restrict__ pmax) {
+    __shared__ float sh[8];
+    const int64_t unit = blockIdx.x, r = unit / P, j = unit - r * P;
+    int64_t c0, c1;
+    slice_bounds<T>(cols, P, j, &c0, &c1);
+    const T* xr = x + r * cols;
+    float m = -INFINITY;
+    for (int64_t c = c0 + threadIdx.x; c < c1; c += kLongThreads) m = max_nan(m, to_f(xr[c]));
+    m = block_combine<true>(m, sh);
+    if (threadIdx.x == 0) pmax[unit] = m;
+}
+
+__device__ __forceinline__ float row_max(const float* pmax, int64_t r, int64_t P) {
+    float m = -INFINITY;
+    for (int64_t i = 0; i < P; ++i) m = max_nan(m, pmax[r * P + i]);
+    return m;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kLongThreads) k_softmax_long_sum(const T* __restrict__ x, int64_t rows,
+                                                                   int64_t cols, int64_t P,
+                                                                   const float* __restrict__ pmax,
+                                                                   float* __restrict__ psum) {
+    __shared__ float sh[8];
+    const int64_t unit = blockIdx.x, r = unit / P, j = unit - r * P;
+    int64_t c0, c1;
+    slice_bounds<T>(cols, P, j, &c0, &c1);
+    const float m = row_max(pmax, r, P);
+    const T* xr = x + r * cols;
+    float s = 0.0f;
+    for (int64_t c = c0 + threadIdx.x; c < c1; c += kLongThreads) s = __fadd_rn(s, expf(__fsub_rn(to_f(xr[c]), m)));
+    s = block_combine<false>(s, sh);
+    if (threadIdx.x == 0) psum[unit] = s;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kLongThreads) k_softmax_long_out(const T* __restrict__ x, T* __restrict__ y,
+                                                                   int64_t rows, int64_t cols, int64_t P,
+                                                                   const float* __restrict__ pmax,
+                                                                   const float* __restrict__ psum) {
+    const int64_t unit = blockIdx.x, r = unit / P, j = unit - r * P;
+    int64_t c0, c1;
+    slice_bounds<T>(cols, P, j, &c0, &c1);
+    const float m = row_max(pmax, r, P);
+    float s = 0.0f;
+    for (int64_t i = 0; i < P; ++i) s = __fadd_rn(s, psum[r * P + i]);
+    const float inv = __frcp_rn(s);
+    const T* xr = x + r * cols;
+    T* yr = y + r * cols;
+    for (int64_t c = c0 + threadIdx.x; c < c1; c += kLongThreads)
+        from_f(__fmul_rn(expf(__fsub_rn(to_f(xr[c]), m)), inv), &yr[c]);
+}
+
+template <typename T>
+qsml_status_t run_long_rows(Context* ctx, const T* x, T* y, int64_t rows, int64_t cols) {
+    // about 8 CTAs per SM over all rows, slices of at least 8192 elements
+    int64_t P = (int64_t(ctx->num_sms) * 8 + rows - 1) / rows;
+    const int64_t by_size = (cols + 8191) / 8192;
+    if (P > by_size) P = by_size;
+    if (P < 1) P = 1;
+    const int64_t units = rows * P;
+    if (units > INT32_MAX) return set_error(ctx, QSML_E_UNSUPPORTED, "qsml_softmax: too many slices");
+    void* scratch = nullptr;
+    QSML_TRY_STATUS(get_scratch(ctx, kScratchCounterBytes + static_cast<size_t>(units) * 2 * sizeof(float), &scratch));
+    float* pmax = reinterpret_cast<float*>(static_cast<char*>(scratch) + kScratchCounterBytes);
+    float* psum = pmax + units;
+    const unsigned g = static_cast<unsigned>(units);
+    k_softmax_long_max<T><<<g, kLongThreads, 0, ctx->stream>>>(x, rows, cols, P, pmax);
+    QSML_TRY_STATUS(after_launch(ctx, "k_softmax_long_max"));
+    k_softmax_long_sum<T><<<g, kLongThreads, 0, ctx->stream>>>(x, rows, cols, P, pmax, psum);
+    QSML_TRY_STATUS(after_launch(ctx, "k_softmax_long_sum"));
+    k_softmax_long_out<T><<<g, kLongThreads, 0, ctx->stream>>>(x, y, rows, cols, P, pmax, psum);
+    return after_launch(ctx, "k_softmax_long_out");
+}
+
 template <typename T, int NV>
 qsml_status_t launch_rows(Context* ctx, const T* x, T* y, int64_t rows, int cols, unsigned th) {
     static std::mutex mu;
@@ -208,6 +303,8 @@ qsml_status_t run_softmax(Context* ctx, const T* x, T* y, int64_t outer, int64_t
                 }
             }
         }
+        // Few long rows: a CTA per row would leave most SMs idle.
+        if (rows < ctx->num_sms && cols >= 16384) return run_long_rows<T>(ctx, x, y, rows, cols);
         int64_t grid = rows < int64_t(ctx->num_sms) * 16 ? rows : int64_t(ctx->num_sms) * 16;
         const unsigned th = cols >= 256 ? 256 : (cols >= 128 ? 128 : (cols >= 64 ? 64 : 32));
         k_softmax_rows_generic<T><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, y, rows, cols);

@@ -120,3 +120,26 @@ def test_fault_injection_alloc_reports_oom():
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr
     assert f"STATUS {abi.E_OOM}" in r.stdout and "RECOVERED" in r.stdout, r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("nbytes", [(8 << 20) - 16, 8 << 20, (40 << 20) + 12, 67 << 20])
+def test_staged_pageable_copies_round_trip(ctx, nbytes):
+    """Pageable host buffers of 8 MiB and more go through pinned staging in
+    chunks (including a ragged last chunk); both directions are exact, and an
+    upload may be followed at once by reuse of the host buffer."""
+    import torch
+    rng = np.random.default_rng(nbytes)
+    src = rng.integers(0, 256, nbytes, dtype=np.uint8)
+    dev_buf = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    ctx.h2d(dev_buf.data_ptr(), src.ctypes.data, nbytes)
+    expect = src.copy()
+    src[:] = 0  # the call returned: the source may be overwritten
+    back = np.empty(nbytes, dtype=np.uint8)
+    ctx.d2h(back.ctypes.data, dev_buf.data_ptr(), nbytes)
+    assert np.array_equal(back, expect)
+    # offset (unaligned) device destination and host source
+    ctx.h2d(dev_buf.data_ptr() + 3, expect.ctypes.data + 5, nbytes - 8)
+    part = np.empty(nbytes - 8, dtype=np.uint8)
+    ctx.d2h(part.ctypes.data, dev_buf.data_ptr() + 3, nbytes - 8)
+    assert np.array_equal(part, expect[5:nbytes - 3])

@@ -23,6 +23,8 @@ CASES = [
     ((64, 512, 1024), 1),  # column kernel
     ((64, 512, 32), 0),    # column kernel, outer 1
     ((7,), 0),             # 1-D
+    ((1 << 20,), 0),       # one long row: sliced over many CTAs
+    ((3, 200000), -1),     # a few long rows: sliced
 ]
 
 
@@ -47,6 +49,18 @@ def test_matches_oracle(ctx, orc, case, dtype):
     assert np.max(err) <= atol, (shape, axis, float(np.max(err)))
     if dtype == np.float32:
         assert np.max(np.abs(got.sum(axis=axis) - 1.0)) <= 1e-5
+
+
+def test_long_rows_leave_reduction_counters_intact(ctx, orc):
+    """The sliced softmax uses the context scratch after the reductions'
+    ticket counters; a full reduction right after it must still be right."""
+    x = datagen.normal(5, (1 << 20,), 0.0, 1.0)
+    y = run(ctx, x, 0)
+    tx = dev(x)
+    out = empty((1,), np.float32)
+    ctx.reduce(abi.RED_SUM, d(tx), abi.AXIS_ALL, False, d(out))
+    assert abs(float(host(out)[0]) - float(x.astype(np.float64).sum())) <= 1e-5 * float(np.abs(x).sum())
+    assert abs(float(y.astype(np.float64).sum()) - 1.0) <= 1e-4
 
 
 def test_special_values(ctx, orc):
