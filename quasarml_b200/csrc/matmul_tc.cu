@@ -12,6 +12,8 @@
 //                B = Bhi + Blo; Ahi*Bhi + Ahi*Blo + Alo*Bhi, the Alo*Blo term
 //                is below fp32 resolution), C tile 128 x 128, k-blocks of 32,
 //                three kind::tf32 MMAs (K=8) per 8-wide k slice, 3-stage ring.
+// A third kernel, k_gemm_tc2, runs fp16 on pairs of SMs (tcgen05 cta_group::2,
+// C tile 256 x 256); it is described where it is defined.
 // Common structure:
 //   * A [M,K] row-major is K-major in shared memory, B [K,N] row-major is
 //     MN-major (N contiguous); both use a 128-byte swizzle written by TMA
@@ -29,6 +31,8 @@
 //     (again bounded), frees its TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <cstdlib>
 
 #include "matmul.cuh"
 
@@ -457,6 +461,303 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Two-SM variant (fp16 inputs): a cluster of two CTAs computes a 256 x 256
+// tile with tcgen05.mma.cta_group::2.  Each CTA holds 128 rows of A and 128
+// of the 256 columns of B per k-block (32 KiB per stage instead of 48 KiB for
+// the same work per SM), so six stages fit and the operand feed, which bounds
+// short-K problems, needs two thirds of the bytes per flop.
+//   * both CTAs' producers load their halves with cta_group::2 TMA loads that
+//     complete on the leader's (rank 0) full barrier; only the leader's
+//     producer arms it (expect_tx of both halves);
+//   * the leader's MMA warp issues the MMAs (D rows 0-127 land in its TMEM,
+//     rows 128-255 in the peer's) and commits each stage to both CTAs' empty
+//     barriers and each finished tile to both CTAs' tfull barriers;
+//   * each CTA drains its own TMEM rows; its epilogue warps release the
+//     accumulator with remote arrivals on the leader's tempty barrier;
+//   * cluster barriers order barrier initialisation and the final TMEM free.
+// No load is multicast.  Every wait is bounded as in k_gemm_tc; after an
+// abort each CTA waits a bounded time before tearing down so that copies in
+// flight (they complete on the leader's barrier) have landed.
+// ---------------------------------------------------------------------------
+constexpr int P_BK = 64;
+constexpr int P_STAGES = 6;
+constexpr int P_A_TILE = 128 * P_BK * 2;              // this CTA's 128 rows of A
+constexpr int P_B_BOX = P_BK * 128;                   // 64 columns x 64 k of B
+constexpr int P_B_TILE = 2 * P_B_BOX;                 // this CTA's 128 columns of B
+constexpr int P_STAGE = P_A_TILE + P_B_TILE;          // 32 KiB
+constexpr int P_BN = 256;                             // tile columns (both CTAs)
+constexpr int P_TMEM_COLS = 2 * P_BN;
+constexpr size_t P_SMEM = size_t(P_STAGES) * P_STAGE + C_STAGE_BYTES + 1024 + 256;
+static_assert(P_SMEM <= 232448, "shared memory budget of the two-SM kernel");
+constexpr uint32_t P_IDESC = (1u << 4) | (0u << 7) | (0u << 10) | (1u << 16) | (uint32_t(P_BN >> 3) << 17) |
+                             (uint32_t(256 >> 4) << 24);  // f16 x f16 -> f32, B MN-major, N=256, M=256
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
+    return out;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t cluster_bar, int c0,
+                                                 int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(cluster_bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(P_IDESC), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on the barrier at this shared-memory offset in both CTAs of the pair
+// once the MMAs issued so far have completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"(static_cast<uint16_t>(0x3))
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_pair_local(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+template <bool OUT_F16>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    k_gemm_tc2(const __grid_constant__ OperandMaps ops, const __grid_constant__ CUtensorMap tmC, int M, int N, int K,
+               TileMap tm, int a_batched, int b_batched, int* status) {
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* gbase = smem_raw + (base - raw);
+    auto a_tile = [&](int s) { return base + s * P_STAGE; };
+    auto b_tile = [&](int s) { return base + s * P_STAGE + P_A_TILE; };
+    const uint32_t sC_stage = base + P_STAGES * P_STAGE;
+    const uint32_t bars = sC_stage + C_STAGE_BYTES;
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (P_STAGES + s); };
+    auto tfull_bar = [&](int a) { return bars + 8u * (2 * P_STAGES + a); };
+    auto tempty_bar = [&](int a) { return bars + 8u * (2 * P_STAGES + 2 + a); };
+    const uint32_t drain_bar = bars + 8u * (2 * P_STAGES + 4);
+    unsigned char* gmisc = gbase + P_STAGES * P_STAGE + C_STAGE_BYTES + 8 * (2 * P_STAGES + 5);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gmisc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gmisc + 4);
+
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; ++s) {
+            mbar_init(full_bar(s), 1);   // the leader's producer arms it
+            mbar_init(empty_bar(s), 1);  // one commit per consumed stage
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 8);  // 4 epilogue warps in each CTA
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(P_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int total = tm.tiles_m * tm.tiles_n * tm.batch;
+    const int nclusters = static_cast<int>(gridDim.x >> 1);
+    const int cid = static_cast<int>(blockIdx.x >> 1);
+    const int num_kb = (K + P_BK - 1) / P_BK;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- producer (both CTAs): this CTA's halves of A and B ----
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int t = cid; t < total && ok; t += nclusters) {
+                int b, mt, nt;
+                tm.decode(t, b, mt, nt);
+                const int ab = a_batched ? b : 0, bb = b_batched ? b : 0;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_expect_tx(full_bar(stage), 2 * P_STAGE);
+                    const uint32_t lbar = map_to_rank(full_bar(stage), 0);
+                    tma_load_3d_pair(a_tile(stage), &ops.a[0], lbar, kb * P_BK, mt * 256 + static_cast<int>(rank) * 128,
+                                     ab);
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        tma_load_3d_pair(b_tile(stage) + j * P_B_BOX, &ops.b[0], lbar,
+                                         nt * P_BN + static_cast<int>(rank) * 128 + j * 64, kb * P_BK, bb);
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ---- MMA issuer (leader only) ----
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = cid; t < total && ok; t += nclusters) {
+                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * P_BN);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int k = 0; k < P_BK / 16; ++k) {
+                        const uint32_t acc_in = (kb > 0 || k > 0) ? 1u : 0u;
+                        mma_pair(d_tmem, smem_desc(a_tile(stage) + k * 32, 16, 1024),
+                                 smem_desc(b_tile(stage) + k * 16 * 128, P_B_BOX, 1024), acc_in);
+                    }
+                    mma_commit_pair(empty_bar(stage));  // the stage is free in both CTAs
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                mma_commit_pair(tfull_bar(acc));  // both halves of the accumulator are ready
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            mma_commit_pair_local(drain_bar);
+            const long long t0 = clock64();
+            while (!mbar_test(drain_bar, 0) && clock64() - t0 < WAIT_CYCLES) {
+            }
+        }
+    } else {
+        // ---- epilogue (both CTAs): this CTA's 128 rows of the tile ----
+        const int quarter = warp & 3;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        const uint32_t tempty_leader0 = map_to_rank(tempty_bar(0), 0);
+        const uint32_t tempty_leader1 = map_to_rank(tempty_bar(1), 0);
+        for (int t = cid; t < total; t += nclusters) {
+            int ready = 0;
+            if (lane == 0) ready = mbar_wait(tfull_bar(acc), acc_phase, abort_flag) ? 1 : 0;
+            ready = __shfl_sync(0xffffffffu, ready, 0);
+            if (!ready) break;
+            tc_fence_after();
+            int b, mt, nt;
+            tm.decode(t, b, mt, nt);
+            const int row0 = mt * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+            const uint32_t taddr =
+                tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * P_BN);
+            constexpr int CHUNK_COLS = OUT_F16 ? 64 : 32;
+            for (int c0 = 0; c0 < P_BN; c0 += CHUNK_COLS) {
+                if (nt * P_BN + c0 >= N) break;
+                uint32_t words[32];
+                if (OUT_F16) {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(taddr + c0, r0);
+                    tmem_ld32(taddr + c0 + 32, r1);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        __half2 h = __floats2half2_rn(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+                        words[i] = *reinterpret_cast<uint32_t*>(&h);
+                        __half2 g = __floats2half2_rn(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+                        words[16 + i] = *reinterpret_cast<uint32_t*>(&g);
+                    }
+                } else {
+                    tmem_ld32(taddr + c0, words);
+                }
+                const int buf = (c0 / CHUNK_COLS) & 1;
+                const uint32_t stage = sC_stage + static_cast<uint32_t>((quarter * 2 + buf) * C_BOX_BYTES);
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t a = stage + lane * 128 + ((j ^ (lane & 7)) << 4);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(words[4 * j]),
+                                 "r"(words[4 * j + 1]), "r"(words[4 * j + 2]), "r"(words[4 * j + 3])
+                                 : "memory");
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                const int col = nt * P_BN + c0;
+                if (lane == 0 && row0 < M && col < N) {
+                    asm volatile(
+                        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                        ::"l"(reinterpret_cast<uint64_t>(&tmC)), "r"(col), "r"(row0), "r"(b), "r"(stage)
+                        : "memory");
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(acc == 0 ? tempty_leader0 : tempty_leader1);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag) {
+        if (threadIdx.x == 0) atomicExch(status, QSML_E_TIMEOUT);
+        // copies still in flight complete on the leader's barrier: give them
+        // time to land before the CTA pair's shared memory is released
+        const long long t0 = clock64();
+        while (clock64() - t0 < 20000000LL) {
+        }
+    }
+    cluster_sync();  // the leader's MMAs are drained and both epilogues are done
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(P_TMEM_COLS)
+                     : "memory");
+    }
+}
+
 // fp32 -> (hi, lo) for 3xTF32: hi is x rounded to tf32 (cvt.rna, low 13 bits
 // zero), lo = x - hi exactly, itself rounded to tf32 (its own error is below
 // 2^-22 |x|).
@@ -573,6 +874,85 @@ qsml_status_t launch_tc(Context* ctx, const MatmulArgs& g, const Operands& o) {
     return after_launch(ctx, Cfg::TF32 ? "k_gemm_tc<3xtf32>" : "k_gemm_tc<f16>");
 }
 
+// The two-SM kernel: same operand and output maps as CfgF16 (A boxes of 128
+// rows x 64 k, B boxes of 64 columns x 64 k), 256 x 256 tiles, one cluster of
+// two CTAs per SM pair.
+template <bool OUT_F16>
+qsml_status_t launch_tc2(Context* ctx, const MatmulArgs& g, const Operands& o) {
+    const uint64_t a_batch = o.sA ? static_cast<uint64_t>(g.batch) : 1;
+    const uint64_t b_batch = o.sB ? static_cast<uint64_t>(g.batch) : 1;
+    OperandMaps maps;
+    if (!make_map(&maps.a[0], o.a[0], g.K, g.M, a_batch, o.lda * 2, (o.sA ? o.sA : o.lda * g.M) * 2, 64, 128,
+                  CU_TENSOR_MAP_DATA_TYPE_FLOAT16) ||
+        !make_map(&maps.b[0], o.b[0], g.N, g.K, b_batch, o.ldb * 2, (o.sB ? o.sB : o.ldb * g.K) * 2, 64, P_BK,
+                  CU_TENSOR_MAP_DATA_TYPE_FLOAT16))
+        return QSML_E_UNSUPPORTED;
+    maps.a[1] = maps.a[0];
+    maps.b[1] = maps.b[0];
+    CUtensorMap tmC;
+    const uint64_t c_es = OUT_F16 ? 2 : 4;
+    if (!make_map(&tmC, g.C, g.N, g.M, g.batch, g.N * c_es, g.M * g.N * c_es, static_cast<uint32_t>(128 / c_es), 32,
+                  OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
+        return QSML_E_UNSUPPORTED;
+
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = P_SMEM;
+    cfg.stream = ctx->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+
+    // Shared-memory opt-in and the number of co-resident clusters, once per device.
+    static std::mutex mu;
+    static int max_clusters[64] = {};
+    int clusters = 0;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        int& mc = max_clusters[ctx->device & 63];
+        if (mc == 0) {
+            cudaError_t e = cudaFuncSetAttribute(k_gemm_tc2<OUT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(P_SMEM));
+            if (e != cudaSuccess) return check_cuda(ctx, e, "matmul: shared-memory attribute");
+            cfg.gridDim = dim3(2 * (ctx->num_sms / 2));
+            e = cudaOccupancyMaxActiveClusters(&mc, k_gemm_tc2<OUT_F16>, &cfg);
+            if (e != cudaSuccess || mc <= 0) {
+                cudaGetLastError();
+                mc = -1;  // no cluster of two fits: the one-SM kernel serves this device
+            }
+        }
+        clusters = mc;
+    }
+    if (clusters < 0) return QSML_E_UNSUPPORTED;
+    TileMap tm;
+    tm.tiles_m = static_cast<int>((g.M + 255) / 256);
+    tm.tiles_n = static_cast<int>((g.N + P_BN - 1) / P_BN);
+    tm.batch = static_cast<int>(g.batch);
+    const int64_t total = static_cast<int64_t>(tm.tiles_m) * tm.tiles_n * tm.batch;
+    if (total < clusters) clusters = static_cast<int>(total);
+    cfg.gridDim = dim3(2 * clusters);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc2<OUT_F16>, maps, tmC, static_cast<int>(g.M),
+                                       static_cast<int>(g.N), static_cast<int>(g.K), tm, o.sA ? 1 : 0, o.sB ? 1 : 0,
+                                       ctx->status);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "k_gemm_tc2<f16>");
+    return after_launch(ctx, "k_gemm_tc2<f16>");
+}
+
+// Which fp16 kernel: QSML_GEMM_2SM=1 forces the two-SM kernel, =0 the one-SM
+// kernel; otherwise the two-SM kernel runs when the 256 x 256 tiles fill the
+// SM pairs at least once.
+bool use_two_sm(const Context* ctx, const MatmulArgs& g) {
+    const char* env = std::getenv("QSML_GEMM_2SM");
+    if (env && env[0] == '0') return false;
+    if (env && env[0] == '1') return true;
+    const int64_t tiles = ((g.M + 255) / 256) * ((g.N + 255) / 256) * g.batch;
+    return tiles >= ctx->num_sms / 2;
+}
+
 // What the kernels take: 16-byte aligned operands and row strides (TMA), N a
 // multiple of 8 (128-byte output boxes stay inside rows of whole 16-byte units).
 bool tc_shape_ok(const MatmulArgs& g, int es) {
@@ -586,6 +966,10 @@ bool tc_shape_ok(const MatmulArgs& g, int es) {
 qsml_status_t matmul_tc_f16(Context* ctx, const MatmulArgs& g, bool out_f16) {
     if (!tc_shape_ok(g, 2) || !ctx->status) return QSML_E_UNSUPPORTED;
     Operands o{{g.A, g.A}, {g.B, g.B}, g.lda, g.ldb, g.sA, g.sB};
+    if (use_two_sm(ctx, g)) {
+        const qsml_status_t st = out_f16 ? launch_tc2<true>(ctx, g, o) : launch_tc2<false>(ctx, g, o);
+        if (st != QSML_E_UNSUPPORTED) return st;
+    }
     return out_f16 ? launch_tc<CfgF16, true>(ctx, g, o) : launch_tc<CfgF16, false>(ctx, g, o);
 }
 
