@@ -2,15 +2,18 @@
 // with the biased (population) variance.  The reference snapshot has no
 // layer norm; this is a new op of the same API family.
 //
-// k_layer_norm_reg: persistent CTAs, one row at a time held in registers
-// (16-byte loads) with the next two rows already in flight, so x is read from HBM
-// exactly once and y written once; gamma/beta stay in shared memory.  Each
-// thread's values give a local (mean, M2); warps merge them with Chan's
-// pairwise update (equal counts, written symmetrically so partner lanes hold
-// identical bits), then the warps' results merge the same way.
+// k_layer_norm_pipe: rows of 2-8 KiB, one warp per row, rows streamed through
+// shared memory by bulk copies (row_pipe.cuh); x is read from HBM once and y
+// written once.
+// k_layer_norm_reg: wider rows, persistent CTAs, one row at a time held in
+// registers (16-byte loads) with the next two rows already in flight, so x is
+// read once and y written once; gamma/beta stay in shared memory.  The row
+// statistics are two block sums (row sum, then squared deviations from the
+// mean), so the variance is a true two-pass variance.
 // k_layer_norm_generic: any width or alignment, Welford over global memory
 // (reads x twice).
 #include "qsml_internal.cuh"
+#include "row_pipe.cuh"
 
 namespace qsml {
 namespace {
@@ -25,41 +28,85 @@ __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 __device__ __forceinline__ float from_f_tag(float v, float*) { return v; }
 __device__ __forceinline__ __half from_f_tag(float v, __half*) { return __float2half_rn(v); }
 
-// Merge (mean, m2) statistics of two equal-count halves of n elements each.
-__device__ __forceinline__ void chan_equal(float& mean, float& m2, float mo, float m2o, float n) {
-    float d = __fsub_rn(mo, mean);
-    float dd = __fmul_rn(d, d);  // (a-b)^2 == (b-a)^2 bit for bit
-    mean = __fmul_rn(__fadd_rn(mean, mo), 0.5f);
-    m2 = __fadd_rn(__fadd_rn(m2, m2o), __fmul_rn(dd, __fmul_rn(n, 0.5f)));
+// gamma/beta live in shared memory as binary32 in a split layout: for pack p
+// (columns p*PV .. p*PV+PV-1) and k < PV/4, the float4 of columns
+// p*PV+4k .. +3 sits at float4 index k*packs + p, so lanes reading
+// consecutive packs read consecutive 16-byte words (no bank conflicts for
+// binary16 packs of 8 columns).
+template <int PV>
+__device__ __forceinline__ int param_slot(int p, int k, int packs) {
+    return k * packs + p;
 }
 
-// PV consecutive gamma/beta values as binary32, with 16-byte loads.
+// Columns p*PV .. p*PV+PV-1 of a gamma/beta vector into the split layout.
 template <typename GT, int PV>
-__device__ __forceinline__ void load_params(const GT* p, float* out) {
+__device__ __forceinline__ void load_params(const GT* src, float4* dst, int p, int packs) {
+    const GT* q = src + static_cast<int64_t>(p) * PV;
     if constexpr (sizeof(GT) == 4) {
 #pragma unroll
-        for (int i = 0; i < PV; i += 4) {
-            float4 v = *reinterpret_cast<const float4*>(p + i);
-            out[i] = v.x; out[i + 1] = v.y; out[i + 2] = v.z; out[i + 3] = v.w;
-        }
+        for (int k = 0; k < PV / 4; ++k)
+            dst[param_slot<PV>(p, k, packs)] = *reinterpret_cast<const float4*>(q + 4 * k);
     } else {
 #pragma unroll
-        for (int i = 0; i < PV; i += 8) {
-            Pack<__half> v = *reinterpret_cast<const Pack<__half>*>(p + i);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) out[i + e] = __half2float(v.v[e]);
+        for (int k = 0; k < PV / 4; ++k) {
+            float4 f;
+            f.x = __half2float(q[4 * k]);
+            f.y = __half2float(q[4 * k + 1]);
+            f.z = __half2float(q[4 * k + 2]);
+            f.w = __half2float(q[4 * k + 3]);
+            dst[param_slot<PV>(p, k, packs)] = f;
         }
     }
 }
 
-// Persistent CTAs; the next two rows' x are loaded before the current row is
-// reduced, so each CTA always has a row in flight.  gamma/beta (as binary32)
-// sit in dynamic shared memory, each thread holding exactly the columns it
-// reads, so they need no barrier and no registers.  Per-warp statistics go to
-// slots double-buffered by row parity; after one barrier every warp merges
-// all slots itself (identical bits in every warp), so a row costs one
-// barrier: row r+2 rewrites row r's slots only after every thread has passed
-// row r+1's barrier, i.e. after it read row r's slots.
+// Binary32 values to a pack (binary16: two at a time).
+template <typename T>
+__device__ __forceinline__ Pack<T> to_pack(const float* z) {
+    Pack<T> o;
+    if constexpr (sizeof(T) == 4) {
+#pragma unroll
+        for (int e = 0; e < Pack<T>::N; ++e) o.v[e] = z[e];
+    } else {
+#pragma unroll
+        for (int e = 0; e < Pack<T>::N; e += 2) {
+            const __half2 h = __floats2half2_rn(z[e], z[e + 1]);
+            o.v[e] = __low2half(h);
+            o.v[e + 1] = __high2half(h);
+        }
+    }
+    return o;
+}
+
+// Block-wide binary32 sum: xor butterflies inside warps, one slot per warp,
+// one barrier, then every thread adds the slots in a fixed order (a butterfly
+// over the slots when the warp count is a power of two), so every thread
+// holds the same bits.
+__device__ __forceinline__ float block_sum(float v, float* slot) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+    if (lane == 0) slot[w] = v;
+    __syncthreads();
+    if ((nw & (nw - 1)) == 0) {
+        float a = slot[lane & (nw - 1)];
+        for (int m = 1; m < nw; m <<= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, m));
+        return a;
+    }
+    float a = slot[0];
+    for (int j = 1; j < nw; ++j) a = __fadd_rn(a, slot[j]);
+    return a;
+}
+
+// Persistent CTAs, one row at a time held in registers (16-byte loads) with
+// the next two rows in flight; the loop body is unrolled three times so the
+// three row buffers change roles without register copies.  gamma/beta (as
+// binary32) sit in dynamic shared memory, each thread holding exactly the
+// columns it reads.  Statistics are two block sums per row: the row sum
+// (mean = sum * (1/n)), then the sum of squared deviations from that mean
+// (var = sum * (1/n)); rstd = rsqrtf(var + eps).  Each sum has its own slots:
+// a thread rewrites the sum slots of the next row only after passing this
+// row's second barrier, which every thread reaches after reading them, and
+// the deviation slots only after the next row's first barrier, likewise.
 template <typename T, typename GT, int NV>
 __global__ void __launch_bounds__(256) k_layer_norm_reg(const T* __restrict__ x, const GT* __restrict__ gamma,
                                                         const GT* __restrict__ beta, T* __restrict__ y,
@@ -67,121 +114,153 @@ __global__ void __launch_bounds__(256) k_layer_norm_reg(const T* __restrict__ x,
     constexpr int PV = Pack<T>::N;
     constexpr int E = NV * PV;  // elements per thread
     extern __shared__ float4 ln_smem[];
-    float* sg = reinterpret_cast<float*>(ln_smem);
-    float* sb = sg + cols;
-    __shared__ float s_mean[2][8], s_m2[2][8];
-    const int t = threadIdx.x, lane = t & 31, w = t >> 5, nw = blockDim.x >> 5;
-    const int th = blockDim.x;
-    const bool pow2 = (nw & (nw - 1)) == 0;
+    const int packs = cols / PV;
+    float4* sg = ln_smem;
+    float4* sb = ln_smem + cols / 4;
+    __shared__ float s_sum[8], s_dev[8];
+    const int t = threadIdx.x, th = blockDim.x;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-        const int c0 = (t + i * th) * PV;
-        load_params<GT, PV>(gamma + c0, sg + c0);
-        load_params<GT, PV>(beta + c0, sb + c0);
+        load_params<GT, PV>(gamma, sg, t + i * th, packs);
+        load_params<GT, PV>(beta, sb, t + i * th, packs);
     }
-    // Two rows in flight beyond the one being reduced (cur <- nxt <- nxt2).
-    Pack<T> cur[NV], nxt[NV], nxt2[NV];
-    int64_t row = blockIdx.x;
-    if (row < rows) {
-        const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + row * cols);
+    const float inv_n = __frcp_rn(static_cast<float>(cols));
+    auto load_row = [&](Pack<T>(&buf)[NV], int64_t r) {
+        if (r < rows) {
+            const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + r * cols);
 #pragma unroll
-        for (int i = 0; i < NV; ++i) cur[i] = xr[t + i * th];
-    }
-    if (row + gridDim.x < rows) {
-        const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + (row + gridDim.x) * cols);
-#pragma unroll
-        for (int i = 0; i < NV; ++i) nxt[i] = xr[t + i * th];
-    }
-    for (int parity = 0; row < rows; row += gridDim.x, parity ^= 1) {
-        const int64_t nrow = row + 2 * static_cast<int64_t>(gridDim.x);
-        if (nrow < rows) {
-            const Pack<T>* xn = reinterpret_cast<const Pack<T>*>(x + nrow * cols);
-#pragma unroll
-            for (int i = 0; i < NV; ++i) nxt2[i] = xn[t + i * th];
+            for (int i = 0; i < NV; ++i) buf[i] = xr[t + i * th];
         }
+    };
+    auto process = [&](const Pack<T>(&buf)[NV], int64_t r) {
         float v[E];
 #pragma unroll
         for (int i = 0; i < NV; ++i)
 #pragma unroll
-            for (int e = 0; e < PV; ++e) v[i * PV + e] = to_f(cur[i].v[e]);
-        // Thread-local statistics (two passes over registers; E is a power
-        // of two, so the multiply by 1/E is exact).
-        float s = 0.0f;
+            for (int e = 0; e < PV; ++e) v[i * PV + e] = to_f(buf[i].v[e]);
+        float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
-        for (int i = 0; i < E; ++i) s = __fadd_rn(s, v[i]);
-        float mean = __fmul_rn(s, 1.0f / static_cast<float>(E));
-        float m2 = 0.0f;
+        for (int i = 0; i < E; i += 2) {
+            s0 = __fadd_rn(s0, v[i]);
+            s1 = __fadd_rn(s1, v[i + 1]);
+        }
+        const float mean = __fmul_rn(block_sum(__fadd_rn(s0, s1), s_sum), inv_n);
+        float q0 = 0.0f, q1 = 0.0f;
 #pragma unroll
-        for (int i = 0; i < E; ++i) {
-            float d = __fsub_rn(v[i], mean);
-            m2 = __fmaf_rn(d, d, m2);
+        for (int i = 0; i < E; i += 2) {
+            const float d0 = __fsub_rn(v[i], mean), d1 = __fsub_rn(v[i + 1], mean);
+            q0 = __fmaf_rn(d0, d0, q0);
+            q1 = __fmaf_rn(d1, d1, q1);
         }
-        // Warp: butterfly merge, counts double each step.
-        float n = static_cast<float>(E);
-#pragma unroll
-        for (int m = 1; m < 32; m <<= 1) {
-            float mo = __shfl_xor_sync(0xffffffffu, mean, m);
-            float m2o = __shfl_xor_sync(0xffffffffu, m2, m);
-            chan_equal(mean, m2, mo, m2o, n);
-            n = __fmul_rn(n, 2.0f);
-        }
-        if (lane == 0) {
-            s_mean[parity][w] = mean;
-            s_m2[parity][w] = m2;
-        }
-        __syncthreads();
-        // Every warp merges the nw warp results the same way.
-        float gm = lane < nw ? s_mean[parity][lane] : 0.0f, gm2 = lane < nw ? s_m2[parity][lane] : 0.0f;
-        if (pow2) {
-            // equal counts again: butterfly inside aligned groups of nw lanes
-            float gn = n;
-            for (int m = 1; m < nw; m <<= 1) {
-                float mo = __shfl_xor_sync(0xffffffffu, gm, m);
-                float m2o = __shfl_xor_sync(0xffffffffu, gm2, m);
-                chan_equal(gm, gm2, mo, m2o, gn);
-                gn = __fmul_rn(gn, 2.0f);
-            }
-        } else if (lane == 0) {
-            float gn = n;
-            for (int j = 1; j < nw; ++j) {
-                float tot = __fadd_rn(gn, n);
-                float d = __fsub_rn(s_mean[parity][j], gm);
-                gm = __fadd_rn(gm, __fmul_rn(d, __fdiv_rn(n, tot)));
-                gm2 = __fadd_rn(__fadd_rn(gm2, s_m2[parity][j]),
-                                __fmul_rn(__fmul_rn(d, d), __fdiv_rn(__fmul_rn(gn, n), tot)));
-                gn = tot;
-            }
-        }
-        gm = __shfl_sync(0xffffffffu, gm, 0);
-        gm2 = __shfl_sync(0xffffffffu, gm2, 0);
-        const float var = __fdiv_rn(gm2, static_cast<float>(cols));
-        const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-        Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
+        const float var = __fmul_rn(block_sum(__fadd_rn(q0, q1), s_dev), inv_n);
+        const float rstd = rsqrtf(__fadd_rn(var, eps));
+        Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + r * cols);
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
-            const int c0 = (t + i * th) * PV;
-            float g[PV], b[PV];
+            const int p = t + i * th;
+            float z[PV];
 #pragma unroll
             for (int e = 0; e < PV; e += 4) {
-                const float4 gv = *reinterpret_cast<const float4*>(sg + c0 + e);
-                const float4 bv = *reinterpret_cast<const float4*>(sb + c0 + e);
-                g[e] = gv.x; g[e + 1] = gv.y; g[e + 2] = gv.z; g[e + 3] = gv.w;
-                b[e] = bv.x; b[e + 1] = bv.y; b[e + 2] = bv.z; b[e + 3] = bv.w;
-            }
-            Pack<T> o;
+                const float4 gv = sg[param_slot<PV>(p, e / 4, packs)];
+                const float4 bv = sb[param_slot<PV>(p, e / 4, packs)];
+                const float g[4] = {gv.x, gv.y, gv.z, gv.w}, b[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-            for (int e = 0; e < PV; ++e) {
-                float z = __fmul_rn(__fsub_rn(v[i * PV + e], gm), rstd);
-                o.v[e] = from_f_tag(__fmaf_rn(z, g[e], b[e]), static_cast<T*>(nullptr));
+                for (int k = 0; k < 4; ++k)
+                    z[e + k] = __fmaf_rn(__fmul_rn(__fsub_rn(v[i * PV + e + k], mean), rstd), g[k], b[k]);
             }
-            yr[t + i * th] = o;
+            yr[t + i * th] = to_pack<T>(z);
         }
-#pragma unroll
-        for (int i = 0; i < NV; ++i) {
-            cur[i] = nxt[i];
-            nxt[i] = nxt2[i];
-        }
+    };
+    const int64_t G = gridDim.x;
+    Pack<T> A[NV], B[NV], C[NV];
+    int64_t row = blockIdx.x;
+    load_row(A, row);
+    load_row(B, row + G);
+    while (row < rows) {
+        load_row(C, row + 2 * G);
+        process(A, row);
+        if ((row += G) >= rows) break;
+        load_row(A, row + 2 * G);
+        process(B, row);
+        if ((row += G) >= rows) break;
+        load_row(B, row + 2 * G);
+        process(C, row);
+        row += G;
     }
+}
+
+// Rows streamed through shared memory (row_pipe.cuh), one warp per row:
+// gamma/beta as binary32 in front of the row buffers; per row three passes
+// over the buffer -- the sum (PV interleaved partial sums per lane, then the
+// warp), the squared deviations from the mean the same way, and the output.
+template <typename T, typename GT>
+__global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
+    k_layer_norm_pipe(const T* __restrict__ x, const GT* __restrict__ gamma, const GT* __restrict__ beta,
+                      T* __restrict__ y, int64_t rows, int cols, float eps, int slots, int* status) {
+    constexpr int PV = Pack<T>::N;
+    extern __shared__ float4 ln_pipe_smem[];
+    __shared__ uint64_t bars[rowpipe::kMaxWarps * rowpipe::kMaxSlots];
+    const int packs = cols / PV, lane = threadIdx.x & 31;
+    float4* sg = ln_pipe_smem;
+    float4* sb = ln_pipe_smem + cols / 4;
+    unsigned char* ring = reinterpret_cast<unsigned char*>(sb + cols / 4);
+    for (int p = threadIdx.x; p < packs; p += blockDim.x) {
+        load_params<GT, PV>(gamma, sg, p, packs);
+        load_params<GT, PV>(beta, sb, p, packs);
+    }
+    __syncthreads();
+    const float n = static_cast<float>(cols);
+    const bool ok = rowpipe::stream_rows(
+        reinterpret_cast<const unsigned char*>(x), rows, static_cast<uint32_t>(cols * sizeof(T)), slots, ring, bars,
+        [&](int64_t row, unsigned char* buf) {
+            const Pack<T>* xs = reinterpret_cast<const Pack<T>*>(buf);
+            float part[PV];
+#pragma unroll
+            for (int e = 0; e < PV; ++e) part[e] = 0.0f;
+#pragma unroll 4
+            for (int p = lane; p < packs; p += 32) {
+                const Pack<T> v = xs[p];
+#pragma unroll
+                for (int e = 0; e < PV; ++e) part[e] = __fadd_rn(part[e], to_f(v.v[e]));
+            }
+            float s = part[0];
+#pragma unroll
+            for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
+            const float mean = __fdiv_rn(rowpipe::warp_sum(s), n);
+#pragma unroll
+            for (int e = 0; e < PV; ++e) part[e] = 0.0f;
+#pragma unroll 4
+            for (int p = lane; p < packs; p += 32) {
+                const Pack<T> v = xs[p];
+#pragma unroll
+                for (int e = 0; e < PV; ++e) {
+                    const float d = __fsub_rn(to_f(v.v[e]), mean);
+                    part[e] = __fmaf_rn(d, d, part[e]);
+                }
+            }
+            float q = part[0];
+#pragma unroll
+            for (int e = 1; e < PV; ++e) q = __fadd_rn(q, part[e]);
+            const float var = __fdiv_rn(rowpipe::warp_sum(q), n);
+            const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+            Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
+#pragma unroll 2
+            for (int p = lane; p < packs; p += 32) {
+                const Pack<T> v = xs[p];
+                float z[PV];
+#pragma unroll
+                for (int e = 0; e < PV; e += 4) {
+                    const float4 gv = sg[param_slot<PV>(p, e / 4, packs)];
+                    const float4 bv = sb[param_slot<PV>(p, e / 4, packs)];
+                    const float g[4] = {gv.x, gv.y, gv.z, gv.w}, b[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        z[e + k] = __fmaf_rn(__fmul_rn(__fsub_rn(to_f(v.v[e + k]), mean), rstd), g[k], b[k]);
+                }
+                yr[p] = to_pack<T>(z);
+            }
+        });
+    if (!ok && lane == 0) atomicExch(status, QSML_E_TIMEOUT);
 }
 
 template <typename T, typename GT>
@@ -279,8 +358,33 @@ qsml_status_t launch_reg(Context* ctx, const T* x, const GT* g, const GT* b, T* 
 }
 
 template <typename T, typename GT>
+qsml_status_t launch_pipe(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int cols, float eps,
+                          const rowpipe::Plan& p) {
+    static std::mutex mu;
+    static size_t attr_set = 0;  // largest dynamic shared memory opted in so far
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (p.smem > 48 * 1024 && p.smem > attr_set) {
+            QSML_TRY_STATUS(check_cuda(ctx,
+                                       cudaFuncSetAttribute(k_layer_norm_pipe<T, GT>,
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                            static_cast<int>(p.smem)),
+                                       "layer norm: shared-memory attribute"));
+            attr_set = p.smem;
+        }
+    }
+    k_layer_norm_pipe<T, GT><<<p.grid, p.warps * 32, p.smem, ctx->stream>>>(x, g, b, y, rows, cols, eps, p.slots,
+                                                                          ctx->status);
+    return after_launch(ctx, "k_layer_norm_pipe");
+}
+
+template <typename T, typename GT>
 qsml_status_t run_ln(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int64_t cols, float eps) {
     constexpr int PV = Pack<T>::N;
+    rowpipe::Plan plan;
+    if (rowpipe::use_pipe(cols * sizeof(T), sizeof(T)) && aligned16(x) && aligned16(y) && ctx->status && cols <= INT32_MAX &&
+        rowpipe::plan(ctx, rows, static_cast<uint64_t>(cols) * sizeof(T), static_cast<size_t>(cols) * 8, &plan))
+        return launch_pipe<T, GT>(ctx, x, g, b, y, rows, static_cast<int>(cols), eps, plan);
     if (cols % PV == 0 && aligned16(x) && aligned16(y) && aligned16(g) && aligned16(b) && cols <= INT32_MAX) {
         const int64_t packs = cols / PV;
         int nv = 0;

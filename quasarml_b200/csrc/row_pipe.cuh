@@ -1,0 +1,171 @@
+// Warp-per-row streaming through shared memory, for row-wise ops whose rows
+// are a few KiB to a few tens of KiB (layer norm, softmax over the last axis).
+//
+// Each warp owns `slots` row buffers in dynamic shared memory and one
+// mbarrier per buffer.  Lane 0 fills a buffer with one bulk copy
+// (cp.async.bulk, completion counted in bytes on the buffer's mbarrier); the
+// warp waits for it, runs the op on the row from shared memory, and refills
+// the buffer with the warp's next-but-(slots-1) row.  The bytes in flight per
+// SM are set by shared memory (one CTA per SM, up to ~220 KiB of rows), not by
+// registers, and no barrier couples the warps: each row is reduced with warp
+// shuffles only.
+//
+// Waits are bounded: a copy that has not landed after kWaitCycles makes the
+// warp stop, wait (bounded again) for its other copies in flight and report
+// failure; the kernel then records QSML_E_TIMEOUT in the context status word.
+#pragma once
+
+#include "qsml_internal.cuh"
+
+namespace qsml {
+namespace rowpipe {
+
+constexpr int kMaxWarps = 16;
+constexpr int kMaxSlots = 4;
+constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 2 GHz
+constexpr size_t kRingBudget = 220 * 1024;       // dynamic shared memory per CTA
+constexpr uint32_t kMinRowBytes = 2048;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool bar_test(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+    if (bar_test(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!bar_test(bar, parity))
+        if (clock64() - t0 > kWaitCycles) return false;
+    return true;
+}
+
+// One bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// into shared memory, counted on `bar`.  Called by one lane.
+__device__ __forceinline__ void fill(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+// xor butterflies: every lane ends with the same bits
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+
+// Streams this warp's rows (warp g of G in the grid takes rows g, g + G, ...)
+// through its buffers, calling body(row, buffer) with the whole warp.  `ring`
+// is the CTA's row area (warp w's buffer s at (w * slots + s) * row_bytes) and
+// `bars` the CTA's kMaxWarps * kMaxSlots mbarriers.  Returns false if a copy
+// did not land in time.
+template <class Body>
+__device__ bool stream_rows(const unsigned char* src, int64_t rows, uint32_t row_bytes, int slots,
+                            unsigned char* ring, uint64_t* bars, Body&& body) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
+    unsigned char* mine = ring + static_cast<size_t>(warp) * slots * row_bytes;
+    const uint32_t bar0 = smem_addr(bars + warp * kMaxSlots);
+    if (lane == 0) {
+        for (int s = 0; s < slots; ++s)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8u * s) : "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int s = 0; s < slots; ++s) {
+            const int64_t r = first + s * nwarps;
+            if (r < rows) fill(smem_addr(mine + s * row_bytes), src + r * row_bytes, row_bytes, bar0 + 8u * s);
+        }
+    }
+    __syncwarp();
+    bool ok = true;
+    int64_t i = 0;
+    for (int64_t row = first; row < rows; row += nwarps, ++i) {
+        const int s = static_cast<int>(i % slots);
+        const uint32_t parity = static_cast<uint32_t>((i / slots) & 1);
+        int landed = 0;
+        if (lane == 0) landed = bar_wait(bar0 + 8u * s, parity) ? 1 : 0;
+        landed = __shfl_sync(0xffffffffu, landed, 0);
+        if (!landed) {
+            ok = false;
+            // copies already issued into the other buffers land before the CTA exits
+            if (lane == 0)
+                for (int k = 1; k < slots; ++k) {
+                    const int64_t j = i + k;
+                    if (first + j * nwarps >= rows) break;
+                    const int sk = static_cast<int>(j % slots);
+                    const long long t0 = clock64();
+                    while (!bar_test(bar0 + 8u * sk, static_cast<uint32_t>((j / slots) & 1)) &&
+                           clock64() - t0 < kWaitCycles) {
+                    }
+                }
+            __syncwarp();
+            break;
+        }
+        unsigned char* buf = mine + s * row_bytes;
+        body(row, buf);
+        __syncwarp();  // every lane is done with the buffer
+        const int64_t next = row + static_cast<int64_t>(slots) * nwarps;
+        if (lane == 0 && next < rows) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            fill(smem_addr(buf), src + next * row_bytes, row_bytes, bar0 + 8u * s);
+        }
+    }
+    return ok;
+}
+
+// Which rows go through the pipeline (measured on B200 with 16K-64K rows):
+// binary16 rows of 2-8 KiB and binary32 rows of 2-4 KiB.  Wider rows leave too
+// few warps per SM (one warp reduces a whole row), and binary32 rows of 8 KiB
+// already reach ~0.95 of the copy bandwidth as one CTA per row.
+inline bool use_pipe(uint64_t row_bytes, uint32_t elem_bytes) {
+    const uint64_t max_bytes = elem_bytes == 2 ? 8192 : 4096;
+    return row_bytes >= kMinRowBytes && row_bytes <= max_bytes;
+}
+
+// Launch shape: one CTA per SM, `warps` warps with `slots` buffers each, the
+// op's per-CTA parameters (`param_bytes`, e.g. gamma and beta) in front of
+// the buffers.
+struct Plan {
+    int warps = 0, slots = 0;
+    size_t smem = 0;
+    unsigned grid = 0;
+};
+
+// Rows of `row_bytes` (16-byte multiple, at least kMinRowBytes) with every
+// row start 16-byte aligned; false if the op should use another kernel.
+inline bool plan(const Context* ctx, int64_t rows, uint64_t row_bytes, size_t param_bytes, Plan* p) {
+    if (rows <= 0 || row_bytes < kMinRowBytes || row_bytes % 16 || param_bytes % 16) return false;
+    if (param_bytes + 2 * row_bytes > kRingBudget) return false;
+    const size_t nbuf = (kRingBudget - param_bytes) / row_bytes;
+    // two buffers per warp (one row reduced, one in flight): more warps per
+    // SM measured faster than deeper per-warp rings
+    const int slots = 2;
+    int warps = static_cast<int>(nbuf / slots);
+    if (warps > kMaxWarps) warps = kMaxWarps;
+    // no more warps in the grid than rows
+    const int64_t per_cta = (rows + ctx->num_sms - 1) / ctx->num_sms;
+    if (warps > per_cta) warps = static_cast<int>(per_cta);
+    if (warps < 1) return false;
+    int64_t grid = (rows + warps - 1) / warps;
+    if (grid > ctx->num_sms) grid = ctx->num_sms;
+    p->warps = warps;
+    p->slots = slots;
+    p->smem = param_bytes + static_cast<size_t>(warps) * slots * row_bytes;
+    p->grid = static_cast<unsigned>(grid);
+    return true;
+}
+
+}  // namespace rowpipe
+}  // namespace qsml

@@ -4,13 +4,17 @@
 // per row with the shader of Elementwise.cpp:98-135: a shared-memory tree for
 // the row max, another for the sum of exp(x - max), then
 // out = exp(x - max) / sum.  Its indexing (offset = row * axis_size) is right
-// for the last axis only.  Here the same arithmetic (max, subtract, expf,
+// for the last axis only.  Here the same arithmetic (max, subtract, exp,
 // binary32 sum; the division as a correctly rounded reciprocal per slice and
 // one multiply per element, within 1.5 ulp of the quotient -- GLSL's `/` is
-// not correctly rounded either) runs over any axis:
-//   * k_softmax_rows -- last axis, row held in registers (16-byte loads):
-//     persistent CTAs with the next two rows in flight, so x is read once and y
-//     written once;
+// not correctly rounded either) runs over any axis.  exp is expf, except in
+// the last-axis row kernels on binary16 rows, which use the hardware base-2
+// exponential (relative error about 2^-22, far below binary16 resolution):
+//   * k_softmax_pipe -- last axis, rows of 2-8 KiB: one warp per row, rows
+//     streamed through shared memory by bulk copies (row_pipe.cuh);
+//   * k_softmax_rows -- last axis, wider rows held in registers (16-byte
+//     loads): persistent CTAs with the next two rows in flight, so x is read
+//     once and y written once;
 //   * k_softmax_rows_generic -- last axis, any width: one CTA per row, three
 //     passes over global memory (max, sum, write);
 //   * k_softmax_long_{max,sum,out} -- last axis, fewer rows than SMs and long
@@ -20,6 +24,7 @@
 // The max is IEEE 754-2019 maximum (a NaN in the row makes the row NaN), and
 // every combine order is fixed by the shape, so results are deterministic.
 #include "qsml_internal.cuh"
+#include "row_pipe.cuh"
 
 namespace qsml {
 namespace {
@@ -62,6 +67,43 @@ __device__ __forceinline__ float block_combine(float v, float* sh) {
     return a;
 }
 
+// exp(x - m) in the last-axis row kernels, given mk = m * log2(e): expf for
+// binary32 rows; for binary16 rows 2^(x*log2(e) - mk), one fma and the
+// hardware base-2 exponential (ex2.approx, relative error about 2^-22; the
+// rounding of mk adds |m| * 2^-24 to the exponent), far below binary16
+// resolution.
+template <typename T>
+__device__ __forceinline__ float row_exp(float x, float m, float mk) {
+    if constexpr (sizeof(T) == 4) {
+        return expf(__fsub_rn(x, m));
+    } else {
+        float r;
+        asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fmaf_rn(x, 1.4426950408889634f, -mk)));
+        return r;
+    }
+}
+
+// Binary32 values to a pack (binary16: two at a time).
+template <typename T>
+__device__ __forceinline__ Pack<T> to_pack(const float* z) {
+    Pack<T> o;
+    if constexpr (sizeof(T) == 4) {
+#pragma unroll
+        for (int e = 0; e < Pack<T>::N; ++e) o.v[e] = z[e];
+    } else {
+#pragma unroll
+        for (int e = 0; e < Pack<T>::N; e += 2) {
+            const __half2 h = __floats2half2_rn(z[e], z[e + 1]);
+            o.v[e] = __low2half(h);
+            o.v[e + 1] = __high2half(h);
+        }
+    }
+    return o;
+}
+
+// Persistent CTAs, one row at a time held in registers with the next two rows
+// in flight; the loop body is unrolled three times so the three row buffers
+// change roles without register copies.
 template <typename T, int NV>
 __global__ void __launch_bounds__(256) k_softmax_rows(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
                                                       int cols) {
@@ -69,57 +111,150 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const T* __restrict__ x, T
     constexpr int E = NV * PV;
     __shared__ float sh_max[8], sh_sum[8];
     const int t = threadIdx.x, th = blockDim.x;
-    // Two rows in flight beyond the one being reduced (cur <- nxt <- nxt2).
-    Pack<T> cur[NV], nxt[NV], nxt2[NV];
-    int64_t row = blockIdx.x;
-    if (row < rows) {
-        const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + row * cols);
+    auto load_row = [&](Pack<T>(&buf)[NV], int64_t r) {
+        if (r < rows) {
+            const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + r * cols);
 #pragma unroll
-        for (int i = 0; i < NV; ++i) cur[i] = xr[t + i * th];
-    }
-    if (row + gridDim.x < rows) {
-        const Pack<T>* xr = reinterpret_cast<const Pack<T>*>(x + (row + gridDim.x) * cols);
-#pragma unroll
-        for (int i = 0; i < NV; ++i) nxt[i] = xr[t + i * th];
-    }
-    for (; row < rows; row += gridDim.x) {
-        const int64_t nrow = row + 2 * static_cast<int64_t>(gridDim.x);
-        if (nrow < rows) {
-            const Pack<T>* xn = reinterpret_cast<const Pack<T>*>(x + nrow * cols);
-#pragma unroll
-            for (int i = 0; i < NV; ++i) nxt2[i] = xn[t + i * th];
+            for (int i = 0; i < NV; ++i) buf[i] = xr[t + i * th];
         }
+    };
+    auto process = [&](const Pack<T>(&buf)[NV], int64_t r) {
         float v[E];
 #pragma unroll
         for (int i = 0; i < NV; ++i)
 #pragma unroll
-            for (int e = 0; e < PV; ++e) v[i * PV + e] = to_f(cur[i].v[e]);
-        float m = -INFINITY;
+            for (int e = 0; e < PV; ++e) v[i * PV + e] = to_f(buf[i].v[e]);
+        float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-        for (int k = 0; k < E; ++k) m = max_nan(m, v[k]);
-        m = block_combine<true>(m, sh_max);
-        float s = 0.0f;
-#pragma unroll
-        for (int k = 0; k < E; ++k) {
-            v[k] = expf(__fsub_rn(v[k], m));
-            s = __fadd_rn(s, v[k]);
+        for (int k = 0; k < E; k += 2) {
+            m0 = max_nan(m0, v[k]);
+            m1 = max_nan(m1, v[k + 1]);
         }
-        s = block_combine<false>(s, sh_sum);
-        const float inv = __frcp_rn(s);
-        Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
+        const float m = block_combine<true>(max_nan(m0, m1), sh_max);
+        float s0 = 0.0f, s1 = 0.0f;
+        const float mk = __fmul_rn(m, 1.4426950408889634f);
+#pragma unroll
+        for (int k = 0; k < E; k += 2) {
+            v[k] = row_exp<T>(v[k], m, mk);
+            v[k + 1] = row_exp<T>(v[k + 1], m, mk);
+            s0 = __fadd_rn(s0, v[k]);
+            s1 = __fadd_rn(s1, v[k + 1]);
+        }
+        const float inv = __frcp_rn(block_combine<false>(__fadd_rn(s0, s1), sh_sum));
+        Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + r * cols);
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
-            Pack<T> o;
+            float z[PV];
 #pragma unroll
-            for (int e = 0; e < PV; ++e) from_f(__fmul_rn(v[i * PV + e], inv), &o.v[e]);
-            yr[t + i * th] = o;
+            for (int e = 0; e < PV; ++e) z[e] = __fmul_rn(v[i * PV + e], inv);
+            yr[t + i * th] = to_pack<T>(z);
         }
-#pragma unroll
-        for (int i = 0; i < NV; ++i) {
-            cur[i] = nxt[i];
-            nxt[i] = nxt2[i];
-        }
+    };
+    const int64_t G = gridDim.x;
+    Pack<T> A[NV], B[NV], C[NV];
+    int64_t row = blockIdx.x;
+    load_row(A, row);
+    load_row(B, row + G);
+    while (row < rows) {
+        load_row(C, row + 2 * G);
+        process(A, row);
+        if ((row += G) >= rows) break;
+        load_row(A, row + 2 * G);
+        process(B, row);
+        if ((row += G) >= rows) break;
+        load_row(B, row + 2 * G);
+        process(C, row);
+        row += G;
     }
+}
+
+// Rows streamed through shared memory (row_pipe.cuh), one warp per row:
+// the max (interleaved partial maxima per lane -- binary16 rows as half2
+// pairs, exact -- then the warp), the sum of exp(x - max) the same way, then
+// the output.  binary32 rows keep exp(x - max) in the buffer between the sum
+// and the output; binary16 rows recompute it (the same function in both
+// passes, so the sum and the outputs agree).
+template <typename T>
+__device__ __forceinline__ float pack_max(const Pack<T>* xs, int packs, int lane) {
+    constexpr int PV = Pack<T>::N;
+    if constexpr (sizeof(T) == 4) {
+        float part[PV];
+#pragma unroll
+        for (int e = 0; e < PV; ++e) part[e] = -INFINITY;
+#pragma unroll 4
+        for (int p = lane; p < packs; p += 32) {
+            const Pack<T> v = xs[p];
+#pragma unroll
+            for (int e = 0; e < PV; ++e) part[e] = max_nan(part[e], v.v[e]);
+        }
+        float m = part[0];
+#pragma unroll
+        for (int e = 1; e < PV; ++e) m = max_nan(m, part[e]);
+        return m;
+    } else {
+        __half2 part[PV / 2];
+#pragma unroll
+        for (int e = 0; e < PV / 2; ++e) part[e] = __float2half2_rn(-INFINITY);
+#pragma unroll 4
+        for (int p = lane; p < packs; p += 32) {
+            const Pack<T> v = xs[p];
+            const __half2* h = reinterpret_cast<const __half2*>(v.v);
+#pragma unroll
+            for (int e = 0; e < PV / 2; ++e) part[e] = __hmax2_nan(part[e], h[e]);
+        }
+#pragma unroll
+        for (int e = 1; e < PV / 2; ++e) part[0] = __hmax2_nan(part[0], part[e]);
+        return max_nan(__low2float(part[0]), __high2float(part[0]));
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
+    k_softmax_pipe(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int cols, int slots, int* status) {
+    constexpr int PV = Pack<T>::N;
+    constexpr bool F32 = sizeof(T) == 4;
+    extern __shared__ float4 sm_pipe_smem[];
+    __shared__ uint64_t bars[rowpipe::kMaxWarps * rowpipe::kMaxSlots];
+    unsigned char* ring = reinterpret_cast<unsigned char*>(sm_pipe_smem);
+    const int packs = cols / PV, lane = threadIdx.x & 31;
+    const bool ok = rowpipe::stream_rows(
+        reinterpret_cast<const unsigned char*>(x), rows, static_cast<uint32_t>(cols * sizeof(T)), slots, ring, bars,
+        [&](int64_t row, unsigned char* buf) {
+            Pack<T>* xs = reinterpret_cast<Pack<T>*>(buf);
+            float m = pack_max<T>(xs, packs, lane);
+#pragma unroll
+            for (int k = 16; k >= 1; k >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, k));
+            const float mk = __fmul_rn(m, 1.4426950408889634f);
+            float part[PV];
+#pragma unroll
+            for (int e = 0; e < PV; ++e) part[e] = 0.0f;
+#pragma unroll 4
+            for (int p = lane; p < packs; p += 32) {
+                Pack<T> v = xs[p];
+#pragma unroll
+                for (int e = 0; e < PV; ++e) {
+                    const float ex = row_exp<T>(to_f(v.v[e]), m, mk);
+                    part[e] = __fadd_rn(part[e], ex);
+                    if constexpr (F32) from_f(ex, &v.v[e]);
+                }
+                if constexpr (F32) xs[p] = v;
+            }
+            float s = part[0];
+#pragma unroll
+            for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
+            const float inv = __frcp_rn(rowpipe::warp_sum(s));
+            Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
+#pragma unroll 2
+            for (int p = lane; p < packs; p += 32) {
+                const Pack<T> v = xs[p];
+                float z[PV];
+#pragma unroll
+                for (int e = 0; e < PV; ++e)
+                    z[e] = __fmul_rn(F32 ? to_f(v.v[e]) : row_exp<T>(to_f(v.v[e]), m, mk), inv);
+                yr[p] = to_pack<T>(z);
+            }
+        });
+    if (!ok && lane == 0) atomicExch(status, QSML_E_TIMEOUT);
 }
 
 template <typename T>
@@ -277,10 +412,32 @@ qsml_status_t launch_rows(Context* ctx, const T* x, T* y, int64_t rows, int cols
 }
 
 template <typename T>
+qsml_status_t launch_pipe(Context* ctx, const T* x, T* y, int64_t rows, int cols, const rowpipe::Plan& p) {
+    static std::mutex mu;
+    static size_t attr_set = 0;  // largest dynamic shared memory opted in so far
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (p.smem > 48 * 1024 && p.smem > attr_set) {
+            QSML_TRY_STATUS(check_cuda(ctx,
+                                       cudaFuncSetAttribute(k_softmax_pipe<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                            static_cast<int>(p.smem)),
+                                       "softmax: shared-memory attribute"));
+            attr_set = p.smem;
+        }
+    }
+    k_softmax_pipe<T><<<p.grid, p.warps * 32, p.smem, ctx->stream>>>(x, y, rows, cols, p.slots, ctx->status);
+    return after_launch(ctx, "k_softmax_pipe");
+}
+
+template <typename T>
 qsml_status_t run_softmax(Context* ctx, const T* x, T* y, int64_t outer, int64_t k, int64_t inner) {
     constexpr int PV = Pack<T>::N;
     if (inner == 1) {
         const int64_t rows = outer, cols = k;
+        rowpipe::Plan plan;
+        if (rowpipe::use_pipe(cols * sizeof(T), sizeof(T)) && aligned16(x) && aligned16(y) && ctx->status && cols <= INT32_MAX &&
+            rows >= ctx->num_sms && rowpipe::plan(ctx, rows, static_cast<uint64_t>(cols) * sizeof(T), 0, &plan))
+            return launch_pipe<T>(ctx, x, y, rows, static_cast<int>(cols), plan);
         if (cols % PV == 0 && aligned16(x) && aligned16(y) && cols <= INT32_MAX) {
             const int64_t packs = cols / PV;
             int nv = 0;
