@@ -476,9 +476,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //   * each CTA drains its own TMEM rows; its epilogue warps release the
 //     accumulator with remote arrivals on the leader's tempty barrier;
 //   * cluster barriers order barrier initialisation and the final TMEM free.
-// No load is multicast.  Every wait is bounded as in k_gemm_tc; after an
-// abort each CTA waits a bounded time before tearing down so that copies in
-// flight (they complete on the leader's barrier) have landed.
+// Every load writes only its own CTA's shared memory.  Every wait is bounded
+// as in k_gemm_tc; after an abort each CTA waits a bounded time before tearing
+// down so that copies in flight (they complete on the leader's barrier) have
+// landed.
 // ---------------------------------------------------------------------------
 constexpr int P_BK = 64;
 constexpr int P_STAGES = 6;
