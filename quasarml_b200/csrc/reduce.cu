@@ -7,7 +7,7 @@
 // (Reduction.cpp:293-345); axis max/min are stubs (Reduction.cpp:366-382).
 //
 // Here the input is viewed as [outer, k, inner] (Reduction.cpp:310-312) and
-// one of three kernels runs, chosen from the shape alone:
+// one of these kernels runs, chosen from the shape alone:
 //   * k_reduce_seg   -- inner == 1 with few long rows, including the full
 //                       reduction (one row).  Each row is cut into a number
 //                       of interleaved slices fixed by the shape; a slice is
@@ -19,7 +19,10 @@
 //   * k_reduce_rows  -- inner == 1 with many rows: one warp per row.
 //   * k_reduce_cols  -- inner > 1: lanes own 16-byte column vectors (loads
 //                       coalesced along inner), the CTA's warps split k into
-//                       contiguous slices, slices combine in warp order.
+//                       contiguous slices, slices combine in warp order;
+//   * k_reduce_cols_wide -- inner > 1 with 16-byte column vectors, k <= 64 and
+//                       many columns: each warp one column span over all k,
+//                       the CTA's 8 warps neighbouring spans of the same rows.
 // Accumulation is binary32 (binary16 inputs widen exactly); max/min use PTX
 // max.NaN/min.NaN, so the result is exact and order-free (IEEE 754-2019
 // maximum/minimum: -0 < +0, NaN wins as 0x7fffffff).
@@ -34,8 +37,9 @@ namespace {
 
 constexpr int kRT = 256;             // threads of the segment kernel
 constexpr int kSegIters = 8;         // 16-byte loads in flight per thread
-constexpr int64_t kSegSlots = 1184;  // slices per launch (148 SMs x 8 CTAs), a constant
-constexpr int64_t kSegMinSlice = 4096;  // elements: short rows use fewer slices
+constexpr int64_t kSegMaxUnits = 8192;  // slices per launch, all rows together
+constexpr int64_t kSegSliceElems = 32768;  // elements per slice of a long row
+constexpr int64_t kWideMaxK = 64;       // longest k the wide column kernel takes
 constexpr int kMaxSegments = 16384;  // ticket counters kept in scratch
 constexpr size_t kCounterBytes = kMaxSegments * sizeof(unsigned);
 static_assert(kCounterBytes == kScratchCounterBytes, "counters fill the reserved scratch region");
@@ -49,6 +53,17 @@ __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 __device__ __forceinline__ void from_f(float v, float* o) { *o = v; }
 __device__ __forceinline__ void from_f(float v, __half* o) { *o = __float2half_rn(v); }
+
+// Slices per row of the segment kernel, from the shape alone: about
+// kSegSliceElems elements per slice (measured best on B200 for 33.5M-element
+// rows in binary32 and binary16 alike), at most kSegMaxUnits slices in all.
+inline int64_t seg_slices(int64_t rows, int64_t k) {
+    int64_t P = (k + kSegSliceElems - 1) / kSegSliceElems;
+    const int64_t cap = kSegMaxUnits / rows;
+    if (P > cap) P = cap;
+    if (P < 1) P = 1;
+    return P;
+}
 
 template <int OP> struct Red;
 template <> struct Red<QSML_RED_SUM> {
@@ -128,8 +143,8 @@ __device__ __forceinline__ typename Red<OP>::V block_reduce(typename Red<OP>::V 
 
 // ---------------------------------------------------------------------------
 // Segment kernel: x = [nseg rows, len] contiguous.  Each row is split into
-// P interleaved slices (P depends on the shape only); work unit (s, j)
-// reduces slice j of row s with 16-byte loads, kSegIters in flight per
+// P interleaved slices (P depends on the shape only); work unit (s, j), one
+// CTA, reduces slice j of row s with 16-byte loads, kSegIters in flight per
 // thread, in a fixed order, then one block reduction gives partial (s, j).
 // The unit that takes the row's last ticket combines its P partials in slice
 // order.  The result depends on the shape alone, not on the grid size.
@@ -151,7 +166,8 @@ __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int
         V acc = R::ident();
         // Slice j of a row is the interleaved set of 256-thread blocks
         // j, j + P, j + 2P, ...: at any moment the P units of a row stream
-        // through one contiguous region, which keeps DRAM pages hot.
+        // through one contiguous region (measured faster on B200 than
+        // contiguous slices).
         const int64_t stride = P * kRT;
         if (VEC) {
             const int64_t npk = len / PV;
@@ -305,6 +321,52 @@ __global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k,
 }
 
 // ---------------------------------------------------------------------------
+// Wide column kernel (16-byte column vectors, short k, many columns): a CTA
+// takes 8 neighbouring spans (warp w: span w, 32 lanes x PV columns) over all
+// k rows, so each of its load instructions reads 4 KiB of one row in one
+// piece and the CTAs in flight together read whole rows.  Each lane's
+// columns are reduced in k order.
+// ---------------------------------------------------------------------------
+template <typename T, typename OT, int OP>
+__global__ void __launch_bounds__(256) k_reduce_cols_wide(const T* __restrict__ x, int64_t outer, int64_t k,
+                                                          int64_t inner, int64_t tiles_per_o, int64_t groups_per_o,
+                                                          OT* __restrict__ out, float scale) {
+    using R = Red<OP>;
+    using V = typename R::V;
+    constexpr int PV = Pack<T>::N;
+    constexpr int U = 8;
+    constexpr int NCOL = 32 * PV;
+    const int lane = threadIdx.x, w = threadIdx.y;
+    const int64_t grp = blockIdx.x;
+    const int64_t o = grp / groups_per_o;
+    const int64_t span = (grp - o * groups_per_o) * 8 + w;  // tile within o
+    const int64_t c0 = span * NCOL + static_cast<int64_t>(lane) * PV;
+    if (span >= tiles_per_o || c0 >= inner) return;
+    V acc[PV];
+#pragma unroll
+    for (int e = 0; e < PV; ++e) acc[e] = R::ident();
+    const T* base = x + (o * k) * inner + c0;
+    int64_t kk = 0;
+    for (; kk + U <= k; kk += U) {
+        Pack<T> v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) v[u] = *reinterpret_cast<const Pack<T>*>(base + (kk + u) * inner);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v[u].v[e])));
+    }
+    for (; kk < k; ++kk) {
+        Pack<T> v = *reinterpret_cast<const Pack<T>*>(base + kk * inner);
+#pragma unroll
+        for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v.v[e])));
+    }
+#pragma unroll
+    for (int e = 0; e < PV; ++e)
+        if (c0 + e < inner) from_f(R::fin(acc[e], scale), &out[o * inner + c0 + e]);
+}
+
+// ---------------------------------------------------------------------------
 // Host dispatch
 // ---------------------------------------------------------------------------
 template <typename T, typename OT, int OP>
@@ -319,17 +381,13 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
         // One row may end in a partial pack (handled in-kernel); several rows
         // need every row start 16-byte aligned.
         const bool vec = x_al && (outer == 1 || (k * static_cast<int64_t>(sizeof(T))) % 16 == 0);
-        int64_t P = kSegSlots / outer;
-        const int64_t by_size = (k + kSegMinSlice - 1) / kSegMinSlice;
-        if (P > by_size) P = by_size;
-        if (P < 1) P = 1;
+        const int64_t P = seg_slices(outer, k);
         const int64_t units = outer * P;
         void* scratch = nullptr;
         QSML_TRY_STATUS(get_scratch(ctx, kCounterBytes + static_cast<size_t>(units) * sizeof(V), &scratch));
         unsigned* counters = static_cast<unsigned*>(scratch);
         V* partials = reinterpret_cast<V*>(static_cast<char*>(scratch) + kCounterBytes);
-        int64_t grid = static_cast<int64_t>(ctx->num_sms) * 8;
-        if (grid > units) grid = units;
+        const int64_t grid = units;  // one slice per CTA
         if (vec)
             k_reduce_seg<T, OT, OP, true><<<static_cast<unsigned>(grid), kRT, 0, ctx->stream>>>(
                 x, outer, k, P, out, scale, counters, partials);
@@ -350,6 +408,17 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
         return after_launch(ctx, "k_reduce_rows");
     }
     const bool vec = x_al && (inner * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+    if (vec && inner >= 8 * 32 * PV && k <= kWideMaxK) {
+        // Wide column kernel, when its CTAs are enough to fill the SMs twice.
+        const int64_t tiles_per_o = (inner + 32 * PV - 1) / (32 * PV);
+        const int64_t groups_per_o = (tiles_per_o + 7) / 8;
+        const int64_t groups = groups_per_o * outer;
+        if (groups >= 2 * static_cast<int64_t>(ctx->num_sms) && groups <= INT32_MAX) {
+            k_reduce_cols_wide<T, OT, OP><<<static_cast<unsigned>(groups), dim3(32, 8), 0, ctx->stream>>>(
+                x, outer, k, inner, tiles_per_o, groups_per_o, out, scale);
+            return after_launch(ctx, "k_reduce_cols_wide");
+        }
+    }
     const int pv = vec ? PV : 1;
     const int64_t tiles_per_o = (inner + 32 * pv - 1) / (32 * pv);
     const int64_t tiles = tiles_per_o * outer;
@@ -507,10 +576,7 @@ qsml_status_t run_noalloc(cudaStream_t stream, const T* x, int64_t rows, int64_t
     const float scale = 1.0f / static_cast<float>(k);
     const bool vec = aligned16(x) && (rows == 1 || (k * static_cast<int64_t>(sizeof(T))) % 16 == 0);
     // Same slicing rule as the context path, so both give identical bits.
-    int64_t P = kSegSlots / rows;
-    const int64_t by_size = (k + kSegMinSlice - 1) / kSegMinSlice;
-    if (P > by_size) P = by_size;
-    if (P < 1) P = 1;
+    const int64_t P = seg_slices(rows, k);
     const int64_t units = rows * P;
     if (units > kNoAllocMaxUnits)
         return set_error(nullptr, QSML_E_UNSUPPORTED, "qsml_reduce_noalloc: needs more partials than its fixed scratch holds");
@@ -521,11 +587,7 @@ qsml_status_t run_noalloc(cudaStream_t stream, const T* x, int64_t rows, int64_t
         cudaGetLastError();
         return set_error(nullptr, QSML_E_CUDA, std::string("qsml_reduce_noalloc: counter clear: ") + cudaGetErrorString(e));
     }
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int64_t grid = static_cast<int64_t>(sms) * 8;
-    if (grid > units) grid = units;
+    const int64_t grid = units;  // one slice per CTA
     if (vec)
         k_reduce_seg<T, OT, OP, true><<<static_cast<unsigned>(grid), kRT, 0, stream>>>(x, rows, k, P, out, scale,
                                                                                         counters, partials);

@@ -79,7 +79,11 @@ def test_f16_input_f32_output(ctx, orc, x3):
 
 ODD = [((10,), None), ((10,), 0), ((4, 100003), 1), ((4, 100003), -1), ((33, 1001), 1), ((7, 13, 5), 1),
        ((7, 13, 5), 0), ((7, 13, 5), 2), ((1, 33), 0), ((5,), None), ((3, 70000), None), ((2, 3, 4, 5), 2),
-       ((300, 8192), 1), ((8192, 3), 0), ((1, 1 << 20), 1), ((1000, 17), 1)]
+       ((300, 8192), 1), ((8192, 3), 0), ((1, 1 << 20), 1), ((1000, 17), 1),
+       # column kernel: long and short k, ragged tiles, unaligned rows
+       ((3, 1000, 96), 1), ((2, 777, 1030), 1), ((5, 64, 2048), 0), ((9, 130, 4100), 1),
+       # wide column kernel (short k, many 16-byte columns; ragged last span)
+       ((37, 310000), 0), ((3, 50, 200000), 1), ((20, 620000), 0)]
 
 
 @pytest.mark.parametrize("shape,axis", ODD)
@@ -155,3 +159,11 @@ def test_prod(ctx, orc, shape, axis):
     _, o64, _ = orc.reduce(orc.PROD, x, axis)
     n = x.size if axis is None else x.shape[axis]
     assert np.all(np.abs(g.reshape(o64.shape) - o64) <= n * 2.0 ** -24 * np.abs(o64))
+
+
+def test_long_column_reduction(ctx, orc):
+    """A long column reduction: 2.1 million columns, k = 66."""
+    x = datagen.normal(22, (66, 2_100_000), 0.3, 1.5)
+    t = dev(x)
+    for name, op in OPS.items():
+        check(orc, name, x, 0, gpu_reduce(ctx, op, t, 0), False)
