@@ -9,6 +9,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <utility>
 #include <string>
 #include <unordered_map>
 
@@ -72,6 +73,35 @@ qsml_status_t set_error(Context* ctx, qsml_status_t st, const std::string& msg);
 qsml_status_t check_cuda(Context* ctx, cudaError_t e, const char* what);
 // Checks the launch that was just enqueued and counts it.
 qsml_status_t after_launch(Context* ctx, const char* kernel);
+
+// Programmatic dependent launch for short memory-bound kernels that run back
+// to back: the kernel is launched with programmatic stream serialization, so
+// its CTAs may become resident while the previous kernel on the stream drains;
+// it must begin with pdl_begin(), which waits until that kernel has completed
+// and its writes are visible (griddepcontrol.wait) before touching memory, and
+// then lets the next such kernel launch early.  Correct whatever the previous
+// kernel on the stream is; without the launch attribute the wait returns at
+// once.
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Scratch of at least `bytes`.  Its first kScratchCounterBytes hold the
 // reductions' ticket counters, which every kernel that uses them leaves at

@@ -23,6 +23,9 @@
 //   * k_reduce_cols_wide -- inner > 1 with 16-byte column vectors, k <= 64 and
 //                       many columns: each warp one column span over all k,
 //                       the CTA's 8 warps neighbouring spans of the same rows.
+// The kernels are launched with programmatic dependent launch (launch_pdl):
+// each waits for the previous kernel on the stream before touching memory, but
+// its CTAs are already resident when that kernel drains.
 // Accumulation is binary32 (binary16 inputs widen exactly); max/min use PTX
 // max.NaN/min.NaN, so the result is exact and order-free (IEEE 754-2019
 // maximum/minimum: -0 < +0, NaN wins as 0x7fffffff).
@@ -154,6 +157,7 @@ __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int
                                                     int64_t P, OT* __restrict__ out, float scale,
                                                     unsigned* __restrict__ counters,
                                                     typename Red<OP>::V* __restrict__ partials) {
+    pdl_begin();
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
@@ -221,6 +225,7 @@ __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int
 template <typename T, typename OT, int OP, bool VEC>
 __global__ void __launch_bounds__(256) k_reduce_rows(const T* __restrict__ x, int64_t rows, int64_t len,
                                                      OT* __restrict__ out, float scale) {
+    pdl_begin();
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
@@ -262,6 +267,7 @@ __global__ void __launch_bounds__(256) k_reduce_rows(const T* __restrict__ x, in
 template <typename T, typename OT, int OP, bool VEC>
 __global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k, int64_t inner,
                               int64_t tiles_per_o, OT* __restrict__ out, float scale) {
+    pdl_begin();
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = VEC ? Pack<T>::N : 1;
@@ -331,6 +337,7 @@ template <typename T, typename OT, int OP>
 __global__ void __launch_bounds__(256) k_reduce_cols_wide(const T* __restrict__ x, int64_t outer, int64_t k,
                                                           int64_t inner, int64_t tiles_per_o, int64_t groups_per_o,
                                                           OT* __restrict__ out, float scale) {
+    pdl_begin();
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
@@ -388,12 +395,12 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
         unsigned* counters = static_cast<unsigned*>(scratch);
         V* partials = reinterpret_cast<V*>(static_cast<char*>(scratch) + kCounterBytes);
         const int64_t grid = units;  // one slice per CTA
-        if (vec)
-            k_reduce_seg<T, OT, OP, true><<<static_cast<unsigned>(grid), kRT, 0, ctx->stream>>>(
-                x, outer, k, P, out, scale, counters, partials);
-        else
-            k_reduce_seg<T, OT, OP, false><<<static_cast<unsigned>(grid), kRT, 0, ctx->stream>>>(
-                x, outer, k, P, out, scale, counters, partials);
+        const cudaError_t e =
+            vec ? launch_pdl(k_reduce_seg<T, OT, OP, true>, dim3(static_cast<unsigned>(grid)), dim3(kRT), 0,
+                             ctx->stream, x, outer, k, P, out, scale, counters, partials)
+                : launch_pdl(k_reduce_seg<T, OT, OP, false>, dim3(static_cast<unsigned>(grid)), dim3(kRT), 0,
+                             ctx->stream, x, outer, k, P, out, scale, counters, partials);
+        if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_seg");
         return after_launch(ctx, "k_reduce_seg");
     }
     if (inner == 1) {
@@ -401,10 +408,12 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
         int64_t grid = (outer + 7) / 8;  // 8 warps per CTA
         int64_t cap = static_cast<int64_t>(ctx->num_sms) * 32;
         if (grid > cap) grid = cap;
-        if (vec)
-            k_reduce_rows<T, OT, OP, true><<<static_cast<unsigned>(grid), 256, 0, ctx->stream>>>(x, outer, k, out, scale);
-        else
-            k_reduce_rows<T, OT, OP, false><<<static_cast<unsigned>(grid), 256, 0, ctx->stream>>>(x, outer, k, out, scale);
+        const cudaError_t e =
+            vec ? launch_pdl(k_reduce_rows<T, OT, OP, true>, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
+                             ctx->stream, x, outer, k, out, scale)
+                : launch_pdl(k_reduce_rows<T, OT, OP, false>, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
+                             ctx->stream, x, outer, k, out, scale);
+        if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_rows");
         return after_launch(ctx, "k_reduce_rows");
     }
     const bool vec = x_al && (inner * static_cast<int64_t>(sizeof(T))) % 16 == 0;
@@ -414,8 +423,10 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
         const int64_t groups_per_o = (tiles_per_o + 7) / 8;
         const int64_t groups = groups_per_o * outer;
         if (groups >= 2 * static_cast<int64_t>(ctx->num_sms) && groups <= INT32_MAX) {
-            k_reduce_cols_wide<T, OT, OP><<<static_cast<unsigned>(groups), dim3(32, 8), 0, ctx->stream>>>(
-                x, outer, k, inner, tiles_per_o, groups_per_o, out, scale);
+            const cudaError_t e = launch_pdl(k_reduce_cols_wide<T, OT, OP>, dim3(static_cast<unsigned>(groups)),
+                                             dim3(32, 8), 0, ctx->stream, x, outer, k, inner, tiles_per_o,
+                                             groups_per_o, out, scale);
+            if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_cols_wide");
             return after_launch(ctx, "k_reduce_cols_wide");
         }
     }
@@ -429,12 +440,12 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
     dim3 block(32, static_cast<unsigned>(W));
     size_t smem = static_cast<size_t>(W) * 32 * pv * sizeof(V);
     if (tiles > INT32_MAX) return set_error(ctx, QSML_E_UNSUPPORTED, "reduction too large");
-    if (vec)
-        k_reduce_cols<T, OT, OP, true><<<static_cast<unsigned>(tiles), block, smem, ctx->stream>>>(
-            x, outer, k, inner, tiles_per_o, out, scale);
-    else
-        k_reduce_cols<T, OT, OP, false><<<static_cast<unsigned>(tiles), block, smem, ctx->stream>>>(
-            x, outer, k, inner, tiles_per_o, out, scale);
+    const cudaError_t e =
+        vec ? launch_pdl(k_reduce_cols<T, OT, OP, true>, dim3(static_cast<unsigned>(tiles)), block, smem, ctx->stream,
+                         x, outer, k, inner, tiles_per_o, out, scale)
+            : launch_pdl(k_reduce_cols<T, OT, OP, false>, dim3(static_cast<unsigned>(tiles)), block, smem,
+                         ctx->stream, x, outer, k, inner, tiles_per_o, out, scale);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_cols");
     return after_launch(ctx, "k_reduce_cols");
 }
 
