@@ -13,6 +13,7 @@
 //   * k_arg_rows -- inner == 1 with many rows: one warp per row;
 //   * k_arg_cols -- inner > 1: lanes own 16-byte column vectors, warps split
 //                   k into contiguous ranges.
+// All three are launched with programmatic dependent launch (launch_pdl).
 // Each thread scans its elements in increasing index order keeping the first
 // strictly better one, in the input's own arithmetic (float for F32/F16,
 // integers for the integer dtypes).  Threads then combine through a 64-bit
@@ -135,6 +136,7 @@ template <typename T, int OP, bool VEC>
 __global__ void __launch_bounds__(kAT) k_arg_seg(const T* __restrict__ x, int64_t nseg, int64_t len, int64_t P,
                                                  uint32_t* __restrict__ out, unsigned* __restrict__ counters,
                                                  unsigned long long* __restrict__ partials) {
+    pdl_begin();
     using C = typename Cmp<T>::C;
     constexpr int PV = APack<T>::N;
     __shared__ bool s_last;
@@ -199,6 +201,7 @@ __global__ void __launch_bounds__(kAT) k_arg_seg(const T* __restrict__ x, int64_
 template <typename T, int OP, bool VEC>
 __global__ void __launch_bounds__(256) k_arg_rows(const T* __restrict__ x, int64_t rows, int64_t len,
                                                   uint32_t* __restrict__ out) {
+    pdl_begin();
     using C = typename Cmp<T>::C;
     constexpr int PV = APack<T>::N;
     const int lane = threadIdx.x & 31;
@@ -241,6 +244,7 @@ __global__ void __launch_bounds__(256) k_arg_rows(const T* __restrict__ x, int64
 template <typename T, int OP, bool VEC>
 __global__ void k_arg_cols(const T* __restrict__ x, int64_t outer, int64_t k, int64_t inner, int64_t tiles_per_o,
                            uint32_t* __restrict__ out) {
+    pdl_begin();
     using C = typename Cmp<T>::C;
     constexpr int PV = VEC ? APack<T>::N : 1;
     extern __shared__ unsigned long long red[];
@@ -316,12 +320,12 @@ qsml_status_t run_arg(Context* ctx, const T* x, int64_t outer, int64_t k, int64_
         auto* partials = reinterpret_cast<unsigned long long*>(static_cast<char*>(scratch) + kArgCounterBytes);
         int64_t grid = static_cast<int64_t>(ctx->num_sms) * 8;
         if (grid > units) grid = units;
-        if (vec)
-            k_arg_seg<T, OP, true><<<static_cast<unsigned>(grid), kAT, 0, ctx->stream>>>(x, outer, k, P, out, counters,
-                                                                                         partials);
-        else
-            k_arg_seg<T, OP, false><<<static_cast<unsigned>(grid), kAT, 0, ctx->stream>>>(x, outer, k, P, out,
-                                                                                          counters, partials);
+        const cudaError_t e =
+            vec ? launch_pdl(k_arg_seg<T, OP, true>, dim3(static_cast<unsigned>(grid)), dim3(kAT), 0, ctx->stream, x,
+                             outer, k, P, out, counters, partials)
+                : launch_pdl(k_arg_seg<T, OP, false>, dim3(static_cast<unsigned>(grid)), dim3(kAT), 0, ctx->stream, x,
+                             outer, k, P, out, counters, partials);
+        if (e != cudaSuccess) return check_cuda(ctx, e, "k_arg_seg");
         return after_launch(ctx, "k_arg_seg");
     }
     if (inner == 1) {
@@ -329,10 +333,12 @@ qsml_status_t run_arg(Context* ctx, const T* x, int64_t outer, int64_t k, int64_
         int64_t grid = (outer + 7) / 8;  // 8 warps per CTA
         const int64_t cap = static_cast<int64_t>(ctx->num_sms) * 32;
         if (grid > cap) grid = cap;
-        if (vec)
-            k_arg_rows<T, OP, true><<<static_cast<unsigned>(grid), 256, 0, ctx->stream>>>(x, outer, k, out);
-        else
-            k_arg_rows<T, OP, false><<<static_cast<unsigned>(grid), 256, 0, ctx->stream>>>(x, outer, k, out);
+        const cudaError_t e =
+            vec ? launch_pdl(k_arg_rows<T, OP, true>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, ctx->stream, x,
+                             outer, k, out)
+                : launch_pdl(k_arg_rows<T, OP, false>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, ctx->stream, x,
+                             outer, k, out);
+        if (e != cudaSuccess) return check_cuda(ctx, e, "k_arg_rows");
         return after_launch(ctx, "k_arg_rows");
     }
     const bool vec = x_al && (inner * static_cast<int64_t>(sizeof(T))) % 16 == 0;
@@ -349,12 +355,12 @@ qsml_status_t run_arg(Context* ctx, const T* x, int64_t outer, int64_t k, int64_
     if (W < 1) W = 1;
     dim3 block(32, static_cast<unsigned>(W));
     const size_t smem = static_cast<size_t>(W) * 32 * pv * 8;
-    if (vec)
-        k_arg_cols<T, OP, true><<<static_cast<unsigned>(tiles), block, smem, ctx->stream>>>(x, outer, k, inner,
-                                                                                            tiles_per_o, out);
-    else
-        k_arg_cols<T, OP, false><<<static_cast<unsigned>(tiles), block, smem, ctx->stream>>>(x, outer, k, inner,
-                                                                                             tiles_per_o, out);
+    const cudaError_t e =
+        vec ? launch_pdl(k_arg_cols<T, OP, true>, dim3(static_cast<unsigned>(tiles)), block, smem, ctx->stream, x,
+                         outer, k, inner, tiles_per_o, out)
+            : launch_pdl(k_arg_cols<T, OP, false>, dim3(static_cast<unsigned>(tiles)), block, smem, ctx->stream, x,
+                         outer, k, inner, tiles_per_o, out);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "k_arg_cols");
     return after_launch(ctx, "k_arg_cols");
 }
 
