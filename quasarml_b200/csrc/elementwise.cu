@@ -43,6 +43,7 @@ __device__ __forceinline__ C apply(const Op& op, C a, C b) {
 // 0 (one value per row, splatted) or 1 (16-byte vectors).
 template <typename T, int NIN, typename Op, typename IDX>
 __global__ void __launch_bounds__(kThreads) k_ew_rows(Ptrs<T, NIN> P, EwPlan plan, IDX items, IDX cpr, Op op) {
+    pdl_begin();
     using E = Elem<T>;
     using CT = typename E::C;
     constexpr int V = Pack<T>::N;
@@ -87,6 +88,7 @@ __global__ void __launch_bounds__(kThreads) k_ew_rows(Ptrs<T, NIN> P, EwPlan pla
 // 1-D contiguous (or scalar-broadcast) operands: vector body + scalar tail.
 template <typename T, int NIN, typename Op, bool VEC>
 __global__ void __launch_bounds__(kThreads) k_ew_flat(Ptrs<T, NIN> P, EwPlan plan, int64_t n, Op op) {
+    pdl_begin();
     using E = Elem<T>;
     using CT = typename E::C;
     constexpr int V = VEC ? Pack<T>::N : 1;
@@ -198,10 +200,18 @@ qsml_status_t launch_ew(Context* ctx, const EwPlan& p, const qsml_tdesc* const* 
             int64_t npk = n / V;
             int64_t blocks = (npk + kThreads * kUnroll - 1) / (kThreads * kUnroll);
             if (blocks < 1) blocks = 1;
-            k_ew_flat<T, NIN, Op, true><<<static_cast<unsigned>(blocks), kThreads, 0, ctx->stream>>>(P, p, n, op);
+            {
+                const cudaError_t e = launch_pdl(k_ew_flat<T, NIN, Op, true>, dim3(static_cast<unsigned>(blocks)),
+                                                 dim3(kThreads), 0, ctx->stream, P, p, n, op);
+                if (e != cudaSuccess) return check_cuda(ctx, e, "k_ew_flat");
+            }
         } else {
             int64_t blocks = (n + kThreads * kUnroll - 1) / (kThreads * kUnroll);
-            k_ew_flat<T, NIN, Op, false><<<static_cast<unsigned>(blocks), kThreads, 0, ctx->stream>>>(P, p, n, op);
+            {
+                const cudaError_t e = launch_pdl(k_ew_flat<T, NIN, Op, false>, dim3(static_cast<unsigned>(blocks)),
+                                                 dim3(kThreads), 0, ctx->stream, P, p, n, op);
+                if (e != cudaSuccess) return check_cuda(ctx, e, "k_ew_flat");
+            }
         }
         return after_launch(ctx, "k_ew_flat");
     }
@@ -222,11 +232,20 @@ qsml_status_t launch_ew(Context* ctx, const EwPlan& p, const qsml_tdesc* const* 
             for (int d = 0; d < p.nd; ++d)
                 if (p.shape[d] >= (int64_t(1) << 31)) small = false;
             if (small) {
-                k_ew_rows<T, NIN, Op, uint32_t><<<static_cast<unsigned>(blocks), kThreads, 0, ctx->stream>>>(
-                    P, p, static_cast<uint32_t>(items), static_cast<uint32_t>(cpr), op);
+                {
+                    const cudaError_t e = launch_pdl(k_ew_rows<T, NIN, Op, uint32_t>,
+                                                     dim3(static_cast<unsigned>(blocks)), dim3(kThreads), 0,
+                                                     ctx->stream, P, p, static_cast<uint32_t>(items),
+                                                     static_cast<uint32_t>(cpr), op);
+                    if (e != cudaSuccess) return check_cuda(ctx, e, "k_ew_rows");
+                }
             } else {
-                k_ew_rows<T, NIN, Op, int64_t><<<static_cast<unsigned>(blocks), kThreads, 0, ctx->stream>>>(
-                    P, p, items, cpr, op);
+                {
+                    const cudaError_t e = launch_pdl(k_ew_rows<T, NIN, Op, int64_t>,
+                                                     dim3(static_cast<unsigned>(blocks)), dim3(kThreads), 0,
+                                                     ctx->stream, P, p, items, cpr, op);
+                    if (e != cudaSuccess) return check_cuda(ctx, e, "k_ew_rows");
+                }
             }
             return after_launch(ctx, "k_ew_rows");
         }

@@ -59,6 +59,7 @@ constexpr int kGU = 4;
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(kGT) k_gather_rows(const T* __restrict__ src, T* __restrict__ dst, GPlan p,
                                                      int64_t items, int64_t per_row) {
+    pdl_begin();
     const int64_t base = static_cast<int64_t>(blockIdx.x) * (kGT * kGU) + threadIdx.x;
     if (VEC) {
         constexpr int PV = 16 / sizeof(T);
@@ -95,6 +96,7 @@ __global__ void __launch_bounds__(kGT) k_gather_rows(const T* __restrict__ src, 
 template <typename T, int G>
 __global__ void __launch_bounds__(kGT) k_gather_small(const T* __restrict__ src, T* __restrict__ dst, GPlan p,
                                                       int64_t items, int64_t per_row) {
+    pdl_begin();
     struct alignas(G * sizeof(T)) Out { T v[G]; };
     const int64_t s = p.st[p.nd - 1];
     const int64_t base = static_cast<int64_t>(blockIdx.x) * (kGT * 2) + threadIdx.x;
@@ -119,6 +121,7 @@ constexpr int kTile = 64;
 template <typename T>
 __global__ void __launch_bounds__(256) k_gather_tiled(const T* __restrict__ src, T* __restrict__ dst, GPlan p,
                                                       int dP, int64_t ptiles, int64_t qtiles) {
+    pdl_begin();
     __shared__ T tile[kTile][kTile + 1];
     const int tx = threadIdx.x, ty = threadIdx.y;  // (32, 8)
     const int dQ = p.nd - 1;
@@ -237,10 +240,18 @@ qsml_status_t gather_typed(Context* ctx, const GPlan& p, const void* srcv, void*
         if (vec) {
             int64_t per_row = C / PV, items = n / PV;
             int64_t blocks = (items + kGT * kGU - 1) / (kGT * kGU);
-            k_gather_rows<T, true><<<static_cast<unsigned>(blocks), kGT, 0, ctx->stream>>>(src, dst, p, items, per_row);
+            {
+                const cudaError_t e = launch_pdl(k_gather_rows<T, true>, dim3(static_cast<unsigned>(blocks)),
+                                                 dim3(kGT), 0, ctx->stream, src, dst, p, items, per_row);
+                if (e != cudaSuccess) return check_cuda(ctx, e, "k_gather_rows");
+            }
         } else {
             int64_t blocks = (n + kGT * kGU - 1) / (kGT * kGU);
-            k_gather_rows<T, false><<<static_cast<unsigned>(blocks), kGT, 0, ctx->stream>>>(src, dst, p, n, C);
+            {
+                const cudaError_t e = launch_pdl(k_gather_rows<T, false>, dim3(static_cast<unsigned>(blocks)),
+                                                 dim3(kGT), 0, ctx->stream, src, dst, p, n, C);
+                if (e != cudaSuccess) return check_cuda(ctx, e, "k_gather_rows");
+            }
         }
         return after_launch(ctx, "k_gather_rows");
     }
@@ -258,14 +269,22 @@ qsml_status_t gather_typed(Context* ctx, const GPlan& p, const void* srcv, void*
         int64_t batch = n / (p.shape[dP] * C);
         int64_t blocks = ptiles * qtiles * batch;
         if (blocks > INT32_MAX) return set_error(ctx, QSML_E_UNSUPPORTED, "gather too large");
-        k_gather_tiled<T><<<static_cast<unsigned>(blocks), dim3(32, 8), 0, ctx->stream>>>(src, dst, p, dP, ptiles, qtiles);
+        {
+            const cudaError_t e = launch_pdl(k_gather_tiled<T>, dim3(static_cast<unsigned>(blocks)), dim3(32, 8), 0,
+                                             ctx->stream, src, dst, p, dP, ptiles, qtiles);
+            if (e != cudaSuccess) return check_cuda(ctx, e, "k_gather_tiled");
+        }
         return after_launch(ctx, "k_gather_tiled");
     }
 
     if (as <= 32 && C % PV == 0 && aligned16(dst)) {
         int64_t per_row = C / PV, items = n / PV;
         int64_t blocks = (items + kGT * 2 - 1) / (kGT * 2);
-        k_gather_small<T, PV><<<static_cast<unsigned>(blocks), kGT, 0, ctx->stream>>>(src, dst, p, items, per_row);
+        {
+            const cudaError_t e = launch_pdl(k_gather_small<T, PV>, dim3(static_cast<unsigned>(blocks)), dim3(kGT), 0,
+                                             ctx->stream, src, dst, p, items, per_row);
+            if (e != cudaSuccess) return check_cuda(ctx, e, "k_gather_small");
+        }
         return after_launch(ctx, "k_gather_small");
     }
 

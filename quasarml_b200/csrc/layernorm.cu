@@ -111,6 +111,7 @@ template <typename T, typename GT, int NV>
 __global__ void __launch_bounds__(256) k_layer_norm_reg(const T* __restrict__ x, const GT* __restrict__ gamma,
                                                         const GT* __restrict__ beta, T* __restrict__ y,
                                                         int64_t rows, int cols, float eps) {
+    pdl_begin();
     constexpr int PV = Pack<T>::N;
     constexpr int E = NV * PV;  // elements per thread
     extern __shared__ float4 ln_smem[];
@@ -197,6 +198,7 @@ template <typename T, typename GT>
 __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
     k_layer_norm_pipe(const T* __restrict__ x, const GT* __restrict__ gamma, const GT* __restrict__ beta,
                       T* __restrict__ y, int64_t rows, int cols, float eps, int slots, int* status) {
+    pdl_begin();
     constexpr int PV = Pack<T>::N;
     extern __shared__ float4 ln_pipe_smem[];
     __shared__ uint64_t bars[rowpipe::kMaxWarps * rowpipe::kMaxSlots];
@@ -353,7 +355,11 @@ qsml_status_t launch_reg(Context* ctx, const T* x, const GT* g, const GT* b, T* 
     }
     int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
     if (grid > rows) grid = rows;
-    k_layer_norm_reg<T, GT, NV><<<static_cast<unsigned>(grid), th, smem, ctx->stream>>>(x, g, b, y, rows, cols, eps);
+    {
+        const cudaError_t e = launch_pdl(k_layer_norm_reg<T, GT, NV>, dim3(static_cast<unsigned>(grid)), dim3(th),
+                                         smem, ctx->stream, x, g, b, y, rows, cols, eps);
+        if (e != cudaSuccess) return check_cuda(ctx, e, "k_layer_norm_reg");
+    }
     return after_launch(ctx, "k_layer_norm_reg");
 }
 
@@ -373,8 +379,11 @@ qsml_status_t launch_pipe(Context* ctx, const T* x, const GT* g, const GT* b, T*
             attr_set = p.smem;
         }
     }
-    k_layer_norm_pipe<T, GT><<<p.grid, p.warps * 32, p.smem, ctx->stream>>>(x, g, b, y, rows, cols, eps, p.slots,
-                                                                          ctx->status);
+    {
+        const cudaError_t e = launch_pdl(k_layer_norm_pipe<T, GT>, dim3(p.grid), dim3(p.warps * 32), p.smem,
+                                         ctx->stream, x, g, b, y, rows, cols, eps, p.slots, ctx->status);
+        if (e != cudaSuccess) return check_cuda(ctx, e, "k_layer_norm_pipe");
+    }
     return after_launch(ctx, "k_layer_norm_pipe");
 }
 

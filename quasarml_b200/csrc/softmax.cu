@@ -107,6 +107,7 @@ __device__ __forceinline__ Pack<T> to_pack(const float* z) {
 template <typename T, int NV>
 __global__ void __launch_bounds__(256) k_softmax_rows(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
                                                       int cols) {
+    pdl_begin();
     constexpr int PV = Pack<T>::N;
     constexpr int E = NV * PV;
     __shared__ float sh_max[8], sh_sum[8];
@@ -211,6 +212,7 @@ __device__ __forceinline__ float pack_max(const Pack<T>* xs, int packs, int lane
 template <typename T>
 __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
     k_softmax_pipe(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int cols, int slots, int* status) {
+    pdl_begin();
     constexpr int PV = Pack<T>::N;
     constexpr bool F32 = sizeof(T) == 4;
     extern __shared__ float4 sm_pipe_smem[];
@@ -407,7 +409,11 @@ qsml_status_t launch_rows(Context* ctx, const T* x, T* y, int64_t rows, int cols
     }
     int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
     if (grid > rows) grid = rows;
-    k_softmax_rows<T, NV><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, y, rows, cols);
+    {
+        const cudaError_t e = launch_pdl(k_softmax_rows<T, NV>, dim3(static_cast<unsigned>(grid)), dim3(th), 0,
+                                         ctx->stream, x, y, rows, cols);
+        if (e != cudaSuccess) return check_cuda(ctx, e, "k_softmax_rows");
+    }
     return after_launch(ctx, "k_softmax_rows");
 }
 
@@ -425,7 +431,11 @@ qsml_status_t launch_pipe(Context* ctx, const T* x, T* y, int64_t rows, int cols
             attr_set = p.smem;
         }
     }
-    k_softmax_pipe<T><<<p.grid, p.warps * 32, p.smem, ctx->stream>>>(x, y, rows, cols, p.slots, ctx->status);
+    {
+        const cudaError_t e = launch_pdl(k_softmax_pipe<T>, dim3(p.grid), dim3(p.warps * 32), p.smem, ctx->stream, x,
+                                         y, rows, cols, p.slots, ctx->status);
+        if (e != cudaSuccess) return check_cuda(ctx, e, "k_softmax_pipe");
+    }
     return after_launch(ctx, "k_softmax_pipe");
 }
 
