@@ -636,9 +636,13 @@ def family_times(wl, stream, reps: int = 5):
     """Average device duration of one launch of each kernel family: the
     family's calls of one step captured alone in a CUDA graph and replayed."""
     import torch
+    # each call's family is the kernel the library chose for it
     fams = {}
-    for c in wl.calls:
-        fams.setdefault(c[4], []).append(c)
+    with torch.cuda.stream(stream):
+        for c in wl.calls:
+            wl.compute([c])
+            fams.setdefault(wl.ctx.last_kernel(), []).append(c)
+    torch.cuda.synchronize()
     out = {}
     with torch.cuda.stream(stream):
         for fam, calls in fams.items():

@@ -384,6 +384,10 @@ QSML_API qsml_status_t qsml_reduce_noalloc(void* stream, int32_t op, const qsml_
 
 /* Kernels this context has launched since qsml_init. */
 QSML_API qsml_status_t qsml_launch_count(qsml_ctx* ctx, uint64_t* count);
+/* Name of the last kernel this context launched ("" before the first), at
+ * most len-1 characters and a terminating NUL into buf: which of an op's
+ * kernels the shape selected (e.g. "k_reduce_cols_wide", "k_gemm_tc2<f16>"). */
+QSML_API qsml_status_t qsml_last_kernel(qsml_ctx* ctx, char* buf, size_t len);
 /* Ops that ran on the CPU instead of the GPU: always 0 (there is no CPU
  * path).  Backs qsml::cpu_fallback_count(). */
 QSML_API qsml_status_t qsml_cpu_fallback_count(qsml_ctx* ctx, uint64_t* count);

@@ -142,6 +142,7 @@ _SIGS = {
     "qsml_matmul": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_int32]),
     "qsml_reduce_noalloc": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_int32, _c.c_int32, _P(TDesc)]),
     "qsml_launch_count": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64)]),
+    "qsml_last_kernel": (_c.c_int32, [_c.c_void_p, _c.c_char_p, _c.c_size_t]),
     "qsml_cpu_fallback_count": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64)]),
     "qsml_allocator_stats": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64), _P(_c.c_uint64),
                                           _P(_c.c_uint64), _P(_c.c_uint64)]),
@@ -316,6 +317,12 @@ class Context:
         n = ctypes.c_uint64()
         self.check(self.lib.qsml_launch_count(self.h, ctypes.byref(n)))
         return n.value
+
+    def last_kernel(self) -> str:
+        """Name of the last kernel this context launched ("" before any)."""
+        buf = ctypes.create_string_buffer(128)
+        self.check(self.lib.qsml_last_kernel(self.h, buf, len(buf)))
+        return buf.value.decode()
 
     def cpu_fallback_count(self) -> int:
         n = ctypes.c_uint64()

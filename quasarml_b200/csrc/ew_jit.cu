@@ -317,6 +317,7 @@ qsml_status_t fused_jit(Context* ctx, const qsml_fuse_node* nodes, int n_nodes, 
     const CUresult lr = r.launch(fn, static_cast<unsigned>(blocks), 1, 1, kJitThreads, 1, 1, 0,
                                  reinterpret_cast<CUstream>(ctx->stream), args.data(), nullptr);
     ctx->launches++;
+    ctx->last_kernel = "qsml_fused_kernel";
     if (lr != CUDA_SUCCESS)
         return set_error(ctx, QSML_E_CUDA, "launch of the fused kernel failed (CUresult " + std::to_string(lr) + ")");
     *ran = true;

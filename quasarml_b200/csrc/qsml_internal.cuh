@@ -60,6 +60,7 @@ struct Context {
     // qsml_synchronize reads and clears it.
     int* status = nullptr;
     uint64_t launches = 0;
+    const char* last_kernel = "";  // a string literal of the launch site
     // Fused elementwise expressions: QSML_FUSE_MODE_* and which kernel ran.
     int fuse_mode = 0;
     uint64_t fuse_jit_launches = 0, fuse_interp_launches = 0;

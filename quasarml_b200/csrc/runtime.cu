@@ -33,6 +33,7 @@ qsml_status_t check_cuda(Context* ctx, cudaError_t e, const char* what) {
 
 qsml_status_t after_launch(Context* ctx, const char* kernel) {
     ctx->launches++;
+    ctx->last_kernel = kernel;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         return set_error(ctx, QSML_E_CUDA,
@@ -428,6 +429,13 @@ qsml_status_t qsml_launch_count(qsml_ctx* handle, uint64_t* count) {
     QSML_CTX(handle);
     if (!count) return QSML_E_INVALID;
     *count = C_->launches;
+    return QSML_OK;
+}
+
+qsml_status_t qsml_last_kernel(qsml_ctx* handle, char* buf, size_t len) {
+    QSML_CTX(handle);
+    if (!buf || len == 0) return QSML_E_INVALID;
+    std::snprintf(buf, len, "%s", C_->last_kernel);
     return QSML_OK;
 }
 

@@ -42,6 +42,7 @@ def test_fp16_shapes(ctx, orc, kernel, mkn, out):
     b = datagen.uniform(62, (K, N), -1, 1).astype(np.float16)
     tb = dev(b)
     c = mm(ctx, dev(a), d(tb), (M, N), out).astype(np.float64)
+    assert ctx.last_kernel().startswith("k_gemm_tc2<" if kernel == "1" else "k_gemm_tc<"), ctx.last_kernel()
     ref = orc.matmul_f64(a, b)
     err = np.max(np.abs(c - ref)) / np.max(np.abs(ref))
     assert err <= (1e-5 if out == np.float32 else 1e-3), (kernel, err)
@@ -70,3 +71,15 @@ def test_kernels_agree(ctx, monkeypatch):
         outs.append(mm(ctx, ta, d(tb), (4, 1024, 1024), np.float32))
     scale = float(np.max(np.abs(outs[0])))
     assert float(np.max(np.abs(outs[0] - outs[1]))) <= 1e-6 * scale
+
+
+def test_auto_choice(ctx, monkeypatch):
+    """Without QSML_GEMM_2SM the SM-pair kernel runs when the 256 x 256 tiles
+    fill the SM pairs at least once, the one-SM kernel otherwise."""
+    monkeypatch.delenv("QSML_GEMM_2SM", raising=False)
+    big = dev(np.zeros((4096, 64), np.float16)), dev(np.zeros((64, 4096), np.float16))
+    mm(ctx, big[0], d(big[1]), (4096, 4096), np.float32)
+    assert ctx.last_kernel().startswith("k_gemm_tc2<"), ctx.last_kernel()
+    small = dev(np.zeros((512, 64), np.float16)), dev(np.zeros((64, 512), np.float16))
+    mm(ctx, small[0], d(small[1]), (512, 512), np.float32)
+    assert ctx.last_kernel().startswith("k_gemm_tc<"), ctx.last_kernel()

@@ -167,3 +167,15 @@ def test_long_column_reduction(ctx, orc):
     t = dev(x)
     for name, op in OPS.items():
         check(orc, name, x, 0, gpu_reduce(ctx, op, t, 0), False)
+
+
+@pytest.mark.parametrize("shape,axis,kernel", [((64, 512, 1024), 0, "k_reduce_cols_wide"),
+                                               ((64, 512, 1024), 1, "k_reduce_cols"),
+                                               ((64, 512, 1024), 2, "k_reduce_rows"),
+                                               ((64, 512, 1024), None, "k_reduce_seg"),
+                                               ((37, 310000), 0, "k_reduce_cols_wide")])
+def test_kernel_choice(ctx, shape, axis, kernel):
+    """The workload shapes reach the kernel each was tuned for (fp32)."""
+    t = dev(np.zeros(shape, np.float32))
+    gpu_reduce(ctx, abi.RED_SUM, t, axis)
+    assert ctx.last_kernel() == kernel

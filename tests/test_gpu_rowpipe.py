@@ -1,14 +1,14 @@
 """Layer norm and last-axis softmax on rows streamed through shared memory
 (one warp per row, bulk copies into per-warp buffers).
 
-Rows of at least 2 KiB whose size is a multiple of 16 bytes take this path.
-The shapes below cover: rows whose 16-byte packs do not divide evenly over
-the 32 lanes, rows just above and far above the SM count, two and three
-buffers per warp, one warp per CTA, the largest rows the layer norm takes
-this way (gamma/beta and two row buffers fill the shared memory), and
-special values.  Bars as in the other layer norm and softmax tests:
-binary32 |y - ref| <= 1e-5 * (1 + |ref|) (layer norm) or 1e-5 * ref + 1e-30
-(softmax); binary16 1e-3 relative.
+Rows of 2-8 KiB (binary16) or 2-4 KiB (binary32) whose size is a multiple of
+16 bytes take this path; the shapes below also include wider rows, which
+take the register-resident or the generic kernels, and each case checks
+which kernel ran (qsml_last_kernel).  Covered: rows whose 16-byte packs do
+not divide evenly over the 32 lanes, rows just above and far above the SM
+count, 16 warps per CTA, and special values.  Bars as in the other layer
+norm and softmax tests: binary32 |y - ref| <= 1e-5 * (1 + |ref|) (layer norm)
+or 1e-5 * ref + 1e-30 (softmax); binary16 1e-3 relative.
 """
 import numpy as np
 import pytest
@@ -18,14 +18,15 @@ from quasarml_b200 import abi, datagen
 
 pytestmark = pytest.mark.gpu
 
+# (shape, dtype, streamed through shared memory?)
 SHAPES = [
-    ((5000, 1000), np.float32),   # 4000-byte rows, 250 packs: ragged over the lanes
-    ((3000, 1032), np.float16),   # 2064-byte rows, 129 packs
-    ((149, 2048), np.float32),    # one row more than a B200 has SMs
-    ((20000, 512), np.float32),   # 2 KiB rows: 16 warps x 3 buffers per CTA
-    ((16384, 4096), np.float16),
-    ((300, 12000), np.float32),   # 48000-byte rows: two buffers, few warps
-    ((400, 18000), np.float16),   # layer norm: gamma/beta 144,000 B + two 36,000 B rows
+    ((5000, 1000), np.float32, True),    # 4000-byte rows, 250 packs: ragged over the lanes
+    ((3000, 1032), np.float16, True),    # 2064-byte rows, 129 packs
+    ((20000, 512), np.float32, True),    # 2 KiB rows: 16 warps per CTA
+    ((16384, 4096), np.float16, True),
+    ((149, 2048), np.float32, False),    # 8 KiB binary32 rows: register kernel
+    ((300, 12000), np.float32, False),   # wide rows: generic kernels
+    ((400, 18000), np.float16, False),
 ]
 
 
@@ -45,11 +46,12 @@ def softmax(ctx, x):
 
 @pytest.mark.parametrize("case", range(len(SHAPES)))
 def test_layer_norm(ctx, orc, case):
-    shape, dtype = SHAPES[case]
+    shape, dtype, piped = SHAPES[case]
     x = datagen.normal(70 + case, shape, 0.5, 2.0).astype(dtype)
     g = datagen.normal(80 + case, shape[-1:], 1.0, 0.1)
     b = datagen.normal(90 + case, shape[-1:], 0.0, 0.1)
     y = ln(ctx, x, g, b).astype(np.float64)
+    assert (ctx.last_kernel() == "k_layer_norm_pipe") == piped, ctx.last_kernel()
     ref = orc.layer_norm(x, g, b, 1e-5).astype(np.float64)
     tol = 1e-5 if dtype == np.float32 else 1e-3
     worst = np.max(np.abs(y - ref) / (tol * (1.0 + np.abs(ref))))
@@ -58,9 +60,10 @@ def test_layer_norm(ctx, orc, case):
 
 @pytest.mark.parametrize("case", range(len(SHAPES)))
 def test_softmax(ctx, orc, case):
-    shape, dtype = SHAPES[case]
+    shape, dtype, piped = SHAPES[case]
     x = datagen.normal(100 + case, shape, 0.5, 2.0).astype(dtype)
     got = softmax(ctx, x).astype(np.float64)
+    assert (ctx.last_kernel() == "k_softmax_pipe") == piped, ctx.last_kernel()
     ref = orc.softmax(x, -1)
     rtol, atol = (1e-5, 1e-30) if dtype == np.float32 else (1e-3, 1e-7)
     assert np.max(np.abs(got - ref) - rtol * ref) <= atol, (shape, dtype)
@@ -70,20 +73,21 @@ def test_softmax(ctx, orc, case):
 
 @pytest.mark.parametrize("dtype", [np.float32, np.float16])
 def test_softmax_special_rows(ctx, orc, dtype):
-    x = datagen.normal(111, (300, 2048), 0.0, 1.0).astype(np.float32)
+    x = datagen.normal(111, (300, 1024), 0.0, 1.0).astype(np.float32)
     x[5, 17] = np.nan
     x[6, :] = 2.5
     x[7, :] = -np.inf
     x[7, 100] = 0.0
-    x[7, 1999] = 0.0
+    x[7, 999] = 0.0
     x[8, 3] = np.inf
     x[9, 0] = 80.0
     x[9, 1] = -80.0
     x = x.astype(dtype)
     got = softmax(ctx, x)
+    assert ctx.last_kernel() == "k_softmax_pipe"
     assert np.all(np.isnan(got[5]))
-    assert np.all(got[6] == dtype(1.0 / 2048))
-    assert got[7][100] == dtype(0.5) and got[7][1999] == dtype(0.5)
+    assert np.all(got[6] == dtype(1.0 / 1024))
+    assert got[7][100] == dtype(0.5) and got[7][999] == dtype(0.5)
     assert np.count_nonzero(got[7]) == 2
     assert np.isnan(got[8][3])  # inf - inf
     ref = orc.softmax(x, -1)
@@ -99,6 +103,7 @@ def test_layer_norm_constant_rows_and_determinism(ctx, orc):
     g = np.ones(1024, np.float32)
     b = np.full(1024, 0.25, np.float32)
     y1 = ln(ctx, x, g, b)
+    assert ctx.last_kernel() == "k_layer_norm_pipe"
     y2 = ln(ctx, x, g, b)
     assert np.array_equal(y1.view(np.uint32), y2.view(np.uint32))
     assert np.all(y1[::3] == np.float32(0.25))
