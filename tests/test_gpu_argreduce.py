@@ -102,6 +102,26 @@ def test_nan_and_signed_zero_rules(ctx, orc):
     assert gpu_arg(ctx, abi.ARG_MIN, u, None)[0] == 2
 
 
+WORST_SHAPES = [((1000003,), None), ((8, 100000), -1), ((4096, 300), 1), ((8, 64, 256), 1), ((3, 1000, 7), 1)]
+
+
+@pytest.mark.parametrize("shape,axis", WORST_SHAPES)
+@pytest.mark.parametrize("dtype,op,fill", [
+    (np.float32, abi.ARG_MAX, -np.inf), (np.float32, abi.ARG_MIN, np.inf), (np.float16, abi.ARG_MAX, -np.inf),
+    (np.int32, abi.ARG_MAX, np.iinfo(np.int32).min), (np.int32, abi.ARG_MIN, np.iinfo(np.int32).max),
+    (np.uint32, abi.ARG_MAX, 0), (np.uint32, abi.ARG_MIN, np.iinfo(np.uint32).max), (np.int8, abi.ARG_MAX, -128)])
+def test_worst_values_every_kernel(ctx, orc, shape, axis, dtype, op, fill):
+    """Slices made only of the value every element is at least as good as
+    (every kernel starts its running best there), then one better element."""
+    x = np.full(shape, fill, dtype)
+    want = orc.argreduce(op, x, axis)
+    np.testing.assert_array_equal(gpu_arg(ctx, op, x, axis).reshape(-1), np.asarray(want).reshape(-1))
+    flat = x.reshape(-1)
+    flat[flat.size // 3] = np.array(7, dtype) if fill != 7 else np.array(8, dtype)
+    want = orc.argreduce(op, x, axis)
+    np.testing.assert_array_equal(gpu_arg(ctx, op, x, axis).reshape(-1), np.asarray(want).reshape(-1))
+
+
 def test_keepdims_and_u32_out(ctx, orc):
     x = make((6, 33, 40), np.float32, seed=9)
     got = gpu_arg(ctx, abi.ARG_MAX, x, 1, keepdims=True, out_dtype=np.uint32)
