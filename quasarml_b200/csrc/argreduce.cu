@@ -346,8 +346,11 @@ qsml_status_t run_arg(Context* ctx, const T* x, int64_t outer, int64_t k, int64_
     const int64_t tiles_per_o = (inner + 32 * pv - 1) / (32 * pv);
     const int64_t tiles = tiles_per_o * outer;
     if (tiles > INT32_MAX) return set_error(ctx, QSML_E_UNSUPPORTED, "qsml_arg_reduce: too large");
-    // enough warps in flight (~8192 per GPU), keys in at most 32 KiB of shared memory
-    int64_t W = (8192 + tiles - 1) / tiles;
+    // about 4096 warps per launch for 4-byte elements, more for narrower ones
+    // (more comparisons per 16-byte load); keys in at most 32 KiB of shared
+    // memory
+    const int64_t target = 4096 * (4 / static_cast<int64_t>(sizeof(T) < 4 ? sizeof(T) : 4));
+    int64_t W = (target + tiles - 1) / tiles;
     const int64_t w_smem = 32768 / (32 * pv * 8);
     if (W > 16) W = 16;
     if (W > w_smem) W = w_smem;
