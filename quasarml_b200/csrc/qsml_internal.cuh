@@ -88,6 +88,16 @@ __device__ __forceinline__ void pdl_begin() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Prefetch of `bytes` bytes (a multiple of 16, from a 16-byte aligned address)
+// into L2.  A hint: it moves no data into the thread and does not take part
+// in memory ordering (L2 is where global writes become coherent), so a kernel
+// may issue it before pdl_begin() to start its first DRAM reads while the
+// previous kernel on the stream drains; its loads after pdl_begin() still see
+// every write that kernel made.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                        Args&&... args) {

@@ -25,7 +25,10 @@
 //                       the CTA's 8 warps neighbouring spans of the same rows.
 // The kernels are launched with programmatic dependent launch (launch_pdl):
 // each waits for the previous kernel on the stream before touching memory, but
-// its CTAs are already resident when that kernel drains.
+// its CTAs are already resident when that kernel drains.  For binary16 inputs
+// (10-15 us launches) each warp first prefetches its first batch of loads into
+// L2, so DRAM reads start during that drain (measured on B200: +2 to +8 % for
+// binary16, a loss for the longer binary32 launches, which do not prefetch).
 // Accumulation is binary32 (binary16 inputs widen exactly); max/min use PTX
 // max.NaN/min.NaN, so the result is exact and order-free (IEEE 754-2019
 // maximum/minimum: -0 < +0, NaN wins as 0x7fffffff).
@@ -157,13 +160,23 @@ __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int
                                                     int64_t P, OT* __restrict__ out, float scale,
                                                     unsigned* __restrict__ counters,
                                                     typename Red<OP>::V* __restrict__ partials) {
-    pdl_begin();
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
     __shared__ bool s_last;
     const int t = threadIdx.x;
     const int64_t units = nseg * P;
+    if (VEC && sizeof(T) == 2 && t < kSegIters && blockIdx.x < units) {
+        // the first batch of this CTA's first slice: kSegIters blocks of 256 packs
+        const int64_t s = blockIdx.x / P, j = blockIdx.x - s * P;
+        const int64_t npk = len / PV;
+        const int64_t q = j * kRT + t * P * kRT;
+        if (q < npk) {
+            const int64_t n = npk - q < kRT ? npk - q : kRT;
+            prefetch_l2(reinterpret_cast<const Pack<T>*>(x + s * len) + q, static_cast<uint32_t>(n * 16));
+        }
+    }
+    pdl_begin();
     for (int64_t w = blockIdx.x; w < units; w += gridDim.x) {
         const int64_t s = w / P, j = w - s * P;
         const T* row = x + s * len;
@@ -225,12 +238,18 @@ __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int
 template <typename T, typename OT, int OP, bool VEC>
 __global__ void __launch_bounds__(256) k_reduce_rows(const T* __restrict__ x, int64_t rows, int64_t len,
                                                      OT* __restrict__ out, float scale) {
-    pdl_begin();
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
     constexpr int U = 4;
     const int lane = threadIdx.x & 31;
+    if (VEC && sizeof(T) == 2 && lane == 0) {
+        // this warp's first row, up to 16 KiB of it
+        const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        const int64_t bytes = (len / PV) * 16;
+        if (r < rows && bytes > 0) prefetch_l2(x + r * len, static_cast<uint32_t>(bytes < 16384 ? bytes : 16384));
+    }
+    pdl_begin();
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
         const T* row = x + r * len;
@@ -267,7 +286,6 @@ __global__ void __launch_bounds__(256) k_reduce_rows(const T* __restrict__ x, in
 template <typename T, typename OT, int OP, bool VEC>
 __global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k, int64_t inner,
                               int64_t tiles_per_o, OT* __restrict__ out, float scale) {
-    pdl_begin();
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = VEC ? Pack<T>::N : 1;
@@ -277,10 +295,17 @@ __global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k,
     const int lane = threadIdx.x, w = threadIdx.y, W = blockDim.y;
     const int64_t tile = blockIdx.x;
     const int64_t o = tile / tiles_per_o;
-    const int64_t c0 = (tile - o * tiles_per_o) * (32 * PV) + static_cast<int64_t>(lane) * PV;
+    const int64_t tc0 = (tile - o * tiles_per_o) * (32 * PV);
+    const int64_t c0 = tc0 + static_cast<int64_t>(lane) * PV;
     const int64_t kper = (k + W - 1) / W;
     const int64_t k0 = w * kper;
     const int64_t k1 = k0 + kper < k ? k0 + kper : k;
+    if (VEC && sizeof(T) == 2 && lane < U && k0 + lane < k1 && o < outer) {
+        // the warp's first batch: U rows of the tile's 32 x 16-byte span
+        const int64_t span = inner - tc0 < 32 * PV ? inner - tc0 : 32 * PV;
+        prefetch_l2(x + (o * k + k0 + lane) * inner + tc0, static_cast<uint32_t>(span * sizeof(T)));
+    }
+    pdl_begin();
     V acc[PV];
 #pragma unroll
     for (int e = 0; e < PV; ++e) acc[e] = R::ident();
@@ -337,7 +362,6 @@ template <typename T, typename OT, int OP>
 __global__ void __launch_bounds__(256) k_reduce_cols_wide(const T* __restrict__ x, int64_t outer, int64_t k,
                                                           int64_t inner, int64_t tiles_per_o, int64_t groups_per_o,
                                                           OT* __restrict__ out, float scale) {
-    pdl_begin();
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
@@ -348,6 +372,12 @@ __global__ void __launch_bounds__(256) k_reduce_cols_wide(const T* __restrict__ 
     const int64_t o = grp / groups_per_o;
     const int64_t span = (grp - o * groups_per_o) * 8 + w;  // tile within o
     const int64_t c0 = span * NCOL + static_cast<int64_t>(lane) * PV;
+    if (sizeof(T) == 2 && lane < U && lane < k && span < tiles_per_o) {
+        // the warp's first batch: U rows of its 32 x 16-byte span
+        const int64_t n = inner - span * NCOL < NCOL ? inner - span * NCOL : NCOL;
+        prefetch_l2(x + (o * k + lane) * inner + span * NCOL, static_cast<uint32_t>(n * sizeof(T)));
+    }
+    pdl_begin();
     if (span >= tiles_per_o || c0 >= inner) return;
     V acc[PV];
 #pragma unroll
