@@ -55,6 +55,8 @@ struct Rtc {
     CUresult (*get_function)(CUfunction*, CUmodule, const char*);
     CUresult (*launch)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream,
                        void**, void**);
+    // cuLaunchKernelEx, for programmatic dependent launch; null if absent
+    CUresult (*launch_ex)(const CUlaunchConfig*, CUfunction, void**, void**) = nullptr;
     std::string why;  // reason when !ok
 };
 
@@ -89,6 +91,7 @@ const Rtc& rtc() {
                   sym(lib, "nvrtcDestroyProgram", &t.destroy);
         ok = ok && drv("cuModuleLoadData", &t.load) && drv("cuModuleGetFunction", &t.get_function) &&
              drv("cuLaunchKernel", &t.launch);
+        if (!drv("cuLaunchKernelEx", &t.launch_ex)) t.launch_ex = nullptr;
         t.ok = ok;
         if (!ok) t.why = "NVRTC or driver entry points missing";
         return t;
@@ -144,6 +147,10 @@ std::string generate(const qsml_fuse_node* nodes, int n, const JitInput* ins, in
     s << "extern \"C\" __global__ void __launch_bounds__(" << kJitThreads << ") qsml_fused_kernel(";
     for (int j = 0; j < nin; ++j) s << "const " << T << "* __restrict__ p" << j << ", long long r" << j << ", ";
     s << T << "* __restrict__ out, unsigned items, unsigned cpr, unsigned magic, unsigned sh1, unsigned sh2) {\n";
+    // programmatic dependent launch: wait for the previous kernel on the stream
+    // before touching memory, then let the next one launch
+    s << "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
+    s << "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n";
     s << "  const int V = " << V << ", U = " << U << ";\n";
     s << "  const unsigned base = blockIdx.x * (" << kJitThreads << "u * U) + threadIdx.x;\n";
     for (int j = 0; j < nin; ++j) s << "  float x" << j << "[U * V];\n";
@@ -314,8 +321,27 @@ qsml_status_t fused_jit(Context* ctx, const qsml_fuse_node* nodes, int n_nodes, 
     args.push_back(&sh2);
     const int per_block = kJitThreads * (kJitElems / (half ? 8 : 4));
     const int64_t blocks = (items + per_block - 1) / per_block;
-    const CUresult lr = r.launch(fn, static_cast<unsigned>(blocks), 1, 1, kJitThreads, 1, 1, 0,
-                                 reinterpret_cast<CUstream>(ctx->stream), args.data(), nullptr);
+    CUresult lr;
+    if (r.launch_ex) {
+        CUlaunchAttribute attr[1];
+        std::memset(attr, 0, sizeof(attr));
+        attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+        attr[0].value.programmaticStreamSerializationAllowed = 1;
+        CUlaunchConfig cfg;
+        std::memset(&cfg, 0, sizeof(cfg));
+        cfg.gridDimX = static_cast<unsigned>(blocks);
+        cfg.gridDimY = cfg.gridDimZ = 1;
+        cfg.blockDimX = kJitThreads;
+        cfg.blockDimY = cfg.blockDimZ = 1;
+        cfg.sharedMemBytes = 0;
+        cfg.hStream = reinterpret_cast<CUstream>(ctx->stream);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        lr = r.launch_ex(&cfg, fn, args.data(), nullptr);
+    } else {
+        lr = r.launch(fn, static_cast<unsigned>(blocks), 1, 1, kJitThreads, 1, 1, 0,
+                      reinterpret_cast<CUstream>(ctx->stream), args.data(), nullptr);
+    }
     ctx->launches++;
     ctx->last_kernel = "qsml_fused_kernel";
     if (lr != CUDA_SUCCESS)
