@@ -109,3 +109,16 @@ def test_layer_norm_constant_rows_and_determinism(ctx, orc):
     assert np.all(y1[::3] == np.float32(0.25))
     ref = orc.layer_norm(x, g, b, 1e-5)
     assert np.max(np.abs(y1 - ref) / (1e-5 * (1.0 + np.abs(ref)))) <= 1.0
+
+
+def test_layer_norm_f16_params_and_few_rows(ctx, orc):
+    """binary16 gamma/beta through the streamed kernel, and fewer rows than SMs
+    (one warp per CTA)."""
+    for shape in ((2000, 1024), (5, 2048)):
+        x = datagen.normal(113, shape, 0.5, 2.0).astype(np.float16)
+        g = datagen.normal(114, shape[-1:], 1.0, 0.1).astype(np.float16)
+        b = datagen.normal(115, shape[-1:], 0.0, 0.1).astype(np.float16)
+        y = ln(ctx, x, g, b).astype(np.float64)
+        assert ctx.last_kernel() == "k_layer_norm_pipe"
+        ref = orc.layer_norm(x, g.astype(np.float32), b.astype(np.float32), 1e-5).astype(np.float64)
+        assert np.max(np.abs(y - ref) / (1e-3 * (1.0 + np.abs(ref)))) <= 1.0, shape
