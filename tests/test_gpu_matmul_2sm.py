@@ -60,6 +60,19 @@ def test_batched_shared_b(ctx, orc, kernel):
         assert err <= 1e-5, (kernel, i, err)
 
 
+def test_batched_shared_a(ctx, orc, kernel):
+    a = datagen.uniform(67, (200, 136), -1, 1).astype(np.float16)
+    b = datagen.uniform(68, (5, 136, 520), -1, 1).astype(np.float16)
+    ta = dev(a)
+    aview = abi.make_desc(ta.data_ptr(), abi.F16, (5, 200, 136), (0, 136, 1))
+    c = empty((5, 200, 520), np.float32)
+    ctx.matmul(aview, d(dev(b)), d(c), abi.MM_FP16_F32ACC)
+    got = host(c).astype(np.float64)
+    for i in range(5):
+        ref = orc.matmul_f64(a, b[i])
+        assert np.max(np.abs(got[i] - ref)) / np.max(np.abs(ref)) <= 1e-5, (kernel, i)
+
+
 def test_kernels_agree(ctx, monkeypatch):
     s = 1.0 / np.sqrt(1024.0)
     a = datagen.uniform(65, (4, 1024, 1024), -s, s).astype(np.float16)
