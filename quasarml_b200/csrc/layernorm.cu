@@ -10,6 +10,8 @@
 // read once and y written once; gamma/beta stay in shared memory.  The row
 // statistics are two block sums (row sum, then squared deviations from the
 // mean), so the variance is a true two-pass variance.
+// k_layer_norm_wide: rows of 32-108 KiB, one CTA per row, rows streamed
+// through two shared-memory buffers.
 // k_layer_norm_generic: any width or alignment, Welford over global memory
 // (reads x twice).
 #include "qsml_internal.cuh"
@@ -75,6 +77,27 @@ __device__ __forceinline__ Pack<T> to_pack(const float* z) {
         }
     }
     return o;
+}
+
+// PV consecutive gamma/beta values as binary32, with 16-byte loads from global
+// memory (read-only path).
+template <typename GT, int PV>
+__device__ __forceinline__ void load_pack_params(const GT* p, float* out) {
+    if constexpr (sizeof(GT) == 4) {
+#pragma unroll
+        for (int i = 0; i < PV; i += 4) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(p + i));
+            out[i] = v.x; out[i + 1] = v.y; out[i + 2] = v.z; out[i + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < PV; i += 8) {
+            const uint4 u = __ldg(reinterpret_cast<const uint4*>(p + i));
+            const __half* h = reinterpret_cast<const __half*>(&u);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) out[i + e] = __half2float(h[e]);
+        }
+    }
 }
 
 // Block-wide binary32 sum: xor butterflies inside warps, one slot per warp,
@@ -265,6 +288,70 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
     if (!ok && lane == 0) atomicExch(status, QSML_E_TIMEOUT);
 }
 
+// Rows of 32-108 KiB: one CTA of 512 threads per row, rows streamed through
+// two shared-memory buffers (row_pipe.cuh, stream_rows_cta): the sum, the
+// squared deviations from the mean and the output as three passes over the
+// buffer; gamma/beta are read from global memory (L2-resident after the first
+// row) with 16-byte loads.
+template <typename T, typename GT>
+__global__ void __launch_bounds__(512) k_layer_norm_wide(const T* __restrict__ x, const GT* __restrict__ gamma,
+                                                         const GT* __restrict__ beta, T* __restrict__ y,
+                                                         int64_t rows, int cols, float eps, int* status) {
+    pdl_begin();
+    constexpr int PV = Pack<T>::N;
+    extern __shared__ float4 ln_wide_smem[];
+    __shared__ uint64_t bars[2];
+    __shared__ float s_sum[32], s_dev[32];
+    const int packs = cols / PV, t = threadIdx.x, th = blockDim.x;
+    const float n = static_cast<float>(cols);
+    const bool ok = rowpipe::stream_rows_cta(
+        reinterpret_cast<const unsigned char*>(x), rows, static_cast<uint32_t>(cols * sizeof(T)),
+        reinterpret_cast<unsigned char*>(ln_wide_smem), bars, [&](int64_t row, unsigned char* buf) {
+            const Pack<T>* xs = reinterpret_cast<const Pack<T>*>(buf);
+            float part[PV];
+#pragma unroll
+            for (int e = 0; e < PV; ++e) part[e] = 0.0f;
+#pragma unroll 2
+            for (int p = t; p < packs; p += th) {
+                const Pack<T> v = xs[p];
+#pragma unroll
+                for (int e = 0; e < PV; ++e) part[e] = __fadd_rn(part[e], to_f(v.v[e]));
+            }
+            float s = part[0];
+#pragma unroll
+            for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
+            const float mean = __fdiv_rn(rowpipe::cta_combine<false>(s, s_sum), n);
+#pragma unroll
+            for (int e = 0; e < PV; ++e) part[e] = 0.0f;
+#pragma unroll 2
+            for (int p = t; p < packs; p += th) {
+                const Pack<T> v = xs[p];
+#pragma unroll
+                for (int e = 0; e < PV; ++e) {
+                    const float d = __fsub_rn(to_f(v.v[e]), mean);
+                    part[e] = __fmaf_rn(d, d, part[e]);
+                }
+            }
+            float q = part[0];
+#pragma unroll
+            for (int e = 1; e < PV; ++e) q = __fadd_rn(q, part[e]);
+            const float var = __fdiv_rn(rowpipe::cta_combine<false>(q, s_dev), n);
+            const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+            Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
+            for (int p = t; p < packs; p += th) {
+                const Pack<T> v = xs[p];
+                float g[PV], b[PV];
+                load_pack_params<GT, PV>(gamma + static_cast<int64_t>(p) * PV, g);
+                load_pack_params<GT, PV>(beta + static_cast<int64_t>(p) * PV, b);
+                float z[PV];
+#pragma unroll
+                for (int e = 0; e < PV; ++e) z[e] = __fmaf_rn(__fmul_rn(__fsub_rn(to_f(v.v[e]), mean), rstd), g[e], b[e]);
+                yr[p] = to_pack<T>(z);
+            }
+        });
+    if (!ok && t == 0) atomicExch(status, QSML_E_TIMEOUT);
+}
+
 template <typename T, typename GT>
 __global__ void __launch_bounds__(256) k_layer_norm_generic(const T* __restrict__ x, const GT* __restrict__ gamma,
                                                             const GT* __restrict__ beta, T* __restrict__ y,
@@ -388,6 +475,30 @@ qsml_status_t launch_pipe(Context* ctx, const T* x, const GT* g, const GT* b, T*
 }
 
 template <typename T, typename GT>
+qsml_status_t launch_wide(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int cols,
+                          float eps) {
+    const size_t smem = 2 * static_cast<size_t>(cols) * sizeof(T);
+    static std::mutex mu;
+    static bool attr_set = false;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_set) {
+            QSML_TRY_STATUS(check_cuda(ctx,
+                                       cudaFuncSetAttribute(k_layer_norm_wide<T, GT>,
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                            static_cast<int>(2 * rowpipe::kWideMaxRowBytes)),
+                                       "layer norm: shared-memory attribute"));
+            attr_set = true;
+        }
+    }
+    const int64_t grid = rows < ctx->num_sms ? rows : ctx->num_sms;
+    const cudaError_t e = launch_pdl(k_layer_norm_wide<T, GT>, dim3(static_cast<unsigned>(grid)), dim3(512), smem,
+                                     ctx->stream, x, g, b, y, rows, cols, eps, ctx->status);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "k_layer_norm_wide");
+    return after_launch(ctx, "k_layer_norm_wide");
+}
+
+template <typename T, typename GT>
 qsml_status_t run_ln(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int64_t cols, float eps) {
     constexpr int PV = Pack<T>::N;
     rowpipe::Plan plan;
@@ -417,6 +528,10 @@ qsml_status_t run_ln(Context* ctx, const T* x, const GT* g, const GT* b, T* y, i
             }
         }
     }
+    const uint64_t row_bytes = static_cast<uint64_t>(cols) * sizeof(T);
+    if (rowpipe::use_wide(row_bytes) && row_bytes % 16 == 0 && cols % PV == 0 && aligned16(x) && aligned16(y) &&
+        aligned16(g) && aligned16(b) && ctx->status)
+        return launch_wide<T, GT>(ctx, x, g, b, y, rows, static_cast<int>(cols), eps);
     int64_t grid = rows < 65535 * 16 ? rows : 65535 * 16;
     k_layer_norm_generic<T, GT><<<static_cast<unsigned>(grid), 256, 0, ctx->stream>>>(x, g, b, y, rows, cols, eps);
     return after_launch(ctx, "k_layer_norm_generic");

@@ -134,6 +134,86 @@ inline bool use_pipe(uint64_t row_bytes, uint32_t elem_bytes) {
     return row_bytes >= kMinRowBytes && row_bytes <= max_bytes;
 }
 
+// Wide rows (tens of KiB): the whole CTA works on one row at a time, held in
+// one of two shared-memory buffers; while it reduces row i from one buffer,
+// the bulk copy of its next row fills the other.  Same bounded waits as
+// stream_rows; body(row, buffer) is called by every thread of the CTA and
+// must end with the buffer no longer being read by any thread.
+constexpr uint32_t kWideMinRowBytes = 32 * 1024 + 16;  // beyond the register kernels
+constexpr size_t kWideMaxRowBytes = 108 * 1024;        // two buffers in ~216 KiB
+
+template <class Body>
+__device__ bool stream_rows_cta(const unsigned char* src, int64_t rows, uint32_t row_bytes, unsigned char* ring,
+                                uint64_t* bars, Body&& body) {
+    const int64_t G = gridDim.x;
+    const uint32_t bar0 = smem_addr(bars);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 2; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8u * s) : "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int s = 0; s < 2; ++s) {
+            const int64_t r = blockIdx.x + s * G;
+            if (r < rows) fill(smem_addr(ring + s * row_bytes), src + r * row_bytes, row_bytes, bar0 + 8u * s);
+        }
+    }
+    __syncthreads();
+    int64_t i = 0;
+    for (int64_t row = blockIdx.x; row < rows; row += G, ++i) {
+        const int s = static_cast<int>(i & 1);
+        const uint32_t parity = static_cast<uint32_t>((i >> 1) & 1);
+        const bool landed = bar_wait(bar0 + 8u * s, parity);
+        if (__syncthreads_or(!landed)) {
+            // the other buffer's copy (if any) lands before the CTA exits
+            if (threadIdx.x == 0 && row + G < rows) {
+                const long long t0 = clock64();
+                while (!bar_test(bar0 + 8u * (s ^ 1), static_cast<uint32_t>(((i + 1) >> 1) & 1)) &&
+                       clock64() - t0 < kWaitCycles) {
+                }
+            }
+            return false;
+        }
+        unsigned char* buf = ring + s * row_bytes;
+        body(row, buf);
+        __syncthreads();  // every thread is done with the buffer
+        const int64_t next = row + 2 * G;
+        if (threadIdx.x == 0 && next < rows) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            fill(smem_addr(buf), src + next * row_bytes, row_bytes, bar0 + 8u * s);
+        }
+    }
+    return true;
+}
+
+// Block-wide sum or max over the CTA (at most 32 warps): warp butterflies,
+// one slot per warp, every thread combines the slots in warp order (same bits
+// everywhere).  `slot` must not be reused before every thread has returned:
+// callers alternate two slot arrays.
+template <bool MAX>
+__device__ __forceinline__ float cta_combine(float v, float* slot) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+        const float o = __shfl_xor_sync(0xffffffffu, v, m);
+        if (MAX) {
+            asm("max.NaN.f32 %0, %1, %2;" : "=f"(v) : "f"(v), "f"(o));
+        } else {
+            v = __fadd_rn(v, o);
+        }
+    }
+    if (lane == 0) slot[w] = v;
+    __syncthreads();
+    float a = slot[0];
+    for (int j = 1; j < nw; ++j) {
+        if (MAX) {
+            asm("max.NaN.f32 %0, %1, %2;" : "=f"(a) : "f"(a), "f"(slot[j]));
+        } else {
+            a = __fadd_rn(a, slot[j]);
+        }
+    }
+    return a;
+}
+
+inline bool use_wide(uint64_t row_bytes) { return row_bytes >= kWideMinRowBytes && row_bytes <= kWideMaxRowBytes; }
+
 // Launch shape: one CTA per SM, `warps` warps with `slots` buffers each, the
 // op's per-CTA parameters (`param_bytes`, e.g. gamma and beta) in front of
 // the buffers.

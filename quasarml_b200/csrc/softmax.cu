@@ -15,6 +15,8 @@
 //   * k_softmax_rows -- last axis, wider rows held in registers (16-byte
 //     loads): persistent CTAs with the next two rows in flight, so x is read
 //     once and y written once;
+//   * k_softmax_wide -- last axis, rows of 32-108 KiB: one CTA per row, rows
+//     streamed through two shared-memory buffers (row_pipe.cuh);
 //   * k_softmax_rows_generic -- last axis, any width: one CTA per row, three
 //     passes over global memory (max, sum, write);
 //   * k_softmax_long_{max,sum,out} -- last axis, fewer rows than SMs and long
@@ -176,14 +178,14 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const T* __restrict__ x, T
 // and the output; binary16 rows recompute it (the same function in both
 // passes, so the sum and the outputs agree).
 template <typename T>
-__device__ __forceinline__ float pack_max(const Pack<T>* xs, int packs, int lane) {
+__device__ __forceinline__ float pack_max(const Pack<T>* xs, int packs, int lane, int stride = 32) {
     constexpr int PV = Pack<T>::N;
     if constexpr (sizeof(T) == 4) {
         float part[PV];
 #pragma unroll
         for (int e = 0; e < PV; ++e) part[e] = -INFINITY;
 #pragma unroll 4
-        for (int p = lane; p < packs; p += 32) {
+        for (int p = lane; p < packs; p += stride) {
             const Pack<T> v = xs[p];
 #pragma unroll
             for (int e = 0; e < PV; ++e) part[e] = max_nan(part[e], v.v[e]);
@@ -197,7 +199,7 @@ __device__ __forceinline__ float pack_max(const Pack<T>* xs, int packs, int lane
 #pragma unroll
         for (int e = 0; e < PV / 2; ++e) part[e] = __float2half2_rn(-INFINITY);
 #pragma unroll 4
-        for (int p = lane; p < packs; p += 32) {
+        for (int p = lane; p < packs; p += stride) {
             const Pack<T> v = xs[p];
             const __half2* h = reinterpret_cast<const __half2*>(v.v);
 #pragma unroll
@@ -257,6 +259,58 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
             }
         });
     if (!ok && lane == 0) atomicExch(status, QSML_E_TIMEOUT);
+}
+
+// Rows of 32-108 KiB: one CTA of 512 threads per row, rows streamed through
+// two shared-memory buffers (row_pipe.cuh, stream_rows_cta): the max, the sum
+// of exp(x - max) and the output as three passes over the buffer, each thread
+// striding over the row's 16-byte packs.
+template <typename T>
+__global__ void __launch_bounds__(512) k_softmax_wide(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
+                                                      int cols, int* status) {
+    pdl_begin();
+    constexpr int PV = Pack<T>::N;
+    constexpr bool F32 = sizeof(T) == 4;
+    extern __shared__ float4 sm_wide_smem[];
+    __shared__ uint64_t bars[2];
+    __shared__ float s_max[32], s_sum[32];
+    const int packs = cols / PV, t = threadIdx.x, th = blockDim.x;
+    const bool ok = rowpipe::stream_rows_cta(
+        reinterpret_cast<const unsigned char*>(x), rows, static_cast<uint32_t>(cols * sizeof(T)),
+        reinterpret_cast<unsigned char*>(sm_wide_smem), bars, [&](int64_t row, unsigned char* buf) {
+            Pack<T>* xs = reinterpret_cast<Pack<T>*>(buf);
+            const float m = rowpipe::cta_combine<true>(pack_max<T>(xs, packs, t, th), s_max);
+            const float mk = __fmul_rn(m, 1.4426950408889634f);
+            float part[PV];
+#pragma unroll
+            for (int e = 0; e < PV; ++e) part[e] = 0.0f;
+#pragma unroll 2
+            for (int p = t; p < packs; p += th) {
+                Pack<T> v = xs[p];
+#pragma unroll
+                for (int e = 0; e < PV; ++e) {
+                    const float ex = row_exp<T>(to_f(v.v[e]), m, mk);
+                    part[e] = __fadd_rn(part[e], ex);
+                    if constexpr (F32) from_f(ex, &v.v[e]);
+                }
+                if constexpr (F32) xs[p] = v;
+            }
+            float s = part[0];
+#pragma unroll
+            for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
+            const float inv = __frcp_rn(rowpipe::cta_combine<false>(s, s_sum));
+            Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
+#pragma unroll 2
+            for (int p = t; p < packs; p += th) {
+                const Pack<T> v = xs[p];
+                float z[PV];
+#pragma unroll
+                for (int e = 0; e < PV; ++e)
+                    z[e] = __fmul_rn(F32 ? to_f(v.v[e]) : row_exp<T>(to_f(v.v[e]), m, mk), inv);
+                yr[p] = to_pack<T>(z);
+            }
+        });
+    if (!ok && t == 0) atomicExch(status, QSML_E_TIMEOUT);
 }
 
 template <typename T>
@@ -440,6 +494,28 @@ qsml_status_t launch_pipe(Context* ctx, const T* x, T* y, int64_t rows, int cols
 }
 
 template <typename T>
+qsml_status_t launch_wide(Context* ctx, const T* x, T* y, int64_t rows, int cols) {
+    const size_t smem = 2 * static_cast<size_t>(cols) * sizeof(T);
+    static std::mutex mu;
+    static bool attr_set = false;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!attr_set) {
+            QSML_TRY_STATUS(check_cuda(ctx,
+                                       cudaFuncSetAttribute(k_softmax_wide<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                            static_cast<int>(2 * rowpipe::kWideMaxRowBytes)),
+                                       "softmax: shared-memory attribute"));
+            attr_set = true;
+        }
+    }
+    const int64_t grid = rows < ctx->num_sms ? rows : ctx->num_sms;
+    const cudaError_t e = launch_pdl(k_softmax_wide<T>, dim3(static_cast<unsigned>(grid)), dim3(512), smem, ctx->stream,
+                                     x, y, rows, cols, ctx->status);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "k_softmax_wide");
+    return after_launch(ctx, "k_softmax_wide");
+}
+
+template <typename T>
 qsml_status_t run_softmax(Context* ctx, const T* x, T* y, int64_t outer, int64_t k, int64_t inner) {
     constexpr int PV = Pack<T>::N;
     if (inner == 1) {
@@ -472,6 +548,9 @@ qsml_status_t run_softmax(Context* ctx, const T* x, T* y, int64_t outer, int64_t
         }
         // Few long rows: a CTA per row would leave most SMs idle.
         if (rows < ctx->num_sms && cols >= 16384) return run_long_rows<T>(ctx, x, y, rows, cols);
+        const uint64_t row_bytes = static_cast<uint64_t>(cols) * sizeof(T);
+        if (rowpipe::use_wide(row_bytes) && row_bytes % 16 == 0 && aligned16(x) && aligned16(y) && ctx->status)
+            return launch_wide<T>(ctx, x, y, rows, static_cast<int>(cols));
         int64_t grid = rows < int64_t(ctx->num_sms) * 16 ? rows : int64_t(ctx->num_sms) * 16;
         const unsigned th = cols >= 256 ? 256 : (cols >= 128 ? 128 : (cols >= 64 ? 64 : 32));
         k_softmax_rows_generic<T><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, y, rows, cols);

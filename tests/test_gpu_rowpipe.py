@@ -1,10 +1,8 @@
-"""Layer norm and last-axis softmax on rows streamed through shared memory
-(one warp per row, bulk copies into per-warp buffers).
-
-Rows of 2-8 KiB (binary16) or 2-4 KiB (binary32) whose size is a multiple of
-16 bytes take this path; the shapes below also include wider rows, which
-take the register-resident or the generic kernels, and each case checks
-which kernel ran (qsml_last_kernel).  Covered: rows whose 16-byte packs do
+"""Layer norm and last-axis softmax on rows streamed through shared memory by
+bulk copies: one warp per row for rows of 2-8 KiB (binary16) or 2-4 KiB
+(binary32), one CTA per row for rows of 32-108 KiB.  The shapes below also
+include rows that take the register-resident or the generic kernels, and each
+case checks which kernel ran (qsml_last_kernel).  Covered: rows whose 16-byte packs do
 not divide evenly over the 32 lanes, rows just above and far above the SM
 count, 16 warps per CTA, and special values.  Bars as in the other layer
 norm and softmax tests: binary32 |y - ref| <= 1e-5 * (1 + |ref|) (layer norm)
@@ -18,15 +16,19 @@ from quasarml_b200 import abi, datagen
 
 pytestmark = pytest.mark.gpu
 
-# (shape, dtype, streamed through shared memory?)
+# (shape, dtype, kernel family: "pipe" = a warp per row, "wide" = a CTA per row,
+# both streamed through shared memory; None = the register or generic kernels)
 SHAPES = [
-    ((5000, 1000), np.float32, True),    # 4000-byte rows, 250 packs: ragged over the lanes
-    ((3000, 1032), np.float16, True),    # 2064-byte rows, 129 packs
-    ((20000, 512), np.float32, True),    # 2 KiB rows: 16 warps per CTA
-    ((16384, 4096), np.float16, True),
-    ((149, 2048), np.float32, False),    # 8 KiB binary32 rows: register kernel
-    ((300, 12000), np.float32, False),   # wide rows: generic kernels
-    ((400, 18000), np.float16, False),
+    ((5000, 1000), np.float32, "pipe"),    # 4000-byte rows, 250 packs: ragged over the lanes
+    ((3000, 1032), np.float16, "pipe"),    # 2064-byte rows, 129 packs
+    ((20000, 512), np.float32, "pipe"),    # 2 KiB rows: 16 warps per CTA
+    ((16384, 4096), np.float16, "pipe"),
+    ((149, 2048), np.float32, None),       # 8 KiB binary32 rows: register kernel
+    ((300, 12000), np.float32, "wide"),    # 48,000-byte rows
+    ((400, 18000), np.float16, "wide"),    # 36,000-byte rows
+    ((1024, 16384), np.float32, "wide"),   # 64 KiB rows
+    ((160, 27648), np.float32, "wide"),    # 108 KiB rows: the widest streamed
+    ((50, 27652), np.float32, None),       # wider: generic kernels
 ]
 
 
@@ -46,12 +48,14 @@ def softmax(ctx, x):
 
 @pytest.mark.parametrize("case", range(len(SHAPES)))
 def test_layer_norm(ctx, orc, case):
-    shape, dtype, piped = SHAPES[case]
+    shape, dtype, family = SHAPES[case]
     x = datagen.normal(70 + case, shape, 0.5, 2.0).astype(dtype)
     g = datagen.normal(80 + case, shape[-1:], 1.0, 0.1)
     b = datagen.normal(90 + case, shape[-1:], 0.0, 0.1)
     y = ln(ctx, x, g, b).astype(np.float64)
-    assert (ctx.last_kernel() == "k_layer_norm_pipe") == piped, ctx.last_kernel()
+    want = {"pipe": "k_layer_norm_pipe", "wide": "k_layer_norm_wide"}.get(family)
+    assert ctx.last_kernel() == want if want else ctx.last_kernel() not in ("k_layer_norm_pipe", "k_layer_norm_wide"), \
+        ctx.last_kernel()
     ref = orc.layer_norm(x, g, b, 1e-5).astype(np.float64)
     tol = 1e-5 if dtype == np.float32 else 1e-3
     worst = np.max(np.abs(y - ref) / (tol * (1.0 + np.abs(ref))))
@@ -60,10 +64,12 @@ def test_layer_norm(ctx, orc, case):
 
 @pytest.mark.parametrize("case", range(len(SHAPES)))
 def test_softmax(ctx, orc, case):
-    shape, dtype, piped = SHAPES[case]
+    shape, dtype, family = SHAPES[case]
     x = datagen.normal(100 + case, shape, 0.5, 2.0).astype(dtype)
     got = softmax(ctx, x).astype(np.float64)
-    assert (ctx.last_kernel() == "k_softmax_pipe") == piped, ctx.last_kernel()
+    want = {"pipe": "k_softmax_pipe", "wide": "k_softmax_wide"}.get(family)
+    assert ctx.last_kernel() == want if want else ctx.last_kernel() not in ("k_softmax_pipe", "k_softmax_wide"), \
+        ctx.last_kernel()
     ref = orc.softmax(x, -1)
     rtol, atol = (1e-5, 1e-30) if dtype == np.float32 else (1e-3, 1e-7)
     assert np.max(np.abs(got - ref) - rtol * ref) <= atol, (shape, dtype)
