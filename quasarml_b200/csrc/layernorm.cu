@@ -293,12 +293,26 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
 // squared deviations from the mean and the output as three passes over the
 // buffer; gamma/beta are read from global memory (L2-resident after the first
 // row) with 16-byte loads.
-template <typename T, typename GT>
+// With REG > 0 (rows of at most 512 * REG packs) each thread keeps the
+// gamma/beta of its packs in registers for all its rows instead.
+template <typename T, typename GT, int REG>
 __global__ void __launch_bounds__(512) k_layer_norm_wide(const T* __restrict__ x, const GT* __restrict__ gamma,
                                                          const GT* __restrict__ beta, T* __restrict__ y,
                                                          int64_t rows, int cols, float eps, int* status) {
     pdl_begin();
     constexpr int PV = Pack<T>::N;
+    float rg[REG > 0 ? REG : 1][PV], rb[REG > 0 ? REG : 1][PV];
+    if constexpr (REG > 0) {
+        const int packs = cols / PV;
+#pragma unroll
+        for (int j = 0; j < REG; ++j) {
+            const int p = static_cast<int>(threadIdx.x) + j * static_cast<int>(blockDim.x);
+            if (p < packs) {
+                load_pack_params<GT, PV>(gamma + static_cast<int64_t>(p) * PV, rg[j]);
+                load_pack_params<GT, PV>(beta + static_cast<int64_t>(p) * PV, rb[j]);
+            }
+        }
+    }
     extern __shared__ float4 ln_wide_smem[];
     __shared__ uint64_t bars[2];
     __shared__ float s_sum[32], s_dev[32];
@@ -338,15 +352,31 @@ __global__ void __launch_bounds__(512) k_layer_norm_wide(const T* __restrict__ x
             const float var = __fdiv_rn(rowpipe::cta_combine<false>(q, s_dev), n);
             const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
             Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
-            for (int p = t; p < packs; p += th) {
-                const Pack<T> v = xs[p];
-                float g[PV], b[PV];
-                load_pack_params<GT, PV>(gamma + static_cast<int64_t>(p) * PV, g);
-                load_pack_params<GT, PV>(beta + static_cast<int64_t>(p) * PV, b);
-                float z[PV];
+            if constexpr (REG > 0) {
 #pragma unroll
-                for (int e = 0; e < PV; ++e) z[e] = __fmaf_rn(__fmul_rn(__fsub_rn(to_f(v.v[e]), mean), rstd), g[e], b[e]);
-                yr[p] = to_pack<T>(z);
+                for (int j = 0; j < REG; ++j) {
+                    const int p = t + j * th;
+                    if (p < packs) {
+                        const Pack<T> v = xs[p];
+                        float z[PV];
+#pragma unroll
+                        for (int e = 0; e < PV; ++e)
+                            z[e] = __fmaf_rn(__fmul_rn(__fsub_rn(to_f(v.v[e]), mean), rstd), rg[j][e], rb[j][e]);
+                        yr[p] = to_pack<T>(z);
+                    }
+                }
+            } else {
+                for (int p = t; p < packs; p += th) {
+                    const Pack<T> v = xs[p];
+                    float g[PV], b[PV];
+                    load_pack_params<GT, PV>(gamma + static_cast<int64_t>(p) * PV, g);
+                    load_pack_params<GT, PV>(beta + static_cast<int64_t>(p) * PV, b);
+                    float z[PV];
+#pragma unroll
+                    for (int e = 0; e < PV; ++e)
+                        z[e] = __fmaf_rn(__fmul_rn(__fsub_rn(to_f(v.v[e]), mean), rstd), g[e], b[e]);
+                    yr[p] = to_pack<T>(z);
+                }
             }
         });
     if (!ok && t == 0) atomicExch(status, QSML_E_TIMEOUT);
@@ -474,9 +504,9 @@ qsml_status_t launch_pipe(Context* ctx, const T* x, const GT* g, const GT* b, T*
     return after_launch(ctx, "k_layer_norm_pipe");
 }
 
-template <typename T, typename GT>
-qsml_status_t launch_wide(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int cols,
-                          float eps) {
+template <typename T, typename GT, int REG>
+qsml_status_t launch_wide_as(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int cols,
+                             float eps) {
     const size_t smem = 2 * static_cast<size_t>(cols) * sizeof(T);
     static std::mutex mu;
     static bool attr_set = false;
@@ -484,7 +514,7 @@ qsml_status_t launch_wide(Context* ctx, const T* x, const GT* g, const GT* b, T*
         std::lock_guard<std::mutex> lk(mu);
         if (!attr_set) {
             QSML_TRY_STATUS(check_cuda(ctx,
-                                       cudaFuncSetAttribute(k_layer_norm_wide<T, GT>,
+                                       cudaFuncSetAttribute(k_layer_norm_wide<T, GT, REG>,
                                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                             static_cast<int>(2 * rowpipe::kWideMaxRowBytes)),
                                        "layer norm: shared-memory attribute"));
@@ -492,10 +522,18 @@ qsml_status_t launch_wide(Context* ctx, const T* x, const GT* g, const GT* b, T*
         }
     }
     const int64_t grid = rows < ctx->num_sms ? rows : ctx->num_sms;
-    const cudaError_t e = launch_pdl(k_layer_norm_wide<T, GT>, dim3(static_cast<unsigned>(grid)), dim3(512), smem,
-                                     ctx->stream, x, g, b, y, rows, cols, eps, ctx->status);
+    const cudaError_t e = launch_pdl(k_layer_norm_wide<T, GT, REG>, dim3(static_cast<unsigned>(grid)), dim3(512),
+                                     smem, ctx->stream, x, g, b, y, rows, cols, eps, ctx->status);
     if (e != cudaSuccess) return check_cuda(ctx, e, "k_layer_norm_wide");
     return after_launch(ctx, "k_layer_norm_wide");
+}
+
+// gamma/beta in registers when a thread has at most 8 packs of the row.
+template <typename T, typename GT>
+qsml_status_t launch_wide(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int cols,
+                          float eps) {
+    if (cols / Pack<T>::N <= 512 * 8) return launch_wide_as<T, GT, 8>(ctx, x, g, b, y, rows, cols, eps);
+    return launch_wide_as<T, GT, 0>(ctx, x, g, b, y, rows, cols, eps);
 }
 
 template <typename T, typename GT>
