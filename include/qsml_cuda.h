@@ -360,10 +360,10 @@ QSML_API qsml_status_t qsml_group_destroy(qsml_group* group);
 
 /* Allocation-free sum / mean / max / min over all elements (axis =
  * QSML_AXIS_ALL) or over an axis followed only by unit dims, for callers that
- * cannot allocate device memory at that point: work enqueued while a stream
- * is being captured into a CUDA graph (cudaMalloc is not allowed there),
- * latency-critical paths that must not block in the driver's allocator, and
- * hosts whose own allocator already owns all of HBM.  It needs no qsml_ctx:
+ * cannot allocate device memory at that point: latency-critical paths that
+ * must not block in the driver's allocator (cudaMalloc and cudaFree can
+ * synchronise the device), hosts whose own allocator already owns all of
+ * HBM, and plugins handed only a stream.  It needs no qsml_ctx:
  * it enqueues on `stream` (a cudaStream_t of the current device; NULL = the
  * legacy default stream) and never calls cudaMalloc, cudaFree or any
  * allocating routine.  Results are bit-identical to qsml_reduce's segment
@@ -375,7 +375,7 @@ QSML_API qsml_status_t qsml_group_destroy(qsml_group* group);
  * message).  The first call on a device looks up that array's device address
  * (cudaGetSymbolAddress), so make that first call before any stream capture.
  * All calls share the array and clear its counters before each launch:
- * calls whose work overlaps on the GPU race on it.  Errors are reported
+ * calls on the same GPU whose work overlaps race on it.  Errors are reported
  * through qsml_last_error(NULL).  No counterpart in the reference. */
 QSML_API qsml_status_t qsml_reduce_noalloc(void* stream, int32_t op, const qsml_tdesc* a, int32_t axis,
                                            int32_t keepdims, const qsml_tdesc* out);

@@ -554,11 +554,12 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
 // ---------------------------------------------------------------------------
 // Allocation-free entry point.
 //
-// Some callers cannot allocate device memory when they reduce: code that
-// enqueues work while a stream is being captured into a CUDA graph (where
-// cudaMalloc is not allowed), latency-critical serving paths that must not
-// block on the driver's allocator, and host frameworks whose allocator
-// already owns every byte of HBM.  qsml_reduce_noalloc gives them the
+// Some callers cannot allocate device memory when they reduce:
+// latency-critical serving paths that must not block on the driver's
+// allocator (cudaMalloc and cudaFree can synchronise the device), host
+// frameworks whose own allocator already owns every byte of HBM, and plugins
+// that are handed only a stream and hold no qsml_ctx with its scratch
+// buffer.  qsml_reduce_noalloc gives them the
 // segment reduction with its scratch (ticket counters + partials) in the
 // fixed device array below instead of the context's scratch buffer, and it
 // needs no qsml_ctx at all -- only the caller's stream.
@@ -569,8 +570,8 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
 // cudaGetSymbolAddress once per device (first call on that device, with the
 // device current) and passed to the kernel.  All calls share the array and it
 // keeps the last call's contents, so the counters are cleared before every
-// launch; calls whose work overlaps on the GPU (different streams, or
-// concurrent devices sharing nothing but a stream) race on it.
+// launch; calls on the same GPU whose work overlaps (on different streams,
+// say) race on it.
 // ---------------------------------------------------------------------------
 namespace qsml {
 namespace {

@@ -1,9 +1,9 @@
 """qsml_reduce_noalloc: the reduction entry point that allocates nothing.
 
 It serves callers that cannot allocate device memory when they reduce --
-work enqueued during CUDA-graph capture, latency-critical serving paths, hosts
-whose allocator owns all of HBM -- by keeping its scratch in a fixed device
-array inside libqsml_cuda.so.  This file is named to be collected last.
+latency-critical serving paths (cudaMalloc and cudaFree can synchronise the
+device), hosts whose allocator owns all of HBM -- by keeping its scratch in a
+fixed device array inside libqsml_cuda.so.  This file is named to be collected last.
 
 Checked through the C ABI: two calls in a row on the same inputs must agree
 with qsml_reduce (the context entry point) within the reduction tests'
