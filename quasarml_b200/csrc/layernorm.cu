@@ -10,8 +10,8 @@
 // read once and y written once; gamma/beta stay in shared memory.  The row
 // statistics are two block sums (row sum, then squared deviations from the
 // mean), so the variance is a true two-pass variance.
-// k_layer_norm_wide: rows of 32-108 KiB, one CTA per row, rows streamed
-// through two shared-memory buffers.
+// k_layer_norm_wide: binary16 rows of 8-108 KiB and binary32 rows of 32-108
+// KiB, one CTA per row, rows streamed through two shared-memory buffers.
 // k_layer_norm_generic: any width or alignment, Welford over global memory
 // (reads x twice).
 #include "qsml_internal.cuh"
@@ -288,15 +288,15 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
     if (!ok && lane == 0) atomicExch(status, QSML_E_TIMEOUT);
 }
 
-// Rows of 32-108 KiB: one CTA of 512 threads per row, rows streamed through
-// two shared-memory buffers (row_pipe.cuh, stream_rows_cta): the sum, the
-// squared deviations from the mean and the output as three passes over the
-// buffer; gamma/beta are read from global memory (L2-resident after the first
-// row) with 16-byte loads.
-// With REG > 0 (rows of at most 512 * REG packs) each thread keeps the
+// Binary16 rows of 8-108 KiB and binary32 rows of 32-108 KiB: one CTA of TH
+// threads per row, rows streamed through two shared-memory buffers
+// (row_pipe.cuh, stream_rows_cta): the sum, the squared deviations from the
+// mean and the output as three passes over the buffer; gamma/beta are read
+// from global memory (L2-resident after the first row) with 16-byte loads.
+// With REG > 0 (rows of at most TH * REG packs) each thread keeps the
 // gamma/beta of its packs in registers for all its rows instead.
-template <typename T, typename GT, int REG>
-__global__ void __launch_bounds__(512) k_layer_norm_wide(const T* __restrict__ x, const GT* __restrict__ gamma,
+template <typename T, typename GT, int REG, int TH>
+__global__ void __launch_bounds__(TH) k_layer_norm_wide(const T* __restrict__ x, const GT* __restrict__ gamma,
                                                          const GT* __restrict__ beta, T* __restrict__ y,
                                                          int64_t rows, int cols, float eps, int* status) {
     pdl_begin();
@@ -504,36 +504,64 @@ qsml_status_t launch_pipe(Context* ctx, const T* x, const GT* g, const GT* b, T*
     return after_launch(ctx, "k_layer_norm_pipe");
 }
 
-template <typename T, typename GT, int REG>
+template <typename T, typename GT, int REG, int TH>
 qsml_status_t launch_wide_as(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int cols,
                              float eps) {
     const size_t smem = 2 * static_cast<size_t>(cols) * sizeof(T);
     static std::mutex mu;
     static bool attr_set = false;
+    int per_sm = 1;
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!attr_set) {
             QSML_TRY_STATUS(check_cuda(ctx,
-                                       cudaFuncSetAttribute(k_layer_norm_wide<T, GT, REG>,
+                                       cudaFuncSetAttribute(k_layer_norm_wide<T, GT, REG, TH>,
                                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                             static_cast<int>(2 * rowpipe::kWideMaxRowBytes)),
                                        "layer norm: shared-memory attribute"));
             attr_set = true;
         }
+        if (TH < 512) {
+            // several CTAs per SM when their buffers and registers fit
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_layer_norm_wide<T, GT, REG, TH>, TH, smem);
+            if (per_sm < 1) per_sm = 1;
+        }
     }
-    const int64_t grid = rows < ctx->num_sms ? rows : ctx->num_sms;
-    const cudaError_t e = launch_pdl(k_layer_norm_wide<T, GT, REG>, dim3(static_cast<unsigned>(grid)), dim3(512),
+    int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
+    if (grid > rows) grid = rows;
+    const cudaError_t e = launch_pdl(k_layer_norm_wide<T, GT, REG, TH>, dim3(static_cast<unsigned>(grid)), dim3(TH),
                                      smem, ctx->stream, x, g, b, y, rows, cols, eps, ctx->status);
     if (e != cudaSuccess) return check_cuda(ctx, e, "k_layer_norm_wide");
     return after_launch(ctx, "k_layer_norm_wide");
 }
 
-// gamma/beta in registers when a thread has at most 8 packs of the row.
+// Thread count and gamma/beta placement by row width (measured on binary16
+// rows of 12-80 KiB: these choices ran 15-45 % faster than the register
+// kernel or the other thread counts there):
+//   * up to 1024 packs: 128 threads, gamma/beta in registers (8 packs each);
+//   * binary16 rows up to 2048 packs: binary32 gamma/beta in registers with
+//     512 threads (4 packs each), binary16 gamma/beta from L1/L2 with 256
+//     threads (several CTAs per SM);
+//   * binary16 rows up to 52 KiB (two CTAs' buffers fit an SM): 256 threads,
+//     gamma/beta from L1/L2;
+//   * binary32 rows up to 4096 packs: 512 threads, registers (8 packs each);
+//   * wider: 512 threads, gamma/beta from L1/L2 (16 gamma/beta values per
+//     binary16 pack in registers would spill).
 template <typename T, typename GT>
 qsml_status_t launch_wide(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int cols,
                           float eps) {
-    if (cols / Pack<T>::N <= 512 * 8) return launch_wide_as<T, GT, 8>(ctx, x, g, b, y, rows, cols, eps);
-    return launch_wide_as<T, GT, 0>(ctx, x, g, b, y, rows, cols, eps);
+    const int packs = cols / Pack<T>::N;
+    if (packs <= 128 * 8) return launch_wide_as<T, GT, 8, 128>(ctx, x, g, b, y, rows, cols, eps);
+    if constexpr (sizeof(T) == 2) {
+        if (packs <= 512 * 4) {
+            if constexpr (sizeof(GT) == 4) return launch_wide_as<T, GT, 4, 512>(ctx, x, g, b, y, rows, cols, eps);
+            else return launch_wide_as<T, GT, 0, 256>(ctx, x, g, b, y, rows, cols, eps);
+        }
+        if (packs <= rowpipe::kWide256MaxPacks) return launch_wide_as<T, GT, 0, 256>(ctx, x, g, b, y, rows, cols, eps);
+    } else {
+        if (packs <= 512 * 8) return launch_wide_as<T, GT, 8, 512>(ctx, x, g, b, y, rows, cols, eps);
+    }
+    return launch_wide_as<T, GT, 0, 512>(ctx, x, g, b, y, rows, cols, eps);
 }
 
 template <typename T, typename GT>
@@ -543,6 +571,10 @@ qsml_status_t run_ln(Context* ctx, const T* x, const GT* g, const GT* b, T* y, i
     if (rowpipe::use_pipe(cols * sizeof(T), sizeof(T)) && aligned16(x) && aligned16(y) && ctx->status && cols <= INT32_MAX &&
         rowpipe::plan(ctx, rows, static_cast<uint64_t>(cols) * sizeof(T), static_cast<size_t>(cols) * 8, &plan))
         return launch_pipe<T, GT>(ctx, x, g, b, y, rows, static_cast<int>(cols), eps, plan);
+    const uint64_t row_bytes = static_cast<uint64_t>(cols) * sizeof(T);
+    if (rowpipe::use_wide(row_bytes, sizeof(T)) && row_bytes % 16 == 0 && aligned16(x) && aligned16(y) &&
+        aligned16(g) && aligned16(b) && ctx->status)
+        return launch_wide<T, GT>(ctx, x, g, b, y, rows, static_cast<int>(cols), eps);
     if (cols % PV == 0 && aligned16(x) && aligned16(y) && aligned16(g) && aligned16(b) && cols <= INT32_MAX) {
         const int64_t packs = cols / PV;
         int nv = 0;
@@ -566,10 +598,6 @@ qsml_status_t run_ln(Context* ctx, const T* x, const GT* g, const GT* b, T* y, i
             }
         }
     }
-    const uint64_t row_bytes = static_cast<uint64_t>(cols) * sizeof(T);
-    if (rowpipe::use_wide(row_bytes) && row_bytes % 16 == 0 && cols % PV == 0 && aligned16(x) && aligned16(y) &&
-        aligned16(g) && aligned16(b) && ctx->status)
-        return launch_wide<T, GT>(ctx, x, g, b, y, rows, static_cast<int>(cols), eps);
     int64_t grid = rows < 65535 * 16 ? rows : 65535 * 16;
     k_layer_norm_generic<T, GT><<<static_cast<unsigned>(grid), 256, 0, ctx->stream>>>(x, g, b, y, rows, cols, eps);
     return after_launch(ctx, "k_layer_norm_generic");

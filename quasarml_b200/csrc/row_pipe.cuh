@@ -141,6 +141,8 @@ inline bool use_pipe(uint64_t row_bytes, uint32_t elem_bytes) {
 // must end with the buffer no longer being read by any thread.
 constexpr uint32_t kWideMinRowBytes = 32 * 1024 + 16;  // beyond the register kernels
 constexpr size_t kWideMaxRowBytes = 108 * 1024;        // two buffers in ~216 KiB
+// Widest row (16-byte packs) for which two CTAs' buffers share an SM.
+constexpr int kWide256MaxPacks = 52 * 1024 / 16;
 
 template <class Body>
 __device__ bool stream_rows_cta(const unsigned char* src, int64_t rows, uint32_t row_bytes, unsigned char* ring,
@@ -212,7 +214,12 @@ __device__ __forceinline__ float cta_combine(float v, float* slot) {
     return a;
 }
 
-inline bool use_wide(uint64_t row_bytes) { return row_bytes >= kWideMinRowBytes && row_bytes <= kWideMaxRowBytes; }
+// binary16 rows from 8 KiB up (the register kernels are instruction-bound
+// there), binary32 rows beyond what the register kernels hold.
+inline bool use_wide(uint64_t row_bytes, uint32_t elem_bytes) {
+    const uint64_t lo = elem_bytes == 2 ? 8192 + 16 : kWideMinRowBytes;
+    return row_bytes >= lo && row_bytes <= kWideMaxRowBytes;
+}
 
 // Launch shape: one CTA per SM, `warps` warps with `slots` buffers each, the
 // op's per-CTA parameters (`param_bytes`, e.g. gamma and beta) in front of

@@ -15,7 +15,8 @@
 //   * k_softmax_rows -- last axis, wider rows held in registers (16-byte
 //     loads): persistent CTAs with the next two rows in flight, so x is read
 //     once and y written once;
-//   * k_softmax_wide -- last axis, rows of 32-108 KiB: one CTA per row, rows
+//   * k_softmax_wide -- last axis, binary16 rows of 8-108 KiB (tried before
+//     k_softmax_rows) and binary32 rows of 32-108 KiB: one CTA per row, rows
 //     streamed through two shared-memory buffers (row_pipe.cuh);
 //   * k_softmax_rows_generic -- last axis, any width: one CTA per row, three
 //     passes over global memory (max, sum, write);
@@ -261,12 +262,13 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
     if (!ok && lane == 0) atomicExch(status, QSML_E_TIMEOUT);
 }
 
-// Rows of 32-108 KiB: one CTA of 512 threads per row, rows streamed through
-// two shared-memory buffers (row_pipe.cuh, stream_rows_cta): the max, the sum
-// of exp(x - max) and the output as three passes over the buffer, each thread
-// striding over the row's 16-byte packs.
-template <typename T>
-__global__ void __launch_bounds__(512) k_softmax_wide(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
+// Binary16 rows of 8-108 KiB and binary32 rows of 32-108 KiB: one CTA of TH
+// threads per row, rows streamed through two shared-memory buffers
+// (row_pipe.cuh, stream_rows_cta): the max, the sum of exp(x - max) and the
+// output as three passes over the buffer, each thread striding over the row's
+// 16-byte packs.
+template <typename T, int TH>
+__global__ void __launch_bounds__(TH) k_softmax_wide(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
                                                       int cols, int* status) {
     pdl_begin();
     constexpr int PV = Pack<T>::N;
@@ -493,26 +495,45 @@ qsml_status_t launch_pipe(Context* ctx, const T* x, T* y, int64_t rows, int cols
     return after_launch(ctx, "k_softmax_pipe");
 }
 
-template <typename T>
-qsml_status_t launch_wide(Context* ctx, const T* x, T* y, int64_t rows, int cols) {
+template <typename T, int TH>
+qsml_status_t launch_wide_as(Context* ctx, const T* x, T* y, int64_t rows, int cols) {
     const size_t smem = 2 * static_cast<size_t>(cols) * sizeof(T);
     static std::mutex mu;
     static bool attr_set = false;
+    int per_sm = 1;
     {
         std::lock_guard<std::mutex> lk(mu);
         if (!attr_set) {
             QSML_TRY_STATUS(check_cuda(ctx,
-                                       cudaFuncSetAttribute(k_softmax_wide<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       cudaFuncSetAttribute(k_softmax_wide<T, TH>,
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                             static_cast<int>(2 * rowpipe::kWideMaxRowBytes)),
                                        "softmax: shared-memory attribute"));
             attr_set = true;
         }
+        if (TH < 512) {
+            // several CTAs per SM when their buffers and registers fit
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_softmax_wide<T, TH>, TH, smem);
+            if (per_sm < 1) per_sm = 1;
+        }
     }
-    const int64_t grid = rows < ctx->num_sms ? rows : ctx->num_sms;
-    const cudaError_t e = launch_pdl(k_softmax_wide<T>, dim3(static_cast<unsigned>(grid)), dim3(512), smem, ctx->stream,
-                                     x, y, rows, cols, ctx->status);
+    int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
+    if (grid > rows) grid = rows;
+    const cudaError_t e = launch_pdl(k_softmax_wide<T, TH>, dim3(static_cast<unsigned>(grid)), dim3(TH), smem,
+                                     ctx->stream, x, y, rows, cols, ctx->status);
     if (e != cudaSuccess) return check_cuda(ctx, e, "k_softmax_wide");
     return after_launch(ctx, "k_softmax_wide");
+}
+
+// 128 threads per row up to 1024 packs, 256 for binary16 rows up to 52 KiB
+// (at least two CTAs per SM), 512 beyond.
+template <typename T>
+qsml_status_t launch_wide(Context* ctx, const T* x, T* y, int64_t rows, int cols) {
+    if (cols / Pack<T>::N <= 1024) return launch_wide_as<T, 128>(ctx, x, y, rows, cols);
+    if constexpr (sizeof(T) == 2) {
+        if (cols / Pack<T>::N <= rowpipe::kWide256MaxPacks) return launch_wide_as<T, 256>(ctx, x, y, rows, cols);
+    }
+    return launch_wide_as<T, 512>(ctx, x, y, rows, cols);
 }
 
 template <typename T>
@@ -524,6 +545,10 @@ qsml_status_t run_softmax(Context* ctx, const T* x, T* y, int64_t outer, int64_t
         if (rowpipe::use_pipe(cols * sizeof(T), sizeof(T)) && aligned16(x) && aligned16(y) && ctx->status && cols <= INT32_MAX &&
             rows >= ctx->num_sms && rowpipe::plan(ctx, rows, static_cast<uint64_t>(cols) * sizeof(T), 0, &plan))
             return launch_pipe<T>(ctx, x, y, rows, static_cast<int>(cols), plan);
+        const uint64_t row_bytes = static_cast<uint64_t>(cols) * sizeof(T);
+        const bool wide = rowpipe::use_wide(row_bytes, sizeof(T)) && row_bytes % 16 == 0 && aligned16(x) &&
+                          aligned16(y) && ctx->status;
+        if (wide && sizeof(T) == 2 && rows >= ctx->num_sms) return launch_wide<T>(ctx, x, y, rows, static_cast<int>(cols));
         if (cols % PV == 0 && aligned16(x) && aligned16(y) && cols <= INT32_MAX) {
             const int64_t packs = cols / PV;
             int nv = 0;
@@ -548,9 +573,7 @@ qsml_status_t run_softmax(Context* ctx, const T* x, T* y, int64_t outer, int64_t
         }
         // Few long rows: a CTA per row would leave most SMs idle.
         if (rows < ctx->num_sms && cols >= 16384) return run_long_rows<T>(ctx, x, y, rows, cols);
-        const uint64_t row_bytes = static_cast<uint64_t>(cols) * sizeof(T);
-        if (rowpipe::use_wide(row_bytes) && row_bytes % 16 == 0 && aligned16(x) && aligned16(y) && ctx->status)
-            return launch_wide<T>(ctx, x, y, rows, static_cast<int>(cols));
+        if (wide) return launch_wide<T>(ctx, x, y, rows, static_cast<int>(cols));
         int64_t grid = rows < int64_t(ctx->num_sms) * 16 ? rows : int64_t(ctx->num_sms) * 16;
         const unsigned th = cols >= 256 ? 256 : (cols >= 128 ? 128 : (cols >= 64 ? 64 : 32));
         k_softmax_rows_generic<T><<<static_cast<unsigned>(grid), th, 0, ctx->stream>>>(x, y, rows, cols);

@@ -1,6 +1,9 @@
 """Layer norm and last-axis softmax on rows streamed through shared memory by
 bulk copies: one warp per row for rows of 2-8 KiB (binary16) or 2-4 KiB
-(binary32), one CTA per row for rows of 32-108 KiB.  The shapes below also
+(binary32), one CTA per row for binary16 rows above 8 KiB and binary32 rows
+from 32 KiB, both up to 108 KiB (128 threads per CTA up to 16 KiB rows;
+binary16 rows up to 52 KiB 256 threads, except layer norm with binary32
+gamma/beta on rows of 16-32 KiB, 512; 512 beyond).  The shapes below also
 include rows that take the register-resident or the generic kernels, and each
 case checks which kernel ran (qsml_last_kernel).  Covered: rows whose 16-byte packs do
 not divide evenly over the 32 lanes, rows just above and far above the SM
@@ -24,6 +27,10 @@ SHAPES = [
     ((20000, 512), np.float32, "pipe"),    # 2 KiB rows: 16 warps per CTA
     ((16384, 4096), np.float16, "pipe"),
     ((149, 2048), np.float32, None),       # 8 KiB binary32 rows: register kernel
+    ((200, 4104), np.float16, "wide"),     # 8208-byte binary16 rows: 128 threads
+    ((300, 6000), np.float16, "wide"),     # 12,000-byte rows, 750 packs over 128 threads
+    ((150, 12288), np.float16, "wide"),    # 24 KiB binary16 rows
+    ((200, 16384), np.float16, "wide"),    # 32 KiB binary16 rows: 8 packs per thread at 256
     ((300, 12000), np.float32, "wide"),    # 48,000-byte rows
     ((400, 18000), np.float16, "wide"),    # 36,000-byte rows
     ((1024, 16384), np.float32, "wide"),   # 64 KiB rows
@@ -128,3 +135,17 @@ def test_layer_norm_f16_params_and_few_rows(ctx, orc):
         assert ctx.last_kernel() == "k_layer_norm_pipe"
         ref = orc.layer_norm(x, g.astype(np.float32), b.astype(np.float32), 1e-5).astype(np.float64)
         assert np.max(np.abs(y - ref) / (1e-3 * (1.0 + np.abs(ref)))) <= 1.0, shape
+
+
+@pytest.mark.parametrize("shape", [(300, 6000), (150, 12288), (100, 24576), (60, 40000)])
+def test_layer_norm_wide_f16_params(ctx, orc, shape):
+    """binary16 gamma/beta through each CTA-per-row variant: in registers
+    (12,000-byte rows), from L1/L2 with 256 threads (24 and 48 KiB) and with
+    512 threads (80,000-byte rows)."""
+    x = datagen.normal(116, shape, 0.5, 2.0).astype(np.float16)
+    g = datagen.normal(117, shape[-1:], 1.0, 0.1).astype(np.float16)
+    b = datagen.normal(118, shape[-1:], 0.0, 0.1).astype(np.float16)
+    y = ln(ctx, x, g, b).astype(np.float64)
+    assert ctx.last_kernel() == "k_layer_norm_wide"
+    ref = orc.layer_norm(x, g.astype(np.float32), b.astype(np.float32), 1e-5).astype(np.float64)
+    assert np.max(np.abs(y - ref) / (1e-3 * (1.0 + np.abs(ref)))) <= 1.0, shape
