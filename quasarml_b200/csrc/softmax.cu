@@ -10,13 +10,14 @@
 // not correctly rounded either) runs over any axis.  exp is expf, except in
 // the last-axis row kernels on binary16 rows, which use the hardware base-2
 // exponential (relative error about 2^-22, far below binary16 resolution):
-//   * k_softmax_pipe -- last axis, rows of 2-8 KiB: one warp per row, rows
-//     streamed through shared memory by bulk copies (row_pipe.cuh);
+//   * k_softmax_pipe -- last axis, rows of 2-8 KiB (binary16: below 8 KiB):
+//     one warp per row, rows streamed through shared memory by bulk copies
+//     (row_pipe.cuh);
 //   * k_softmax_rows -- last axis, wider rows held in registers (16-byte
 //     loads): persistent CTAs with the next two rows in flight, so x is read
 //     once and y written once;
 //   * k_softmax_wide -- last axis, binary16 rows of 8-108 KiB (tried before
-//     k_softmax_rows) and binary32 rows of 32-108 KiB: one CTA per row, rows
+//     the other kernels) and binary32 rows of 32-108 KiB: one CTA per row, rows
 //     streamed through two shared-memory buffers (row_pipe.cuh);
 //   * k_softmax_rows_generic -- last axis, any width: one CTA per row, three
 //     passes over global memory (max, sum, write);
@@ -541,14 +542,18 @@ qsml_status_t run_softmax(Context* ctx, const T* x, T* y, int64_t outer, int64_t
     constexpr int PV = Pack<T>::N;
     if (inner == 1) {
         const int64_t rows = outer, cols = k;
+        const uint64_t row_bytes = static_cast<uint64_t>(cols) * sizeof(T);
+        const bool wide_ok = row_bytes % 16 == 0 && row_bytes <= rowpipe::kWideMaxRowBytes && aligned16(x) &&
+                             aligned16(y) && ctx->status;
+        // binary16 rows from 8 KiB up: a CTA per row (X[16384,4096]: 5.5 TB/s
+        // against 4.8 for a warp per row; 4 KiB rows run faster on a warp)
+        if (sizeof(T) == 2 && wide_ok && row_bytes >= 8192 && rows >= ctx->num_sms)
+            return launch_wide<T>(ctx, x, y, rows, static_cast<int>(cols));
         rowpipe::Plan plan;
         if (rowpipe::use_pipe(cols * sizeof(T), sizeof(T)) && aligned16(x) && aligned16(y) && ctx->status && cols <= INT32_MAX &&
             rows >= ctx->num_sms && rowpipe::plan(ctx, rows, static_cast<uint64_t>(cols) * sizeof(T), 0, &plan))
             return launch_pipe<T>(ctx, x, y, rows, static_cast<int>(cols), plan);
-        const uint64_t row_bytes = static_cast<uint64_t>(cols) * sizeof(T);
-        const bool wide = rowpipe::use_wide(row_bytes, sizeof(T)) && row_bytes % 16 == 0 && aligned16(x) &&
-                          aligned16(y) && ctx->status;
-        if (wide && sizeof(T) == 2 && rows >= ctx->num_sms) return launch_wide<T>(ctx, x, y, rows, static_cast<int>(cols));
+        const bool wide = rowpipe::use_wide(row_bytes, sizeof(T)) && wide_ok;
         if (cols % PV == 0 && aligned16(x) && aligned16(y) && cols <= INT32_MAX) {
             const int64_t packs = cols / PV;
             int nv = 0;

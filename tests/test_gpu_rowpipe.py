@@ -1,15 +1,16 @@
 """Layer norm and last-axis softmax on rows streamed through shared memory by
 bulk copies: one warp per row for rows of 2-8 KiB (binary16) or 2-4 KiB
-(binary32), one CTA per row for binary16 rows above 8 KiB and binary32 rows
-from 32 KiB, both up to 108 KiB (128 threads per CTA up to 16 KiB rows;
-binary16 rows up to 52 KiB 256 threads, except layer norm with binary32
-gamma/beta on rows of 16-32 KiB, 512; 512 beyond).  The shapes below also
-include rows that take the register-resident or the generic kernels, and each
-case checks which kernel ran (qsml_last_kernel).  Covered: rows whose 16-byte packs do
-not divide evenly over the 32 lanes, rows just above and far above the SM
-count, 16 warps per CTA, and special values.  Bars as in the other layer
-norm and softmax tests: binary32 |y - ref| <= 1e-5 * (1 + |ref|) (layer norm)
-or 1e-5 * ref + 1e-30 (softmax); binary16 1e-3 relative.
+(binary32); one CTA per row for binary16 rows above 8 KiB (softmax: from 8
+KiB) and binary32 rows from 32 KiB, both up to 108 KiB.  The CTA has 128
+threads up to 16 KiB rows, 256 for binary16 rows up to 52 KiB (layer norm
+with binary32 gamma/beta on 16-32 KiB rows: 512) and 512 beyond.  The shapes
+below also include rows that take the register-resident or the generic
+kernels, and each case checks which kernel ran (qsml_last_kernel).  Covered:
+rows whose 16-byte packs do not divide evenly over the 32 lanes, rows just
+above and far above the SM count, 16 warps per CTA, and special values.
+Bars as in the other layer norm and softmax tests: binary32
+|y - ref| <= 1e-5 * (1 + |ref|) (layer norm) or 1e-5 * ref + 1e-30
+(softmax); binary16 1e-3 relative.
 """
 import numpy as np
 import pytest
@@ -20,12 +21,13 @@ from quasarml_b200 import abi, datagen
 pytestmark = pytest.mark.gpu
 
 # (shape, dtype, kernel family: "pipe" = a warp per row, "wide" = a CTA per row,
-# both streamed through shared memory; None = the register or generic kernels)
+# both streamed through shared memory; None = the register or generic kernels;
+# a pair = (layer norm, softmax) where they differ)
 SHAPES = [
     ((5000, 1000), np.float32, "pipe"),    # 4000-byte rows, 250 packs: ragged over the lanes
     ((3000, 1032), np.float16, "pipe"),    # 2064-byte rows, 129 packs
     ((20000, 512), np.float32, "pipe"),    # 2 KiB rows: 16 warps per CTA
-    ((16384, 4096), np.float16, "pipe"),
+    ((16384, 4096), np.float16, ("pipe", "wide")),  # 8 KiB binary16 rows: softmax a CTA per row
     ((149, 2048), np.float32, None),       # 8 KiB binary32 rows: register kernel
     ((200, 4104), np.float16, "wide"),     # 8208-byte binary16 rows: 128 threads
     ((300, 6000), np.float16, "wide"),     # 12,000-byte rows, 750 packs over 128 threads
@@ -56,6 +58,7 @@ def softmax(ctx, x):
 @pytest.mark.parametrize("case", range(len(SHAPES)))
 def test_layer_norm(ctx, orc, case):
     shape, dtype, family = SHAPES[case]
+    family = family[0] if isinstance(family, tuple) else family
     x = datagen.normal(70 + case, shape, 0.5, 2.0).astype(dtype)
     g = datagen.normal(80 + case, shape[-1:], 1.0, 0.1)
     b = datagen.normal(90 + case, shape[-1:], 0.0, 0.1)
@@ -72,6 +75,7 @@ def test_layer_norm(ctx, orc, case):
 @pytest.mark.parametrize("case", range(len(SHAPES)))
 def test_softmax(ctx, orc, case):
     shape, dtype, family = SHAPES[case]
+    family = family[1] if isinstance(family, tuple) else family
     x = datagen.normal(100 + case, shape, 0.5, 2.0).astype(dtype)
     got = softmax(ctx, x).astype(np.float64)
     want = {"pipe": "k_softmax_pipe", "wide": "k_softmax_wide"}.get(family)
