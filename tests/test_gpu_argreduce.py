@@ -85,6 +85,31 @@ def test_matches_oracle(ctx, orc, dtype, case, op):
     np.testing.assert_array_equal(got.reshape(-1), np.asarray(want).reshape(-1))
 
 
+TIE_CASES = [((1000003,), None), ((8, 100000), -1), ((4096, 300), 1), ((64, 512, 1024), 0), ((64, 512, 1024), 1),
+              ((16, 64, 520), 1)]
+
+
+@pytest.mark.parametrize("case", range(len(TIE_CASES)))
+@pytest.mark.parametrize("op", [abi.ARG_MAX, abi.ARG_MIN])
+def test_f16_ties_zeros_and_nans(ctx, orc, case, op):
+    """binary16 through the packed (two halves per instruction) scans: values
+    drawn from {-0, +0, 1, -1} so that ties are everywhere and -0/+0 must
+    compare equal, NaN in a few slices (sometimes first), whole slices of NaN
+    and of -inf/+inf."""
+    shape, axis = TIE_CASES[case]
+    rng = np.random.default_rng(300 + case)
+    x = rng.choice(np.array([-0.0, 0.0, 1.0, -1.0], np.float16), size=shape)
+    flat = x.reshape(-1)
+    flat[rng.choice(flat.size, size=max(3, flat.size // 200000), replace=False)] = np.nan
+    if x.ndim >= 2:
+        flat[0] = np.nan
+        x[(0,) * (x.ndim - 2) + (slice(None), 1)] = np.nan                # a NaN column
+        x[(min(1, x.shape[0] - 1),) + (slice(None),) * (x.ndim - 1)] = -np.inf if op == abi.ARG_MAX else np.inf
+    got = gpu_arg(ctx, op, x, axis)
+    want = orc.argreduce(op, x, axis)
+    np.testing.assert_array_equal(got.reshape(-1), np.asarray(want).reshape(-1))
+
+
 def test_nan_and_signed_zero_rules(ctx, orc):
     x = np.array([1, 5, np.nan, 5, np.nan, -0.0], np.float32)
     assert gpu_arg(ctx, abi.ARG_MAX, x, None)[0] == 2
