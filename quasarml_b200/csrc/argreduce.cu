@@ -142,7 +142,7 @@ template <int OP, typename C> struct Best {
 // the worst number (-inf for argmax) at ordinal 0: a position whose elements
 // are all that value reports its first one.  Pack ordinals must stay below
 // 65536.  Used by the column kernel, where the 8 positions are 8 columns with
-// their own results (binary16 X[64,512,1024] over axis 0 / 1: 3.5 -> 3.8 /
+// their own results (binary16 X[64,512,1024] over axis 0 / 1: 3.5 -> 4.2 /
 // 4.3 TB/s); in the row and segment kernels a thread would have to merge its
 // 8 positions into one key, which at their usual few packs per thread cost
 // more than the packed updates saved (measured slower there).
@@ -419,10 +419,12 @@ qsml_status_t run_arg(Context* ctx, const T* x, int64_t outer, int64_t k, int64_
     const int64_t tiles_per_o = (inner + 32 * pv - 1) / (32 * pv);
     const int64_t tiles = tiles_per_o * outer;
     if (tiles > INT32_MAX) return set_error(ctx, QSML_E_UNSUPPORTED, "qsml_arg_reduce: too large");
-    // about 4096 warps per launch for 4-byte elements, more for narrower ones
-    // (more comparisons per 16-byte load); keys in at most 32 KiB of shared
-    // memory
-    const int64_t target = 4096 * (4 / static_cast<int64_t>(sizeof(T) < 4 ? sizeof(T) : 4));
+    // about 4096 warps per launch for 4-byte elements and binary16 (compared
+    // two halves at a time), more for the narrower integers (more
+    // comparisons per 16-byte load); keys in at most 32 KiB of shared memory
+    const int64_t target = std::is_same<T, __half>::value
+                               ? 4096
+                               : 4096 * (4 / static_cast<int64_t>(sizeof(T) < 4 ? sizeof(T) : 4));
     int64_t W = (target + tiles - 1) / tiles;
     const int64_t w_smem = 32768 / (32 * pv * 8);
     if (W > 16) W = 16;
