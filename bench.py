@@ -812,6 +812,8 @@ def run_single(which: str, reps: int = 3):
             wl.compute()
     elif which.startswith("argmax"):
         x = _t(datagen.normal(datagen.SEEDS["red_X"], (64, 512, 1024), 0.0, 1.0))
+        if which.endswith("_f16"):
+            x = x.half()
         axis = None if which == "argmax_all" else 1
         out = torch.empty(abi.reduced_shape(tuple(x.shape), axis, False), dtype=torch.int32, device="cuda")
         for _ in range(reps):
@@ -882,7 +884,8 @@ def main():
     ap.add_argument("--single", default=None,
                     choices=["reduce_all", "reduce_axis0", "reduce_axis1", "reduce_axis2", "reduce_all_f16",
                              "chain_add", "chain_fused", "gather_t", "gather_s", "layernorm", "matmul_f16",
-                             "matmul_3xtf32", "bmm_f16", "argmax_all", "argmax_axis1", "softmax", "softmax_f16",
+                             "matmul_3xtf32", "bmm_f16", "argmax_all", "argmax_axis1", "argmax_axis1_f16", "softmax",
+                             "softmax_f16",
                              "layernorm_f16"],
                     help="run one kernel of the workloads a few times and exit (profiling aid, prints nothing)")
     args = ap.parse_args()
