@@ -522,9 +522,17 @@ qsml_status_t launch_wide_as(Context* ctx, const T* x, const GT* g, const GT* b,
             attr_set = true;
         }
         if (TH < 512) {
-            // several CTAs per SM when their buffers and registers fit
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_layer_norm_wide<T, GT, REG, TH>, TH, smem);
-            if (per_sm < 1) per_sm = 1;
+            // several CTAs per SM when their buffers and registers fit (one
+            // occupancy query per row width)
+            static std::unordered_map<size_t, int> per_sm_by_smem;
+            auto it = per_sm_by_smem.find(smem);
+            if (it == per_sm_by_smem.end()) {
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_layer_norm_wide<T, GT, REG, TH>, TH, smem);
+                if (per_sm < 1) per_sm = 1;
+                per_sm_by_smem[smem] = per_sm;
+            } else {
+                per_sm = it->second;
+            }
         }
     }
     int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
