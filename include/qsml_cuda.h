@@ -50,7 +50,7 @@ typedef int32_t qsml_status_t;
 #define QSML_E_CUDA 5        /* CUDA runtime error                            */
 #define QSML_E_NCCL 6        /* collective error                              */
 #define QSML_E_TIMEOUT 7     /* bounded device-side wait expired              */
-#define QSML_E_UNSUPPORTED 8 /* valid request this build does not implement   */
+#define QSML_E_UNSUPPORTED 8 /* valid request the library does not implement */
 
 /* Element types, same order and sizes as QuasarML::DataType
  * (QuasarML/src/Common/Types.h:80-103). */

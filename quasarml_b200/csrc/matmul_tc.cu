@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
-            // one lane waits, the warp follows its verdict (tcgen05.ld needs
+            // one lane waits, the warp follows its result (tcgen05.ld needs
             // the whole warp converged)
             int ready = 0;
             if (lane == 0) ready = mbar_wait(tfull_bar(acc), acc_phase, abort_flag) ? 1 : 0;
