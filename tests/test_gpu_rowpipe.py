@@ -31,6 +31,7 @@ SHAPES = [
     ((149, 2048), np.float32, None),       # 8 KiB binary32 rows: register kernel
     ((200, 4104), np.float16, "wide"),     # 8208-byte binary16 rows: 128 threads
     ((300, 6000), np.float16, "wide"),     # 12,000-byte rows, 750 packs over 128 threads
+    ((100, 6000), np.float16, "wide"),     # the same rows, fewer than the SMs
     ((150, 12288), np.float16, "wide"),    # 24 KiB binary16 rows
     ((200, 16384), np.float16, "wide"),    # 32 KiB binary16 rows: 8 packs per thread at 256
     ((300, 12000), np.float32, "wide"),    # 48,000-byte rows
