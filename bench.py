@@ -827,12 +827,13 @@ def run_single(which: str, reps: int = 3):
             out = torch.empty((2729, 4096), dtype=torch.int32, device="cuda")
         for _ in range(reps):
             ctx.gather(v, d(out))
-    elif which in ("layernorm", "layernorm_f16"):
-        X = _t(datagen.normal(10, (16384, 4096), 0.5, 2.0))
-        if which == "layernorm_f16":
+    elif which in ("layernorm", "layernorm_f16", "layernorm_f16_8192"):
+        R, C = (8192, 8192) if which == "layernorm_f16_8192" else (16384, 4096)
+        X = _t(datagen.normal(10, (R, C), 0.5, 2.0))
+        if which != "layernorm":
             X = X.half()
-        g = _t(datagen.normal(11, (4096,), 1.0, 0.1))
-        b = _t(datagen.normal(12, (4096,), 0.0, 0.1))
+        g = _t(datagen.normal(11, (C,), 1.0, 0.1))
+        b = _t(datagen.normal(12, (C,), 0.0, 0.1))
         Y = torch.empty_like(X)
         for _ in range(reps):
             ctx.layer_norm(d(X), d(g), d(b), 1e-5, d(Y))
@@ -886,7 +887,7 @@ def main():
                              "chain_add", "chain_fused", "gather_t", "gather_s", "layernorm", "matmul_f16",
                              "matmul_3xtf32", "bmm_f16", "argmax_all", "argmax_axis1", "argmax_axis1_f16", "softmax",
                              "softmax_f16",
-                             "layernorm_f16"],
+                             "layernorm_f16", "layernorm_f16_8192"],
                     help="run one kernel of the workloads a few times and exit (profiling aid, prints nothing)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
