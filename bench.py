@@ -758,10 +758,20 @@ def cpu_baseline(min_seconds=10.0, max_seconds=30.0):
             "sample": f"the same 32 reductions on X[8,512,1024] (1/8 of one X) fp32+fp16, {n} passes in {el:.1f} s"}
 
 
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def run_reference(args, dist: Dist):
     if dist.rank != 0:
         return
     s = CpuReduceSample()
+    # rank 0 alone runs: every host thread, whatever OMP_NUM_THREADS the
+    # launcher set for its ranks
+    s.orc.lib().orc_set_num_threads(host_threads())
     for _ in range(max(args.warmup, 0)):
         s.run()
     t0 = time.perf_counter()
