@@ -744,6 +744,7 @@ class CpuReduceSample:
 
 def cpu_baseline(min_seconds=10.0, max_seconds=30.0):
     s = CpuReduceSample()
+    s.orc.lib().orc_set_num_threads(host_threads())
     s.run()
     t0 = time.perf_counter()
     n = 0
