@@ -149,6 +149,18 @@ QSML_API qsml_status_t qsml_get_stream(qsml_ctx* ctx, void** stream);
  * QuasarML/src/Backend/Vulkan/VulkanBackend.cpp:613-658). */
 QSML_API qsml_status_t qsml_synchronize(qsml_ctx* ctx);
 
+/* Limit, in SM clock cycles, after which a kernel that waits for data on an
+ * mbarrier (the one-SM tensor-core GEMM, the layer-norm and softmax row
+ * pipelines) gives up: it stops, lets every copy and MMA it already issued
+ * finish, records QSML_E_TIMEOUT for the next qsml_synchronize and returns,
+ * so the context stays usable.  0 restores the default (2e9 cycles, about
+ * 1 s).  Stream-ordered: applies to kernels enqueued after the call.  Meant
+ * for failure-detection tests and watchdogs; a limit below a kernel's
+ * normal wait times makes it give up on healthy work.  No reference
+ * counterpart (its fence waits are unbounded,
+ * QuasarML/src/Backend/Vulkan/VulkanBackend.cpp:613-658). */
+QSML_API qsml_status_t qsml_set_wait_limit(qsml_ctx* ctx, int64_t cycles);
+
 /* Message of the last failed call on ctx (or of the last failed
  * context-free call when ctx is NULL).  Never NULL. */
 QSML_API const char* qsml_last_error(qsml_ctx* ctx);
@@ -358,6 +370,55 @@ QSML_API qsml_status_t qsml_allreduce(qsml_group* group, int32_t local, void* bu
                                       int32_t op);
 QSML_API qsml_status_t qsml_group_destroy(qsml_group* group);
 
+/* ---- Sharded reductions -----------------------------------------------------
+ * A tensor split by rows (axis 0) over the ranks of a group, each rank holding
+ * its own row block (blocks may differ in length; the other dims agree).  A
+ * reduction over any other axis needs no exchange: qsml_reduce of the block is
+ * the rank's row block of the global result.  A reduction over axis 0 or over
+ * all elements combines one partial per rank:
+ *   1. qsml_reduce with a binary32 `out` (F16 input is fine) gives the rank's
+ *      partial: SUM for sum and mean, MAX / MIN for max / min;
+ *   2. qsml_allreduce_partials combines the partials of all ranks in place,
+ *      several reductions' partials at once if the caller packs them into one
+ *      buffer;
+ *   3. qsml_finish_partial writes the result in out's dtype; a mean is the
+ *      combined sum * (1.0f / (float)n), n = the elements reduced into each
+ *      output over all ranks, the reference's definition of mean
+ *      (QuasarML/src/Ops/Reduction.cpp:347-356).
+ * qsml_reduce_sharded does all three for one reduction.  Sums combine in
+ * binary32 (binary16 inputs are never summed in binary16); max / min cross
+ * the group as order-preserving 32-bit keys, so NaN propagation (as
+ * 0x7fffffff) and -0 < +0 are exactly those of qsml_reduce on one GPU.  The
+ * reference has no multi-GPU path (README.md:84, Core/DeviceManager.cpp:52-66
+ * open independent devices); these replace nothing there. */
+
+/* In place over `count` binary32 partials at buf (device memory of local
+ * rank `local`'s context), on that context's stream: op SUM or MEAN adds,
+ * MAX / MIN take the IEEE 754-2019 maximum / minimum.  Not inside
+ * qsml_group_start / qsml_group_end. */
+QSML_API qsml_status_t qsml_allreduce_partials(qsml_group* group, int32_t local, int32_t op, void* buf,
+                                               int64_t count);
+
+/* out (F32 or F16, as many elements as `partial`, F32) from combined
+ * partials: SUM / MAX / MIN as they are, MEAN times 1.0f / (float)n; rounded
+ * once to out's dtype.  out may be `partial` itself. */
+QSML_API qsml_status_t qsml_finish_partial(qsml_ctx* ctx, int32_t op, const qsml_tdesc* partial, int64_t n,
+                                           const qsml_tdesc* out);
+
+/* One sharded reduction (sum, mean, max or min) of this rank's row block `a`
+ * with qsml_reduce's axis / keepdims / out rules; out is identical on every
+ * rank for axis 0 and QSML_AXIS_ALL.  global_rows = the rows of all ranks
+ * together (0: this rank's rows times the number of ranks).  A rank without
+ * rows contributes 0 to sums and the identity (-inf / +inf) to max / min. */
+QSML_API qsml_status_t qsml_reduce_sharded(qsml_group* group, int32_t local, int32_t op, const qsml_tdesc* a,
+                                           int32_t axis, int32_t keepdims, const qsml_tdesc* out,
+                                           int64_t global_rows);
+
+/* Rows [*begin, *begin + *count) of `rows` that rank `rank` of `nranks` holds
+ * under the balanced contiguous split every sharded workload here uses (the
+ * first rows % nranks ranks hold one row more). */
+QSML_API qsml_status_t qsml_shard_rows(int64_t rows, int32_t nranks, int32_t rank, int64_t* begin, int64_t* count);
+
 /* Allocation-free sum / mean / max / min over all elements (axis =
  * QSML_AXIS_ALL) or over an axis followed only by unit dims, for callers that
  * cannot allocate device memory at that point: latency-critical paths that
@@ -366,14 +427,21 @@ QSML_API qsml_status_t qsml_group_destroy(qsml_group* group);
  * HBM, and plugins handed only a stream.  It needs no qsml_ctx:
  * it enqueues on `stream` (a cudaStream_t of the current device; NULL = the
  * legacy default stream) and never calls cudaMalloc, cudaFree or any
- * allocating routine.  Results are bit-identical to qsml_reduce's segment
- * kernel for the same shape.
+ * allocating routine.  It runs qsml_reduce's segment kernel with the same
+ * slicing, so its results are bit-identical to qsml_reduce's wherever
+ * qsml_reduce picks that kernel too: the full reduction, a single row, or
+ * fewer than 592 rows of at least 8192 elements each.  For other shapes
+ * (many short rows, where qsml_reduce uses a warp per row) the two agree
+ * within the reductions' rounding tolerance but not bit for bit.  An empty
+ * reduced axis is rejected with QSML_E_SHAPE (qsml_reduce instead writes 0
+ * for sum and NaN for mean).
  *
  * Its scratch is a fixed 64 KiB device array inside this library, which every
  * GPU that loads the library holds until the process exits; it limits a call
  * to at most 64 output rows (larger requests return QSML_E_UNSUPPORTED with a
- * message).  The first call on a device looks up that array's device address
- * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * message).  The first call in each CUDA context looks up that array's
+ * device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture; after a device reset the next call looks it up again.
  * All calls share the array and clear its counters before each launch:
  * calls on the same GPU whose work overlaps race on it.  Errors are reported
  * through qsml_last_error(NULL).  No counterpart in the reference. */

@@ -269,3 +269,40 @@ def ulp_diff_f32(x: np.ndarray, y: np.ndarray) -> np.ndarray:
     d = np.abs(xi - yi)
     both_nan = np.isnan(x) & np.isnan(y)
     return np.where(both_nan, 0, d)
+
+
+def matmul_check(c: np.ndarray, a: np.ndarray, b: np.ndarray, rows_per_block: int = 1024):
+    """Every output of a product c = a @ b (rank 2, or rank 3 batched) against
+    binary64, for the floating-point matmul bars (LinAlg.cpp:84-158 computes
+    each output as one dot product over k).  The binary64 product and the
+    componentwise error scale |a| @ |b| (the factor in the classical bound
+    |fl(a.b) - a.b| <= gamma_k |a|.|b| of any summation order) come from
+    NumPy's binary64 matmul, a block of rows at a time.  a and b are the
+    inputs as the kernel saw them (binary16 inputs widen exactly).
+
+    Returns (worst componentwise error / scale, normwise error
+    ||c - ref||_F / ||ref||_F, max|err| / max|ref|)."""
+    a3 = a[None] if a.ndim == 2 else a
+    b3 = b[None] if b.ndim == 2 else b
+    c3 = c[None] if c.ndim == 2 else c
+    worst = 0.0
+    err2 = 0.0
+    ref2 = 0.0
+    maxerr = 0.0
+    maxref = 0.0
+    for bi in range(a3.shape[0]):
+        B = b3[bi].astype(np.float64)
+        Babs = np.abs(B)
+        for r0 in range(0, a3.shape[1], rows_per_block):
+            A = a3[bi, r0:r0 + rows_per_block].astype(np.float64)
+            ref = A @ B
+            scale = np.abs(A) @ Babs
+            err = np.abs(c3[bi, r0:r0 + rows_per_block].astype(np.float64) - ref)
+            with np.errstate(divide="ignore", invalid="ignore"):
+                q = np.where(scale > 0, err / scale, np.where(err > 0, np.inf, 0.0))
+            worst = max(worst, float(q.max()))
+            err2 += float(np.sum(err * err))
+            ref2 += float(np.sum(ref * ref))
+            maxerr = max(maxerr, float(err.max()))
+            maxref = max(maxref, float(np.abs(ref).max()))
+    return worst, (err2 ** 0.5) / (ref2 ** 0.5 if ref2 > 0 else 1.0), maxerr / (maxref if maxref > 0 else 1.0)

@@ -108,6 +108,7 @@ _SIGS = {
     "qsml_set_stream": (_c.c_int32, [_c.c_void_p, _c.c_void_p]),
     "qsml_get_stream": (_c.c_int32, [_c.c_void_p, _P(_c.c_void_p)]),
     "qsml_synchronize": (_c.c_int32, [_c.c_void_p]),
+    "qsml_set_wait_limit": (_c.c_int32, [_c.c_void_p, _c.c_int64]),
     "qsml_last_error": (_c.c_char_p, [_c.c_void_p]),
     "qsml_alloc": (_c.c_int32, [_c.c_void_p, _c.c_size_t, _P(_c.c_void_p)]),
     "qsml_free": (_c.c_int32, [_c.c_void_p, _c.c_void_p]),
@@ -141,6 +142,11 @@ _SIGS = {
     "qsml_layer_norm": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_float, _P(TDesc)]),
     "qsml_matmul": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_int32]),
     "qsml_reduce_noalloc": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_int32, _c.c_int32, _P(TDesc)]),
+    "qsml_allreduce_partials": (_c.c_int32, [_c.c_void_p, _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_int64]),
+    "qsml_finish_partial": (_c.c_int32, [_c.c_void_p, _c.c_int32, _P(TDesc), _c.c_int64, _P(TDesc)]),
+    "qsml_reduce_sharded": (_c.c_int32, [_c.c_void_p, _c.c_int32, _c.c_int32, _P(TDesc), _c.c_int32, _c.c_int32,
+                                         _P(TDesc), _c.c_int64]),
+    "qsml_shard_rows": (_c.c_int32, [_c.c_int64, _c.c_int32, _c.c_int32, _P(_c.c_int64), _P(_c.c_int64)]),
     "qsml_launch_count": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64)]),
     "qsml_last_kernel": (_c.c_int32, [_c.c_void_p, _c.c_char_p, _c.c_size_t]),
     "qsml_cpu_fallback_count": (_c.c_int32, [_c.c_void_p, _P(_c.c_uint64)]),
@@ -214,10 +220,33 @@ class Group:
         if st != OK:
             raise QsmlError(st, load().qsml_last_error(self.ctxs[local].h).decode())
 
+    def _check_local(self, st: int, local: int) -> None:
+        if st != OK:
+            raise QsmlError(st, load().qsml_last_error(self.ctxs[local].h).decode())
+
+    def allreduce_partials(self, local: int, op: int, ptr: int, count: int) -> None:
+        """Combines `count` binary32 partials of reduction `op` across the group, in place."""
+        self._check_local(load().qsml_allreduce_partials(self.h, int(local), int(op), ctypes.c_void_p(ptr),
+                                                         int(count)), local)
+
+    def reduce_sharded(self, local: int, op: int, a: TDesc, axis: int, keepdims: bool, out: TDesc,
+                       global_rows: int = 0) -> None:
+        """One reduction of a tensor whose rows are split over the group's ranks."""
+        self._check_local(load().qsml_reduce_sharded(self.h, int(local), int(op), ctypes.byref(a), int(axis),
+                                                     int(bool(keepdims)), ctypes.byref(out), int(global_rows)),
+                          local)
+
     def destroy(self) -> None:
         if self.h:
             _check_global(load().qsml_group_destroy(self.h))
             self.h = None
+
+
+def shard_rows(rows: int, nranks: int, rank: int) -> tuple:
+    """(begin, count) of rank `rank`'s rows under the library's balanced split."""
+    b, c = ctypes.c_int64(), ctypes.c_int64()
+    _check_global(load().qsml_shard_rows(int(rows), int(nranks), int(rank), ctypes.byref(b), ctypes.byref(c)))
+    return b.value, c.value
 
 
 def group_start() -> None:
@@ -312,6 +341,15 @@ class Context:
 
     def synchronize(self) -> None:
         self.check(self.lib.qsml_synchronize(self.h))
+
+    def set_wait_limit(self, cycles: int) -> None:
+        """SM cycles after which a kernel waiting for data gives up with
+        QSML_E_TIMEOUT (0 = the default, about 1 s)."""
+        self.check(self.lib.qsml_set_wait_limit(self.h, cycles))
+
+    def finish_partial(self, op: int, partial: TDesc, n: int, out: TDesc) -> None:
+        """out from combined binary32 partials (a mean divides by n)."""
+        self.check(self.lib.qsml_finish_partial(self.h, int(op), ctypes.byref(partial), int(n), ctypes.byref(out)))
 
     def launch_count(self) -> int:
         n = ctypes.c_uint64()

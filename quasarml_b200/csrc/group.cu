@@ -147,6 +147,53 @@ bool map_op(int32_t op, ncclRedOp_t* out) {
     return false;
 }
 
+// Max/min partials cross the group as order-preserving unsigned keys, so the
+// exchange (an integer max/min) gives exactly what qsml_reduce's max.NaN /
+// min.NaN give on one GPU: -0 below +0, and any NaN wins (NaN maps to the
+// largest key for max and the smallest for min; it decodes to 0x7fffffff).
+// A float max/min in the collective would let a NaN or the sign of zero
+// depend on the order of ranks.
+__device__ __forceinline__ uint32_t key_of(uint32_t u, bool is_max) {
+    if ((u & 0x7fffffffu) > 0x7f800000u) return is_max ? 0xffffffffu : 0u;  // NaN
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ uint32_t value_of(uint32_t k, bool is_max) {
+    if (k == (is_max ? 0xffffffffu : 0u)) return 0x7fffffffu;
+    return (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+}
+
+__global__ void k_partial_keys(uint32_t* p, int64_t n, int is_max, int decode) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        p[i] = decode ? value_of(p[i], is_max != 0) : key_of(p[i], is_max != 0);
+}
+
+// out = partial (times scale for a mean), rounded once to out's dtype.
+template <typename OT>
+__global__ void k_partial_finish(const float* p, OT* out, int64_t n, float scale, int mul) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float v = mul ? __fmul_rn(p[i], scale) : p[i];
+        if constexpr (sizeof(OT) == 2) out[i] = __float2half_rn(v);
+        else out[i] = v;
+    }
+}
+
+unsigned grid_for(const Context* ctx, int64_t n) {
+    int64_t g = (n + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(ctx->num_sms) * 8;
+    if (g > cap) g = cap;
+    return static_cast<unsigned>(g < 1 ? 1 : g);
+}
+
+qsml_status_t keys_pass(Context* ctx, void* buf, int64_t n, int32_t op, bool decode) {
+    if (n == 0) return QSML_OK;
+    k_partial_keys<<<grid_for(ctx, n), 256, 0, ctx->stream>>>(static_cast<uint32_t*>(buf), n,
+                                                              op == QSML_RED_MAX ? 1 : 0, decode ? 1 : 0);
+    return after_launch(ctx, "k_partial_keys");
+}
+
 }  // namespace
 }  // namespace qsml
 
@@ -301,6 +348,118 @@ qsml_status_t qsml_allreduce(qsml_group* g, int32_t local, void* buf, int64_t co
     const qsml_status_t st = settle(C_, {g->comms[local]}, "qsml_allreduce");
     if (st != QSML_OK) g->failed = true;
     return st;
+}
+
+qsml_status_t qsml_allreduce_partials(qsml_group* g, int32_t local, int32_t op, void* buf, int64_t count) {
+    if (!g || local < 0 || local >= static_cast<int32_t>(g->comms.size()))
+        return set_error(nullptr, QSML_E_INVALID, "qsml_allreduce_partials: bad group or local rank");
+    Context* C_ = g->ctxs[local];
+    if (cudaSetDevice(C_->device) != cudaSuccess) return set_error(C_, QSML_E_CUDA, "cudaSetDevice failed");
+    if (g_group_depth > 0)
+        return set_error(C_, QSML_E_INVALID,
+                         "qsml_allreduce_partials: not inside qsml_group_start/end (its key decoding follows the exchange)");
+    if (op < QSML_RED_SUM || op > QSML_RED_MIN) return set_error(C_, QSML_E_INVALID, "qsml_allreduce_partials: unknown op");
+    if (count < 0 || (count > 0 && !buf)) return set_error(C_, QSML_E_INVALID, "qsml_allreduce_partials: bad buffer");
+    if (count == 0) return QSML_OK;
+    const bool keys = op == QSML_RED_MAX || op == QSML_RED_MIN;
+    if (keys) QSML_TRY_STATUS(keys_pass(C_, buf, count, op, false));
+    const ncclResult_t r = nccl().all_reduce(buf, buf, static_cast<size_t>(count), keys ? ncclUint32 : ncclFloat32,
+                                             op == QSML_RED_MAX ? ncclMax : op == QSML_RED_MIN ? ncclMin : ncclSum,
+                                             g->comms[local], C_->stream);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        g->failed = true;
+        return nccl_error(C_, r, "ncclAllReduce (partials)");
+    }
+    qsml_status_t st = settle(C_, {g->comms[local]}, "qsml_allreduce_partials");
+    if (st != QSML_OK) {
+        g->failed = true;
+        return st;
+    }
+    if (keys) QSML_TRY_STATUS(keys_pass(C_, buf, count, op, true));
+    return QSML_OK;
+}
+
+qsml_status_t qsml_finish_partial(qsml_ctx* handle, int32_t op, const qsml_tdesc* partial, int64_t n,
+                                  const qsml_tdesc* out) {
+    QSML_CTX(handle);
+    QSML_TRY_STATUS(check_desc(C_, partial, "partial"));
+    QSML_TRY_STATUS(check_desc(C_, out, "out"));
+    if (op < QSML_RED_SUM || op > QSML_RED_MIN) return set_error(C_, QSML_E_INVALID, "qsml_finish_partial: unknown op");
+    if (partial->dtype != QSML_F32) return set_error(C_, QSML_E_DTYPE, "qsml_finish_partial: partial must be F32");
+    if (out->dtype != QSML_F32 && out->dtype != QSML_F16)
+        return set_error(C_, QSML_E_DTYPE, "qsml_finish_partial: out must be F32 or F16");
+    if (!is_contiguous(partial) || !is_contiguous(out) || numel(partial) != numel(out))
+        return set_error(C_, QSML_E_SHAPE, "qsml_finish_partial: partial and out must be contiguous and equally long");
+    if (op == QSML_RED_MEAN && n < 1) return set_error(C_, QSML_E_INVALID, "qsml_finish_partial: mean needs n >= 1");
+    const int64_t count = numel(out);
+    const bool mul = op == QSML_RED_MEAN;
+    if (count == 0 || (!mul && out->dtype == QSML_F32 && out->data == partial->data)) return QSML_OK;
+    // the reference's mean: sum * (1.0f / (float)n) (Ops/Reduction.cpp:347-356)
+    const float scale = mul ? 1.0f / static_cast<float>(n) : 1.0f;
+    const float* p = static_cast<const float*>(partial->data);
+    if (out->dtype == QSML_F32)
+        k_partial_finish<float><<<grid_for(C_, count), 256, 0, C_->stream>>>(p, static_cast<float*>(out->data), count,
+                                                                           scale, mul ? 1 : 0);
+    else
+        k_partial_finish<__half><<<grid_for(C_, count), 256, 0, C_->stream>>>(p, static_cast<__half*>(out->data),
+                                                                             count, scale, mul ? 1 : 0);
+    return after_launch(C_, "k_partial_finish");
+}
+
+qsml_status_t qsml_reduce_sharded(qsml_group* g, int32_t local, int32_t op, const qsml_tdesc* a, int32_t axis,
+                                  int32_t keepdims, const qsml_tdesc* out, int64_t global_rows) {
+    if (!g || local < 0 || local >= static_cast<int32_t>(g->comms.size()))
+        return set_error(nullptr, QSML_E_INVALID, "qsml_reduce_sharded: bad group or local rank");
+    Context* C_ = g->ctxs[local];
+    qsml_ctx* h = reinterpret_cast<qsml_ctx*>(C_);
+    QSML_TRY_STATUS(check_desc(C_, a, "a"));
+    QSML_TRY_STATUS(check_desc(C_, out, "out"));
+    if (op < QSML_RED_SUM || op > QSML_RED_MIN) return set_error(C_, QSML_E_INVALID, "qsml_reduce_sharded: unknown op");
+    if (a->ndim < 1) return set_error(C_, QSML_E_SHAPE, "qsml_reduce_sharded: a needs a row axis");
+    const int ax = axis == QSML_AXIS_ALL ? QSML_AXIS_ALL : (axis < 0 ? axis + a->ndim : axis);
+    // Any axis but the row axis: this rank's rows of the result, no exchange.
+    if (ax != 0 && ax != QSML_AXIS_ALL) return qsml_reduce(h, op, a, axis, keepdims, out);
+    if (global_rows == 0) global_rows = a->shape[0] * g->nranks;
+    if (global_rows < a->shape[0]) return set_error(C_, QSML_E_SHAPE, "qsml_reduce_sharded: global_rows below this rank's rows");
+    int64_t row_elems = 1;
+    for (int i = 1; i < a->ndim; ++i) row_elems *= a->shape[i];
+    const int64_t n = ax == 0 ? global_rows : global_rows * row_elems;
+    const int64_t count = numel(out);
+    // the partial: out itself when it is binary32, else scratch
+    void* pbuf = out->data;
+    const bool scratch = out->dtype != QSML_F32;
+    if (scratch) {
+        std::string err;
+        qsml_status_t st = C_->allocator->alloc(static_cast<size_t>(count) * 4, &pbuf, &err);
+        if (st != QSML_OK) return set_error(C_, st, "qsml_reduce_sharded: " + err);
+    }
+    qsml_tdesc pd = *out;
+    pd.data = pbuf;
+    pd.dtype = QSML_F32;
+    qsml_status_t st = QSML_OK;
+    if (a->shape[0] == 0 && (op == QSML_RED_MAX || op == QSML_RED_MIN)) {
+        // no rows here: the identity of max / min
+        const float v = op == QSML_RED_MAX ? -INFINITY : INFINITY;
+        st = qsml_fill(h, pbuf, &v, 4, count);
+    } else {
+        st = qsml_reduce(h, op == QSML_RED_MEAN ? QSML_RED_SUM : op, a, axis, keepdims, &pd);
+    }
+    if (st == QSML_OK) st = qsml_allreduce_partials(g, local, op, pbuf, count);
+    if (st == QSML_OK) st = qsml_finish_partial(h, op, &pd, n, out);
+    if (scratch) {
+        std::string err;
+        C_->allocator->free(pbuf, &err);  // reused in stream order
+    }
+    return st;
+}
+
+qsml_status_t qsml_shard_rows(int64_t rows, int32_t nranks, int32_t rank, int64_t* begin, int64_t* count) {
+    if (rows < 0 || nranks < 1 || rank < 0 || rank >= nranks || !begin || !count)
+        return set_error(nullptr, QSML_E_INVALID, "qsml_shard_rows: bad arguments");
+    const int64_t base = rows / nranks, extra = rows % nranks;
+    *count = base + (rank < extra ? 1 : 0);
+    *begin = rank * base + (rank < extra ? rank : extra);
+    return QSML_OK;
 }
 
 qsml_status_t qsml_group_destroy(qsml_group* g) {

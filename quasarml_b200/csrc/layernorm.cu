@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
     const float n = static_cast<float>(cols);
     const bool ok = rowpipe::stream_rows(
         reinterpret_cast<const unsigned char*>(x), rows, static_cast<uint32_t>(cols * sizeof(T)), slots, ring, bars,
-        [&](int64_t row, unsigned char* buf) {
+        wait_limit(status), [&](int64_t row, unsigned char* buf) {
             const Pack<T>* xs = reinterpret_cast<const Pack<T>*>(buf);
             float part[PV];
 #pragma unroll
@@ -320,7 +320,8 @@ __global__ void __launch_bounds__(TH) k_layer_norm_wide(const T* __restrict__ x,
     const float n = static_cast<float>(cols);
     const bool ok = rowpipe::stream_rows_cta(
         reinterpret_cast<const unsigned char*>(x), rows, static_cast<uint32_t>(cols * sizeof(T)),
-        reinterpret_cast<unsigned char*>(ln_wide_smem), bars, [&](int64_t row, unsigned char* buf) {
+        reinterpret_cast<unsigned char*>(ln_wide_smem), bars, wait_limit(status),
+        [&](int64_t row, unsigned char* buf) {
             const Pack<T>* xs = reinterpret_cast<const Pack<T>*>(buf);
             float part[PV];
 #pragma unroll

@@ -42,7 +42,7 @@ namespace {
 constexpr int BM = 128;
 constexpr int GROUP_M = 16;
 constexpr int NUM_THREADS = 192;                    // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
-constexpr long long WAIT_CYCLES = 2000000000LL;     // ~1 s at 2 GHz
+constexpr long long WAIT_CYCLES = kDefaultWaitCycles;  // ~1 s at 2 GHz
 constexpr int C_BOX_BYTES = 32 * 128;               // epilogue staging: 32 rows x 128 bytes
 constexpr int C_STAGE_BYTES = 4 * 2 * C_BOX_BYTES;  // 4 epilogue warps x 2 buffers = 32 KiB
 
@@ -137,16 +137,32 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
+__device__ __forceinline__ bool mbar_probe(uint32_t bar, uint32_t parity) {  // never suspends
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // Bounded wait for the phase of `bar` with parity `parity`.  Returns false
-// (and raises the CTA's abort flag) if it does not complete in WAIT_CYCLES or
-// another role already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-    if (mbar_test(bar, parity)) return true;
+// (and raises the CTA's abort flag) if it does not complete in `limit` cycles
+// or another role already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          long long limit) {
+    // A lowered limit decides alone: poll with test_wait, which never
+    // suspends (try_wait may suspend the thread for a hardware-chosen time).
+    const bool short_limit = limit < WAIT_CYCLES;
+    if (!short_limit && mbar_test(bar, parity)) return true;
     const long long t0 = clock64();
     for (;;) {
-        if (mbar_test(bar, parity)) return true;
+        if (short_limit ? mbar_probe(bar, parity) : mbar_test(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (clock64() - t0 > WAIT_CYCLES) {
+        if (clock64() - t0 > limit) {
             *abort_flag = 1;
             return false;
         }
@@ -244,6 +260,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     unsigned char* gmisc = gbase + STAGES * L::STAGE + C_STAGE_BYTES + 8 * (2 * STAGES + 5);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gmisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gmisc + 4);
+    // Waits for data give up after the context's limit; the drain waits
+    // before exit keep the full WAIT_CYCLES.
+    const long long limit = wait_limit(status);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -287,7 +306,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tm.decode(t, b, mt, nt);
                 const int ab = a_batched ? b : 0, bb = b_batched ? b : 0;
                 for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, limit)) {
                         ok = false;
                         break;
                     }
@@ -325,11 +344,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t acc_phase = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
+                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag, limit)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
                 for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
+                    if (!mbar_wait(full_bar(stage), phase, abort_flag, limit)) {
                         ok = false;
                         break;
                     }
@@ -382,7 +401,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // one lane waits, the warp follows its result (tcgen05.ld needs
             // the whole warp converged)
             int ready = 0;
-            if (lane == 0) ready = mbar_wait(tfull_bar(acc), acc_phase, abort_flag) ? 1 : 0;
+            if (lane == 0) ready = mbar_wait(tfull_bar(acc), acc_phase, abort_flag, limit) ? 1 : 0;
             ready = __shfl_sync(0xffffffffu, ready, 0);
             if (!ready) break;
             tc_fence_after();
@@ -611,7 +630,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tm.decode(t, b, mt, nt);
                 const int ab = a_batched ? b : 0, bb = b_batched ? b : 0;
                 for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag, WAIT_CYCLES)) {
                         ok = false;
                         break;
                     }
@@ -639,11 +658,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t acc_phase = 0;
             bool ok = true;
             for (int t = cid; t < total && ok; t += nclusters) {
-                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
+                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag, WAIT_CYCLES)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * P_BN);
                 for (int kb = 0; kb < num_kb; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
+                    if (!mbar_wait(full_bar(stage), phase, abort_flag, WAIT_CYCLES)) {
                         ok = false;
                         break;
                     }
@@ -681,7 +700,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t tempty_leader1 = map_to_rank(tempty_bar(1), 0);
         for (int t = cid; t < total; t += nclusters) {
             int ready = 0;
-            if (lane == 0) ready = mbar_wait(tfull_bar(acc), acc_phase, abort_flag) ? 1 : 0;
+            if (lane == 0) ready = mbar_wait(tfull_bar(acc), acc_phase, abort_flag, WAIT_CYCLES) ? 1 : 0;
             ready = __shfl_sync(0xffffffffu, ready, 0);
             if (!ready) break;
             tc_fence_after();

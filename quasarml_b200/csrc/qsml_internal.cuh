@@ -57,7 +57,9 @@ struct Context {
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
     // Device word where kernels with bounded waits report QSML_E_TIMEOUT;
-    // qsml_synchronize reads and clears it.
+    // qsml_synchronize reads and clears it.  Layout of the 256-byte block:
+    // int at [0] the status code; int64 at byte 8 the wait limit in SM
+    // cycles (0 = kDefaultWaitCycles), set with qsml_set_wait_limit.
     int* status = nullptr;
     uint64_t launches = 0;
     const char* last_kernel = "";  // a string literal of the launch site
@@ -68,6 +70,19 @@ struct Context {
     std::mutex err_mu;
     std::string last_error;
 };
+
+// Bounded device-side waits ---------------------------------------------------
+// A kernel that waits on an mbarrier for data (a TMA or bulk copy, an MMA, a
+// peer warp) gives up after this many SM clock cycles (~1 s at 2 GHz),
+// records QSML_E_TIMEOUT in the context's status word and returns.  The
+// context may lower the limit (qsml_set_wait_limit); the waits that only let
+// a kernel's own copies and MMAs finish before it exits always keep this one.
+constexpr long long kDefaultWaitCycles = 2000000000LL;
+
+__device__ __forceinline__ long long wait_limit(const int* status) {
+    const long long v = *reinterpret_cast<const volatile long long*>(status + 2);
+    return v > 0 ? v : kDefaultWaitCycles;
+}
 
 // Error recording helpers ----------------------------------------------------
 qsml_status_t set_error(Context* ctx, qsml_status_t st, const std::string& msg);

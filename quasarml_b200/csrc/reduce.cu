@@ -36,6 +36,8 @@
 // Reduction.cpp:347-356; the reciprocal is rounded on the host.
 #include "qsml_internal.cuh"
 
+#include <cuda.h>
+
 #include <climits>
 
 namespace qsml {
@@ -568,10 +570,13 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
 // library holds its kNoAllocScratchBytes until the process exits.  In host
 // code its name is only a stand-in, so its device address is looked up with
 // cudaGetSymbolAddress once per device (first call on that device, with the
-// device current) and passed to the kernel.  All calls share the array and it
-// keeps the last call's contents, so the counters are cleared before every
-// launch; calls on the same GPU whose work overlaps (on different streams,
-// say) race on it.
+// device current) and passed to the kernel.  The address is cached per CUDA
+// context (its unique id from cuCtxGetId), so a host that resets the device
+// (cudaDeviceReset) and gets a new primary context, in which this module is
+// loaded afresh at another address, gets a fresh lookup on its next call.
+// All calls share the array and it keeps the last call's contents, so the
+// counters are cleared before every launch; calls on the same GPU whose work
+// overlaps (on different streams, say) race on it.
 // ---------------------------------------------------------------------------
 namespace qsml {
 namespace {
@@ -581,11 +586,42 @@ constexpr int64_t kNoAllocMaxRows = 64;                           // ticket coun
 constexpr size_t kNoAllocCounterBytes = 256;                      // 64 x u32
 constexpr int64_t kNoAllocMaxUnits =
     static_cast<int64_t>((kNoAllocScratchBytes - kNoAllocCounterBytes) / 4);  // 4-byte partials
+// The slicing rule caps every launch at kSegMaxUnits partials, so any request
+// that passes the row limit fits the array.
+static_assert(kNoAllocCounterBytes + kSegMaxUnits * 4 <= kNoAllocScratchBytes, "partials fit the array");
+static_assert(kNoAllocMaxRows * 4 <= static_cast<int64_t>(kNoAllocCounterBytes), "counters fit their region");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mu;
-std::map<int, void*> g_noalloc_addr;  // device -> device address of g_noalloc_scratch
+// (device, context id) -> device address of g_noalloc_scratch in that context
+std::map<std::pair<int, unsigned long long>, void*> g_noalloc_addr;
+
+// Unique id of the calling thread's current CUDA context (0 when the driver
+// cannot say, which then keys the cache by device alone).
+unsigned long long current_context_id() {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    using GetId = CUresult (*)(CUcontext, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(p);
+        cudaGetLastError();
+    });
+    CUcontext c = nullptr;
+    unsigned long long id = 0;
+    if (get_current && get_id && get_current(&c) == CUDA_SUCCESS && c && get_id(c, &id) == CUDA_SUCCESS) return id;
+    return 0;
+}
 
 qsml_status_t noalloc_scratch(void** ptr) {
     int dev = 0;
@@ -596,7 +632,10 @@ qsml_status_t noalloc_scratch(void** ptr) {
                                                    cudaGetErrorString(e));
     }
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    auto it = g_noalloc_addr.find(dev);
+    // With no context current yet (id 0) the lookup below creates the
+    // device's primary context; the address is then filed under its id.
+    const unsigned long long id = current_context_id();
+    auto it = g_noalloc_addr.find(std::make_pair(dev, id));
     if (it != g_noalloc_addr.end()) {
         *ptr = it->second;
         return QSML_OK;
@@ -608,7 +647,7 @@ qsml_status_t noalloc_scratch(void** ptr) {
         return set_error(nullptr, QSML_E_CUDA, std::string("qsml_reduce_noalloc: cudaGetSymbolAddress: ") +
                                                    cudaGetErrorString(e));
     }
-    g_noalloc_addr[dev] = p;
+    g_noalloc_addr[std::make_pair(dev, id != 0 ? id : current_context_id())] = p;
     *ptr = p;
     return QSML_OK;
 }

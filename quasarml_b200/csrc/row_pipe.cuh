@@ -10,9 +10,11 @@
 // registers, and no barrier couples the warps: each row is reduced with warp
 // shuffles only.
 //
-// Waits are bounded: a copy that has not landed after kWaitCycles makes the
-// warp stop, wait (bounded again) for its other copies in flight and report
-// failure; the kernel then records QSML_E_TIMEOUT in the context status word.
+// Waits are bounded: a copy that has not landed after the context's wait
+// limit (qsml_set_wait_limit; ~1 s by default) makes the warp stop, wait for
+// every copy it still has in flight -- the late one included, each bounded
+// by the full kWaitCycles -- and report failure; the kernel then records
+// QSML_E_TIMEOUT in the context status word.
 #pragma once
 
 #include "qsml_internal.cuh"
@@ -22,7 +24,7 @@ namespace rowpipe {
 
 constexpr int kMaxWarps = 16;
 constexpr int kMaxSlots = 4;
-constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 2 GHz
+constexpr long long kWaitCycles = kDefaultWaitCycles;  // ~1 s at 2 GHz
 constexpr size_t kRingBudget = 220 * 1024;       // dynamic shared memory per CTA
 constexpr uint32_t kMinRowBytes = 2048;
 
@@ -42,12 +44,40 @@ __device__ __forceinline__ bool bar_test(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
-__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
+// Never suspends the thread (mbarrier.try_wait, used above, may suspend it
+// for a hardware-chosen time before it answers).
+__device__ __forceinline__ bool bar_probe(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, long long limit) {
+    if (limit < kWaitCycles) {
+        // a lowered limit decides alone: poll without the hardware's suspend
+        const long long t0 = clock64();
+        while (!bar_probe(bar, parity))
+            if (clock64() - t0 > limit) return false;
+        return true;
+    }
     if (bar_test(bar, parity)) return true;
     const long long t0 = clock64();
     while (!bar_test(bar, parity))
-        if (clock64() - t0 > kWaitCycles) return false;
+        if (clock64() - t0 > limit) return false;
     return true;
+}
+
+// Waits up to kWaitCycles for a copy this kernel issued, before it exits.
+__device__ __forceinline__ void bar_drain(uint32_t bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!bar_test(bar, parity) && clock64() - t0 < kWaitCycles) {
+    }
 }
 
 // One bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
@@ -70,10 +100,10 @@ __device__ __forceinline__ float warp_sum(float v) {
 // through its buffers, calling body(row, buffer) with the whole warp.  `ring`
 // is the CTA's row area (warp w's buffer s at (w * slots + s) * row_bytes) and
 // `bars` the CTA's kMaxWarps * kMaxSlots mbarriers.  Returns false if a copy
-// did not land in time.
+// did not land within `limit` cycles.
 template <class Body>
 __device__ bool stream_rows(const unsigned char* src, int64_t rows, uint32_t row_bytes, int slots,
-                            unsigned char* ring, uint64_t* bars, Body&& body) {
+                            unsigned char* ring, uint64_t* bars, long long limit, Body&& body) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     const int64_t first = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
@@ -95,20 +125,17 @@ __device__ bool stream_rows(const unsigned char* src, int64_t rows, uint32_t row
         const int s = static_cast<int>(i % slots);
         const uint32_t parity = static_cast<uint32_t>((i / slots) & 1);
         int landed = 0;
-        if (lane == 0) landed = bar_wait(bar0 + 8u * s, parity) ? 1 : 0;
+        if (lane == 0) landed = bar_wait(bar0 + 8u * s, parity, limit) ? 1 : 0;
         landed = __shfl_sync(0xffffffffu, landed, 0);
         if (!landed) {
             ok = false;
-            // copies already issued into the other buffers land before the CTA exits
+            // every copy already issued -- the late one into buffer s and
+            // those into the other buffers -- lands before the CTA exits
             if (lane == 0)
-                for (int k = 1; k < slots; ++k) {
+                for (int k = 0; k < slots; ++k) {
                     const int64_t j = i + k;
                     if (first + j * nwarps >= rows) break;
-                    const int sk = static_cast<int>(j % slots);
-                    const long long t0 = clock64();
-                    while (!bar_test(bar0 + 8u * sk, static_cast<uint32_t>((j / slots) & 1)) &&
-                           clock64() - t0 < kWaitCycles) {
-                    }
+                    bar_drain(bar0 + 8u * static_cast<int>(j % slots), static_cast<uint32_t>((j / slots) & 1));
                 }
             __syncwarp();
             break;
@@ -146,7 +173,7 @@ constexpr int kWide256MaxPacks = 52 * 1024 / 16;
 
 template <class Body>
 __device__ bool stream_rows_cta(const unsigned char* src, int64_t rows, uint32_t row_bytes, unsigned char* ring,
-                                uint64_t* bars, Body&& body) {
+                                uint64_t* bars, long long limit, Body&& body) {
     const int64_t G = gridDim.x;
     const uint32_t bar0 = smem_addr(bars);
     if (threadIdx.x == 0) {
@@ -162,15 +189,15 @@ __device__ bool stream_rows_cta(const unsigned char* src, int64_t rows, uint32_t
     for (int64_t row = blockIdx.x; row < rows; row += G, ++i) {
         const int s = static_cast<int>(i & 1);
         const uint32_t parity = static_cast<uint32_t>((i >> 1) & 1);
-        const bool landed = bar_wait(bar0 + 8u * s, parity);
+        const bool landed = bar_wait(bar0 + 8u * s, parity, limit);
         if (__syncthreads_or(!landed)) {
-            // the other buffer's copy (if any) lands before the CTA exits
-            if (threadIdx.x == 0 && row + G < rows) {
-                const long long t0 = clock64();
-                while (!bar_test(bar0 + 8u * (s ^ 1), static_cast<uint32_t>(((i + 1) >> 1) & 1)) &&
-                       clock64() - t0 < kWaitCycles) {
-                }
+            // the late copy into buffer s and the other buffer's copy (if
+            // any) land before the CTA exits
+            if (threadIdx.x == 0) {
+                bar_drain(bar0 + 8u * s, parity);
+                if (row + G < rows) bar_drain(bar0 + 8u * (s ^ 1), static_cast<uint32_t>(((i + 1) >> 1) & 1));
             }
+            __syncthreads();
             return false;
         }
         unsigned char* buf = ring + s * row_bytes;

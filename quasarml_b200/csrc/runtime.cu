@@ -217,6 +217,10 @@ qsml_status_t get_scratch(Context* ctx, size_t bytes, void** ptr) {
     return QSML_OK;
 }
 
+__global__ void k_set_wait_limit(int* status, long long cycles) {
+    *reinterpret_cast<long long*>(status + 2) = cycles;
+}
+
 }  // namespace qsml
 
 using qsml::Context;
@@ -343,6 +347,14 @@ qsml_status_t qsml_synchronize(qsml_ctx* handle) {
                                              std::to_string(code) + ")");
     }
     return QSML_OK;
+}
+
+qsml_status_t qsml_set_wait_limit(qsml_ctx* handle, int64_t cycles) {
+    QSML_CTX(handle);
+    if (cycles < 0) return qsml::set_error(C_, QSML_E_INVALID, "qsml_set_wait_limit: negative limit");
+    // stream-ordered: kernels enqueued after this call see the new limit
+    qsml::k_set_wait_limit<<<1, 1, 0, C_->stream>>>(C_->status, static_cast<long long>(cycles));
+    return qsml::after_launch(C_, "k_set_wait_limit");
 }
 
 const char* qsml_last_error(qsml_ctx* handle) {

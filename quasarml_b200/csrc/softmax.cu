@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
     const int packs = cols / PV, lane = threadIdx.x & 31;
     const bool ok = rowpipe::stream_rows(
         reinterpret_cast<const unsigned char*>(x), rows, static_cast<uint32_t>(cols * sizeof(T)), slots, ring, bars,
-        [&](int64_t row, unsigned char* buf) {
+        wait_limit(status), [&](int64_t row, unsigned char* buf) {
             Pack<T>* xs = reinterpret_cast<Pack<T>*>(buf);
             float m = pack_max<T>(xs, packs, lane);
 #pragma unroll
@@ -280,7 +280,8 @@ __global__ void __launch_bounds__(TH) k_softmax_wide(const T* __restrict__ x, T*
     const int packs = cols / PV, t = threadIdx.x, th = blockDim.x;
     const bool ok = rowpipe::stream_rows_cta(
         reinterpret_cast<const unsigned char*>(x), rows, static_cast<uint32_t>(cols * sizeof(T)),
-        reinterpret_cast<unsigned char*>(sm_wide_smem), bars, [&](int64_t row, unsigned char* buf) {
+        reinterpret_cast<unsigned char*>(sm_wide_smem), bars, wait_limit(status),
+        [&](int64_t row, unsigned char* buf) {
             Pack<T>* xs = reinterpret_cast<Pack<T>*>(buf);
             const float m = rowpipe::cta_combine<true>(pack_max<T>(xs, packs, t, th), s_max);
             const float mk = __fmul_rn(m, 1.4426950408889634f);

@@ -1,23 +1,36 @@
-"""Data-parallel sharding of the reductions across ranks (one process per GPU).
+"""Row sharding of the workloads across ranks (one process per GPU).
 
-A global tensor X[N*64, 512, 1024] is split along axis 0; rank r holds rows
-[64r, 64r+64) (for batch entry b, elements start at flat offset
-(b*world + r) * shard_numel of the seeded stream).  Per-rank results combine:
+Every workload splits its global tensor along axis 0 and gives each rank a
+contiguous block of rows (qsml_shard_rows; in the benchmark every rank holds
+the configuration's full size, so the global tensor has N times its rows --
+weak scaling).  For batch entry b, rank r's block starts at flat offset
+(b*world + r) * shard_numel of the seeded stream, so the global tensor is the
+same whatever N.
 
-* axis 1 / axis 2: each rank's output is its own slice of the global output,
-  no exchange;
-* axis 0 / all elements: partial outputs are all-reduced -- sums and max/min
-  with the matching reduction; means as the all-reduced sum of per-rank means
-  times 1/world (every shard has the same size).
+Reductions (the only workload with an exchange):
 
-Exchanged outputs live in one flat buffer per (dtype, group), group one of
-"sum", "mean", "max", "min", so a step issues one all-reduce per buffer and
-one rescale per mean buffer.  The same plan drives bench.py (NCCL over
-NVLink) and the CPU test with gloo.
+* axis 1 / axis 2: each rank's output is its own row block of the global
+  output, no exchange;
+* axis 0 / all elements: each rank computes a binary32 partial with
+  qsml_reduce (SUM for sum and mean, MAX / MIN for max / min; binary16 inputs
+  give binary32 partials too, so sums are never combined in binary16), the
+  partials are packed into one flat buffer per combine group ("sum", "max",
+  "min": one qsml_allreduce_partials each, whatever the dtypes) and combined
+  across ranks, and qsml_finish_partial writes each output in its dtype.  A
+  mean is finished from the combined sum of the same input and axis as
+  sum * (1.0f / (float)n), n the elements reduced over all ranks -- the
+  reference's definition of mean (Ops/Reduction.cpp:347-356) -- so it needs
+  no partial of its own.
+
+ExchangePlan lays this out; bench.py drives it with the library (NCCL over
+NVLink) and tests/test_dist_cpu.py drives the same plan with gloo on CPU.
 """
 from __future__ import annotations
 
 SUM, MEAN, MAX, MIN = range(4)  # qsml_reduce codes
+AXIS_ALL = -1000
+
+GROUP_OF = {SUM: "sum", MEAN: "sum", MAX: "max", MIN: "min"}
 
 
 def shard_offset(batch_index: int, world: int, rank: int, shard_numel: int) -> int:
@@ -25,46 +38,50 @@ def shard_offset(batch_index: int, world: int, rank: int, shard_numel: int) -> i
     return (batch_index * world + rank) * shard_numel
 
 
+def shard_rows(rows: int, world: int, rank: int) -> tuple:
+    """(begin, count): the balanced contiguous split of qsml_shard_rows (the
+    first rows % world ranks hold one row more)."""
+    base, extra = divmod(rows, world)
+    return rank * base + min(rank, extra), base + (1 if rank < extra else 0)
+
+
 def needs_exchange(axis) -> bool:
     """Axis-0 and full reductions combine partials across ranks."""
-    return axis is None or axis == 0 or axis == -1000
+    return axis is None or axis == 0 or axis == AXIS_ALL
 
 
-def group(op: int) -> str:
-    """Flat-buffer group of reduction `op`'s exchanged outputs."""
-    return {SUM: "sum", MEAN: "mean", MAX: "max", MIN: "min"}[op]
+class ExchangePlan:
+    """Partials and finishing of the exchanged reductions of one step.
 
+    add(key, op, axis, count, n) registers the output of reduction `op` over
+    `axis` of input `key` (any hashable naming the input), `count` elements,
+    n elements reduced into each over all ranks.  Afterwards:
 
-def _group_of(key) -> str:
-    return key[-1] if isinstance(key, tuple) else key
+    * partials: (key, axis, group, offset, count) -- one local qsml_reduce
+      into the flat buffer of `group` at `offset` per entry; a mean shares the
+      sum's entry (its sum is added for it if the step has none);
+    * finishes: (op, group, offset, count, n, out_index) -- one
+      qsml_finish_partial per registered output, in registration order;
+    * sizes[group]: elements of each flat buffer.
+    """
 
+    def __init__(self):
+        self.sizes = {"sum": 0, "max": 0, "min": 0}
+        self.partials = []
+        self.finishes = []
+        self._slot = {}
 
-def exchange_start(dist, buffers: dict) -> list:
-    """Starts the all-reduce of every flat buffer (keys end in the group name)
-    and returns the work handles.  With NCCL the collectives run on NCCL's
-    stream after the work already enqueued on the current stream, so kernels
-    enqueued next overlap them."""
-    ops = {"sum": dist.ReduceOp.SUM, "mean": dist.ReduceOp.SUM, "max": dist.ReduceOp.MAX,
-           "min": dist.ReduceOp.MIN}
-    return [dist.all_reduce(buf, op=ops[_group_of(key)], async_op=True) for key, buf in buffers.items()]
+    def _partial(self, key, axis, group, count):
+        k = (key, axis, group)
+        if k not in self._slot:
+            off = self.sizes[group]
+            self.sizes[group] += count
+            self._slot[k] = off
+            self.partials.append((key, axis, group, off, count))
+        return self._slot[k]
 
-
-def exchange_finish(works: list, buffers: dict, world: int, scale_fn=None) -> None:
-    """Waits for the all-reduces (the current stream waits; the host does not
-    block with NCCL), then scales the mean buffers by 1/world.  `scale_fn(key,
-    factor)` rescales a buffer in place (the GPU path issues one
-    qsml_binary_scalar per buffer); without it the tensor's mul_ is used."""
-    for w in works:
-        w.wait()
-    if world > 1:
-        for key, buf in buffers.items():
-            if _group_of(key) == "mean":
-                if scale_fn is None:
-                    buf.mul_(1.0 / world)
-                else:
-                    scale_fn(key, 1.0 / world)
-
-
-def exchange(dist, buffers: dict, world: int, scale_fn=None) -> None:
-    """exchange_start + exchange_finish."""
-    exchange_finish(exchange_start(dist, buffers), buffers, world, scale_fn)
+    def add(self, key, op: int, axis, count: int, n: int) -> int:
+        group = GROUP_OF[op]
+        off = self._partial(key, axis, group, count)
+        self.finishes.append((op, group, off, count, n, len(self.finishes)))
+        return len(self.finishes) - 1

@@ -1,7 +1,10 @@
 """GPU layer norm (through the C ABI) against the oracle's binary64 result.
 
-Tolerance: |y - ref| <= 1e-5 * (1 + |ref|) for binary32 and
-1e-3 * (1 + |ref|) for binary16 (ref = binary64 result rounded once)."""
+Tolerance (ref = the binary64 result rounded once to the output dtype):
+|y - ref| <= bar * max(|ref|, 0.1), i.e. bar relative wherever |ref| >= 0.1
+and an absolute floor of bar * 0.1 for outputs nearer zero (where a relative
+bound would only measure the cancellation of (x - mean) * rstd * gamma
+against beta); bar = 1e-5 for binary32 and 1e-3 for binary16."""
 import numpy as np
 import pytest
 
@@ -20,7 +23,11 @@ def run(ctx, x, g, b, eps=1e-5):
 
 def assert_close(y, ref, tol):
     y64, r64 = y.astype(np.float64), ref.astype(np.float64)
-    worst = np.max(np.abs(y64 - r64) / (tol * (1.0 + np.abs(r64))))
+    err = np.abs(y64 - r64)
+    worst = np.max(err / (tol * np.maximum(np.abs(r64), 0.1)))
+    big = np.abs(r64) >= 0.1
+    rel = float(np.max(err[big] / np.abs(r64[big]))) if np.any(big) else 0.0
+    print(f"max relative error where |y| >= 0.1: {rel:.3g}; worst {worst:.3g} x tolerance (bar {tol:g})")
     assert worst <= 1.0, f"error {worst:.3g} x tolerance"
 
 

@@ -224,3 +224,18 @@ def test_argreduce_matches_numpy(orc):
     assert orc.argreduce(orc.ARGMIN, z) == np.argmin(z) == 0
     with pytest.raises(ValueError):
         orc.argreduce(orc.ARGMAX, np.zeros((3, 0), np.float32), 1)
+
+
+def test_matmul_check_sees_one_bad_output(orc):
+    """The full-matrix matmul check accepts a binary32 product and flags a
+    single output pushed outside the bar (a defect confined to one tile)."""
+    rng = np.random.default_rng(3)
+    a = rng.uniform(-1, 1, (2, 300, 200)).astype(np.float32)
+    b = rng.uniform(-1, 1, (2, 200, 150)).astype(np.float32)
+    c = np.matmul(a, b)
+    worst, normwise, _ = orc.matmul_check(c, a, b, rows_per_block=64)
+    assert worst <= 1e-5 and normwise <= 1e-6
+    bad = c.copy()
+    bad[1, 257, 149] += 1e-2 * np.abs(a[1, 257]) @ np.abs(b[1, :, 149])
+    worst, _, _ = orc.matmul_check(bad, a, b, rows_per_block=64)
+    assert worst >= 1e-2 * 0.99
