@@ -1,29 +1,36 @@
 #!/usr/bin/env python
 """Benchmark of the QuasarML B200 backend (libqsml_cuda.so through its C ABI).
 
-Headline workload (N=1 and every N): the reductions configuration --
-sum/mean/max/min over axis 0, 1, 2 and all elements of X[64,512,1024] ~ N(0,1),
-in fp32 and again with X in fp16 (fp32 accumulation).  One step processes a
-batch of 8 distinct X per dtype (1.5 GB of input, so no input is L2-resident
-when it is read again), i.e. 256 reduction calls.  Under torchrun each rank
-holds its own [64,512,1024] shards of a [64N,512,1024] tensor (weak scaling);
-axis-0 and full reductions combine their per-rank partials with NCCL
-all-reduces (torch.distributed) that run while the axis-1/2 reductions, which
-need no exchange, compute (two CUDA graphs per step, collectives between).
+Headline workload (every N): the reductions configuration -- sum/mean/max/min
+over axis 0, 1, 2 and all elements of X[64,512,1024] ~ N(0,1), in fp32 and
+again with X in fp16 (fp32 accumulation).  One step processes a batch of 8
+distinct X per dtype (1.5 GB of input, so no input is L2-resident when it is
+read again), i.e. 256 reduction calls at N=1.  Under torchrun X is
+row-sharded: each rank holds its own [64,512,1024] block of a
+[64N,512,1024] tensor (weak scaling).  The axis-1/2 reductions need no
+exchange; the axis-0 and full reductions write binary32 partials that the
+library combines across ranks (qsml_allreduce_partials, NCCL over NVLink, on
+a second stream while the axis-1/2 reductions run) and qsml_finish_partial
+turns into the outputs (means from the combined sums, sum * 1/n).
 
 value     : algorithmic bytes (each input read once, each output written once)
             of all ranks / max-over-ranks device time, inputs resident in HBM.
 e2e       : the same through the C ABI from pinned host buffers: every step
             copies X host->device and the results device->host inside the
             timed region.
-roofline  : the dominant kernel family of the step, its algorithmic bytes per
-            launch / its CUDA-event duration, against the measured HBM copy
-            bandwidth (MEASURED_PEAKS.json).
+roofline  : the dominant kernel family of the step (per input dtype), its
+            algorithmic bytes per launch / its CUDA-event duration, against
+            the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+exchange  : (N>1) the combine timed alone on its stream.
 cpu_baseline / --impl reference : the oracle's CPU restatement of the same
-            reductions (OpenMP over all host cores) on a bounded sample.
-other_workloads (N=1): the elementwise chain (op by op and fused), strided
+            reductions (OpenMP over all host cores), one X[64,512,1024] per
+            dtype per step.
+other_workloads: the elementwise chain (op by op and fused), strided
             gathers, layer norm, softmax, argmax/argmin and matmul
-            configurations, each timed the same way.
+            configurations, each row-sharded over the ranks and timed the
+            same way: weak scaling at every N (each rank the configuration's
+            size) and, at N>1, strong scaling too (the configuration's tensor
+            split N ways, "<name>_strong").
 """
 from __future__ import annotations
 
@@ -156,6 +163,14 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
+    def sum(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return float(t.item())
+
     def close(self):
         if self.pg:
             self.pg.destroy_process_group()
@@ -182,8 +197,30 @@ def _t(x):
     return torch.from_numpy(np.ascontiguousarray(x)).cuda()
 
 
+class RCall:
+    """One library call of the reductions step: kind "reduce" (qsml_reduce of
+    x over axis into out) or "finish" (qsml_finish_partial of partial x into
+    out, n elements per output); nbytes its algorithmic bytes; out_t the
+    output tensor; entry the batch entry it reads (None for a finish); dt
+    "f32" or "f16", the input dtype (for the per-dtype roofline families)."""
+    __slots__ = ("kind", "op", "x", "axis", "out", "n", "nbytes", "out_t", "entry", "dt")
+
+    def __init__(self, kind, op, x, axis, out, nbytes, out_t, entry, dt, n=0):
+        self.kind, self.op, self.x, self.axis, self.out = kind, op, x, axis, out
+        self.nbytes, self.out_t, self.entry, self.dt, self.n = nbytes, out_t, entry, dt, n
+
+
 class ReduceWorkload(Workload):
-    """sum/mean/max/min over axis 0, 1, 2, all of X[64,512,1024], fp32 + fp16."""
+    """sum/mean/max/min over axis 0, 1, 2, all of X[64,512,1024], fp32 + fp16.
+
+    N=1: 256 qsml_reduce calls per step.  N>1 (X row-sharded, rank r holding
+    rows [64r, 64r+64) of X[64N,512,1024]): the axis-1/2 reductions are local
+    (qsml_reduce, no exchange); for axis 0 and all elements each rank writes
+    binary32 partials (SUM, MAX, MIN) into three flat buffers, the library
+    combines each buffer across ranks (qsml_allreduce_partials on a second
+    context's stream, NCCL over NVLink, while the axis-1/2 reductions run) and
+    qsml_finish_partial writes the outputs: sums and max/min as combined, means
+    as the combined sum * (1/n) with n counted over all ranks."""
     name = "reductions X[64,512,1024] fp32 and fp16: sum/mean/max/min over axis 0, 1, 2 and all"
     SHAPE = (64, 512, 1024)
 
@@ -203,91 +240,144 @@ class ReduceWorkload(Workload):
         torch.cuda.synchronize()
         self.ops = [abi.RED_SUM, abi.RED_MEAN, abi.RED_MAX, abi.RED_MIN]
         self.axes = [None, 0, 1, 2]
-        # Output buffers: the exchanged ones (axis None / 0) live in one flat
-        # buffer per (dtype, combine op) so each step all-reduces few buffers.
-        self.calls = []       # (op, x, axis, out_tensor, family, bytes)
-        self.flat = {}        # (dtype, 'sum'|'max'|'min') -> flat tensor
-        self.bytes_per_step = 0
+        self.sharded = dist.world > 1
+        # calls_l: reductions needing no exchange (all of them at N=1);
+        # calls_x: the local partials of the exchanged ones; finishes: after
+        # the exchange.  Batch entry innermost everywhere: consecutive calls
+        # read different X, and a given X is read again only after the other
+        # seven (>= 448 MB), so no call finds its input in L2.
+        self.calls_l, self.calls_x, self.finishes = [], [], []
+        self.keep = []
         for dt, xs in (("f32", self.x32), ("f16", self.x16)):
             tdt = torch.float32 if dt == "f32" else torch.float16
             es = 4 if dt == "f32" else 2
-            sizes = {"sum": 0, "mean": 0, "max": 0, "min": 0}
-            # batch entry innermost: consecutive calls read different X, and a
-            # given X is read again only after the other seven (>= 448 MB), so
-            # no call finds its input in L2
-            plan = []
             for axis in self.axes:
+                code = abi.AXIS_ALL if axis is None else axis
                 oshape = abi.reduced_shape(self.SHAPE, axis, False)
                 on = int(np.prod(oshape))
+                if self.sharded and sharding.needs_exchange(axis):
+                    continue
                 for op in self.ops:
-                    grp = sharding.group(op)
-                    exch = sharding.needs_exchange(axis)
                     for b in range(batch):
-                        plan.append((b, axis, op, oshape, on, grp, exch))
-                        if exch:
-                            sizes[grp] += on
-            for g, sz in sizes.items():
-                self.flat[(dt, g)] = torch.empty(max(sz, 1), dtype=tdt, device="cuda")
-            offs = {g: 0 for g in sizes}
-            for (b, axis, op, oshape, on, grp, exch) in plan:
-                if exch:
-                    out = self.flat[(dt, grp)][offs[grp]:offs[grp] + on].view(oshape)
-                    offs[grp] += on
-                else:
-                    out = torch.empty(oshape, dtype=tdt, device="cuda")
-                fam = "k_reduce_seg" if axis is None else ("k_reduce_rows" if axis == 2 else "k_reduce_cols")
-                nbytes = n * es + on * es
-                self.calls.append((op, abi.desc_of(xs[b]), abi.AXIS_ALL if axis is None else axis,
-                                   abi.desc_of(out), fam, nbytes, out))
-                self.bytes_per_step += nbytes
+                        out = torch.empty(oshape, dtype=tdt, device="cuda")
+                        self.calls_l.append(RCall("reduce", op, abi.desc_of(xs[b]), code, abi.desc_of(out),
+                                                  n * es + on * es, out, b, dt))
+        if self.sharded:
+            self._plan_exchange(batch, n)
+        self.calls = self.calls_x + self.calls_l + self.finishes
+        self.bytes_per_step = sum(c.nbytes for c in self.calls)
         self.units_per_step = self.bytes_per_step
         self.unit = "GB/s"
-        self.flat_desc = {k: abi.desc_of(v) for k, v in self.flat.items()}
         self.h2d_bytes = sum(x.numel() * 4 for x in self.x32) + sum(x.numel() * 2 for x in self.x16)
-        self.d2h_bytes = sum(c[6].numel() * c[6].element_size() for c in self.calls)
+        self.d2h_bytes = sum(o.numel() * o.element_size() for o in self.outputs())
+
+    def _plan_exchange(self, batch, n):
+        import torch
+        from quasarml_b200 import sharding
+        abi = self.abi
+        plan = sharding.ExchangePlan()
+        G = self.dist.world * self.SHAPE[0]  # rows of the global X
+        runs = []  # (dt, axis, op, per-entry count, finish index)
+        for dt in ("f32", "f16"):
+            for axis in (None, 0):
+                on = int(np.prod(abi.reduced_shape(self.SHAPE, axis, False)))
+                # elements reduced into each output over all ranks
+                nglob = G * (n // self.SHAPE[0]) if axis is None else G
+                for op in self.ops:
+                    runs.append((dt, axis, op, on, plan.add((dt, axis), op, axis, batch * on, nglob)))
+        self.flat = {g: torch.empty(max(sz, 1), dtype=torch.float32, device="cuda") for g, sz in plan.sizes.items()}
+        group_op = {"sum": abi.RED_SUM, "max": abi.RED_MAX, "min": abi.RED_MIN}
+        for (dt, axis), ax, group, off, count in plan.partials:
+            xs, es = (self.x32, 4) if dt == "f32" else (self.x16, 2)
+            oshape = abi.reduced_shape(self.SHAPE, axis, False)
+            on = count // batch
+            for b in range(batch):
+                part = self.flat[group][off + b * on: off + (b + 1) * on].view(oshape)
+                self.calls_x.append(RCall("reduce", group_op[group], abi.desc_of(xs[b]),
+                                          abi.AXIS_ALL if axis is None else axis, abi.desc_of(part),
+                                          n * es + on * 4, part, b, dt))
+        self.exchanged_out = []
+        for (dt, axis, op, on, fi) in runs:
+            fop, group, off, count, nglob, _ = plan.finishes[fi]
+            part = self.flat[group][off:off + count]
+            if dt == "f32" and op != abi.RED_MEAN:
+                out = part  # the combined partial is the result
+            else:
+                out = torch.empty(count, dtype=torch.float32 if dt == "f32" else torch.float16, device="cuda")
+                es = 4 if dt == "f32" else 2
+                self.finishes.append(RCall("finish", op, abi.desc_of(part), None, abi.desc_of(out),
+                                           count * 4 + count * es, out, None, dt, n=nglob))
+            self.exchanged_out.append(out)
+        self.group = None
+
+    def outputs(self):
+        outs = [c.out_t for c in self.calls_l]
+        if self.sharded:
+            outs += self.exchanged_out
+        return outs
 
     def compute(self, calls=None):
         ctx = self.ctx
-        for (op, xd, axis, od, fam, nb, out) in (self.calls if calls is None else calls):
-            ctx.reduce(op, xd, axis, False, od)
+        for c in (self.calls_l if calls is None else calls):
+            if c.kind == "reduce":
+                ctx.reduce(c.op, c.x, c.axis, False, c.out)
+            else:
+                ctx.finish_partial(c.op, c.x, c.n, c.out)
+
+    # The library's own collective: a group over a second context whose stream
+    # runs the combines while the main stream runs the local reductions.
+    def init_exchange(self):
+        if not self.sharded or self.group is not None:
+            return
+        import torch
+        abi = self.abi
+        self.xstream = torch.cuda.Stream()
+        self.xctx = abi.Context(torch.cuda.current_device(), use_torch_stream=False)
+        self.xctx.set_stream(self.xstream.cuda_stream)
+        uid = [abi.group_unique_id() if self.dist.rank == 0 else None]
+        self.dist.pg.broadcast_object_list(uid, src=0)
+        self.group = abi.Group.init_rank(self.xctx, uid[0], self.dist.world, self.dist.rank)
+        self.ev_ready, self.ev_done = torch.cuda.Event(), torch.cuda.Event()
+
+    def close_exchange(self):
+        if getattr(self, "group", None) is not None:
+            import torch
+            torch.cuda.synchronize()
+            self.group.destroy()
+            self.group = None
+            self.xctx.close()
+
+    def exchange_start(self):
+        if not self.sharded:
+            return None
+        import torch
+        abi = self.abi
+        self.init_exchange()
+        self.ev_ready.record(torch.cuda.current_stream())
+        self.xstream.wait_event(self.ev_ready)
+        for g, op in (("sum", abi.RED_SUM), ("max", abi.RED_MAX), ("min", abi.RED_MIN)):
+            self.group.allreduce_partials(0, op, self.flat[g].data_ptr(), self.flat[g].numel())
+        self.ev_done.record(self.xstream)
+        return self.ev_done
+
+    def exchange_finish(self, done):
+        if not self.sharded:
+            return
+        import torch
+        torch.cuda.current_stream().wait_event(done)
+        self.compute(self.finishes)
 
     def exchange(self):
         self.exchange_finish(self.exchange_start())
 
-    # Overlapped step: the exchanged reductions (axis 0 and full) first, their
-    # all-reduces started, the local ones (axes 1, 2) while NCCL runs, then
-    # the wait and the mean rescale.
-    @property
-    def calls_x(self):
-        return [c for c in self.calls if c[2] in (0, self.abi.AXIS_ALL)]
-
-    @property
-    def calls_l(self):
-        return [c for c in self.calls if c[2] not in (0, self.abi.AXIS_ALL)]
-
-    def exchange_start(self):
-        if not self.dist.pg:
-            return []
-        from quasarml_b200 import sharding
-        return sharding.exchange_start(self.dist.pg, self.flat)
-
-    def exchange_finish(self, works):
-        if not self.dist.pg:
-            return
-        from quasarml_b200 import sharding
-        abi, ctx = self.abi, self.ctx
-        sharding.exchange_finish(works, self.flat, self.dist.world,
-                                 scale_fn=lambda key, f: ctx.binary_scalar(abi.OP_MUL, self.flat_desc[key], f,
-                                                                            self.flat_desc[key]))
-
     def step(self):
-        if not self.dist.pg:
+        if not self.sharded:
             self.compute()
             return
         self.compute(self.calls_x)
-        works = self.exchange_start()
+        done = self.exchange_start()
         self.compute(self.calls_l)
-        self.exchange_finish(works)
+        self.exchange_finish(done)
 
     # End-to-end: host -> device copies of X, the reductions, results back.
     # The uploads run on a second library context (its own stream, a copy
@@ -297,9 +387,12 @@ class ReduceWorkload(Workload):
     def e2e_setup(self):
         import torch
         from quasarml_b200 import abi
+        self.init_exchange()
         self.h32 = [x.cpu().pin_memory() for x in self.x32]
         self.h16 = [x.cpu().pin_memory() for x in self.x16]
-        self.hout = [c[6].cpu().pin_memory() for c in self.calls]
+        self.local_out = [c.out_t for c in self.calls_l]
+        self.hout = [o.cpu().pin_memory() for o in self.local_out]
+        self.hxout = [o.cpu().pin_memory() for o in self.exchanged_out] if self.sharded else []
         self.copy_stream = torch.cuda.Stream()
         self.copy_ctx = abi.Context(torch.cuda.current_device())
         self.copy_ctx.set_stream(self.copy_stream.cuda_stream)
@@ -308,14 +401,8 @@ class ReduceWorkload(Workload):
         self.back_ctx.set_stream(self.back_stream.cuda_stream)
         self.landed = [torch.cuda.Event() for _ in range(self.batch)]
         self.reduced = [torch.cuda.Event() for _ in range(self.batch)]
-        self.calls_by_entry = [[i for i, c in enumerate(self.calls) if self._entry(c) == b] for b in range(self.batch)]
-
-    def _entry(self, call):
-        ptr = call[1].data
-        for b in range(self.batch):
-            if ptr in (self.x32[b].data_ptr(), self.x16[b].data_ptr()):
-                return b
-        raise ValueError("call input is not one of the batch entries")
+        self.l_by_entry = [[i for i, c in enumerate(self.calls_l) if c.entry == b] for b in range(self.batch)]
+        self.x_by_entry = [[c for c in self.calls_x if c.entry == b] for b in range(self.batch)]
 
     def e2e_step(self):
         import torch
@@ -325,55 +412,65 @@ class ReduceWorkload(Workload):
             self.copy_ctx.h2d(self.x32[b].data_ptr(), self.h32[b].data_ptr(), self.h32[b].numel() * 4)
             self.copy_ctx.h2d(self.x16[b].data_ptr(), self.h16[b].data_ptr(), self.h16[b].numel() * 2)
             self.landed[b].record(self.copy_stream)
-        # Results travel back on a third stream as each entry finishes (the
-        # other PCIe direction), except the exchanged ones at N > 1, which are
-        # read after the all-reduces.
-        exchanged = set()
-        if self.dist.pg:
-            exchanged = {i for i, c in enumerate(self.calls) if c[2] in (0, self.abi.AXIS_ALL)}
+        # Local results travel back on a third stream as each entry finishes
+        # (the other PCIe direction); exchanged ones after the combine.
         for b in range(self.batch):
             cur.wait_event(self.landed[b])
-            self.compute([self.calls[i] for i in self.calls_by_entry[b]])
+            self.compute(self.x_by_entry[b])
+            self.compute([self.calls_l[i] for i in self.l_by_entry[b]])
             self.reduced[b].record(cur)
             self.back_stream.wait_event(self.reduced[b])
-            for i in self.calls_by_entry[b]:
-                if i not in exchanged:
-                    out = self.calls[i][6]
-                    self.back_ctx.d2h(self.hout[i].data_ptr(), out.data_ptr(), out.numel() * out.element_size(),
-                                      sync=False)
-        if self.dist.pg:
+            for i in self.l_by_entry[b]:
+                out = self.local_out[i]
+                self.back_ctx.d2h(self.hout[i].data_ptr(), out.data_ptr(), out.numel() * out.element_size(),
+                                  sync=False)
+        if self.sharded:
             self.exchange_finish(self.exchange_start())
-            for i in sorted(exchanged):
-                out = self.calls[i][6]
-                self.ctx.d2h(self.hout[i].data_ptr(), out.data_ptr(), out.numel() * out.element_size(), sync=False)
+            for h, out in zip(self.hxout, self.exchanged_out):
+                self.ctx.d2h(h.data_ptr(), out.data_ptr(), out.numel() * out.element_size(), sync=False)
         cur.wait_stream(self.back_stream)
 
 
+def row_block(total_rows: int, dist: Dist, scale: str):
+    """(first global row, rows, global rows) of this rank's block of a
+    tensor whose configuration has `total_rows` rows.  weak: every rank holds
+    `total_rows` rows of an N-times-taller tensor; strong: the configuration's
+    own tensor is split over the ranks (qsml_shard_rows' balanced split)."""
+    if scale == "weak" or dist.world == 1:
+        return dist.rank * total_rows, total_rows, total_rows * dist.world
+    from quasarml_b200 import abi
+    b, c = abi.shard_rows(total_rows, dist.world, dist.rank)
+    return b, c, total_rows
+
+
 class ChainWorkload(Workload):
-    """relu(pow((A+B)*B - A, 2) / D), A[4096,4096], B[1,4096], D[4096,1]."""
+    """relu(pow((A+B)*B - A, 2) / D), A[4096,4096], B[1,4096], D[4096,1]:
+    A and D row-sharded, B replicated."""
     name = "elementwise chain relu(pow((A+B)*B - A, 2.0) / D), A[4096,4096], B[1,4096], D[4096,1] fp32"
 
-    def __init__(self, ctx, dist: Dist, batch: int = 4):
+    def __init__(self, ctx, dist: Dist, batch: int = 4, scale: str = "weak"):
         import torch
         from quasarml_b200 import abi, datagen
         self.ctx, self.abi = ctx, abi
-        N = 4096 * 4096
+        r0, R, G = row_block(4096, dist, scale)
         self.sets = []
         for b in range(batch):
-            A = _t(datagen.uniform(datagen.SEEDS["ew_A"], (4096, 4096), -1, 1, offset=(b * dist.world + dist.rank) * N))
+            off = b * G + r0  # batch entry b is its own [G, 4096] tensor
+            A = _t(datagen.uniform(datagen.SEEDS["ew_A"], (R, 4096), -1, 1, offset=off * 4096))
             B = _t(datagen.uniform(datagen.SEEDS["ew_B"], (1, 4096), -1, 1))
-            D = _t(datagen.uniform(datagen.SEEDS["ew_D"], (4096, 1), 0.5, 2, offset=(b * dist.world + dist.rank) * 4096))
-            ts = [torch.empty((4096, 4096), device="cuda") for _ in range(6)]
+            D = _t(datagen.uniform(datagen.SEEDS["ew_D"], (R, 1), 0.5, 2, offset=off))
+            ts = [torch.empty((R, 4096), device="cuda") for _ in range(6)]
             self.sets.append((A, B, D, ts))
         d = abi.desc_of
+        n4 = R * 4096 * 4
         self.calls = []
         for A, B, D, t in self.sets:
-            self.calls += [("bin", abi.OP_ADD, d(A), d(B), d(t[0]), 134234112),
-                           ("bin", abi.OP_MUL, d(t[0]), d(B), d(t[1]), 134234112),
-                           ("bin", abi.OP_SUB, d(t[1]), d(A), d(t[2]), 201326592),
-                           ("scal", abi.OP_POW, d(t[2]), 2.0, d(t[3]), 134217728),
-                           ("bin", abi.OP_DIV, d(t[3]), d(D), d(t[4]), 134234112),
-                           ("un", abi.UN_RELU, d(t[4]), None, d(t[5]), 134217728)]
+            self.calls += [("bin", abi.OP_ADD, d(A), d(B), d(t[0]), 2 * n4 + 16384),
+                           ("bin", abi.OP_MUL, d(t[0]), d(B), d(t[1]), 2 * n4 + 16384),
+                           ("bin", abi.OP_SUB, d(t[1]), d(A), d(t[2]), 3 * n4),
+                           ("scal", abi.OP_POW, d(t[2]), 2.0, d(t[3]), 2 * n4),
+                           ("bin", abi.OP_DIV, d(t[3]), d(D), d(t[4]), 2 * n4 + R * 4),
+                           ("un", abi.UN_RELU, d(t[4]), None, d(t[5]), 2 * n4)]
         self.units_per_step = sum(c[5] for c in self.calls)
         self.unit = "GB/s"
 
@@ -394,11 +491,11 @@ class FusedChainWorkload(Workload):
     name = ("elementwise chain relu(pow((A+B)*B - A, 2.0) / D) fused into one kernel, A[4096,4096], B[1,4096], "
             "D[4096,1] fp32")
 
-    def __init__(self, ctx, dist: Dist, batch: int = 4):
+    def __init__(self, ctx, dist: Dist, batch: int = 4, scale: str = "weak"):
         import torch
         from quasarml_b200 import abi, datagen
         self.ctx = ctx
-        N = 4096 * 4096
+        r0, R, G = row_block(4096, dist, scale)
         e = abi.Expr()
         a, b, dd = e.input(0), e.input(1), e.input(2)
         t = e.binary(abi.OP_SUB, e.binary(abi.OP_MUL, e.binary(abi.OP_ADD, a, b), b), a)
@@ -407,13 +504,13 @@ class FusedChainWorkload(Workload):
         self.keep, self.calls = [], []
         d = abi.desc_of
         for bi in range(batch):
-            off = (bi * dist.world + dist.rank)
-            A = _t(datagen.uniform(datagen.SEEDS["ew_A"], (4096, 4096), -1, 1, offset=off * N))
+            off = bi * G + r0
+            A = _t(datagen.uniform(datagen.SEEDS["ew_A"], (R, 4096), -1, 1, offset=off * 4096))
             B = _t(datagen.uniform(datagen.SEEDS["ew_B"], (1, 4096), -1, 1))
-            D = _t(datagen.uniform(datagen.SEEDS["ew_D"], (4096, 1), 0.5, 2, offset=off * 4096))
-            out = torch.empty((4096, 4096), device="cuda")
+            D = _t(datagen.uniform(datagen.SEEDS["ew_D"], (R, 1), 0.5, 2, offset=off))
+            out = torch.empty((R, 4096), device="cuda")
             self.keep += [A, B, D, out]
-            self.calls.append(([d(A), d(B), d(D)], d(out), 2 * N * 4 + 2 * 4096 * 4))
+            self.calls.append(([d(A), d(B), d(D)], d(out), 2 * R * 4096 * 4 + 4096 * 4 + R * 4))
         self.units_per_step = sum(c[2] for c in self.calls)
         self.unit = "GB/s"
 
@@ -423,23 +520,35 @@ class FusedChainWorkload(Workload):
 
 
 class GatherWorkload(Workload):
+    """X[5::3, 1::2] and X.T[::4, :] of X[8192,8192], X row-sharded: each rank
+    materialises the output rows whose source rows it holds (X[5::3, 1::2])
+    and the output columns of its rows (X.T[::4, :], out[i, j] = X[j, 4i]),
+    each as a contiguous block."""
     name = "strided gather X[5::3, 1::2] and X.T[::4, :] of X[8192,8192] int32 and fp32"
 
-    def __init__(self, ctx, dist: Dist):
+    def __init__(self, ctx, dist: Dist, scale: str = "weak"):
         import torch
         from quasarml_b200 import abi, datagen
         self.ctx = ctx
-        Xi = _t(datagen.iota_i32((8192, 8192)))
-        Xf = _t(datagen.uniform(datagen.SEEDS["gather_f32"], (8192, 8192), -1, 1))
+        r0, R, G = row_block(8192, dist, scale)
+        rows = (np.arange(R, dtype=np.int64) + r0)[:, None] * 8192 + np.arange(8192, dtype=np.int64)[None, :]
+        Xi = _t(rows.astype(np.int32))  # X[i, j] = i*8192 + j over the global rows
+        Xf = _t(datagen.uniform(datagen.SEEDS["gather_f32"], (R, 8192), -1, 1, offset=r0 * 8192))
         self.keep = [Xi, Xf]
+        # X[5::3, 1::2]: global source rows 5 + 3i inside this block
+        s0 = max(5, r0 + ((5 - r0) % 3))
+        n1 = len(range(s0, r0 + R, 3))
+        self.first_out_row = (s0 - 5) // 3
         self.calls = []
         for X, code in ((Xi, abi.I32), (Xf, abi.F32)):
-            o1 = torch.empty((2729, 4096), dtype=X.dtype, device="cuda")
-            o2 = torch.empty((2048, 8192), dtype=X.dtype, device="cuda")
+            o1 = torch.empty((n1, 4096), dtype=X.dtype, device="cuda")
+            o2 = torch.empty((2048, R), dtype=X.dtype, device="cuda")
             self.keep += [o1, o2]
-            v1 = abi.make_desc(X.data_ptr() + (5 * 8192 + 1) * 4, code, (2729, 4096), (3 * 8192, 2))
-            v2 = abi.make_desc(X.data_ptr(), code, (2048, 8192), (4, 8192))
-            self.calls += [(v1, abi.desc_of(o1), 134135808), (v2, abi.desc_of(o2), 335544320)]
+            v1 = abi.make_desc(X.data_ptr() + ((s0 - r0) * 8192 + 1) * 4, code, (n1, 4096), (3 * 8192, 2))
+            v2 = abi.make_desc(X.data_ptr(), code, (2048, R), (4, 8192))
+            # bytes: writes + the read footprint in 32-byte sectors
+            self.calls += [(v1, abi.desc_of(o1), n1 * (4096 * 4 + 8192 * 4)),
+                           (v2, abi.desc_of(o2), 2048 * R * 4 + R * 8192 * 4)]
         self.units_per_step = sum(c[2] for c in self.calls)
         self.unit = "GB/s"
 
@@ -449,27 +558,36 @@ class GatherWorkload(Workload):
 
 
 class ArgReduceWorkload(Workload):
+    """argmax/argmin of X[64,512,1024], fp32 and fp16.  Under sharding only the
+    axes whose result needs no exchange (1 and 2) run."""
     name = "argmax/argmin X[64,512,1024] fp32 and fp16 over axis 0, 1, 2 and all, I32 indices (4 distinct X per dtype)"
     SHAPE = (64, 512, 1024)
 
-    def __init__(self, ctx, dist: Dist, batch: int = 4):
+    def __init__(self, ctx, dist: Dist, batch: int = 4, scale: str = "weak"):
         import torch
         from quasarml_b200 import abi, datagen
         self.ctx = ctx
-        n = int(np.prod(self.SHAPE))
+        r0, R, G = row_block(self.SHAPE[0], dist, scale)
+        shape = (R,) + self.SHAPE[1:]
+        n = int(np.prod(shape))
+        per_row = int(np.prod(self.SHAPE[1:]))
+        axes = (None, 0, 1, 2) if dist.world == 1 else (1, 2)
+        if dist.world > 1:
+            self.name = ("argmax/argmin X[64,512,1024] fp32 and fp16 over axis 1 and 2 (row-local under sharding), "
+                         "I32 indices (4 distinct X per dtype)")
         # `batch` distinct X per dtype, batch entry innermost in the call order:
         # no call finds its input in L2
         self.keep = []
         xs32, xs16 = [], []
         for b in range(batch):
-            X = _t(datagen.normal(datagen.SEEDS["red_X"], self.SHAPE, 0.0, 1.0, offset=(b * dist.world + dist.rank) * n))
+            X = _t(datagen.normal(datagen.SEEDS["red_X"], shape, 0.0, 1.0, offset=(b * G + r0) * per_row))
             xs32.append(X)
             xs16.append(X.half())
         self.keep += xs32 + xs16
         self.calls = []
         for xs, es in ((xs32, 4), (xs16, 2)):
-            for axis in (None, 0, 1, 2):
-                oshape = abi.reduced_shape(self.SHAPE, axis, False)
+            for axis in axes:
+                oshape = abi.reduced_shape(shape, axis, False)
                 for op in (abi.ARG_MAX, abi.ARG_MIN):
                     for x in xs:
                         out = torch.empty(oshape, dtype=torch.int32, device="cuda")
@@ -487,19 +605,20 @@ class ArgReduceWorkload(Workload):
 class LayerNormWorkload(Workload):
     name = "layer norm X[16384,4096] fp32 and fp16, gamma/beta fp32, eps 1e-5"
 
-    def __init__(self, ctx, dist: Dist):
+    def __init__(self, ctx, dist: Dist, scale: str = "weak"):
         import torch
         from quasarml_b200 import abi, datagen
         self.ctx = ctx
-        n = 16384 * 4096
-        X = _t(datagen.normal(datagen.SEEDS["ln_X"], (16384, 4096), 0.5, 2.0, offset=dist.rank * n))
+        r0, R, G = row_block(16384, dist, scale)
+        X = _t(datagen.normal(datagen.SEEDS["ln_X"], (R, 4096), 0.5, 2.0, offset=r0 * 4096))
         g = _t(datagen.normal(datagen.SEEDS["ln_gamma"], (4096,), 1.0, 0.1))
         b = _t(datagen.normal(datagen.SEEDS["ln_beta"], (4096,), 0.0, 0.1))
         Xh = X.half()
         Y, Yh = torch.empty_like(X), torch.empty_like(Xh)
         self.keep = [X, g, b, Xh, Y, Yh]
         d = abi.desc_of
-        self.calls = [(d(X), d(g), d(b), d(Y), 536903680), (d(Xh), d(g), d(b), d(Yh), 268468224)]
+        n = R * 4096
+        self.calls = [(d(X), d(g), d(b), d(Y), 2 * n * 4 + 32768), (d(Xh), d(g), d(b), d(Yh), 2 * n * 2 + 32768)]
         self.units_per_step = sum(c[4] for c in self.calls)
         self.unit = "GB/s"
 
@@ -511,16 +630,17 @@ class LayerNormWorkload(Workload):
 class SoftmaxWorkload(Workload):
     name = "softmax over the last axis of X[16384,4096] fp32 and fp16"
 
-    def __init__(self, ctx, dist: Dist):
+    def __init__(self, ctx, dist: Dist, scale: str = "weak"):
         import torch
         from quasarml_b200 import abi, datagen
         self.ctx = ctx
-        n = 16384 * 4096
-        X = _t(datagen.normal(datagen.SEEDS["ln_X"], (16384, 4096), 0.5, 2.0, offset=dist.rank * n))
+        r0, R, G = row_block(16384, dist, scale)
+        X = _t(datagen.normal(datagen.SEEDS["ln_X"], (R, 4096), 0.5, 2.0, offset=r0 * 4096))
         Xh = X.half()
         Y, Yh = torch.empty_like(X), torch.empty_like(Xh)
         self.keep = [X, Xh, Y, Yh]
         d = abi.desc_of
+        n = R * 4096
         self.calls = [(d(X), d(Y), 2 * n * 4), (d(Xh), d(Yh), 2 * n * 2)]
         self.units_per_step = sum(c[2] for c in self.calls)
         self.unit = "GB/s"
@@ -531,23 +651,29 @@ class SoftmaxWorkload(Workload):
 
 
 class MatmulWorkload(Workload):
-    def __init__(self, ctx, dist: Dist, dtype: str, batched: bool, fp32_precision: str = "3xtf32"):
+    """C = A.B with A's rows sharded and B replicated (batched: the batch dim
+    sharded)."""
+
+    def __init__(self, ctx, dist: Dist, dtype: str, batched: bool, fp32_precision: str = "3xtf32",
+                 scale: str = "weak"):
         import torch
         from quasarml_b200 import abi, datagen
         self.ctx, self.abi = ctx, abi
         if batched:
             s = 1.0 / np.sqrt(1024.0)
-            A = _t(datagen.uniform(datagen.SEEDS["mm_Ab"], (32, 2048, 1024), -s, s))
-            B = _t(datagen.uniform(datagen.SEEDS["mm_Bb"], (32, 1024, 2048), -s, s))
-            C = torch.empty((32, 2048, 2048), device="cuda")
-            self.flops = 2.0 * 32 * 2048 * 2048 * 1024
+            e0, E, _ = row_block(32, dist, scale)
+            A = _t(datagen.uniform(datagen.SEEDS["mm_Ab"], (E, 2048, 1024), -s, s, offset=e0 * 2048 * 1024))
+            B = _t(datagen.uniform(datagen.SEEDS["mm_Bb"], (E, 1024, 2048), -s, s, offset=e0 * 1024 * 2048))
+            C = torch.empty((E, 2048, 2048), device="cuda")
+            self.flops = 2.0 * E * 2048 * 2048 * 1024
             self.name = f"batched matmul [32,2048,1024]x[32,1024,2048] {dtype}"
         else:
             s = 1.0 / np.sqrt(8192.0)
-            A = _t(datagen.uniform(datagen.SEEDS["mm_A"], (8192, 8192), -s, s))
+            r0, R, _ = row_block(8192, dist, scale)
+            A = _t(datagen.uniform(datagen.SEEDS["mm_A"], (R, 8192), -s, s, offset=r0 * 8192))
             B = _t(datagen.uniform(datagen.SEEDS["mm_B"], (8192, 8192), -s, s))
-            C = torch.empty((8192, 8192), device="cuda")
-            self.flops = 2.0 * 8192 ** 3
+            C = torch.empty((R, 8192), device="cuda")
+            self.flops = 2.0 * R * 8192 * 8192
             self.name = f"matmul 8192x8192x8192 {dtype}"
         if dtype == "f16":
             A, B = A.half(), B.half()
@@ -576,45 +702,52 @@ def capture(fn, stream):
     return g
 
 
+def _launches(wl) -> int:
+    """Kernels launched so far by the workload's library contexts."""
+    n = wl.ctx.launch_count()
+    if getattr(wl, "group", None) is not None:
+        n += wl.xctx.launch_count()
+    return n
+
+
 def time_steps(wl, dist: Dist, stream, steps: int, warmup: int, sampler=None, use_graph=True):
     """Times `steps` steps on `stream` with CUDA events; returns the max over
-    ranks (ms), the kernel launches counted by the library and the graph."""
+    ranks (ms), the kernel launches in the timed steps and the graph(s).
+
+    A step's local kernel calls are replayed from CUDA graphs; a workload
+    with an exchange (ReduceWorkload under sharding) replays two graphs --
+    the partials of the exchanged reductions, then the local reductions --
+    with the combine started between them on its own stream and the
+    finishing calls issued after it."""
     import torch
     with torch.cuda.stream(stream):
         for _ in range(warmup):
             wl.step()
         torch.cuda.synchronize()
-        # Workloads with an exchange and a split step (ReduceWorkload) replay
-        # two graphs with the collectives started between them.
-        split = use_graph and dist.pg is not None and hasattr(wl, "exchange_start")
+        # launches per step, counted by the library on one eager step
+        l0 = _launches(wl)
+        wl.step()
+        torch.cuda.synchronize()
+        per_step = _launches(wl) - l0
+        split = use_graph and getattr(wl, "sharded", False)
         g = None
         if split:
-            gx = capture(lambda: wl.compute(wl.calls_x), stream)
-            gl = capture(lambda: wl.compute(wl.calls_l), stream)
-            g = (gx, gl)
+            g = (capture(lambda: wl.compute(wl.calls_x), stream), capture(lambda: wl.compute(wl.calls_l), stream))
         elif use_graph:
             g = capture(wl.compute, stream)
         torch.cuda.synchronize()
         dist.barrier()
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        per_step = None
-        if g is not None:
-            # launches per step: the library counts each launch it enqueues
-            l0 = wl.ctx.launch_count()
-            wl.compute()
-            per_step = wl.ctx.launch_count() - l0
-            torch.cuda.synchronize()
-        launches0 = wl.ctx.launch_count()
         if sampler:
             sampler.__enter__()
         start.record(stream)
         for _ in range(steps):
             if split:
                 g[0].replay()
-                works = wl.exchange_start()
+                done = wl.exchange_start()
                 g[1].replay()
-                wl.exchange_finish(works)
+                wl.exchange_finish(done)
             elif g is not None:
                 g.replay()
                 wl.exchange()
@@ -624,24 +757,22 @@ def time_steps(wl, dist: Dist, stream, steps: int, warmup: int, sampler=None, us
         torch.cuda.synchronize()
         if sampler:
             sampler.__exit__()
-    launches = wl.ctx.launch_count() - launches0
-    if g is not None:
-        launches += per_step * steps
     ms = start.elapsed_time(end)
     dist.barrier()
-    return dist.max(ms), launches, g
+    return dist.max(ms), per_step * steps, g
 
 
 def family_times(wl, stream, reps: int = 5):
-    """Average device duration of one launch of each kernel family: the
-    family's calls of one step captured alone in a CUDA graph and replayed."""
+    """Average device duration of one launch of each kernel family, per input
+    dtype: the family's calls of one step captured alone in a CUDA graph and
+    replayed."""
     import torch
     # each call's family is the kernel the library chose for it
     fams = {}
     with torch.cuda.stream(stream):
         for c in wl.calls:
             wl.compute([c])
-            fams.setdefault(wl.ctx.last_kernel(), []).append(c)
+            fams.setdefault(f"{wl.ctx.last_kernel()}[{c.dt}]", []).append(c)
     torch.cuda.synchronize()
     out = {}
     with torch.cuda.stream(stream):
@@ -656,7 +787,7 @@ def family_times(wl, stream, reps: int = 5):
             b.record(stream)
             torch.cuda.synchronize()
             ms = a.elapsed_time(b) / reps
-            out[fam] = {"launches": len(calls), "ms": ms, "bytes": sum(c[5] for c in calls)}
+            out[fam] = {"launches": len(calls), "ms": ms, "bytes": sum(c.nbytes for c in calls)}
             del g
     return out
 
@@ -685,7 +816,8 @@ def roofline_from_families(fam, hbm_peak, peak_kind):
     f = fam[dom]
     per_launch_ms = f["ms"] / f["launches"]
     achieved = f["bytes"] / (f["ms"] / 1e3) / 1e9
-    ratio = ncu_traffic().get(dom)
+    traffic_ratios = ncu_traffic()
+    ratio = traffic_ratios.get(dom, traffic_ratios.get(dom.split("[")[0]))
     # DRAM bytes per launch: the captured launch's traffic/algorithmic ratio
     # (profiles/) applied to this family's average algorithmic bytes per launch.
     traffic = round(ratio * f["bytes"] / f["launches"]) if ratio else None
@@ -708,9 +840,10 @@ def roofline_from_families(fam, hbm_peak, peak_kind):
 # CPU side (oracle): baseline and the reference arm
 # ---------------------------------------------------------------------------
 class CpuReduceSample:
-    """The headline reductions on X[8,512,1024] (1/8 of one X), fp32 and fp16,
-    through the oracle's OpenMP restatement."""
-    SHAPE = (8, 512, 1024)
+    """The headline reductions on one X[64,512,1024] per dtype (fp32 and
+    fp16: the configuration's tensor, not a sample of it), through the
+    oracle's OpenMP restatement; a step is these 32 reductions."""
+    SHAPE = (64, 512, 1024)
 
     def __init__(self):
         from oracle import qsml_oracle as orc
@@ -756,7 +889,8 @@ def cpu_baseline(min_seconds=10.0, max_seconds=30.0):
             break
     gbs = s.bytes * n / el / 1e9
     return {"value": round(gbs, 2), "unit": "GB/s", "cores": s.cores(), "kind": "port",
-            "sample": f"the same 32 reductions on X[8,512,1024] (1/8 of one X) fp32+fp16, {n} passes in {el:.1f} s"}
+            "sample": f"the 32 reductions of one X[64,512,1024] fp32 and one fp16 (the configuration's tensor), "
+                      f"{n} passes in {el:.1f} s"}
 
 
 def host_threads() -> int:
@@ -784,10 +918,10 @@ def run_reference(args, dist: Dist):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+f16 (fp32 accumulate)",
             "data": "synthetic (seeded normal)",
-            "config": {"workload": ReduceWorkload.name, "sample": "X[8,512,1024] per step (1/8 of one X)",
+            "config": {"workload": ReduceWorkload.name, "per_step": "one X[64,512,1024] per dtype (32 reductions)",
                        "parallelism": "host cores (OpenMP)"},
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": s.cores(), "kind": "port",
-                             "sample": "X[8,512,1024] fp32+fp16, 32 reductions per step"},
+                             "sample": "one X[64,512,1024] fp32 and one fp16 per step, 32 reductions"},
             "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference's only compute path is Vulkan (no graphics stack on this box); its arithmetic is "
                     "restated by oracle/qsml_oracle.c and timed on the host cores"}
@@ -807,7 +941,7 @@ def run_single(which: str, reps: int = 3):
         if which.endswith("f16"):
             x = x.half()
         axis = {"reduce_all": None, "reduce_all_f16": None, "reduce_axis0": 0, "reduce_axis1": 1,
-                "reduce_axis2": 2}[which]
+                "reduce_axis2": 2, "reduce_axis0_f16": 0, "reduce_axis1_f16": 1, "reduce_axis2_f16": 2}[which]
         out = torch.empty(abi.reduced_shape(tuple(x.shape), axis, False), dtype=x.dtype, device="cuda")
         for _ in range(reps):
             ctx.reduce(abi.RED_SUM, d(x), abi.AXIS_ALL if axis is None else axis, False, d(out))
@@ -817,6 +951,14 @@ def run_single(which: str, reps: int = 3):
         out = torch.empty_like(A)
         for _ in range(reps):
             ctx.binary(abi.OP_ADD, d(A), d(B), d(out))
+    elif which in ("chain_pow", "chain_relu"):
+        A = _t(datagen.uniform(1, (4096, 4096), -1, 1))
+        out = torch.empty_like(A)
+        for _ in range(reps):
+            if which == "chain_pow":
+                ctx.binary_scalar(abi.OP_POW, d(A), 2.0, d(out))
+            else:
+                ctx.unary(abi.UN_RELU, d(A), d(out))
     elif which == "chain_fused":
         wl = FusedChainWorkload(ctx, Dist(), batch=1)
         for _ in range(reps):
@@ -869,6 +1011,13 @@ def run_single(which: str, reps: int = 3):
         C = torch.empty((32, 2048, 2048), device="cuda")
         for _ in range(reps):
             ctx.matmul(d(A), d(B), d(C), abi.MM_FP16_F32ACC)
+    elif which == "matmul_ffma":
+        s = 1.0 / np.sqrt(8192.0)
+        A = _t(datagen.uniform(6, (8192, 8192), -s, s))
+        B = _t(datagen.uniform(7, (8192, 8192), -s, s))
+        C = torch.empty((8192, 8192), device="cuda")
+        for _ in range(reps):
+            ctx.matmul(d(A), d(B), d(C), abi.MM_FP32_FFMA)
     elif which == "matmul_3xtf32":
         s = 1.0 / np.sqrt(8192.0)
         A = _t(datagen.uniform(6, (8192, 8192), -s, s))
@@ -889,12 +1038,14 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-extras", action="store_true", help="skip the other workloads at N=1")
+    ap.add_argument("--no-extras", action="store_true", help="skip the other workloads")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="reduce",
                     choices=["reduce", "chain", "gather", "layernorm", "matmul_f16", "matmul_f32"])
     ap.add_argument("--single", default=None,
                     choices=["reduce_all", "reduce_axis0", "reduce_axis1", "reduce_axis2", "reduce_all_f16",
+                             "reduce_axis0_f16", "reduce_axis1_f16", "reduce_axis2_f16", "chain_pow", "chain_relu",
+                             "matmul_ffma",
                              "chain_add", "chain_fused", "gather_t", "gather_s", "layernorm", "matmul_f16",
                              "matmul_3xtf32", "bmm_f16", "argmax_all", "argmax_axis1", "argmax_axis1_f16", "softmax",
                              "softmax_f16",
@@ -938,6 +1089,7 @@ def main():
     units = wl.units_per_step * args.steps * dist.world
     value = units / (ms / 1e3) / (1e9 if wl.unit == "GB/s" else 1e12)
 
+    sharded = getattr(wl, "sharded", False)
     line = {"metric": METRIC, "value": round(value, 2), "unit": wl.unit, "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -947,12 +1099,18 @@ def main():
                        "l2": "inputs larger than L2: 8 distinct X per dtype per step (1.5 GB), batch entry innermost in the call order so no call finds its input in L2"
                        if args.workload == "reduce" else "inputs larger than L2",
                        "calls_per_step": len(getattr(wl, "calls", [])) or 1,
-                       "launch": "each step's kernel calls replayed from one CUDA graph (N=1); for N>1 two "
-                                 "graphs, the exchanged reductions then the local ones, with the NCCL "
-                                 "all-reduces started between them and waited for after"},
+                       "launch": "each step's kernel calls replayed from one CUDA graph"
+                       if not sharded else
+                       "X row-sharded (each rank X[64,512,1024] of X[64N,512,1024]); per step: graph 1 = the "
+                       "binary32 partials of the axis-0 and full reductions (sum, max, min; means are finished "
+                       "from the combined sums), then qsml_allreduce_partials of the three partial buffers on a "
+                       "second context's stream (NCCL over NVLink) while graph 2 = the axis-1/2 reductions runs, "
+                       "then qsml_finish_partial of the outputs"},
             "gpu_launches": launches, "clocks": sampler.summary()}
     if args.workload == "reduce":
         line["roofline"] = roofline_from_families(family_times(wl, stream), hbm, peak_kind)
+        if sharded:
+            line["exchange"] = exchange_alone(wl, dist, stream)
     if hasattr(wl, "e2e_step"):
         e_steps = max(2, min(args.steps, 5))
         ems = time_e2e(wl, dist, stream, e_steps, 1)
@@ -960,39 +1118,22 @@ def main():
         line["e2e"] = {"value": round(ev, 2), "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes,
                        "d2h_bytes_per_step": wl.d2h_bytes, "ms_per_step": round(ems / e_steps, 3),
                        "path": "pinned host -> qsml_h2d per batch entry on a second context's stream -> "
-                               "qsml_reduce x256, each entry's 32 as soon as its X has landed -> "
-                               "qsml_d2h_async of each entry's results on a third stream, per step"}
+                               "the step's qsml_reduce calls of each entry as soon as its X has landed -> "
+                               "qsml_d2h_async of each entry's results on a third stream"
+                               + ("; the exchanged outputs after qsml_allreduce_partials / "
+                                  "qsml_finish_partial" if sharded else "") + ", per step"}
+    if hasattr(wl, "close_exchange"):
+        wl.close_exchange()
 
-    if dist.world == 1 and not args.no_extras and args.workload == "reduce":
-        extras = {}
+    if not args.no_extras and args.workload == "reduce":
         del wl
         torch.cuda.empty_cache()
-        for key, mk, st in (("elementwise_chain", lambda: ChainWorkload(ctx, dist), 10),
-                            ("elementwise_chain_fused", lambda: FusedChainWorkload(ctx, dist), 20),
-                            ("gather", lambda: GatherWorkload(ctx, dist), 20),
-                            ("layernorm", lambda: LayerNormWorkload(ctx, dist), 20),
-                            ("argmax_argmin", lambda: ArgReduceWorkload(ctx, dist), 20),
-                            ("softmax", lambda: SoftmaxWorkload(ctx, dist), 20),
-                            ("matmul_f16_8192", lambda: MatmulWorkload(ctx, dist, "f16", False), 5),
-                            ("matmul_f32_8192_3xtf32", lambda: MatmulWorkload(ctx, dist, "f32", False), 5),
-                            ("matmul_f32_8192_ffma", lambda: MatmulWorkload(ctx, dist, "f32", False, "ffma"), 3),
-                            ("batched_matmul_f16", lambda: MatmulWorkload(ctx, dist, "f16", True), 5),
-                            ("batched_matmul_f32_3xtf32", lambda: MatmulWorkload(ctx, dist, "f32", True), 5)):
-            try:
-                w = mk()
-                ms_x, l_x, g = time_steps(w, dist, stream, st, 3)
-                del g
-                v = w.units_per_step * st / (ms_x / 1e3) / (1e9 if w.unit == "GB/s" else 1e12)
-                peak = hbm if w.unit == "GB/s" else tf_burst
-                extras[key] = {"workload": w.name, "value": round(v, 2), "unit": w.unit,
-                               "frac_of_peak": round(v / peak, 4), "peak": peak,
-                               "ms_per_step": round(ms_x / st, 3), "launches_per_step": l_x // st}
-                del w
-                torch.cuda.synchronize()
-                torch.cuda.empty_cache()
-            except Exception as e:  # report, do not hide
-                extras[key] = {"error": repr(e)[:300]}
-        line["other_workloads"] = extras
+        line["other_workloads"] = run_extras(ctx, dist, stream, hbm, tf_burst)
+
+    if dist.world == 1 and not args.no_extras and args.workload == "reduce":
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        line["cpp_api"] = run_cpp_api()
 
     if dist.world == 1 and dist.rank == 0 and not args.no_cpu_baseline and args.workload == "reduce":
         line["cpu_baseline"] = cpu_baseline()
@@ -1002,6 +1143,106 @@ def main():
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
     dist.close()
+
+
+CPP_API_PROGRAM = os.path.join(ROOT, "quasarml_b200", "cpp", "_build", "bench_configs")
+
+
+def run_cpp_api(timeout_s: int = 600) -> dict:
+    """The configurations through the unchanged C++ qsml:: API (a separate
+    process: quasarml_b200/cpp/examples/bench_configs.cpp, every op allocating
+    its result as a reference user's code does), wall clock around many steps
+    with qsml::synchronize() on both sides."""
+    import subprocess
+    if not os.path.exists(CPP_API_PROGRAM):
+        return {"error": f"{CPP_API_PROGRAM} not built"}
+    try:
+        r = subprocess.run([CPP_API_PROGRAM], capture_output=True, text=True, timeout=timeout_s)
+    except subprocess.TimeoutExpired:
+        return {"error": "timed out"}
+    out = {}
+    for ln in r.stdout.splitlines():
+        if ln.startswith("{"):
+            j = json.loads(ln)
+            out[j.pop("key")] = j
+    if r.returncode != 0:
+        out["error"] = f"rc={r.returncode}: {r.stderr[-300:]}"
+    out["path"] = "C++ qsml:: API (QuasarML.h), results allocated per op from the caching allocator"
+    return out
+
+
+def exchange_alone(wl, dist: Dist, stream, reps: int = 5) -> dict:
+    """The step's combine alone: the three qsml_allreduce_partials (with their
+    key passes) timed on their stream, max over ranks."""
+    import torch
+    wl.init_exchange()
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            wl.exchange()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(wl.xstream)
+        for _ in range(reps):
+            wl.exchange_start()
+        b.record(wl.xstream)
+        torch.cuda.synchronize()
+    ms = dist.max(a.elapsed_time(b) / reps)
+    nbytes = sum(f.numel() * 4 for f in wl.flat.values())
+    return {"ms": round(ms, 4), "bytes_per_rank": nbytes, "collectives": len(wl.flat),
+            "what": "qsml_allreduce_partials of the sum / max / min partial buffers (binary32 sums, "
+                    "order-preserving 32-bit max/min keys), timed alone on its stream"}
+
+
+EXTRAS = (("elementwise_chain", lambda c, d, s: ChainWorkload(c, d, scale=s), 10),
+          ("elementwise_chain_fused", lambda c, d, s: FusedChainWorkload(c, d, scale=s), 20),
+          ("gather", lambda c, d, s: GatherWorkload(c, d, scale=s), 20),
+          ("layernorm", lambda c, d, s: LayerNormWorkload(c, d, scale=s), 20),
+          ("argmax_argmin", lambda c, d, s: ArgReduceWorkload(c, d, scale=s), 20),
+          ("softmax", lambda c, d, s: SoftmaxWorkload(c, d, scale=s), 20),
+          ("matmul_f16_8192", lambda c, d, s: MatmulWorkload(c, d, "f16", False, scale=s), 5),
+          ("matmul_f32_8192_3xtf32", lambda c, d, s: MatmulWorkload(c, d, "f32", False, scale=s), 5),
+          ("matmul_f32_8192_ffma", lambda c, d, s: MatmulWorkload(c, d, "f32", False, "ffma", scale=s), 3),
+          ("batched_matmul_f16", lambda c, d, s: MatmulWorkload(c, d, "f16", True, scale=s), 5),
+          ("batched_matmul_f32_3xtf32", lambda c, d, s: MatmulWorkload(c, d, "f32", True, scale=s), 5))
+
+
+def run_extras(ctx, dist: Dist, stream, hbm: float, tf_burst: float) -> dict:
+    """The other configurations, each row-sharded over the ranks: weak
+    scaling at every N (each rank the configuration's size), and at N>1 also
+    strong scaling (the configuration's tensor split N ways).  Every rank
+    builds the workload, all agree it was built, then all time it."""
+    import torch
+    extras = {}
+    scales = ("weak",) if dist.world == 1 else ("weak", "strong")
+    for scale in scales:
+        for key, mk, st in EXTRAS:
+            name = key if scale == "weak" else key + "_strong"
+            w, err = None, None
+            try:
+                w = mk(ctx, dist, scale)
+            except Exception as e:  # reported, never hidden
+                err = repr(e)[:300]
+            if dist.max(1.0 if err else 0.0) > 0:
+                extras[name] = {"error": err or "failed on another rank"}
+                w = None
+                torch.cuda.synchronize()
+                torch.cuda.empty_cache()
+                continue
+            ms_x, l_x, g = time_steps(w, dist, stream, st, 3)
+            del g
+            units = w.units_per_step * dist.world if scale == "weak" else dist.sum(w.units_per_step)
+            v = units * st / (ms_x / 1e3) / (1e9 if w.unit == "GB/s" else 1e12)
+            peak = hbm if w.unit == "GB/s" else tf_burst
+            extras[name] = {"workload": w.name, "scaling": scale, "value": round(v, 2),
+                            "per_gpu": round(v / dist.world, 2), "unit": w.unit,
+                            "frac_of_peak": round(v / dist.world / peak, 4), "peak": peak,
+                            "ms_per_step": round(ms_x / st, 3), "launches_per_step": l_x // st}
+            del w
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+    return extras
 
 
 if __name__ == "__main__":

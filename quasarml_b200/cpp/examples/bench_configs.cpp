@@ -1,0 +1,202 @@
+// The five hot-path configurations run through the unchanged qsml:: API --
+// every op allocates its result tensor, as a reference user's code does
+// (QuasarML/include/QuasarML.h:129-251) -- and timed with the wall clock
+// around many steps, qsml::synchronize() on both sides.  The host enqueues
+// asynchronously, so the time is the device's unless the host falls behind.
+// Each step reads inputs that are not in L2 (several distinct input sets,
+// used in turn).  Prints one JSON line per workload: algorithmic bytes (each
+// input read once, each output written once; strided reads at 32-byte
+// sectors) or FLOPs per second.  Inputs come from the seeded generator the
+// Python benchmark uses (libqsml_datagen.so), with the same seeds.
+#include <QuasarML.h>
+
+#include <chrono>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <string>
+#include <vector>
+
+extern "C" {
+void qsml_gen_uniform_f32(uint64_t seed, int64_t offset, int64_t n, double a, double b, float* out);
+void qsml_gen_normal_f32(uint64_t seed, int64_t offset, int64_t n, double mean, double stdv, float* out);
+void qsml_gen_iota_i32(int64_t offset, int64_t n, int32_t* out);
+}
+
+using qsml::TensorPtr;
+using qsml::u32;
+using clk = std::chrono::steady_clock;
+
+namespace {
+
+// binary32 -> binary16, round to nearest even (host side, for uploads)
+uint16_t to_half(float f) {
+    uint32_t x;
+    std::memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t ax = x & 0x7fffffffu;
+    if (ax >= 0x7f800000u) return static_cast<uint16_t>(sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0u));
+    if (ax >= 0x477ff000u) return static_cast<uint16_t>(sign | 0x7c00u);  // rounds to inf
+    if (ax < 0x38800000u) {                                                // subnormal or zero
+        const int shift = 113 - static_cast<int>(ax >> 23);
+        if (shift > 24) return static_cast<uint16_t>(sign);
+        const uint32_t m = (ax & 0x7fffffu) | 0x800000u;
+        uint32_t h = m >> (shift + 13);
+        const uint32_t rem = m & ((1u << (shift + 13)) - 1u), half = 1u << (shift + 12);
+        if (rem > half || (rem == half && (h & 1u))) ++h;
+        return static_cast<uint16_t>(sign | h);
+    }
+    uint32_t h = ((ax - 0x38000000u) >> 13);
+    const uint32_t rem = ax & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+    return static_cast<uint16_t>(sign | h);
+}
+
+TensorPtr upload_f32(const std::vector<float>& v, const std::vector<u32>& shape, bool half) {
+    if (!half) return qsml::from_data(v.data(), shape, qsml::DataType::F32);
+    std::vector<uint16_t> h(v.size());
+    for (size_t i = 0; i < v.size(); ++i) h[i] = to_half(v[i]);
+    return qsml::from_data(h.data(), shape, qsml::DataType::F16);
+}
+
+std::vector<float> uniform(uint64_t seed, int64_t off, int64_t n, double a, double b) {
+    std::vector<float> v(static_cast<size_t>(n));
+    qsml_gen_uniform_f32(seed, off, n, a, b, v.data());
+    return v;
+}
+
+std::vector<float> normal(uint64_t seed, int64_t off, int64_t n, double m, double s) {
+    std::vector<float> v(static_cast<size_t>(n));
+    qsml_gen_normal_f32(seed, off, n, m, s, v.data());
+    return v;
+}
+
+// Times `steps` calls of step() after `warmup`; prints the JSON line.
+void report(const char* key, const std::string& workload, double units_per_step, const char* unit, int warmup,
+            int steps, const std::function<void()>& step) {
+    for (int i = 0; i < warmup; ++i) step();
+    qsml::synchronize();
+    const auto t0 = clk::now();
+    for (int i = 0; i < steps; ++i) step();
+    qsml::synchronize();
+    const double ms = std::chrono::duration<double, std::milli>(clk::now() - t0).count() / steps;
+    const double scale = std::strcmp(unit, "GB/s") == 0 ? 1e9 : 1e12;
+    std::printf("{\"key\": \"%s\", \"workload\": \"%s\", \"value\": %.2f, \"unit\": \"%s\", \"ms_per_step\": %.4f, "
+                "\"steps\": %d}\n",
+                key, workload.c_str(), units_per_step / (ms / 1e3) / scale, unit, ms, steps);
+    std::fflush(stdout);
+}
+
+}  // namespace
+
+int main() {
+    qsml::init();
+    const int64_t R = 4096, N = 4096 * 4096;
+
+    {  // C1: relu(pow((A+B)*B - A, 2) / D), op by op and fused
+        std::vector<TensorPtr> A, D;
+        auto B = upload_f32(uniform(2, 0, 4096, -1, 1), {1, 4096}, false);
+        for (int b = 0; b < 4; ++b) {
+            A.push_back(upload_f32(uniform(1, b * N, N, -1, 1), {4096, 4096}, false));
+            D.push_back(upload_f32(uniform(3, b * R, R, 0.5, 2), {4096, 1}, false));
+        }
+        auto chain = [&](int b) {
+            return qsml::relu(qsml::div(qsml::pow(qsml::sub(qsml::mul(qsml::add(A[b], B), B), A[b]), 2.0f), D[b]));
+        };
+        report("elementwise_chain", "elementwise chain relu(pow((A+B)*B - A, 2.0) / D), A[4096,4096], B[1,4096], "
+               "D[4096,1] fp32, six qsml:: calls",
+               4 * 872464384.0, "GB/s", 2, 10, [&] {
+                   for (int b = 0; b < 4; ++b) chain(b);
+               });
+        qsml::set_fusion(true);
+        report("elementwise_chain_fused", "the same chain with qsml::set_fusion(true): one deferred kernel",
+               4 * (2.0 * N * 4 + 2 * 4096 * 4), "GB/s", 2, 20, [&] {
+                   for (int b = 0; b < 4; ++b) chain(b)->materialize();
+               });
+        qsml::set_fusion(false);
+    }
+
+    {  // C2: sum/mean/max/min over axis 0, 1, 2 and all, fp32 and fp16, 8 X per dtype
+        const int64_t n = 64LL * 512 * 1024;
+        std::vector<TensorPtr> X32, X16;
+        for (int b = 0; b < 8; ++b) {
+            auto v = normal(4, b * n, n, 0.0, 1.0);
+            X32.push_back(upload_f32(v, {64, 512, 1024}, false));
+            X16.push_back(upload_f32(v, {64, 512, 1024}, true));
+        }
+        double bytes = 0;
+        const double outs[4] = {1, 512.0 * 1024, 64.0 * 1024, 64.0 * 512};  // all, axis 0, 1, 2
+        for (int es : {4, 2})
+            for (double o : outs) bytes += 4 * 8 * (n * es + o * es);
+        report("reductions", "reductions X[64,512,1024] fp32 and fp16: sum/mean/max/min over axis 0, 1, 2 and all "
+               "(256 qsml:: calls)",
+               bytes, "GB/s", 2, 10, [&] {
+                   for (auto* xs : {&X32, &X16}) {
+                       for (int ax = -1; ax < 3; ++ax) {
+                           for (int op = 0; op < 4; ++op) {
+                               for (int b = 0; b < 8; ++b) {
+                                   TensorPtr x = (*xs)[b];
+                                   if (ax < 0) {
+                                       if (op == 0) qsml::sum(x);
+                                       else if (op == 1) qsml::mean(x);
+                                       else if (op == 2) qsml::max(x);
+                                       else qsml::min(x);
+                                   } else {
+                                       if (op == 0) qsml::sum(x, ax);
+                                       else if (op == 1) qsml::mean(x, ax);
+                                       else if (op == 2) qsml::max(x, ax);
+                                       else qsml::min(x, ax);
+                                   }
+                               }
+                           }
+                       }
+                   }
+               });
+    }
+
+    {  // C3: X[5::3, 1::2] and X.T[::4, :] of X[8192,8192], int32 and fp32
+        const int64_t n = 8192LL * 8192;
+        std::vector<int32_t> iota(static_cast<size_t>(n));
+        qsml_gen_iota_i32(0, n, iota.data());
+        auto Xi = qsml::from_data(iota.data(), {8192, 8192}, qsml::DataType::I32);
+        auto Xf = upload_f32(uniform(5, 0, n, -1, 1), {8192, 8192}, false);
+        report("gather", "strided gather X[5::3, 1::2] and X.T[::4, :] of X[8192,8192] int32 and fp32 "
+               "(qsml::slice / qsml::transpose views, qsml::contiguous)",
+               2 * (134135808.0 + 335544320.0), "GB/s", 3, 20, [&] {
+                   for (auto& X : {Xi, Xf}) {
+                       qsml::contiguous(qsml::slice(qsml::slice(X, 0, 5, 8192, 3), 1, 1, 8192, 2));
+                       qsml::contiguous(qsml::slice(qsml::transpose(X, 0, 1), 0, 0, 8192, 4));
+                   }
+               });
+    }
+
+    {  // C5: layer norm, fp32 and fp16, gamma/beta fp32
+        const int64_t n = 16384LL * 4096;
+        auto v = normal(10, 0, n, 0.5, 2.0);
+        auto X = upload_f32(v, {16384, 4096}, false), Xh = upload_f32(v, {16384, 4096}, true);
+        auto g = upload_f32(normal(11, 0, 4096, 1.0, 0.1), {4096}, false);
+        auto bt = upload_f32(normal(12, 0, 4096, 0.0, 0.1), {4096}, false);
+        report("layernorm", "layer norm X[16384,4096] fp32 and fp16, gamma/beta fp32, eps 1e-5 (qsml::layer_norm)",
+               536903680.0 + 268468224.0, "GB/s", 3, 20, [&] {
+                   qsml::layer_norm(X, g, bt, 1e-5f);
+                   qsml::layer_norm(Xh, g, bt, 1e-5f);
+               });
+    }
+
+    {  // C4: matmul 8192^3 and batched, fp16 inputs, fp32 output
+        const double s = 1.0 / 90.50966799187809;  // 1/sqrt(8192)
+        auto A = upload_f32(uniform(6, 0, 8192LL * 8192, -s, s), {8192, 8192}, true);
+        auto B = upload_f32(uniform(7, 0, 8192LL * 8192, -s, s), {8192, 8192}, true);
+        report("matmul_f16_8192", "matmul 8192x8192x8192 f16 inputs, f32 out (qsml::matmul)", 2.0 * 8192 * 8192 * 8192,
+               "TFLOP/s", 2, 5, [&] { qsml::matmul(A, B, qsml::DataType::F32); });
+        const double sb = 1.0 / 32.0;  // 1/sqrt(1024)
+        auto Ab = upload_f32(uniform(9, 0, 32LL * 2048 * 1024, -sb, sb), {32, 2048, 1024}, true);
+        auto Bb = upload_f32(uniform(8, 0, 32LL * 1024 * 2048, -sb, sb), {32, 1024, 2048}, true);
+        report("batched_matmul_f16", "batched matmul [32,2048,1024]x[32,1024,2048] f16 inputs and output, fp32 "
+               "accumulate (qsml::batch_matmul keeps the input dtype)",
+               2.0 * 32 * 2048 * 2048 * 1024, "TFLOP/s", 2, 5, [&] { qsml::batch_matmul(Ab, Bb); });
+    }
+    qsml::shutdown();
+    return 0;
+}

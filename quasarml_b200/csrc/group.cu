@@ -108,7 +108,13 @@ qsml_status_t settle(Context* ctx, const std::vector<ncclComm_t>& comms, const c
             std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
         if (ms > timeout_ms())
             return set_error(ctx, QSML_E_TIMEOUT, std::string(what) + ": no progress within QSML_NCCL_TIMEOUT_MS");
-        std::this_thread::sleep_for(std::chrono::microseconds(200));
+        // A collective is normally enqueued within microseconds: poll without
+        // sleeping for the first 2 ms (sleeping would stall the host's launch
+        // stream), then back off.
+        if (ms < 2)
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(100));
     }
 }
 
