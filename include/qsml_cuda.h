@@ -230,7 +230,11 @@ QSML_API qsml_status_t qsml_unary(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a
  * input's dtype; F16 input accumulates in fp32.  mean = sum * (1.0f/(float)n).
  * max/min follow IEEE 754-2019 maximum/minimum (NaN propagates as 0x7fffffff,
  * -0 < +0).  The combine order is fixed by the shape alone, so results are
- * run-to-run deterministic.  Replaces Ops::sum/mean/max/min
+ * run-to-run deterministic.  `a` may be a strided view (slices with a step,
+ * transposes, negative or zero strides): it is read in place, with the
+ * dims other than the reduced one merged where their strides chain; a view
+ * that leaves more than four such dims returns QSML_E_UNSUPPORTED (gather it
+ * with qsml_gather first).  Replaces Ops::sum/mean/max/min
  * (QuasarML/src/Ops/Reduction.cpp:285-382), whose axis max/min are stubs. */
 QSML_API qsml_status_t qsml_reduce(qsml_ctx* ctx, int32_t op, const qsml_tdesc* a,
                                    int32_t axis, int32_t keepdims, const qsml_tdesc* out);

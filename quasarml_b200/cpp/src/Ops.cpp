@@ -175,22 +175,33 @@ std::vector<u32> reduced_shape(const std::vector<u32>& s, i32 axis, bool keepdim
     return out;
 }
 
+// Views (slices with a step, transposes) are reduced in place; only a view
+// whose dims the library cannot collapse (QSML_E_UNSUPPORTED) is gathered
+// into a contiguous copy first.
+void reduce_into(Device& device, int op, const TP& a, int32_t axis, bool keepdims, const TP& out) {
+    a->materialize();
+    qsml_tdesc dx = a->desc(), dout = out->desc();
+    int st = qsml_reduce(device.ctx(), op, &dx, axis, keepdims ? 1 : 0, &dout);
+    if (st == QSML_E_UNSUPPORTED && !a->is_contiguous()) {
+        auto x = a->contiguous();
+        dx = x->desc();
+        st = qsml_reduce(device.ctx(), op, &dx, axis, keepdims ? 1 : 0, &dout);
+    }
+    device.check(st);
+}
+
 TP reduce_all(Device& device, int op, const TP& a) {
     QS_ASSERT(a, "null tensor");
-    auto x = a->contiguous();
     auto out = device.create_tensor({1}, a->dtype());
-    qsml_tdesc dx = x->desc(), dout = out->desc();
-    device.check(qsml_reduce(device.ctx(), op, &dx, QSML_AXIS_ALL, 0, &dout));
+    reduce_into(device, op, a, QSML_AXIS_ALL, false, out);
     return out;
 }
 
 TP reduce_axis(Device& device, int op, const TP& a, i32 axis, bool keepdims) {
     QS_ASSERT(a, "null tensor");
     axis = norm_axis(axis, a->rank());
-    auto x = a->contiguous();
     auto out = device.create_tensor(reduced_shape(a->shape(), axis, keepdims), a->dtype());
-    qsml_tdesc dx = x->desc(), dout = out->desc();
-    device.check(qsml_reduce(device.ctx(), op, &dx, axis, keepdims ? 1 : 0, &dout));
+    reduce_into(device, op, a, axis, keepdims, out);
     return out;
 }
 

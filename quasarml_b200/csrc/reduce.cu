@@ -408,11 +408,14 @@ __global__ void __launch_bounds__(256) k_reduce_cols_wide(const T* __restrict__ 
 // ---------------------------------------------------------------------------
 // Host dispatch
 // ---------------------------------------------------------------------------
+// scale_override > 0 replaces a mean's 1/k (a mean over more elements than
+// this call reduces, as in the second stage of a strided full reduction).
 template <typename T, typename OT, int OP>
-qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int64_t inner, OT* out) {
+qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int64_t inner, OT* out,
+                         float scale_override = 0.0f) {
     using V = typename Red<OP>::V;
     constexpr int PV = Pack<T>::N;
-    const float scale = 1.0f / static_cast<float>(k);
+    const float scale = scale_override > 0.0f ? scale_override : 1.0f / static_cast<float>(k);
     const bool x_al = aligned16(x);
     if (inner == 1 && (outer == 1 || (outer < 592 && k >= 8192))) {
         // Segment kernel.
@@ -483,6 +486,220 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
     return after_launch(ctx, "k_reduce_cols");
 }
 
+// ---------------------------------------------------------------------------
+// Strided inputs (views: slices with a step, transposes, broadcasts).  The
+// view's dims other than the reduced one are collapsed -- neighbours merge
+// where their strides chain -- into at most kStrMaxOut output dims, and the
+// kernels read the view in place: a reduction of a view is one pass over the
+// elements it covers, not a gather copy followed by a reduction.
+//   * k_reduce_strided_lanes  -- a warp per output, lanes striding over k:
+//     when k is the view's more contiguous direction (rows of a slice);
+//   * k_reduce_strided_serial -- a thread per output, k ascending (the
+//     reference's serial order, Reduction.cpp:328): when neighbouring outputs
+//     are the more contiguous direction (columns, transposed views).
+// A full reduction of a view first reduces its most contiguous dim into
+// binary32 scratch (lanes kernel), then the scratch with the segment kernel.
+// ---------------------------------------------------------------------------
+constexpr int kStrMaxOut = 4;
+
+struct StridedPlan {
+    int nd;                              // output dims, outermost first
+    int64_t oshape[kStrMaxOut], ostride[kStrMaxOut];  // extents, strides in elements
+    int64_t k, sk;                       // reduced extent and stride
+    int64_t tail_k;                      // k of the last output (a split 1-D view's ragged end)
+};
+
+__device__ __forceinline__ int64_t strided_base(const StridedPlan& p, int64_t o) {
+    int64_t base = 0;
+#pragma unroll
+    for (int d = kStrMaxOut - 1; d >= 0; --d) {
+        if (d < p.nd) {
+            const int64_t e = p.oshape[d];
+            const int64_t q = o / e;
+            base += (o - q * e) * p.ostride[d];
+            o = q;
+        }
+    }
+    return base;
+}
+
+template <typename T, typename OT, int OP>
+__global__ void __launch_bounds__(256) k_reduce_strided_lanes(const T* __restrict__ x, StridedPlan p, int64_t nout,
+                                                              OT* __restrict__ out, float scale) {
+    using R = Red<OP>;
+    pdl_begin();
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t o = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); o < nout; o += nw) {
+        const T* row = x + strided_base(p, o);
+        const int64_t kn = o == nout - 1 ? p.tail_k : p.k;
+        typename R::V acc = R::ident();
+        int64_t kk = lane;
+        for (; kk + 3 * 32 < kn; kk += 4 * 32) {  // four loads in flight, used in k order
+            const T v0 = row[kk * p.sk], v1 = row[(kk + 32) * p.sk], v2 = row[(kk + 64) * p.sk],
+                    v3 = row[(kk + 96) * p.sk];
+            acc = R::comb(acc, R::lift(to_f(v0)));
+            acc = R::comb(acc, R::lift(to_f(v1)));
+            acc = R::comb(acc, R::lift(to_f(v2)));
+            acc = R::comb(acc, R::lift(to_f(v3)));
+        }
+        for (; kk < kn; kk += 32) acc = R::comb(acc, R::lift(to_f(row[kk * p.sk])));
+        acc = warp_reduce<OP>(acc);
+        if (lane == 0) from_f(R::fin(acc, scale), &out[o]);
+    }
+}
+
+template <typename T, typename OT, int OP>
+__global__ void __launch_bounds__(256) k_reduce_strided_serial(const T* __restrict__ x, StridedPlan p, int64_t nout,
+                                                               OT* __restrict__ out, float scale) {
+    using R = Red<OP>;
+    pdl_begin();
+    const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t o = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < nout; o += nt) {
+        const T* col = x + strided_base(p, o);
+        typename R::V acc = R::ident();
+        int64_t kk = 0;
+        for (; kk + 8 <= p.k; kk += 8) {
+            T v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = col[(kk + u) * p.sk];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc = R::comb(acc, R::lift(to_f(v[u])));
+        }
+        for (; kk < p.k; ++kk) acc = R::comb(acc, R::lift(to_f(col[kk * p.sk])));
+        from_f(R::fin(acc, scale), &out[o]);
+    }
+}
+
+// The plan of a reduction of view `a` over dim `ax`: false if its other dims
+// do not collapse into kStrMaxOut.
+bool strided_plan(const qsml_tdesc* a, int ax, StridedPlan* p) {
+    int64_t sh[kMaxDims], st[kMaxDims];
+    int n = 0;
+    for (int i = 0; i < a->ndim; ++i) {
+        if (i == ax || a->shape[i] == 1) continue;
+        if (n > 0 && st[n - 1] == a->stride[i] * a->shape[i]) {
+            sh[n - 1] *= a->shape[i];
+            st[n - 1] = a->stride[i];
+            continue;
+        }
+        sh[n] = a->shape[i];
+        st[n] = a->stride[i];
+        ++n;
+    }
+    if (n > kStrMaxOut) return false;
+    if (n == 0) {
+        sh[0] = 1;
+        st[0] = 0;
+        n = 1;
+    }
+    p->nd = n;
+    for (int d = 0; d < n; ++d) {
+        p->oshape[d] = sh[d];
+        p->ostride[d] = st[d];
+    }
+    p->k = a->shape[ax];
+    p->sk = a->stride[ax];
+    p->tail_k = p->k;
+    return true;
+}
+
+inline int64_t iabs64(int64_t v) { return v < 0 ? -v : v; }
+
+template <typename T, typename OT, int OP>
+qsml_status_t launch_strided(Context* ctx, const T* x, const StridedPlan& p, int64_t nout, OT* out, float scale,
+                             bool lanes) {
+    int64_t grid;
+    cudaError_t e;
+    if (lanes) {
+        grid = (nout + 7) / 8;
+        const int64_t cap = static_cast<int64_t>(ctx->num_sms) * 32;
+        if (grid > cap) grid = cap;
+        e = launch_pdl(k_reduce_strided_lanes<T, OT, OP>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, ctx->stream,
+                       x, p, nout, out, scale);
+        if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_strided_lanes");
+        return after_launch(ctx, "k_reduce_strided_lanes");
+    }
+    grid = (nout + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(ctx->num_sms) * 8;
+    if (grid > cap) grid = cap;
+    e = launch_pdl(k_reduce_strided_serial<T, OT, OP>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, ctx->stream, x,
+                   p, nout, out, scale);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_strided_serial");
+    return after_launch(ctx, "k_reduce_strided_serial");
+}
+
+// One axis of a view.
+template <typename T, typename OT, int OP>
+qsml_status_t run_reduce_strided(Context* ctx, const qsml_tdesc* a, int ax, OT* out) {
+    StridedPlan p;
+    if (!strided_plan(a, ax, &p))
+        return set_error(ctx, QSML_E_UNSUPPORTED, "qsml_reduce: view has too many non-mergeable dims");
+    int64_t nout = 1;
+    for (int d = 0; d < p.nd; ++d) nout *= p.oshape[d];
+    // read along k when k is the view's more contiguous direction
+    const bool lanes = iabs64(p.sk) <= iabs64(p.ostride[p.nd - 1]);
+    return launch_strided<T, OT, OP>(ctx, static_cast<const T*>(a->data), p, nout, out,
+                                     1.0f / static_cast<float>(p.k), lanes);
+}
+
+// All elements of a view: its most contiguous dim into binary32 scratch, then
+// the scratch (mean: divided by the view's element count).
+template <typename T, typename OT, int OP>
+qsml_status_t run_reduce_strided_all(Context* ctx, const qsml_tdesc* a, OT* out) {
+    constexpr int OP1 = OP == QSML_RED_MEAN ? QSML_RED_SUM : OP;
+    const int64_t n = numel(a);
+    int ax = -1;
+    for (int i = 0; i < a->ndim; ++i)
+        if (a->shape[i] > 1 && (ax < 0 || iabs64(a->stride[i]) < iabs64(a->stride[ax]))) ax = i;
+    StridedPlan p;
+    if (ax < 0 || !strided_plan(a, ax, &p))
+        return set_error(ctx, QSML_E_UNSUPPORTED, "qsml_reduce: view has too many non-mergeable dims");
+    int64_t nout = 1;
+    for (int d = 0; d < p.nd; ++d) nout *= p.oshape[d];
+    if (nout == 1) {
+        // one strided dim: rows of kRowSplit elements (the last one ragged)
+        constexpr int64_t kRowSplit = 8192;
+        const int64_t k = p.k;
+        p.nd = 1;
+        p.oshape[0] = (k + kRowSplit - 1) / kRowSplit;
+        p.ostride[0] = kRowSplit * p.sk;
+        p.k = k < kRowSplit ? k : kRowSplit;
+        p.tail_k = k - (p.oshape[0] - 1) * kRowSplit;
+        nout = p.oshape[0];
+    }
+    const float scale = 1.0f / static_cast<float>(n);
+    if (nout == 1)
+        return launch_strided<T, OT, OP>(ctx, static_cast<const T*>(a->data), p, 1, out, scale, true);
+    void* part = nullptr;
+    std::string err;
+    qsml_status_t st = ctx->allocator->alloc(static_cast<size_t>(nout) * sizeof(float), &part, &err);
+    if (st != QSML_OK) return set_error(ctx, st, "qsml_reduce: strided scratch: " + err);
+    st = launch_strided<T, float, OP1>(ctx, static_cast<const T*>(a->data), p, nout, static_cast<float*>(part), 1.0f,
+                                       true);
+    if (st == QSML_OK) st = run_reduce<float, OT, OP>(ctx, static_cast<const float*>(part), 1, nout, 1, out, scale);
+    ctx->allocator->free(part, &err);  // reused in stream order
+    return st;
+}
+
+template <typename T, typename OT>
+qsml_status_t reduce_strided_op(Context* ctx, int op, const qsml_tdesc* a, int axis, OT* out) {
+    const int ax = axis == QSML_AXIS_ALL ? -1 : (axis < 0 ? axis + a->ndim : axis);
+#define QSML_STRIDED(OPC)                                                                  \
+    case OPC:                                                                              \
+        return ax < 0 ? run_reduce_strided_all<T, OT, OPC>(ctx, a, out)                    \
+                      : run_reduce_strided<T, OT, OPC>(ctx, a, ax, out);
+    switch (op) {
+        QSML_STRIDED(QSML_RED_SUM)
+        QSML_STRIDED(QSML_RED_MEAN)
+        QSML_STRIDED(QSML_RED_MAX)
+        QSML_STRIDED(QSML_RED_MIN)
+        QSML_STRIDED(QSML_RED_PROD)
+    }
+#undef QSML_STRIDED
+    return set_error(ctx, QSML_E_INVALID, "qsml_reduce: unknown op");
+}
+
 template <typename T, typename OT>
 qsml_status_t reduce_op(Context* ctx, int op, const T* x, int64_t outer, int64_t k, int64_t inner, OT* out) {
     switch (op) {
@@ -517,8 +734,6 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
         return set_error(C_, QSML_E_DTYPE, "qsml_reduce: input must be F32 or F16");
     if (out->dtype != a->dtype && out->dtype != QSML_F32)
         return set_error(C_, QSML_E_DTYPE, "qsml_reduce: out dtype must equal the input's or be F32");
-    if (!is_contiguous(a))
-        return set_error(C_, QSML_E_UNSUPPORTED, "qsml_reduce: input must be contiguous (materialise it with qsml_gather)");
     if (!is_contiguous(out)) return set_error(C_, QSML_E_SHAPE, "qsml_reduce: out must be contiguous");
 
     int64_t outer = 1, k = 1, inner = 1;
@@ -542,6 +757,12 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
             k_fill_value<__half><<<static_cast<unsigned>(blocks), 256, 0, C_->stream>>>(static_cast<__half*>(out->data),
                                                                                          __float2half_rn(v), nout);
         return after_launch(C_, "k_fill_value");
+    }
+    if (!is_contiguous(a)) {
+        if (a->dtype == QSML_F32) return reduce_strided_op<float, float>(C_, op, a, axis, static_cast<float*>(out->data));
+        if (out->dtype == QSML_F16)
+            return reduce_strided_op<__half, __half>(C_, op, a, axis, static_cast<__half*>(out->data));
+        return reduce_strided_op<__half, float>(C_, op, a, axis, static_cast<float*>(out->data));
     }
     if (a->dtype == QSML_F32)
         return reduce_op<float, float>(C_, op, static_cast<const float*>(a->data), outer, k, inner,

@@ -179,6 +179,13 @@ static void test_views_and_gathers() {
     check("transpose values", tc[1] == 6 && tc[8] == 1);
     auto ts = get(qsml::slice(T, 0, 0, 6, 4));  // X.T[::4, :]
     check("strided transpose slice", ts.size() == 16 && ts[0] == 0 && ts[8] == 4 && ts[9] == 10);
+    // reductions of views read the view in place (no contiguous copy)
+    auto ss = get(qsml::sum(s, 1));  // rows of X[1::3, 1::2]: 7+9+11, 25+27+29, 43+45+47
+    check("sum over a sliced view", ss.size() == 3 && ss[0] == 27 && ss[1] == 81 && ss[2] == 135);
+    auto st0 = get(qsml::sum(T, 1));  // X.T summed over its columns = X's row sums
+    check("sum over a transposed view", st0.size() == 6 && st0[0] == 0 + 6 + 12 + 18 + 24 + 30 + 36 + 42);
+    check("max of a sliced view", get(qsml::max(s))[0] == 47 && get(qsml::min(s))[0] == 7);
+    check("mean of a transposed view", near(get(qsml::mean(T))[0], 23.5f, 1e-5f));
     auto cat = qsml::concat({X, X}, 1);
     auto cv = get(cat);
     check("concat axis 1", cat->dim(1) == 12 && cv[6] == 0 && cv[13] == 7);
