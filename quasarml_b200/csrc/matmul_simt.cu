@@ -4,11 +4,13 @@
 // acc = fma(A[r][k], B[k][c], acc) for k ascending.  This kernel keeps that
 // exact order per output (one fma chain from k = 0 to K-1, no split-K, no
 // zero padding in k), so fp32 results are bit-identical to the reference's
-// arithmetic.  Tiles: 128x128 outputs per CTA, k-slices of 8 staged in
+// arithmetic.  Tiles: 128x128 outputs per CTA, k-slices of 16 staged in
 // shared memory (A transposed so both fragments are row reads), 8x8 outputs
-// per thread, register prefetch of the next slice while computing this one.
-// Used for QSML_MM_FP32_FFMA and as the fp16-input fallback for shapes the
-// tensor-core kernel does not take.
+// per thread.  The next slice's global loads are in flight while this one is
+// computed (16-byte loads for interior tiles of binary32 operands), and each
+// thread's fragments for step kk+1 are read from shared memory while the 64
+// fmas of step kk issue.  Used for QSML_MM_FP32_FFMA and as the fp16-input
+// fallback for shapes the tensor-core kernel does not take.
 #include "qsml_internal.cuh"
 
 #include "matmul.cuh"
@@ -16,7 +18,7 @@
 namespace qsml {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 8, TM = 8, TN = 8;
+constexpr int BM = 128, BN = 128, BK = 16, TM = 8, TN = 8;
 
 __device__ __forceinline__ float ldf(const float* p) { return *p; }
 __device__ __forceinline__ float ldf(const __half* p) { return __half2float(*p); }
@@ -24,42 +26,70 @@ __device__ __forceinline__ void stf(float* p, float v) { *p = v; }
 __device__ __forceinline__ void stf(__half* p, float v) { *p = __float2half_rn(v); }
 
 template <typename TI, typename TO>
-__global__ void __launch_bounds__(256) k_matmul_simt(const TI* __restrict__ A, const TI* __restrict__ B,
-                                                     TO* __restrict__ C, int M, int N, int K, int64_t lda,
-                                                     int64_t ldb, int64_t sA, int64_t sB, int64_t sC) {
-    __shared__ float As[2][BK][BM];
-    __shared__ float Bs[2][BK][BN];
+__global__ void __launch_bounds__(256, 2) k_matmul_simt(const TI* __restrict__ A, const TI* __restrict__ B,
+                                                        TO* __restrict__ C, int M, int N, int K, int64_t lda,
+                                                        int64_t ldb, int64_t sA, int64_t sB, int64_t sC) {
+    __shared__ __align__(16) float As[2][BK][BM];
+    __shared__ __align__(16) float Bs[2][BK][BN];
     const int tid = threadIdx.x;
-    const int tx = tid % 16, ty = tid / 16;
+    const int tx = tid & 15, ty = tid >> 4;
     const int bz = blockIdx.z;
     A += bz * sA;
     B += bz * sB;
     C += bz * sC;
     const int row0 = blockIdx.y * BM, col0 = blockIdx.x * BN;
 
-    // Each thread loads 4 elements of the A slice (128 x 8) and 4 of B (8 x 128).
-    // A: thread -> (r = tid / 2, k = (tid % 2) * 4 + j); B: (k = tid / 32, c = (tid % 32) * 4 + j).
-    const int ar = tid >> 1, ak = (tid & 1) * 4;
-    const int bk = tid >> 5, bc = (tid & 31) * 4;
-    float ra[4], rb[4];
+    // Loads of a k-slice: A (128 x 16) thread -> row tid / 2, k (tid % 2) * 8 + 0..7;
+    // B (16 x 128) thread -> k tid / 16, columns (tid % 16) * 8 + 0..7.
+    const int ar = tid >> 1, ak = (tid & 1) * 8;
+    const int bk = tid >> 4, bc = (tid & 15) * 8;
+    // Interior tiles of binary32 operands with 16-byte aligned rows take
+    // vector loads; everything else loads element by element with bounds.
+    bool vec = false;
+    if constexpr (sizeof(TI) == 4)
+        vec = row0 + BM <= M && col0 + BN <= N && lda % 4 == 0 && ldb % 4 == 0 &&
+              ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15u) == 0;
+    float ra[8], rb[8];
 
     auto load_slice = [&](int k0) {
+        if constexpr (sizeof(TI) == 4) {
+            if (vec && k0 + BK <= K) {
+                const float4* pa = reinterpret_cast<const float4*>(A + static_cast<int64_t>(row0 + ar) * lda + k0 + ak);
+                const float4 a0 = pa[0], a1 = pa[1];
+                const float4* pb = reinterpret_cast<const float4*>(B + static_cast<int64_t>(k0 + bk) * ldb + col0 + bc);
+                const float4 b0 = pb[0], b1 = pb[1];
+                ra[0] = a0.x; ra[1] = a0.y; ra[2] = a0.z; ra[3] = a0.w;
+                ra[4] = a1.x; ra[5] = a1.y; ra[6] = a1.z; ra[7] = a1.w;
+                rb[0] = b0.x; rb[1] = b0.y; rb[2] = b0.z; rb[3] = b0.w;
+                rb[4] = b1.x; rb[5] = b1.y; rb[6] = b1.z; rb[7] = b1.w;
+                return;
+            }
+        }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            int r = row0 + ar, k = k0 + ak + j;
+        for (int j = 0; j < 8; ++j) {
+            const int r = row0 + ar, k = k0 + ak + j;
             ra[j] = (r < M && k < K) ? ldf(A + static_cast<int64_t>(r) * lda + k) : 0.0f;
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            int k = k0 + bk, c = col0 + bc + j;
+        for (int j = 0; j < 8; ++j) {
+            const int k = k0 + bk, c = col0 + bc + j;
             rb[j] = (k < K && c < N) ? ldf(B + static_cast<int64_t>(k) * ldb + c) : 0.0f;
         }
     };
     auto store_slice = [&](int buf) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) As[buf][ak + j][ar] = ra[j];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) Bs[buf][bk][bc + j] = rb[j];
+        for (int j = 0; j < 8; ++j) As[buf][ak + j][ar] = ra[j];
+        *reinterpret_cast<float4*>(&Bs[buf][bk][bc]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+        *reinterpret_cast<float4*>(&Bs[buf][bk][bc + 4]) = make_float4(rb[4], rb[5], rb[6], rb[7]);
+    };
+    // Thread (tx, ty) owns rows ty*4 + {0..3} + {0, 64} and columns tx*4 + {0..3} + {0, 64}.
+    auto load_frag = [&](int buf, int kk, float* a, float* b) {
+        const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+        const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4 + 64]);
+        const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+        const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4 + 64]);
+        a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w; a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
+        b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
     };
 
     float acc[TM][TN];
@@ -77,49 +107,30 @@ __global__ void __launch_bounds__(256) k_matmul_simt(const TI* __restrict__ A, c
         if (s + 1 < nslices) load_slice((s + 1) * BK);
         const int kn = K - s * BK < BK ? K - s * BK : BK;  // valid k in this slice
         if (kn == BK) {
+            float fa[2][TM], fb[2][TN];
+            load_frag(buf, 0, fa[0], fb[0]);
 #pragma unroll
             for (int kk = 0; kk < BK; ++kk) {
-                float a[TM], b[TN];
-#pragma unroll
-                for (int i = 0; i < TM; i += 4) {
-                    float4 v = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4 + i * 16]);
-                    a[i] = v.x; a[i + 1] = v.y; a[i + 2] = v.z; a[i + 3] = v.w;
-                }
-#pragma unroll
-                for (int j = 0; j < TN; j += 4) {
-                    float4 v = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4 + j * 16]);
-                    b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
-                }
+                if (kk + 1 < BK) load_frag(buf, kk + 1, fa[(kk + 1) & 1], fb[(kk + 1) & 1]);
 #pragma unroll
                 for (int i = 0; i < TM; ++i)
 #pragma unroll
-                    for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+                    for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(fa[kk & 1][i], fb[kk & 1][j], acc[i][j]);
             }
         } else {
+            // the last, partial slice: only the valid k (no fma with padding)
             for (int kk = 0; kk < kn; ++kk) {
                 float a[TM], b[TN];
-#pragma unroll
-                for (int i = 0; i < TM; i += 4) {
-                    float4 v = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4 + i * 16]);
-                    a[i] = v.x; a[i + 1] = v.y; a[i + 2] = v.z; a[i + 3] = v.w;
-                }
-#pragma unroll
-                for (int j = 0; j < TN; j += 4) {
-                    float4 v = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4 + j * 16]);
-                    b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
-                }
+                load_frag(buf, kk, a, b);
 #pragma unroll
                 for (int i = 0; i < TM; ++i)
 #pragma unroll
                     for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
             }
         }
-        if (s + 1 < nslices) {
-            store_slice(buf ^ 1);
-        }
+        if (s + 1 < nslices) store_slice(buf ^ 1);
         __syncthreads();
     }
-    // Thread (tx, ty) owns rows ty*4 + {0..3} + {0, 64} and cols tx*4 + {0..3} + {0, 64}.
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
         const int r = row0 + ty * 4 + (i & 3) + (i >> 2) * 64;
