@@ -142,6 +142,13 @@ class Dist:
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.pg = None
 
+    @classmethod
+    def single(cls) -> "Dist":
+        """One rank without collectives (a rank timing work alone)."""
+        d = cls.__new__(cls)
+        d.world, d.rank, d.local, d.pg = 1, 0, 0, None
+        return d
+
     def init(self, backend="nccl"):
         if self.world > 1:
             import datetime
@@ -1212,7 +1219,10 @@ def run_extras(ctx, dist: Dist, stream, hbm: float, tf_burst: float) -> dict:
     """The other configurations, each row-sharded over the ranks: weak
     scaling at every N (each rank the configuration's size), and at N>1 also
     strong scaling (the configuration's tensor split N ways).  Every rank
-    builds the workload, all agree it was built, then all time it."""
+    builds the workload, all agree it was built, then all time it.  At N>1
+    rank 0 first times each weak-scaling workload alone (the same per-rank
+    work on one GPU, in this run), which gives efficiency_vs_one_gpu =
+    per-GPU value at N / that one-GPU value."""
     import torch
     extras = {}
     scales = ("weak",) if dist.world == 1 else ("weak", "strong")
@@ -1230,15 +1240,28 @@ def run_extras(ctx, dist: Dist, stream, hbm: float, tf_burst: float) -> dict:
                 torch.cuda.synchronize()
                 torch.cuda.empty_cache()
                 continue
+            scale_unit = 1e9 if w.unit == "GB/s" else 1e12
+            alone = None
+            if scale == "weak" and dist.world > 1:
+                # the same per-rank work on one GPU in this run: rank 0 alone
+                # while the other ranks wait at the barrier
+                if dist.rank == 0:
+                    ms_a, _, g = time_steps(w, Dist.single(), stream, st, 3)
+                    del g
+                    alone = w.units_per_step * st / (ms_a / 1e3) / scale_unit
+                dist.barrier()
             ms_x, l_x, g = time_steps(w, dist, stream, st, 3)
             del g
             units = w.units_per_step * dist.world if scale == "weak" else dist.sum(w.units_per_step)
-            v = units * st / (ms_x / 1e3) / (1e9 if w.unit == "GB/s" else 1e12)
+            v = units * st / (ms_x / 1e3) / scale_unit
             peak = hbm if w.unit == "GB/s" else tf_burst
             extras[name] = {"workload": w.name, "scaling": scale, "value": round(v, 2),
                             "per_gpu": round(v / dist.world, 2), "unit": w.unit,
                             "frac_of_peak": round(v / dist.world / peak, 4), "peak": peak,
                             "ms_per_step": round(ms_x / st, 3), "launches_per_step": l_x // st}
+            if alone:
+                extras[name]["one_gpu_same_run"] = round(alone, 2)
+                extras[name]["efficiency_vs_one_gpu"] = round(v / dist.world / alone, 4)
             del w
             torch.cuda.synchronize()
             torch.cuda.empty_cache()
