@@ -398,8 +398,11 @@ QSML_API qsml_status_t qsml_group_destroy(qsml_group* group);
 
 /* In place over `count` binary32 partials at buf (device memory of local
  * rank `local`'s context), on that context's stream: op SUM or MEAN adds,
- * MAX / MIN take the IEEE 754-2019 maximum / minimum.  Not inside
- * qsml_group_start / qsml_group_end. */
+ * MAX / MIN take the IEEE 754-2019 maximum / minimum.  One process driving
+ * several GPUs from one thread brackets its ranks' calls with
+ * qsml_group_start / qsml_group_end (the combine, and for max / min the
+ * decoding of the keys after it, then complete in stream order once
+ * qsml_group_end returns). */
 QSML_API qsml_status_t qsml_allreduce_partials(qsml_group* group, int32_t local, int32_t op, void* buf,
                                                int64_t count);
 
@@ -413,7 +416,10 @@ QSML_API qsml_status_t qsml_finish_partial(qsml_ctx* ctx, int32_t op, const qsml
  * with qsml_reduce's axis / keepdims / out rules; out is identical on every
  * rank for axis 0 and QSML_AXIS_ALL.  global_rows = the rows of all ranks
  * together (0: this rank's rows times the number of ranks).  A rank without
- * rows contributes 0 to sums and the identity (-inf / +inf) to max / min. */
+ * rows contributes 0 to sums and the identity (-inf / +inf) to max / min.
+ * Not inside qsml_group_start / qsml_group_end (it finishes right after its
+ * combine): one process driving several GPUs from one thread uses the three
+ * steps above, with the combines bracketed. */
 QSML_API qsml_status_t qsml_reduce_sharded(qsml_group* group, int32_t local, int32_t op, const qsml_tdesc* a,
                                            int32_t axis, int32_t keepdims, const qsml_tdesc* out,
                                            int64_t global_rows);

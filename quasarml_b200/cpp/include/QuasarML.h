@@ -182,6 +182,21 @@ using QuasarML::ReduceOp;
 inline void all_reduce(const std::vector<TensorPtr>& per_device, ReduceOp op = ReduceOp::Sum) {
     QuasarML::Ops::all_reduce(per_device, op);
 }
+// Row-sharded tensors: one block of rows per device (scatter_rows splits host
+// data over devices 0..n-1), reduced across all of them by sharded_reduce.
+inline std::vector<TensorPtr> scatter_rows(const void* host, const std::vector<u32>& shape, u32 num_devices,
+                                           DataType dtype = DataType::F32) {
+    std::vector<Device*> devs;
+    for (u32 i = 0; i < num_devices; ++i) devs.push_back(&device(i));
+    return QuasarML::Ops::scatter_rows(host, shape, dtype, devs);
+}
+inline std::vector<TensorPtr> sharded_reduce(const std::vector<TensorPtr>& blocks, ReduceOp op, i32 axis,
+                                             bool keepdims = false) {
+    return QuasarML::Ops::sharded_reduce(blocks, op, axis, keepdims);
+}
+inline std::vector<TensorPtr> sharded_reduce(const std::vector<TensorPtr>& blocks, ReduceOp op) {
+    return QuasarML::Ops::sharded_reduce(blocks, op);
+}
 
 // Elementwise fusion (deferred results evaluated as one kernel on access).
 inline void set_fusion(bool on) { device().set_fusion(on); }

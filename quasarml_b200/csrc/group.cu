@@ -85,6 +85,15 @@ int64_t timeout_ms() {
 // collectives issued inside the current bracket (settled at its end).
 thread_local int g_group_depth = 0;
 thread_local std::vector<std::pair<qsml_group*, int>> g_bracket;
+// Key decodings of max/min partials combined inside the current bracket:
+// they follow the collective, which NCCL enqueues at the bracket's end.
+struct PendingDecode {
+    Context* ctx;
+    void* buf;
+    int64_t count;
+    int32_t op;
+};
+thread_local std::vector<PendingDecode> g_decodes;
 
 qsml_status_t nccl_error(Context* ctx, ncclResult_t r, const char* what) {
     return set_error(ctx, QSML_E_NCCL, std::string(what) + ": " + nccl().error_string(r));
@@ -315,6 +324,8 @@ qsml_status_t qsml_group_end(void) {
     if (g_group_depth > 0) return r == ncclSuccess || r == ncclInProgress ? QSML_OK : nccl_error(nullptr, r, "ncclGroupEnd");
     std::vector<std::pair<qsml_group*, int>> issued;
     issued.swap(g_bracket);
+    std::vector<PendingDecode> decodes;
+    decodes.swap(g_decodes);
     qsml_status_t st = QSML_OK;
     if (r != ncclSuccess && r != ncclInProgress) st = nccl_error(nullptr, r, "ncclGroupEnd");
     // The bracket's collectives are enqueued once their communicators settle.
@@ -325,6 +336,15 @@ qsml_status_t qsml_group_end(void) {
         }
         st = settle(e.first->ctxs[e.second], {e.first->comms[e.second]}, "qsml_group_end");
         if (st != QSML_OK) e.first->failed = true;
+    }
+    // then the key decodings, in stream order after their collectives
+    for (auto& d : decodes) {
+        if (st != QSML_OK) break;
+        if (cudaSetDevice(d.ctx->device) != cudaSuccess) {
+            st = set_error(d.ctx, QSML_E_CUDA, "cudaSetDevice failed");
+            break;
+        }
+        st = keys_pass(d.ctx, d.buf, d.count, d.op, true);
     }
     return st;
 }
@@ -361,9 +381,6 @@ qsml_status_t qsml_allreduce_partials(qsml_group* g, int32_t local, int32_t op, 
         return set_error(nullptr, QSML_E_INVALID, "qsml_allreduce_partials: bad group or local rank");
     Context* C_ = g->ctxs[local];
     if (cudaSetDevice(C_->device) != cudaSuccess) return set_error(C_, QSML_E_CUDA, "cudaSetDevice failed");
-    if (g_group_depth > 0)
-        return set_error(C_, QSML_E_INVALID,
-                         "qsml_allreduce_partials: not inside qsml_group_start/end (its key decoding follows the exchange)");
     if (op < QSML_RED_SUM || op > QSML_RED_MIN) return set_error(C_, QSML_E_INVALID, "qsml_allreduce_partials: unknown op");
     if (count < 0 || (count > 0 && !buf)) return set_error(C_, QSML_E_INVALID, "qsml_allreduce_partials: bad buffer");
     if (count == 0) return QSML_OK;
@@ -375,6 +392,12 @@ qsml_status_t qsml_allreduce_partials(qsml_group* g, int32_t local, int32_t op, 
     if (r != ncclSuccess && r != ncclInProgress) {
         g->failed = true;
         return nccl_error(C_, r, "ncclAllReduce (partials)");
+    }
+    if (g_group_depth > 0) {
+        // inside a bracket: qsml_group_end settles the collective, then decodes
+        g_bracket.emplace_back(g, local);
+        if (keys) g_decodes.push_back(PendingDecode{C_, buf, count, op});
+        return QSML_OK;
     }
     qsml_status_t st = settle(C_, {g->comms[local]}, "qsml_allreduce_partials");
     if (st != QSML_OK) {
@@ -418,6 +441,9 @@ qsml_status_t qsml_reduce_sharded(qsml_group* g, int32_t local, int32_t op, cons
         return set_error(nullptr, QSML_E_INVALID, "qsml_reduce_sharded: bad group or local rank");
     Context* C_ = g->ctxs[local];
     qsml_ctx* h = reinterpret_cast<qsml_ctx*>(C_);
+    if (g_group_depth > 0)
+        return set_error(C_, QSML_E_INVALID,
+                         "qsml_reduce_sharded: not inside qsml_group_start/end (it finishes right after its combine)");
     QSML_TRY_STATUS(check_desc(C_, a, "a"));
     QSML_TRY_STATUS(check_desc(C_, out, "out"));
     if (op < QSML_RED_SUM || op > QSML_RED_MIN) return set_error(C_, QSML_E_INVALID, "qsml_reduce_sharded: unknown op");

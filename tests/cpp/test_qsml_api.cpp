@@ -373,6 +373,57 @@ static void test_errors_and_counters() {
     check("cpu_fallback_count == 0", qsml::cpu_fallback_count() == 0);
 }
 
+// Row-sharded reductions over as many devices as there are (two at most):
+// results equal the host's reduction of the whole tensor; -0 and +0 in one
+// column must give +0 for max and -0 for min across the blocks.
+static void test_sharded_reduce() {
+    const unsigned R = 10, C = 6;
+    vector<float> v(R * C);
+    for (size_t i = 0; i < v.size(); ++i) v[i] = std::sin(0.7f * i) * 3.0f;
+    for (unsigned r = 0; r < R; ++r) v[r * C + 4] = (r % 2) ? 0.0f : -0.0f;
+    const unsigned nd = std::min(2u, qsml::device_count());
+    auto blocks = qsml::scatter_rows(v.data(), {R, C}, nd);
+    check("scatter_rows blocks", blocks.size() == nd && blocks[0]->dim(0) == (nd == 2 ? 5 : 10));
+    auto cs = qsml::sharded_reduce(blocks, qsml::ReduceOp::Sum, 0);
+    auto mx = qsml::sharded_reduce(blocks, qsml::ReduceOp::Max, 0);
+    auto mn = qsml::sharded_reduce(blocks, qsml::ReduceOp::Min, 0);
+    auto all = qsml::sharded_reduce(blocks, qsml::ReduceOp::Mean);
+    bool ok_sum = true, ok_max = true, ok_min = true, ok_mean = true;
+    double total = 0;
+    for (float x : v) total += x;
+    for (unsigned d = 0; d < nd; ++d) {
+        auto s = get(cs[d]), m = get(mx[d]), n = get(mn[d]), a = get(all[d]);
+        for (unsigned c = 0; c < C; ++c) {
+            double want = 0;
+            float hi = -INFINITY, lo = INFINITY;
+            for (unsigned r = 0; r < R; ++r) {
+                want += v[r * C + c];
+                hi = std::max(hi, v[r * C + c]);
+                lo = std::min(lo, v[r * C + c]);
+            }
+            ok_sum &= near(s[c], static_cast<float>(want), 1e-4f);
+            if (c == 4) {
+                ok_max &= m[c] == 0.0f && !std::signbit(m[c]);
+                ok_min &= n[c] == 0.0f && std::signbit(n[c]);
+            } else {
+                ok_max &= m[c] == hi;
+                ok_min &= n[c] == lo;
+            }
+        }
+        ok_mean &= a.size() == 1 && near(a[0], static_cast<float>(total / (R * C)), 1e-5f);
+    }
+    check("sharded sum over rows", ok_sum);
+    check("sharded max over rows (+0 beats -0)", ok_max);
+    check("sharded min over rows (-0 beats +0)", ok_min);
+    check("sharded mean of all elements", ok_mean);
+    auto rm = qsml::sharded_reduce(blocks, qsml::ReduceOp::Mean, 1);
+    auto r0 = get(rm[0]);
+    double row0 = 0;
+    for (unsigned c = 0; c < C; ++c) row0 += v[c];
+    check("sharded mean over columns stays row-local", rm[0]->dim(0) == blocks[0]->dim(0) &&
+                                                           near(r0[0], static_cast<float>(row0 / C), 1e-5f));
+}
+
 int main() {
     qsml::init();
     try {
@@ -389,6 +440,7 @@ int main() {
         test_layer_norm_and_matmul();
         test_fusion();
         test_all_reduce();
+        test_sharded_reduce();
         test_errors_and_counters();
     } catch (const std::exception& e) {
         std::cout << "EXCEPTION: " << e.what() << "\n";
