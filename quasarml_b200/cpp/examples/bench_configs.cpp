@@ -106,12 +106,12 @@ int main() {
         };
         report("elementwise_chain", "elementwise chain relu(pow((A+B)*B - A, 2.0) / D), A[4096,4096], B[1,4096], "
                "D[4096,1] fp32, six qsml:: calls",
-               4 * 872464384.0, "GB/s", 2, 10, [&] {
+               4 * 872464384.0, "GB/s", 3, 50, [&] {
                    for (int b = 0; b < 4; ++b) chain(b);
                });
         qsml::set_fusion(true);
         report("elementwise_chain_fused", "the same chain with qsml::set_fusion(true): one deferred kernel",
-               4 * (2.0 * N * 4 + 2 * 4096 * 4), "GB/s", 2, 20, [&] {
+               4 * (2.0 * N * 4 + 2 * 4096 * 4), "GB/s", 3, 100, [&] {
                    for (int b = 0; b < 4; ++b) chain(b)->materialize();
                });
         qsml::set_fusion(false);
@@ -163,7 +163,7 @@ int main() {
         auto Xf = upload_f32(uniform(5, 0, n, -1, 1), {8192, 8192}, false);
         report("gather", "strided gather X[5::3, 1::2] and X.T[::4, :] of X[8192,8192] int32 and fp32 "
                "(qsml::slice / qsml::transpose views, qsml::contiguous)",
-               2 * (134135808.0 + 335544320.0), "GB/s", 3, 20, [&] {
+               2 * (134135808.0 + 335544320.0), "GB/s", 3, 100, [&] {
                    for (auto& X : {Xi, Xf}) {
                        qsml::contiguous(qsml::slice(qsml::slice(X, 0, 5, 8192, 3), 1, 1, 8192, 2));
                        qsml::contiguous(qsml::slice(qsml::transpose(X, 0, 1), 0, 0, 8192, 4));
@@ -178,7 +178,7 @@ int main() {
         auto g = upload_f32(normal(11, 0, 4096, 1.0, 0.1), {4096}, false);
         auto bt = upload_f32(normal(12, 0, 4096, 0.0, 0.1), {4096}, false);
         report("layernorm", "layer norm X[16384,4096] fp32 and fp16, gamma/beta fp32, eps 1e-5 (qsml::layer_norm)",
-               536903680.0 + 268468224.0, "GB/s", 3, 20, [&] {
+               536903680.0 + 268468224.0, "GB/s", 3, 100, [&] {
                    qsml::layer_norm(X, g, bt, 1e-5f);
                    qsml::layer_norm(Xh, g, bt, 1e-5f);
                });
