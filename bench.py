@@ -275,7 +275,7 @@ class ReduceWorkload(Workload):
         self.bytes_per_step = sum(c.nbytes for c in self.calls)
         self.units_per_step = self.bytes_per_step
         self.unit = "GB/s"
-        self.h2d_bytes = sum(x.numel() * 4 for x in self.x32) + sum(x.numel() * 2 for x in self.x16)
+        self.h2d_bytes = sum(x.numel() * 4 for x in self.x32)  # X only: its fp16 copy is cast on the device
         self.d2h_bytes = sum(o.numel() * o.element_size() for o in self.outputs())
 
     def _plan_exchange(self, batch, n):
@@ -396,7 +396,6 @@ class ReduceWorkload(Workload):
         from quasarml_b200 import abi
         self.init_exchange()
         self.h32 = [x.cpu().pin_memory() for x in self.x32]
-        self.h16 = [x.cpu().pin_memory() for x in self.x16]
         self.local_out = [c.out_t for c in self.calls_l]
         self.hout = [o.cpu().pin_memory() for o in self.local_out]
         self.hxout = [o.cpu().pin_memory() for o in self.exchanged_out] if self.sharded else []
@@ -406,6 +405,8 @@ class ReduceWorkload(Workload):
         self.back_stream = torch.cuda.Stream()
         self.back_ctx = abi.Context(torch.cuda.current_device())
         self.back_ctx.set_stream(self.back_stream.cuda_stream)
+        self.d32 = [abi.desc_of(x) for x in self.x32]
+        self.d16 = [abi.desc_of(x) for x in self.x16]
         self.landed = [torch.cuda.Event() for _ in range(self.batch)]
         self.reduced = [torch.cuda.Event() for _ in range(self.batch)]
         self.l_by_entry = [[i for i, c in enumerate(self.calls_l) if c.entry == b] for b in range(self.batch)]
@@ -416,8 +417,9 @@ class ReduceWorkload(Workload):
         cur = torch.cuda.current_stream()
         self.copy_stream.wait_stream(cur)  # the previous step has read X
         for b in range(self.batch):
+            # X crosses PCIe once; its binary16 copy is made on the device
             self.copy_ctx.h2d(self.x32[b].data_ptr(), self.h32[b].data_ptr(), self.h32[b].numel() * 4)
-            self.copy_ctx.h2d(self.x16[b].data_ptr(), self.h16[b].data_ptr(), self.h16[b].numel() * 2)
+            self.copy_ctx.cast(self.d32[b], self.d16[b])
             self.landed[b].record(self.copy_stream)
         # Local results travel back on a third stream as each entry finishes
         # (the other PCIe direction); exchanged ones after the combine.
@@ -562,6 +564,41 @@ class GatherWorkload(Workload):
     def compute(self, calls=None):
         for v, o, _ in (self.calls if calls is None else calls):
             self.ctx.gather(v, o)
+
+
+class ReduceViewWorkload(Workload):
+    """Reductions of non-contiguous views of X[8192,8192] fp32, read in place:
+    X[5::3, 1::2] ([2729,4096], element strides (24576, 2)) and X.T
+    ([8192,8192], strides (1, 8192)), sum over each axis and max over the
+    last.  Bytes: the views' 32-byte-sector read footprint (stride-2 columns
+    touch every sector of their rows) plus the output."""
+    name = "reductions of strided views X[5::3, 1::2] and X.T of X[8192,8192] fp32: sum over each axis, max over the last"
+
+    def __init__(self, ctx, dist: Dist, scale: str = "weak"):
+        import torch
+        from quasarml_b200 import abi, datagen
+        self.ctx = ctx
+        r0, R, G = row_block(8192, dist, scale)
+        X = _t(datagen.uniform(datagen.SEEDS["gather_f32"], (R, 8192), -1, 1, offset=r0 * 8192))
+        self.keep = [X]
+        s0 = max(5, r0 + ((5 - r0) % 3))
+        n1 = len(range(s0, r0 + R, 3))
+        v1 = abi.make_desc(X.data_ptr() + ((s0 - r0) * 8192 + 1) * 4, abi.F32, (n1, 4096), (3 * 8192, 2))
+        v2 = abi.make_desc(X.data_ptr(), abi.F32, (8192, R), (1, 8192))
+        foot1, foot2 = n1 * 8192 * 4, R * 8192 * 4
+        self.calls = []
+        for view, shape, foot in ((v1, (n1, 4096), foot1), (v2, (8192, R), foot2)):
+            for op, axis in ((abi.RED_SUM, 0), (abi.RED_SUM, 1), (abi.RED_MAX, 1)):
+                oshape = abi.reduced_shape(shape, axis, False)
+                out = torch.empty(oshape, device="cuda")
+                self.keep.append(out)
+                self.calls.append((op, view, axis, abi.desc_of(out), foot + out.numel() * 4))
+        self.units_per_step = sum(c[4] for c in self.calls)
+        self.unit = "GB/s"
+
+    def compute(self, calls=None):
+        for op, x, axis, o, _ in (self.calls if calls is None else calls):
+            self.ctx.reduce(op, x, axis, False, o)
 
 
 class ArgReduceWorkload(Workload):
@@ -958,6 +995,19 @@ def run_single(which: str, reps: int = 3):
         out = torch.empty_like(A)
         for _ in range(reps):
             ctx.binary(abi.OP_ADD, d(A), d(B), d(out))
+    elif which in ("view_rows", "view_cols", "cast_f16"):
+        X = _t(datagen.uniform(5, (8192, 8192), -1, 1))
+        if which == "cast_f16":
+            Y = torch.empty((8192, 8192), dtype=torch.float16, device="cuda")
+            for _ in range(reps):
+                ctx.cast(d(X), d(Y))
+        else:
+            # X[5::3, 1::2]: rows read along k (view_rows, axis 1) or a thread per column (view_cols, axis 0)
+            v = abi.make_desc(X.data_ptr() + (5 * 8192 + 1) * 4, abi.F32, (2729, 4096), (3 * 8192, 2))
+            axis = 1 if which == "view_rows" else 0
+            out = torch.empty(abi.reduced_shape((2729, 4096), axis, False), device="cuda")
+            for _ in range(reps):
+                ctx.reduce(abi.RED_SUM, v, axis, False, d(out))
     elif which in ("chain_pow", "chain_relu"):
         A = _t(datagen.uniform(1, (4096, 4096), -1, 1))
         out = torch.empty_like(A)
@@ -1052,7 +1102,7 @@ def main():
     ap.add_argument("--single", default=None,
                     choices=["reduce_all", "reduce_axis0", "reduce_axis1", "reduce_axis2", "reduce_all_f16",
                              "reduce_axis0_f16", "reduce_axis1_f16", "reduce_axis2_f16", "chain_pow", "chain_relu",
-                             "matmul_ffma",
+                             "matmul_ffma", "view_rows", "view_cols", "cast_f16",
                              "chain_add", "chain_fused", "gather_t", "gather_s", "layernorm", "matmul_f16",
                              "matmul_3xtf32", "bmm_f16", "argmax_all", "argmax_axis1", "argmax_axis1_f16", "softmax",
                              "softmax_f16",
@@ -1124,8 +1174,9 @@ def main():
         ev = wl.units_per_step * e_steps * dist.world / (ems / 1e3) / 1e9
         line["e2e"] = {"value": round(ev, 2), "unit": wl.unit, "h2d_bytes_per_step": wl.h2d_bytes,
                        "d2h_bytes_per_step": wl.d2h_bytes, "ms_per_step": round(ems / e_steps, 3),
-                       "path": "pinned host -> qsml_h2d per batch entry on a second context's stream -> "
-                               "the step's qsml_reduce calls of each entry as soon as its X has landed -> "
+                       "path": "pinned host -> qsml_h2d of each batch entry's X (fp32) on a second context's "
+                               "stream, qsml_cast to its fp16 copy there -> the step's qsml_reduce calls of each "
+                               "entry as soon as both have landed -> "
                                "qsml_d2h_async of each entry's results on a third stream"
                                + ("; the exchanged outputs after qsml_allreduce_partials / "
                                   "qsml_finish_partial" if sharded else "") + ", per step"}
@@ -1207,6 +1258,7 @@ EXTRAS = (("elementwise_chain", lambda c, d, s: ChainWorkload(c, d, scale=s), 10
           ("gather", lambda c, d, s: GatherWorkload(c, d, scale=s), 20),
           ("layernorm", lambda c, d, s: LayerNormWorkload(c, d, scale=s), 20),
           ("argmax_argmin", lambda c, d, s: ArgReduceWorkload(c, d, scale=s), 20),
+          ("reduce_views", lambda c, d, s: ReduceViewWorkload(c, d, scale=s), 20),
           ("softmax", lambda c, d, s: SoftmaxWorkload(c, d, scale=s), 20),
           ("matmul_f16_8192", lambda c, d, s: MatmulWorkload(c, d, "f16", False, scale=s), 5),
           ("matmul_f32_8192_3xtf32", lambda c, d, s: MatmulWorkload(c, d, "f32", False, scale=s), 5),

@@ -317,6 +317,13 @@ QSML_API qsml_status_t qsml_fuse_stats(qsml_ctx* ctx, uint64_t* jit_launches, ui
  * materialising transpose (QuasarML/src/Ops/LinAlg.cpp:329-351). */
 QSML_API qsml_status_t qsml_gather(qsml_ctx* ctx, const qsml_tdesc* src, const qsml_tdesc* out);
 
+/* out = src converted to out's dtype, elementwise: F32 -> F16 rounds to
+ * nearest even (values beyond the binary16 range become +-inf), F16 -> F32
+ * is exact, equal dtypes copy.  src and out contiguous, same shape.  No
+ * reference counterpart (the reference's tensors keep their creation dtype;
+ * an fp16 copy of data is built and uploaded from the host). */
+QSML_API qsml_status_t qsml_cast(qsml_ctx* ctx, const qsml_tdesc* src, const qsml_tdesc* out);
+
 /* y = exp(x - max) / sum(exp(x - max)) over one axis (negative counts from
  * the end); x and y F32 or F16 with the same contiguous shape, binary32
  * arithmetic (max, subtract, expf, sum, then multiply by the correctly

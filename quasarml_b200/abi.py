@@ -138,6 +138,7 @@ _SIGS = {
     "qsml_allreduce": (_c.c_int32, [_c.c_void_p, _c.c_int32, _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_int32]),
     "qsml_group_destroy": (_c.c_int32, [_c.c_void_p]),
     "qsml_gather": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc)]),
+    "qsml_cast": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc)]),
     "qsml_softmax": (_c.c_int32, [_c.c_void_p, _P(TDesc), _c.c_int32, _P(TDesc)]),
     "qsml_layer_norm": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_float, _P(TDesc)]),
     "qsml_matmul": (_c.c_int32, [_c.c_void_p, _P(TDesc), _P(TDesc), _P(TDesc), _c.c_int32]),
@@ -433,6 +434,10 @@ class Context:
 
     def gather(self, src: TDesc, out: TDesc) -> None:
         self.check(self.lib.qsml_gather(self.h, ctypes.byref(src), ctypes.byref(out)))
+
+    def cast(self, src: TDesc, out: TDesc) -> None:
+        """out = src converted to out's dtype (F32 <-> F16)."""
+        self.check(self.lib.qsml_cast(self.h, ctypes.byref(src), ctypes.byref(out)))
 
     def softmax(self, x: TDesc, axis: int, y: TDesc) -> None:
         self.check(self.lib.qsml_softmax(self.h, ctypes.byref(x), int(axis), ctypes.byref(y)))

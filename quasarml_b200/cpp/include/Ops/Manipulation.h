@@ -27,6 +27,8 @@ QS_API std::shared_ptr<Tensor> slice(Device& device, std::shared_ptr<Tensor> a, 
 QS_API std::shared_ptr<Tensor> broadcast_to(Device& device, std::shared_ptr<Tensor> a, const std::vector<u32>& shape);
 QS_API std::shared_ptr<Tensor> copy(Device& device, std::shared_ptr<Tensor> a);
 QS_API std::shared_ptr<Tensor> contiguous(Device& device, std::shared_ptr<Tensor> a);
+// A new tensor holding `a` converted to `dtype` (F32 <-> F16; same dtype copies).
+QS_API std::shared_ptr<Tensor> cast(Device& device, std::shared_ptr<Tensor> a, DataType dtype);
 
 }  // namespace Ops
 }  // namespace QuasarML

@@ -1,7 +1,8 @@
 // qsml:: facade of QuasarML (QuasarML/include/QuasarML.h), unchanged in
 // names and signatures, over the B200 backend.  Additions: pow, axis-aware
-// slice with a step, transpose(x, d0, d1) as a view, contiguous, layer_norm,
-// batch_matmul, matmul with an output dtype, cpu_fallback_count.
+// slice with a step, transpose(x, d0, d1) as a view, contiguous, cast,
+// layer_norm, batch_matmul, matmul with an output dtype, cpu_fallback_count,
+// row-sharded reductions over several devices.
 // The Vulkan-only Kernel type (GLSL pipelines) has no counterpart.
 #pragma once
 
@@ -174,6 +175,7 @@ inline TensorPtr slice(TensorPtr x, i32 axis, u64 start, u64 end, u64 step) {
 inline TensorPtr broadcast_to(TensorPtr x, const std::vector<u32>& shape) { return QuasarML::Ops::broadcast_to(device(), x, shape); }
 inline TensorPtr copy(TensorPtr x) { return QuasarML::Ops::copy(device(), x); }
 inline TensorPtr contiguous(TensorPtr x) { return QuasarML::Ops::contiguous(device(), x); }
+inline TensorPtr cast(TensorPtr x, DataType dtype) { return QuasarML::Ops::cast(device(), x, dtype); }
 
 // Ops that ran on the host instead of the GPU: always 0 in this backend.
 // Multi-GPU: in-place all-reduce of one tensor per device (this process

@@ -478,5 +478,14 @@ TP copy(Device& d, TP a) {
 
 TP contiguous(Device&, TP a) { return a->contiguous(); }
 
+TP cast(Device& d, TP a, DataType dtype) {
+    QS_ASSERT(a, "null tensor");
+    auto x = a->contiguous();
+    auto out = d.create_tensor(a->shape(), dtype);
+    qsml_tdesc dx = x->desc(), dout = out->desc();
+    d.check(qsml_cast(d.ctx(), &dx, &dout));
+    return out;
+}
+
 }  // namespace Ops
 }  // namespace QuasarML

@@ -127,9 +127,18 @@ qsml_status_t settle(Context* ctx, const std::vector<ncclComm_t>& comms, const c
     }
 }
 
+// QSML_NCCL_MAX_CTAS caps the CTAs (channels) each collective of the group
+// may occupy: combines that overlap memory-bound kernels take SMs from them.
 ncclConfig_t nonblocking_config() {
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;
+    if (const char* s = std::getenv("QSML_NCCL_MAX_CTAS")) {
+        const int v = std::atoi(s);
+        if (v > 0) {
+            cfg.maxCTAs = v;
+            cfg.minCTAs = 1;
+        }
+    }
     return cfg;
 }
 
