@@ -579,16 +579,19 @@ class ReduceViewWorkload(Workload):
         from quasarml_b200 import abi, datagen
         self.ctx = ctx
         r0, R, G = row_block(8192, dist, scale)
-        X = _t(datagen.uniform(datagen.SEEDS["gather_f32"], (R, 8192), -1, 1, offset=r0 * 8192))
-        self.keep = [X]
+        # one X per view (the views of X[8192N,8192], 2 x 256 MiB), calls
+        # alternating between them: no call finds its input in L2
+        Xa = _t(datagen.uniform(datagen.SEEDS["gather_f32"], (R, 8192), -1, 1, offset=r0 * 8192))
+        Xb = _t(datagen.uniform(datagen.SEEDS["gather_f32"], (R, 8192), -1, 1, offset=(G + r0) * 8192))
+        self.keep = [Xa, Xb]
         s0 = max(5, r0 + ((5 - r0) % 3))
         n1 = len(range(s0, r0 + R, 3))
-        v1 = abi.make_desc(X.data_ptr() + ((s0 - r0) * 8192 + 1) * 4, abi.F32, (n1, 4096), (3 * 8192, 2))
-        v2 = abi.make_desc(X.data_ptr(), abi.F32, (8192, R), (1, 8192))
+        v1 = abi.make_desc(Xa.data_ptr() + ((s0 - r0) * 8192 + 1) * 4, abi.F32, (n1, 4096), (3 * 8192, 2))
+        v2 = abi.make_desc(Xb.data_ptr(), abi.F32, (8192, R), (1, 8192))
         foot1, foot2 = n1 * 8192 * 4, R * 8192 * 4
         self.calls = []
-        for view, shape, foot in ((v1, (n1, 4096), foot1), (v2, (8192, R), foot2)):
-            for op, axis in ((abi.RED_SUM, 0), (abi.RED_SUM, 1), (abi.RED_MAX, 1)):
+        for op, axis in ((abi.RED_SUM, 0), (abi.RED_SUM, 1), (abi.RED_MAX, 1)):
+            for view, shape, foot in ((v1, (n1, 4096), foot1), (v2, (8192, R), foot2)):
                 oshape = abi.reduced_shape(shape, axis, False)
                 out = torch.empty(oshape, device="cuda")
                 self.keep.append(out)
