@@ -1297,16 +1297,23 @@ def run_extras(ctx, dist: Dist, stream, hbm: float, tf_burst: float) -> dict:
                 continue
             scale_unit = 1e9 if w.unit == "GB/s" else 1e12
             alone = None
-            if scale == "weak" and dist.world > 1:
-                # the same per-rank work on one GPU in this run: rank 0 alone
-                # while the other ranks wait at the barrier
-                if dist.rank == 0:
-                    ms_a, _, g = time_steps(w, Dist.single(), stream, st, 3)
-                    del g
-                    alone = w.units_per_step * st / (ms_a / 1e3) / scale_unit
-                dist.barrier()
-            ms_x, l_x, g = time_steps(w, dist, stream, st, 3)
-            del g
+            try:
+                if scale == "weak" and dist.world > 1:
+                    # the same per-rank work on one GPU in this run: rank 0
+                    # alone while the other ranks wait at the barrier
+                    if dist.rank == 0:
+                        ms_a, _, g = time_steps(w, Dist.single(), stream, st, 3)
+                        del g
+                        alone = w.units_per_step * st / (ms_a / 1e3) / scale_unit
+                    dist.barrier()
+                ms_x, l_x, g = time_steps(w, dist, stream, st, 3)
+                del g
+            except Exception as e:  # a library error of this workload: reported, the others still run
+                extras[name] = {"error": repr(e)[:300]}
+                del w
+                torch.cuda.synchronize()
+                torch.cuda.empty_cache()
+                continue
             units = w.units_per_step * dist.world if scale == "weak" else dist.sum(w.units_per_step)
             v = units * st / (ms_x / 1e3) / scale_unit
             peak = hbm if w.unit == "GB/s" else tf_burst
