@@ -1297,19 +1297,28 @@ def run_extras(ctx, dist: Dist, stream, hbm: float, tf_burst: float) -> dict:
                 continue
             scale_unit = 1e9 if w.unit == "GB/s" else 1e12
             alone = None
-            try:
-                if scale == "weak" and dist.world > 1:
-                    # the same per-rank work on one GPU in this run: rank 0
-                    # alone while the other ranks wait at the barrier
-                    if dist.rank == 0:
+            err = None
+            if scale == "weak" and dist.world > 1:
+                # the same per-rank work on one GPU in this run: rank 0 alone
+                # while the other ranks wait at the barrier
+                if dist.rank == 0:
+                    try:
                         ms_a, _, g = time_steps(w, Dist.single(), stream, st, 3)
                         del g
                         alone = w.units_per_step * st / (ms_a / 1e3) / scale_unit
-                    dist.barrier()
-                ms_x, l_x, g = time_steps(w, dist, stream, st, 3)
-                del g
-            except Exception as e:  # a library error of this workload: reported, the others still run
-                extras[name] = {"error": repr(e)[:300]}
+                    except Exception as e:
+                        err = repr(e)[:300]
+                dist.barrier()
+                if dist.max(1.0 if err else 0.0) > 0:
+                    err = err or "failed on rank 0"
+            if err is None:
+                try:
+                    ms_x, l_x, g = time_steps(w, dist, stream, st, 3)
+                    del g
+                except Exception as e:  # a library error of this workload: the same on every rank
+                    err = repr(e)[:300]
+            if err is not None:
+                extras[name] = {"error": err}
                 del w
                 torch.cuda.synchronize()
                 torch.cuda.empty_cache()
