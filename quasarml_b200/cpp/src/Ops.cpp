@@ -266,10 +266,17 @@ TP arg_reduce(Device& device, int op, const TP& a, i32 axis) {
     QS_ASSERT(a, "null tensor");
     axis = norm_axis(axis, a->rank());
     QS_ASSERT(a->dim(axis) > 0, "argmax/argmin of an empty axis");
-    auto x = a->contiguous();
     auto out = device.create_tensor(reduced_shape(a->shape(), axis, false), DataType::I32);
-    qsml_tdesc dx = x->desc(), dout = out->desc();
-    device.check(qsml_arg_reduce(device.ctx(), op, &dx, axis, 0, &dout));
+    // a transpose is read in place; other views are gathered first
+    a->materialize();
+    qsml_tdesc dx = a->desc(), dout = out->desc();
+    int st = qsml_arg_reduce(device.ctx(), op, &dx, axis, 0, &dout);
+    if (st == QSML_E_UNSUPPORTED && !a->is_contiguous()) {
+        auto x = a->contiguous();
+        dx = x->desc();
+        st = qsml_arg_reduce(device.ctx(), op, &dx, axis, 0, &dout);
+    }
+    device.check(st);
     return out;
 }
 TP argmax(Device& d, TP a, i32 axis) { return arg_reduce(d, QSML_ARG_MAX, a, axis); }

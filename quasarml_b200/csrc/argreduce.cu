@@ -463,12 +463,18 @@ extern "C" qsml_status_t qsml_arg_reduce(qsml_ctx* handle, int32_t op, const qsm
     if (op != QSML_ARG_MAX && op != QSML_ARG_MIN) return set_error(C_, QSML_E_INVALID, "qsml_arg_reduce: unknown op");
     if (out->dtype != QSML_I32 && out->dtype != QSML_U32)
         return set_error(C_, QSML_E_DTYPE, "qsml_arg_reduce: out must be I32 or U32");
-    if (!is_contiguous(a))
-        return set_error(C_, QSML_E_UNSUPPORTED,
-                         "qsml_arg_reduce: input must be contiguous (materialise it with qsml_gather)");
     if (!is_contiguous(out)) return set_error(C_, QSML_E_SHAPE, "qsml_arg_reduce: out must be contiguous");
     int64_t outer = 1, k = 1, inner = 1;
     QSML_TRY_STATUS(plan_reduction(C_, a, axis, keepdims, out, "qsml_arg_reduce", &outer, &k, &inner));
+    // A transposed or permuted contiguous block reduced over one axis is the
+    // contiguous arg-reduction of that block (the index along the axis is the
+    // same); a full arg-reduction's flat index follows the view's order, so
+    // it needs a contiguous input.
+    if (!is_contiguous(a) &&
+        (axis == QSML_AXIS_ALL || !dense_view_plan(a, axis, &outer, &k, &inner)))
+        return set_error(C_, QSML_E_UNSUPPORTED,
+                         "qsml_arg_reduce: input must be contiguous or a permuted contiguous block reduced over one "
+                         "axis (materialise other views with qsml_gather)");
     if (outer * inner == 0) return QSML_OK;
     if (k == 0) return set_error(C_, QSML_E_SHAPE, "qsml_arg_reduce: arg-reduction of an empty axis");
     const int64_t kmax_len = out->dtype == QSML_I32 ? int64_t(INT32_MAX) : int64_t(0xFFFFFFFEu);

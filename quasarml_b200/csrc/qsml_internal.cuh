@@ -185,6 +185,16 @@ qsml_status_t plan_reduction(Context* ctx, const qsml_tdesc* a, int32_t axis, in
 
 constexpr int kMaxDims = QSML_MAX_DIMS;
 
+// A view whose elements fill one contiguous block in another dim order (a
+// transpose or permutation of a contiguous tensor; strides >= 0), reduced
+// over `axis`, is the contiguous reduction [outer, k, inner] of that block
+// when the kept dims appear in the view in memory order (strides decreasing),
+// so that the results come out in the view's order.  True (and the block's
+// [outer, k, inner], base = a->data) in that case, and for QSML_AXIS_ALL on
+// any such view; false for every other view, and when the reduced dim has
+// extent 1.
+bool dense_view_plan(const qsml_tdesc* a, int32_t axis, int64_t* outer, int64_t* k, int64_t* inner);
+
 }  // namespace qsml
 
 // Every entry point validates its context with this.

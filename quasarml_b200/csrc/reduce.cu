@@ -20,6 +20,9 @@
 //   * k_reduce_cols  -- inner > 1: lanes own 16-byte column vectors (loads
 //                       coalesced along inner), the CTA's warps split k into
 //                       contiguous slices, slices combine in warp order;
+//   * k_reduce_cols_split -- k_reduce_cols for fewer than 128 column tiles
+//                       over a long k: k also cut over CTAs, partials combined
+//                       in chunk order by the CTA taking the last ticket;
 //   * k_reduce_cols_wide -- inner > 1 with 16-byte column vectors, k <= 64 and
 //                       many columns: each warp one column span over all k,
 //                       the CTA's 8 warps neighbouring spans of the same rows.
@@ -48,6 +51,7 @@ constexpr int kSegIters = 8;         // 16-byte loads in flight per thread
 constexpr int64_t kSegMaxUnits = 8192;  // slices per launch, all rows together
 constexpr int64_t kSegSliceElems = 32768;  // elements per slice of a long row
 constexpr int64_t kWideMaxK = 64;       // longest k the wide column kernel takes
+constexpr int64_t kSplitBelowTiles = 128;  // column tiles below which k is also split over CTAs
 constexpr int kMaxSegments = 16384;  // ticket counters kept in scratch
 constexpr size_t kCounterBytes = kMaxSegments * sizeof(unsigned);
 static_assert(kCounterBytes == kScratchCounterBytes, "counters fill the reserved scratch region");
@@ -354,6 +358,87 @@ __global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k,
 }
 
 // ---------------------------------------------------------------------------
+// Split column kernel, for few column tiles over a long k (X[8192,8192] over
+// axis 0 has 64 tiles of fp32): k_reduce_cols with k also cut into S
+// contiguous chunks over S CTAs (unit = (chunk s, tile), tiles fastest).
+// CTA (s, tile) reduces its chunk like k_reduce_cols (warps take contiguous
+// sub-chunks, combined in warp order) and stores one binary32 partial per
+// column; the CTA taking the tile's last ticket combines the S partials in
+// chunk order.  S comes from the shape alone.  (For the 256-512 tiles of
+// X[64,512,1024] over axis 1 the unsplit kernel measured faster on B200.)
+// ---------------------------------------------------------------------------
+template <typename T, typename OT, int OP>
+__global__ void k_reduce_cols_split(const T* __restrict__ x, int64_t outer, int64_t k, int64_t inner,
+                                    int64_t tiles_per_o, int64_t S, OT* __restrict__ out, float scale,
+                                    unsigned* __restrict__ counters, typename Red<OP>::V* __restrict__ partials) {
+    using R = Red<OP>;
+    using V = typename R::V;
+    constexpr int PV = Pack<T>::N;
+    constexpr int NC = 32 * PV;
+    constexpr int U = 8;
+    extern __shared__ unsigned char smem_raw[];
+    V* red = reinterpret_cast<V*>(smem_raw);
+    __shared__ bool s_last;
+    const int lane = threadIdx.x, w = threadIdx.y, W = blockDim.y;
+    const int64_t tiles = tiles_per_o * outer;
+    const int64_t s = blockIdx.x / tiles;
+    const int64_t tile = blockIdx.x - s * tiles;
+    const int64_t o = tile / tiles_per_o;
+    const int64_t tc0 = (tile - o * tiles_per_o) * NC;
+    const int64_t c0 = tc0 + static_cast<int64_t>(lane) * PV;
+    const int64_t kc = (k + S - 1) / S;
+    const int64_t ks = s * kc, ke = ks + kc < k ? ks + kc : k;
+    const int64_t kper = (kc + W - 1) / W;
+    const int64_t k0 = ks + w * kper;
+    const int64_t k1 = k0 + kper < ke ? k0 + kper : ke;
+    pdl_begin();
+    V acc[PV];
+#pragma unroll
+    for (int e = 0; e < PV; ++e) acc[e] = R::ident();
+    if (c0 < inner) {
+        const T* base = x + (o * k) * inner + c0;
+        int64_t kk = k0;
+        for (; kk + U <= k1; kk += U) {
+            Pack<T> v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) v[u] = *reinterpret_cast<const Pack<T>*>(base + (kk + u) * inner);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v[u].v[e])));
+        }
+        for (; kk < k1; ++kk) {
+            Pack<T> v = *reinterpret_cast<const Pack<T>*>(base + kk * inner);
+#pragma unroll
+            for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v.v[e])));
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < PV; ++e) red[(w * 32 + lane) * PV + e] = acc[e];
+    __syncthreads();
+    const int tid = w * 32 + lane;
+    for (int col = tid; col < NC; col += 32 * W) {
+        V a = red[col];
+        for (int ww = 1; ww < W; ++ww) a = R::comb(a, red[ww * NC + col]);
+        partials[(tile * S + s) * NC + col] = a;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&counters[tile], 1u) == static_cast<unsigned>(S - 1);
+    __syncthreads();
+    if (!s_last) return;
+    // This CTA completed the tile: combine its S partials in chunk order.
+    __threadfence();
+    for (int col = tid; col < NC; col += 32 * W) {
+        V a = __ldcg(&partials[tile * S * NC + col]);
+        for (int64_t j = 1; j < S; ++j) a = R::comb(a, __ldcg(&partials[(tile * S + j) * NC + col]));
+        const int64_t ci = tc0 + col;
+        if (ci < inner) from_f(R::fin(a, scale), &out[o * inner + ci]);
+    }
+    if (tid == 0) counters[tile] = 0;  // ready for the next launch on this stream
+}
+
+// ---------------------------------------------------------------------------
 // Wide column kernel (16-byte column vectors, short k, many columns): a CTA
 // takes 8 neighbouring spans (warp w: span w, 32 lanes x PV columns) over all
 // k rows, so each of its load instructions reads 4 KiB of one row in one
@@ -468,6 +553,27 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
     const int pv = vec ? PV : 1;
     const int64_t tiles_per_o = (inner + 32 * pv - 1) / (32 * pv);
     const int64_t tiles = tiles_per_o * outer;
+    if (vec && tiles < kSplitBelowTiles) {
+        // Few tiles over a long k: 16 warps a CTA, k cut over S CTAs (about
+        // 2 * kSplitBelowTiles CTAs, at least 32 rows per warp).
+        const int64_t W = 16;
+        int64_t S = (2 * kSplitBelowTiles + tiles - 1) / tiles;
+        const int64_t cap = k / (W * 32);
+        if (S > cap) S = cap;
+        if (S > 1) {
+            void* scratch = nullptr;
+            QSML_TRY_STATUS(get_scratch(ctx, kCounterBytes + static_cast<size_t>(tiles * S) * 32 * PV * sizeof(V),
+                                        &scratch));
+            unsigned* counters = static_cast<unsigned*>(scratch);
+            V* partials = reinterpret_cast<V*>(static_cast<char*>(scratch) + kCounterBytes);
+            const cudaError_t e =
+                launch_pdl(k_reduce_cols_split<T, OT, OP>, dim3(static_cast<unsigned>(tiles * S)),
+                           dim3(32, static_cast<unsigned>(W)), static_cast<size_t>(W) * 32 * PV * sizeof(V),
+                           ctx->stream, x, outer, k, inner, tiles_per_o, S, out, scale, counters, partials);
+            if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_cols_split");
+            return after_launch(ctx, "k_reduce_cols_split");
+        }
+    }
     // about 4096 warps per launch (4 KiB of loads in flight each): measured on
     // B200 best for both axes of X[64,512,1024] in binary32 and binary16
     int64_t W = (4096 + tiles - 1) / tiles;
@@ -492,15 +598,19 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
 // where their strides chain -- into at most kStrMaxOut output dims, and the
 // kernels read the view in place: a reduction of a view is one pass over the
 // elements it covers, not a gather copy followed by a reduction.
-//   * k_reduce_strided_lanes  -- a warp per output, lanes striding over k:
+//   * k_reduce_strided_lanes -- a warp per output, lanes striding over k:
 //     when k is the view's more contiguous direction (rows of a slice);
-//   * k_reduce_strided_serial -- a thread per output, k ascending (the
-//     reference's serial order, Reduction.cpp:328): when neighbouring outputs
-//     are the more contiguous direction (columns, transposed views).
+//   * k_reduce_strided_cols  -- a lane per output, warps (and, for few
+//     outputs, CTAs) splitting k into contiguous chunks combined in order:
+//     when neighbouring outputs are the more contiguous direction (columns
+//     of a slice).
+// A view that is a transposed or permuted contiguous block does not come
+// here: qsml_reduce gives it to the contiguous kernels (dense_view_plan).
 // A full reduction of a view first reduces its most contiguous dim into
 // binary32 scratch (lanes kernel), then the scratch with the segment kernel.
 // ---------------------------------------------------------------------------
 constexpr int kStrMaxOut = 4;
+constexpr int64_t kStrTargetWarps = 8192;  // warps of a column-block launch
 
 struct StridedPlan {
     int nd;                              // output dims, outermost first
@@ -535,13 +645,12 @@ __global__ void __launch_bounds__(256) k_reduce_strided_lanes(const T* __restric
         const int64_t kn = o == nout - 1 ? p.tail_k : p.k;
         typename R::V acc = R::ident();
         int64_t kk = lane;
-        for (; kk + 3 * 32 < kn; kk += 4 * 32) {  // four loads in flight, used in k order
-            const T v0 = row[kk * p.sk], v1 = row[(kk + 32) * p.sk], v2 = row[(kk + 64) * p.sk],
-                    v3 = row[(kk + 96) * p.sk];
-            acc = R::comb(acc, R::lift(to_f(v0)));
-            acc = R::comb(acc, R::lift(to_f(v1)));
-            acc = R::comb(acc, R::lift(to_f(v2)));
-            acc = R::comb(acc, R::lift(to_f(v3)));
+        for (; kk + 7 * 32 < kn; kk += 8 * 32) {  // eight loads in flight, used in k order
+            T v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = row[(kk + u * 32) * p.sk];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc = R::comb(acc, R::lift(to_f(v[u])));
         }
         for (; kk < kn; kk += 32) acc = R::comb(acc, R::lift(to_f(row[kk * p.sk])));
         acc = warp_reduce<OP>(acc);
@@ -549,25 +658,69 @@ __global__ void __launch_bounds__(256) k_reduce_strided_lanes(const T* __restric
     }
 }
 
+// Column-block kernel: block (32, W); lane l owns output 32 g + l of the
+// plan's order, the W warps split the CTA's k range into contiguous chunks
+// (each ascending, eight loads in flight), combined in warp order.  With S > 1
+// the k range is also cut into S contiguous chunks over S CTAs (unit = (chunk,
+// group), groups fastest); each stores a binary32 partial per output and the
+// CTA taking the group's last ticket combines the S partials in chunk order.
+// W and S come from the shape alone.
 template <typename T, typename OT, int OP>
-__global__ void __launch_bounds__(256) k_reduce_strided_serial(const T* __restrict__ x, StridedPlan p, int64_t nout,
-                                                               OT* __restrict__ out, float scale) {
+__global__ void __launch_bounds__(512) k_reduce_strided_cols(const T* __restrict__ x, StridedPlan p, int64_t nout,
+                                                             int64_t S, OT* __restrict__ out, float scale,
+                                                             unsigned* __restrict__ counters,
+                                                             typename Red<OP>::V* __restrict__ partials) {
     using R = Red<OP>;
+    using V = typename R::V;
+    constexpr int U = 8;
+    __shared__ V red[16][32];
+    __shared__ bool s_last;
+    const int lane = threadIdx.x, w = threadIdx.y, W = blockDim.y;
+    const int64_t groups = (nout + 31) / 32;
+    const int64_t s = blockIdx.x / groups, g = blockIdx.x - s * groups;
+    const int64_t o = g * 32 + lane;
+    const int64_t kc = (p.k + S - 1) / S;
+    const int64_t ks = s * kc, ke = ks + kc < p.k ? ks + kc : p.k;
+    const int64_t kper = (kc + W - 1) / W;
+    const int64_t k0 = ks + w * kper, k1 = k0 + kper < ke ? k0 + kper : ke;
     pdl_begin();
-    const int64_t nt = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t o = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < nout; o += nt) {
+    V acc = R::ident();
+    if (o < nout) {
         const T* col = x + strided_base(p, o);
-        typename R::V acc = R::ident();
-        int64_t kk = 0;
-        for (; kk + 8 <= p.k; kk += 8) {
-            T v[8];
+        int64_t kk = k0;
+        for (; kk + U <= k1; kk += U) {
+            T v[U];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = col[(kk + u) * p.sk];
+            for (int u = 0; u < U; ++u) v[u] = col[(kk + u) * p.sk];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) acc = R::comb(acc, R::lift(to_f(v[u])));
+            for (int u = 0; u < U; ++u) acc = R::comb(acc, R::lift(to_f(v[u])));
         }
-        for (; kk < p.k; ++kk) acc = R::comb(acc, R::lift(to_f(col[kk * p.sk])));
-        from_f(R::fin(acc, scale), &out[o]);
+        for (; kk < k1; ++kk) acc = R::comb(acc, R::lift(to_f(col[kk * p.sk])));
+    }
+    red[w][lane] = acc;
+    __syncthreads();
+    if (w == 0) {
+        V a = red[0][lane];
+        for (int ww = 1; ww < W; ++ww) a = R::comb(a, red[ww][lane]);
+        if (S == 1) {
+            if (o < nout) from_f(R::fin(a, scale), &out[o]);
+        } else {
+            partials[(g * S + s) * 32 + lane] = a;
+        }
+    }
+    if (S == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (w == 0 && lane == 0) s_last = atomicAdd(&counters[g], 1u) == static_cast<unsigned>(S - 1);
+    __syncthreads();
+    if (!s_last) return;
+    // This CTA completed the group: combine its S partials in chunk order.
+    __threadfence();
+    if (w == 0) {
+        V a = __ldcg(&partials[g * S * 32 + lane]);
+        for (int64_t j = 1; j < S; ++j) a = R::comb(a, __ldcg(&partials[(g * S + j) * 32 + lane]));
+        if (o < nout) from_f(R::fin(a, scale), &out[o]);
+        if (lane == 0) counters[g] = 0;  // ready for the next launch on this stream
     }
 }
 
@@ -620,13 +773,34 @@ qsml_status_t launch_strided(Context* ctx, const T* x, const StridedPlan& p, int
         if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_strided_lanes");
         return after_launch(ctx, "k_reduce_strided_lanes");
     }
-    grid = (nout + 255) / 256;
-    const int64_t cap = static_cast<int64_t>(ctx->num_sms) * 8;
-    if (grid > cap) grid = cap;
-    e = launch_pdl(k_reduce_strided_serial<T, OT, OP>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, ctx->stream, x,
-                   p, nout, out, scale);
-    if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_strided_serial");
-    return after_launch(ctx, "k_reduce_strided_serial");
+    // Column blocks: up to 16 warps of at least 16 rows each per CTA, and k cut
+    // over more CTAs until about kStrTargetWarps warps read (eight loads in
+    // flight each), keeping at least 16 rows per warp.
+    using V = typename Red<OP>::V;
+    const int64_t groups = (nout + 31) / 32;
+    int64_t W = p.k / 16;
+    if (W > 16) W = 16;
+    if (W < 1) W = 1;
+    int64_t S = 1;
+    if (groups * W < kStrTargetWarps && groups <= kMaxSegments) {
+        S = (kStrTargetWarps + groups * W - 1) / (groups * W);
+        const int64_t cap = p.k / (W * 16);
+        if (S > cap) S = cap;
+        if (S < 1) S = 1;
+    }
+    if (groups * S > INT32_MAX) return set_error(ctx, QSML_E_UNSUPPORTED, "reduction too large");
+    unsigned* counters = nullptr;
+    V* partials = nullptr;
+    if (S > 1) {
+        void* scratch = nullptr;
+        QSML_TRY_STATUS(get_scratch(ctx, kCounterBytes + static_cast<size_t>(groups * S) * 32 * sizeof(V), &scratch));
+        counters = static_cast<unsigned*>(scratch);
+        partials = reinterpret_cast<V*>(static_cast<char*>(scratch) + kCounterBytes);
+    }
+    e = launch_pdl(k_reduce_strided_cols<T, OT, OP>, dim3(static_cast<unsigned>(groups * S)),
+                   dim3(32, static_cast<unsigned>(W)), 0, ctx->stream, x, p, nout, S, out, scale, counters, partials);
+    if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_strided_cols");
+    return after_launch(ctx, "k_reduce_strided_cols");
 }
 
 // One axis of a view.
@@ -758,7 +932,8 @@ extern "C" qsml_status_t qsml_reduce(qsml_ctx* handle, int32_t op, const qsml_td
                                                                                          __float2half_rn(v), nout);
         return after_launch(C_, "k_fill_value");
     }
-    if (!is_contiguous(a)) {
+    // a transposed or permuted contiguous block: the contiguous kernels
+    if (!is_contiguous(a) && !dense_view_plan(a, axis, &outer, &k, &inner)) {
         if (a->dtype == QSML_F32) return reduce_strided_op<float, float>(C_, op, a, axis, static_cast<float*>(out->data));
         if (out->dtype == QSML_F16)
             return reduce_strided_op<__half, __half>(C_, op, a, axis, static_cast<__half*>(out->data));

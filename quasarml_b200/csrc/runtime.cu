@@ -92,6 +92,51 @@ qsml_status_t plan_reduction(Context* ctx, const qsml_tdesc* a, int32_t axis, in
     return QSML_OK;
 }
 
+bool dense_view_plan(const qsml_tdesc* a, int32_t axis, int64_t* outer, int64_t* k, int64_t* inner) {
+    const int64_t n = numel(a);
+    if (n == 0) return false;
+    int ax = -1;
+    if (axis != QSML_AXIS_ALL) {
+        ax = axis < 0 ? axis + a->ndim : axis;
+        if (ax < 0 || ax >= a->ndim || a->shape[ax] == 1) return false;
+    }
+    // the non-unit dims, by stride ascending, must tile one block exactly
+    int dims[kMaxDims];
+    int nd = 0;
+    for (int i = 0; i < a->ndim; ++i) {
+        if (a->shape[i] == 1) continue;
+        if (a->stride[i] <= 0) return false;
+        int j = nd++;
+        while (j > 0 && a->stride[dims[j - 1]] > a->stride[i]) {
+            dims[j] = dims[j - 1];
+            --j;
+        }
+        dims[j] = i;
+    }
+    int64_t expect = 1;
+    for (int j = 0; j < nd; ++j) {
+        if (a->stride[dims[j]] != expect) return false;
+        expect *= a->shape[dims[j]];
+    }
+    if (ax < 0) {
+        *outer = 1;
+        *k = n;
+        *inner = 1;
+        return true;
+    }
+    // kept dims in memory order along the view
+    int64_t prev = INT64_MAX;
+    for (int i = 0; i < a->ndim; ++i) {
+        if (i == ax || a->shape[i] == 1) continue;
+        if (a->stride[i] >= prev) return false;
+        prev = a->stride[i];
+    }
+    *k = a->shape[ax];
+    *inner = a->stride[ax];
+    *outer = n / (*k * *inner);
+    return true;
+}
+
 // ---------------------------------------------------------------------------
 // Caching allocator
 // ---------------------------------------------------------------------------

@@ -186,6 +186,16 @@ static void test_views_and_gathers() {
     check("sum over a transposed view", st0.size() == 6 && st0[0] == 0 + 6 + 12 + 18 + 24 + 30 + 36 + 42);
     check("max of a sliced view", get(qsml::max(s))[0] == 47 && get(qsml::min(s))[0] == 7);
     check("mean of a transposed view", near(get(qsml::mean(T))[0], 23.5f, 1e-5f));
+    // argmax over an axis of a transpose reads it in place; of a slice, a copy
+    auto idx = [](const qsml::TensorPtr& t) {
+        vector<int32_t> v(t->numel());
+        t->download(v.data(), v.size() * sizeof(int32_t));
+        return v;
+    };
+    auto amv = idx(qsml::argmax(T, 1));  // X.T [6, 8]: each row's largest is X's last row
+    check("argmax over a transposed view", amv.size() == 6 && amv[0] == 7 && amv[5] == 7);
+    auto as = idx(qsml::argmin(s, 0));  // X[1::3, 1::2] [3, 3]: the first row is smallest
+    check("argmin over a sliced view", as.size() == 3 && as[0] == 0 && as[2] == 0);
     auto cat = qsml::concat({X, X}, 1);
     auto cv = get(cat);
     check("concat axis 1", cat->dim(1) == 12 && cv[6] == 0 && cv[13] == 7);

@@ -172,3 +172,28 @@ def test_errors(ctx):
     # empty outer: nothing to do
     z = dev(np.ones((0, 5), np.float32))
     ctx.arg_reduce(abi.ARG_MAX, d(z), 1, False, d(empty((0,), np.int32)))
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float16, np.int32])
+@pytest.mark.parametrize("op", [abi.ARG_MAX, abi.ARG_MIN])
+def test_transposed_views(ctx, orc, dtype, op):
+    """A transpose is arg-reduced over an axis in place (the contiguous
+    kernels on the underlying block); a full arg-reduction of it, or any other
+    strided view, needs a contiguous input (QSML_E_UNSUPPORTED)."""
+    x = make((300, 500), dtype, seed=31)
+    t = dev(x)
+    code = {np.dtype(np.float32): abi.F32, np.dtype(np.float16): abi.F16, np.dtype(np.int32): abi.I32}[np.dtype(dtype)]
+    view = abi.make_desc(t.data_ptr(), code, (500, 300), (1, 500))
+    xt = np.ascontiguousarray(x.T)
+    oracle_op = orc.ARGMAX if op == abi.ARG_MAX else orc.ARGMIN
+    for axis in (0, 1):
+        out = empty(abi.reduced_shape((500, 300), axis, False), np.int32)
+        ctx.arg_reduce(op, view, axis, False, d(out))
+        np.testing.assert_array_equal(host(out).astype(np.int64), orc.argreduce(oracle_op, xt, axis))
+    with pytest.raises(abi.QsmlError) as e:
+        ctx.arg_reduce(op, view, abi.AXIS_ALL, False, d(empty((1,), np.int32)))
+    assert e.value.status == abi.E_UNSUPPORTED
+    sliced = abi.make_desc(t.data_ptr(), code, (150, 500), (1000, 1))  # X[::2]
+    with pytest.raises(abi.QsmlError) as e:
+        ctx.arg_reduce(op, sliced, 1, False, d(empty((150,), np.int32)))
+    assert e.value.status == abi.E_UNSUPPORTED

@@ -202,7 +202,8 @@ VIEWS = [("X[5::3, 1::2]", (64, 300), 5 * 300 + 1, (20, 150), (900, 2)),
          ("X[::-1, :]", (30, 40), 29 * 40, (30, 40), (-40, 1)),
          ("broadcast [1,500] -> [7,500]", (1, 500), 0, (7, 500), (0, 1)),
          ("X[::3] of 300000", (300000,), 0, (100000,), (3,)),
-         ("X[::2, ::-1] of [4, 70000]", (4, 70000), 69999, (2, 70000), (140000, -1))]
+         ("X[::2, ::-1] of [4, 70000]", (4, 70000), 69999, (2, 70000), (140000, -1)),
+         ("X[1::2, ::3] of [4000, 300]", (4000, 300), 300, (2000, 100), (600, 3))]
 
 
 @pytest.mark.parametrize("view", VIEWS, ids=[v[0] for v in VIEWS])
@@ -226,8 +227,9 @@ def test_strided_views(ctx, orc, view, dtype):
 
 
 def test_strided_view_kernels(ctx):
-    """Rows of a sliced matrix are read along k (a warp per output); columns
-    and transposes a thread per output, k ascending."""
+    """Rows of a sliced matrix are read along k (a warp per output); its
+    columns a lane per output, k split over warps (and, for few outputs over a
+    long k, CTAs with partials combined in order)."""
     base = np.ones((64, 300), np.float32)
     t = dev(base)
     desc, _ = _view(base, t, 5 * 300 + 1, (20, 150), (900, 2))
@@ -237,8 +239,35 @@ def test_strided_view_kernels(ctx):
     assert np.all(host(out) == 150.0)
     out = empty((150,), np.float32)
     ctx.reduce(abi.RED_SUM, desc, 0, False, d(out))
-    assert ctx.last_kernel() == "k_reduce_strided_serial"
+    assert ctx.last_kernel() == "k_reduce_strided_cols"
     assert np.all(host(out) == 20.0)
+    # 2000 rows of 100 columns: k cut over CTAs (7 chunks)
+    base = np.ones((4000, 300), np.float32)
+    t = dev(base)
+    desc, _ = _view(base, t, 300, (2000, 100), (600, 3))
+    out = empty((100,), np.float32)
+    for _ in range(3):  # ticket counters are reset for the next launch
+        ctx.reduce(abi.RED_SUM, desc, 0, False, d(out))
+        assert ctx.last_kernel() == "k_reduce_strided_cols"
+        assert np.all(host(out) == 2000.0)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.float16])
+def test_transposed_views_use_contiguous_kernels(ctx, orc, dtype):
+    """A transpose (a permuted contiguous block) is reduced by the contiguous
+    kernels: X.T over its axis 0 is X's rows, over its axis 1 X's columns (few
+    column tiles over a long k: k also split over CTAs)."""
+    import torch
+    base = datagen.normal(24, (4096, 2048), 0.3, 1.5).astype(dtype)
+    t = dev(base)
+    desc, x = _view(base, t, 0, (2048, 4096), (1, 2048))
+    tdt = torch.float32 if dtype == np.float32 else torch.float16
+    for axis, kernel in ((0, "k_reduce_rows"), (1, "k_reduce_cols_split"), (None, "k_reduce_seg")):
+        for oname, op in OPS.items():
+            out = torch.empty(abi.reduced_shape((2048, 4096), axis, False), dtype=tdt, device="cuda")
+            ctx.reduce(op, desc, abi.AXIS_ALL if axis is None else axis, False, abi.desc_of(out))
+            assert ctx.last_kernel() == kernel, (axis, ctx.last_kernel())
+            check(orc, oname, x, axis, host(out), dtype == np.float16)
 
 
 def test_view_beyond_four_output_dims_is_unsupported(ctx):
@@ -276,7 +305,8 @@ def test_long_column_reduction(ctx, orc):
                                                ((64, 512, 1024), 1, "k_reduce_cols"),
                                                ((64, 512, 1024), 2, "k_reduce_rows"),
                                                ((64, 512, 1024), None, "k_reduce_seg"),
-                                               ((37, 310000), 0, "k_reduce_cols_wide")])
+                                               ((37, 310000), 0, "k_reduce_cols_wide"),
+                                               ((4096, 2048), 0, "k_reduce_cols_split")])
 def test_kernel_choice(ctx, shape, axis, kernel):
     """The workload shapes reach the kernel each was tuned for (fp32)."""
     t = dev(np.zeros(shape, np.float32))
