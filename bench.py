@@ -1102,6 +1102,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="reduce",
                     choices=["reduce", "chain", "gather", "layernorm", "matmul_f16", "matmul_f32"])
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="reductions wait for the previous kernel at their start (qsml_set_overlap off)")
     ap.add_argument("--single", default=None,
                     choices=["reduce_all", "reduce_axis0", "reduce_axis1", "reduce_axis2", "reduce_all_f16",
                              "reduce_axis0_f16", "reduce_axis1_f16", "reduce_axis2_f16", "chain_pow", "chain_relu",
@@ -1136,6 +1138,9 @@ def main():
     stream = torch.cuda.Stream()
     ctx = abi.Context(dist.local, use_torch_stream=False)
     ctx.set_stream(stream.cuda_stream)
+    # independent reductions on the stream overlap (only library kernels and
+    # copies run on it)
+    ctx.set_overlap(not args.no_overlap)
     hbm, tf_burst, tf_sus, peak_kind = peaks()
 
     wl = {"reduce": lambda: ReduceWorkload(ctx, dist), "chain": lambda: ChainWorkload(ctx, dist),
@@ -1167,6 +1172,9 @@ def main():
                        "second context's stream (NCCL over NVLink) while graph 2 = the axis-1/2 reductions runs, "
                        "then qsml_finish_partial of the outputs"},
             "gpu_launches": launches, "clocks": sampler.summary()}
+    line["config"]["overlap"] = ("off" if args.no_overlap else
+                                 "qsml_set_overlap(ctx, 1): a reduction sharing no buffer with the library kernels "
+                                 "still running on the stream starts at once and waits for them at its end")
     if args.workload == "reduce":
         line["roofline"] = roofline_from_families(family_times(wl, stream), hbm, peak_kind)
         if sharded:

@@ -109,6 +109,8 @@ _SIGS = {
     "qsml_get_stream": (_c.c_int32, [_c.c_void_p, _P(_c.c_void_p)]),
     "qsml_synchronize": (_c.c_int32, [_c.c_void_p]),
     "qsml_set_wait_limit": (_c.c_int32, [_c.c_void_p, _c.c_int64]),
+    "qsml_set_overlap": (_c.c_int32, [_c.c_void_p, _c.c_int32]),
+    "qsml_overlap_stats": (_c.c_int32, [_c.c_void_p, _c.POINTER(_c.c_uint64), _c.POINTER(_c.c_uint64)]),
     "qsml_last_error": (_c.c_char_p, [_c.c_void_p]),
     "qsml_alloc": (_c.c_int32, [_c.c_void_p, _c.c_size_t, _P(_c.c_void_p)]),
     "qsml_free": (_c.c_int32, [_c.c_void_p, _c.c_void_p]),
@@ -347,6 +349,19 @@ class Context:
         """SM cycles after which a kernel waiting for data gives up with
         QSML_E_TIMEOUT (0 = the default, about 1 s)."""
         self.check(self.lib.qsml_set_wait_limit(self.h, cycles))
+
+    def set_overlap(self, enable: bool) -> None:
+        """Let independent reductions on this context's stream overlap (each
+        starts reading while the library kernels before it that share no
+        buffer with it still run).  Only for streams on which nothing else
+        launches kernels that trigger programmatic dependent launch early."""
+        self.check(self.lib.qsml_set_overlap(self.h, 1 if enable else 0))
+
+    def overlap_stats(self) -> tuple:
+        """(reduction launches planned, of which overlapped the kernels before them)."""
+        p, d = ctypes.c_uint64(), ctypes.c_uint64()
+        self.check(self.lib.qsml_overlap_stats(self.h, ctypes.byref(p), ctypes.byref(d)))
+        return p.value, d.value
 
     def finish_partial(self, op: int, partial: TDesc, n: int, out: TDesc) -> None:
         """out from combined binary32 partials (a mean divides by n)."""

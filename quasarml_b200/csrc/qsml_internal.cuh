@@ -61,6 +61,14 @@ struct Context {
     // int at [0] the status code; int64 at byte 8 the wait limit in SM
     // cycles (0 = kDefaultWaitCycles), set with qsml_set_wait_limit.
     int* status = nullptr;
+    // Overlap of independent reductions on the stream (qsml_set_overlap) and
+    // the launch count the last plan_launch was made for.
+    bool overlap = false;
+    uint64_t planned_for = 0;
+    uint64_t planned = 0, deferred = 0;  // plan_launch calls, and those that deferred
+    // Scratch is handed out in kScratchSlots slots in turn, so that kernels
+    // in flight together do not share ticket counters or partials.
+    int scratch_slot = 0;
     uint64_t launches = 0;
     const char* last_kernel = "";  // a string literal of the launch site
     // Fused elementwise expressions: QSML_FUSE_MODE_* and which kernel ran.
@@ -89,6 +97,67 @@ qsml_status_t set_error(Context* ctx, qsml_status_t st, const std::string& msg);
 qsml_status_t check_cuda(Context* ctx, cudaError_t e, const char* what);
 // Checks the launch that was just enqueued and counts it.
 qsml_status_t after_launch(Context* ctx, const char* kernel);
+
+// Overlap of independent kernels on one stream --------------------------------
+// A kernel launched with programmatic dependent launch normally starts with
+// pdl_begin(): it waits for the previous kernel on the stream to finish before
+// touching memory.  Between reductions that share no buffer that wait only
+// costs time: each short launch then pays its predecessor's drain and its own
+// ramp.  plan_launch() therefore tracks, per stream, the library kernels that
+// may still be running (the window: every kernel since the last one that
+// waited at its start), each with the address ranges it reads and writes.  A
+// kernel whose writes overlap nothing the window reads or writes, and whose
+// reads overlap nothing the window writes, may "defer": it triggers its own
+// dependents and reads at once (pdl_start(1)), and waits for its predecessor
+// only at its end (pdl_end(1)), so kernels still complete in stream order and
+// a later kernel that waits at its start still sees every write before it.
+// Any other library launch on the stream closes the window (after_launch),
+// and a context defers only after qsml_set_overlap(ctx, 1): the window knows
+// the library's kernels only, not a foreign kernel that triggers early.
+struct Span {
+    uintptr_t lo = 0, hi = 0;  // [lo, hi)
+};
+inline Span span_of(const void* p, size_t bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    return Span{a, a + bytes};
+}
+// The bytes a strided view touches (its lowest to its highest element).
+Span view_span(const qsml_tdesc* d);
+struct Footprint {
+    static constexpr int kMax = 3;
+    Span reads[kMax], writes[kMax];
+    int nr = 0, nw = 0;
+    Footprint& read(Span s) { return add(reads, nr, s); }
+    Footprint& write(Span s) { return add(writes, nw, s); }
+
+private:
+    // a fourth range widens the third (a larger footprint is only more
+    // conservative)
+    Footprint& add(Span* v, int& n, Span s) {
+        if (s.hi <= s.lo) return *this;
+        if (n < kMax) {
+            v[n++] = s;
+        } else {
+            v[kMax - 1].lo = s.lo < v[kMax - 1].lo ? s.lo : v[kMax - 1].lo;
+            v[kMax - 1].hi = s.hi > v[kMax - 1].hi ? s.hi : v[kMax - 1].hi;
+        }
+        return *this;
+    }
+};
+// The defer flag (0 or 1) for the kernel about to be launched on ctx->stream
+// with footprint f; records f in the stream's window.  The launch must follow
+// at once and be checked with after_launch.
+int plan_launch(Context* ctx, const Footprint& f);
+// Forgets the stream's window (the next kernel waits at its start).
+void end_window(cudaStream_t stream);
+
+__device__ __forceinline__ void pdl_start(int defer) {
+    if (!defer) asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_end(int defer) {
+    if (defer) asm volatile("griddepcontrol.wait;" ::: "memory");
+}
 
 // Programmatic dependent launch for short memory-bound kernels that run back
 // to back: the kernel is launched with programmatic stream serialization, so
@@ -129,6 +198,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+constexpr int kScratchSlots = 4;
 // Scratch of at least `bytes`.  Its first kScratchCounterBytes hold the
 // reductions' ticket counters, which every kernel that uses them leaves at
 // zero; other users place their data after that region.

@@ -130,6 +130,25 @@ template <> struct Red<QSML_RED_PROD> {
     static __device__ __forceinline__ V shfl(V v, int m) { return __shfl_xor_sync(0xffffffffu, v, m); }
 };
 
+// One element into a column accumulator.  A binary16 sum uses the sm_100
+// mixed-precision add (add.rn.f32.f16: the half widens exactly, one rounding),
+// the same bits as widening first and adding in binary32, in one instruction
+// (measured on B200: binary16 column launches 3-5 % shorter; the segment
+// kernel's single accumulator chain measured slower with it, so it widens).
+template <int OP>
+__device__ __forceinline__ float accum(float acc, float v) {
+    return Red<OP>::comb(acc, Red<OP>::lift(v));
+}
+template <int OP>
+__device__ __forceinline__ float accum(float acc, __half v) {
+    if constexpr (OP == QSML_RED_SUM || OP == QSML_RED_MEAN) {
+        asm("add.rn.f32.f16 %0, %1, %0;" : "+f"(acc) : "h"(__half_as_ushort(v)));
+        return acc;
+    } else {
+        return Red<OP>::comb(acc, Red<OP>::lift(__half2float(v)));
+    }
+}
+
 // Butterfly: every lane ends with the same bits (each step combines the same
 // two operands on both partner lanes, and the ops are commutative).
 template <int OP>
@@ -165,7 +184,7 @@ template <typename T, typename OT, int OP, bool VEC>
 __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int64_t nseg, int64_t len,
                                                     int64_t P, OT* __restrict__ out, float scale,
                                                     unsigned* __restrict__ counters,
-                                                    typename Red<OP>::V* __restrict__ partials) {
+                                                    typename Red<OP>::V* __restrict__ partials, int defer) {
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
@@ -182,7 +201,7 @@ __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int
             prefetch_l2(reinterpret_cast<const Pack<T>*>(x + s * len) + q, static_cast<uint32_t>(n * 16));
         }
     }
-    pdl_begin();
+    pdl_start(defer);
     for (int64_t w = blockIdx.x; w < units; w += gridDim.x) {
         const int64_t s = w / P, j = w - s * P;
         const T* row = x + s * len;
@@ -236,6 +255,7 @@ __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int
         }
         __syncthreads();
     }
+    pdl_end(defer);
 }
 
 // ---------------------------------------------------------------------------
@@ -243,7 +263,7 @@ __global__ void __launch_bounds__(kRT) k_reduce_seg(const T* __restrict__ x, int
 // ---------------------------------------------------------------------------
 template <typename T, typename OT, int OP, bool VEC>
 __global__ void __launch_bounds__(256) k_reduce_rows(const T* __restrict__ x, int64_t rows, int64_t len,
-                                                     OT* __restrict__ out, float scale) {
+                                                     OT* __restrict__ out, float scale, int defer) {
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
@@ -255,7 +275,7 @@ __global__ void __launch_bounds__(256) k_reduce_rows(const T* __restrict__ x, in
         const int64_t bytes = (len / PV) * 16;
         if (r < rows && bytes > 0) prefetch_l2(x + r * len, static_cast<uint32_t>(bytes < 16384 ? bytes : 16384));
     }
-    pdl_begin();
+    pdl_start(defer);
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
         const T* row = x + r * len;
@@ -284,6 +304,7 @@ __global__ void __launch_bounds__(256) k_reduce_rows(const T* __restrict__ x, in
         acc = warp_reduce<OP>(acc);
         if (lane == 0) from_f(R::fin(acc, scale), &out[r]);
     }
+    pdl_end(defer);
 }
 
 // ---------------------------------------------------------------------------
@@ -291,7 +312,7 @@ __global__ void __launch_bounds__(256) k_reduce_rows(const T* __restrict__ x, in
 // ---------------------------------------------------------------------------
 template <typename T, typename OT, int OP, bool VEC>
 __global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k, int64_t inner,
-                              int64_t tiles_per_o, OT* __restrict__ out, float scale) {
+                              int64_t tiles_per_o, OT* __restrict__ out, float scale, int defer) {
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = VEC ? Pack<T>::N : 1;
@@ -311,7 +332,7 @@ __global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k,
         const int64_t span = inner - tc0 < 32 * PV ? inner - tc0 : 32 * PV;
         prefetch_l2(x + (o * k + k0 + lane) * inner + tc0, static_cast<uint32_t>(span * sizeof(T)));
     }
-    pdl_begin();
+    pdl_start(defer);
     V acc[PV];
 #pragma unroll
     for (int e = 0; e < PV; ++e) acc[e] = R::ident();
@@ -326,12 +347,12 @@ __global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k,
 #pragma unroll
                 for (int u = 0; u < U; ++u)
 #pragma unroll
-                    for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v[u].v[e])));
+                    for (int e = 0; e < PV; ++e) acc[e] = accum<OP>(acc[e], v[u].v[e]);
             }
             for (; kk < k1; ++kk) {
                 Pack<T> v = *reinterpret_cast<const Pack<T>*>(base + kk * inner);
 #pragma unroll
-                for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v.v[e])));
+                for (int e = 0; e < PV; ++e) acc[e] = accum<OP>(acc[e], v.v[e]);
             }
         } else {
             for (; kk + U <= k1; kk += U) {
@@ -355,6 +376,7 @@ __global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k,
         const int64_t ci = (tile - o * tiles_per_o) * (32 * PV) + col;
         if (o < outer && ci < inner) from_f(R::fin(a, scale), &out[o * inner + ci]);
     }
+    pdl_end(defer);
 }
 
 // ---------------------------------------------------------------------------
@@ -370,7 +392,8 @@ __global__ void k_reduce_cols(const T* __restrict__ x, int64_t outer, int64_t k,
 template <typename T, typename OT, int OP>
 __global__ void k_reduce_cols_split(const T* __restrict__ x, int64_t outer, int64_t k, int64_t inner,
                                     int64_t tiles_per_o, int64_t S, OT* __restrict__ out, float scale,
-                                    unsigned* __restrict__ counters, typename Red<OP>::V* __restrict__ partials) {
+                                    unsigned* __restrict__ counters, typename Red<OP>::V* __restrict__ partials,
+                                    int defer) {
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
@@ -391,7 +414,7 @@ __global__ void k_reduce_cols_split(const T* __restrict__ x, int64_t outer, int6
     const int64_t kper = (kc + W - 1) / W;
     const int64_t k0 = ks + w * kper;
     const int64_t k1 = k0 + kper < ke ? k0 + kper : ke;
-    pdl_begin();
+    pdl_start(defer);
     V acc[PV];
 #pragma unroll
     for (int e = 0; e < PV; ++e) acc[e] = R::ident();
@@ -405,12 +428,12 @@ __global__ void k_reduce_cols_split(const T* __restrict__ x, int64_t outer, int6
 #pragma unroll
             for (int u = 0; u < U; ++u)
 #pragma unroll
-                for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v[u].v[e])));
+                for (int e = 0; e < PV; ++e) acc[e] = accum<OP>(acc[e], v[u].v[e]);
         }
         for (; kk < k1; ++kk) {
             Pack<T> v = *reinterpret_cast<const Pack<T>*>(base + kk * inner);
 #pragma unroll
-            for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v.v[e])));
+            for (int e = 0; e < PV; ++e) acc[e] = accum<OP>(acc[e], v.v[e]);
         }
     }
 #pragma unroll
@@ -426,16 +449,18 @@ __global__ void k_reduce_cols_split(const T* __restrict__ x, int64_t outer, int6
     __syncthreads();
     if (tid == 0) s_last = atomicAdd(&counters[tile], 1u) == static_cast<unsigned>(S - 1);
     __syncthreads();
-    if (!s_last) return;
-    // This CTA completed the tile: combine its S partials in chunk order.
-    __threadfence();
-    for (int col = tid; col < NC; col += 32 * W) {
-        V a = __ldcg(&partials[tile * S * NC + col]);
-        for (int64_t j = 1; j < S; ++j) a = R::comb(a, __ldcg(&partials[(tile * S + j) * NC + col]));
-        const int64_t ci = tc0 + col;
-        if (ci < inner) from_f(R::fin(a, scale), &out[o * inner + ci]);
+    if (s_last) {
+        // This CTA completed the tile: combine its S partials in chunk order.
+        __threadfence();
+        for (int col = tid; col < NC; col += 32 * W) {
+            V a = __ldcg(&partials[tile * S * NC + col]);
+            for (int64_t j = 1; j < S; ++j) a = R::comb(a, __ldcg(&partials[(tile * S + j) * NC + col]));
+            const int64_t ci = tc0 + col;
+            if (ci < inner) from_f(R::fin(a, scale), &out[o * inner + ci]);
+        }
+        if (tid == 0) counters[tile] = 0;  // ready for the next launch on this stream
     }
-    if (tid == 0) counters[tile] = 0;  // ready for the next launch on this stream
+    pdl_end(defer);
 }
 
 // ---------------------------------------------------------------------------
@@ -448,7 +473,7 @@ __global__ void k_reduce_cols_split(const T* __restrict__ x, int64_t outer, int6
 template <typename T, typename OT, int OP>
 __global__ void __launch_bounds__(256) k_reduce_cols_wide(const T* __restrict__ x, int64_t outer, int64_t k,
                                                           int64_t inner, int64_t tiles_per_o, int64_t groups_per_o,
-                                                          OT* __restrict__ out, float scale) {
+                                                          OT* __restrict__ out, float scale, int defer) {
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int PV = Pack<T>::N;
@@ -464,8 +489,11 @@ __global__ void __launch_bounds__(256) k_reduce_cols_wide(const T* __restrict__ 
         const int64_t n = inner - span * NCOL < NCOL ? inner - span * NCOL : NCOL;
         prefetch_l2(x + (o * k + lane) * inner + span * NCOL, static_cast<uint32_t>(n * sizeof(T)));
     }
-    pdl_begin();
-    if (span >= tiles_per_o || c0 >= inner) return;
+    pdl_start(defer);
+    if (span >= tiles_per_o || c0 >= inner) {
+        pdl_end(defer);
+        return;
+    }
     V acc[PV];
 #pragma unroll
     for (int e = 0; e < PV; ++e) acc[e] = R::ident();
@@ -478,16 +506,17 @@ __global__ void __launch_bounds__(256) k_reduce_cols_wide(const T* __restrict__ 
 #pragma unroll
         for (int u = 0; u < U; ++u)
 #pragma unroll
-            for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v[u].v[e])));
+            for (int e = 0; e < PV; ++e) acc[e] = accum<OP>(acc[e], v[u].v[e]);
     }
     for (; kk < k; ++kk) {
         Pack<T> v = *reinterpret_cast<const Pack<T>*>(base + kk * inner);
 #pragma unroll
-        for (int e = 0; e < PV; ++e) acc[e] = R::comb(acc[e], R::lift(to_f(v.v[e])));
+        for (int e = 0; e < PV; ++e) acc[e] = accum<OP>(acc[e], v.v[e]);
     }
 #pragma unroll
     for (int e = 0; e < PV; ++e)
         if (c0 + e < inner) from_f(R::fin(acc[e], scale), &out[o * inner + c0 + e]);
+    pdl_end(defer);
 }
 
 // ---------------------------------------------------------------------------
@@ -502,6 +531,10 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
     constexpr int PV = Pack<T>::N;
     const float scale = scale_override > 0.0f ? scale_override : 1.0f / static_cast<float>(k);
     const bool x_al = aligned16(x);
+    // what the launch reads and writes, for overlap with the kernels before it
+    Footprint fp;
+    fp.read(span_of(x, static_cast<size_t>(outer * k * inner) * sizeof(T)))
+        .write(span_of(out, static_cast<size_t>(outer * inner) * sizeof(OT)));
     if (inner == 1 && (outer == 1 || (outer < 592 && k >= 8192))) {
         // Segment kernel.
         if (outer > kMaxSegments) return set_error(ctx, QSML_E_UNSUPPORTED, "too many segments");
@@ -515,11 +548,12 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
         unsigned* counters = static_cast<unsigned*>(scratch);
         V* partials = reinterpret_cast<V*>(static_cast<char*>(scratch) + kCounterBytes);
         const int64_t grid = units;  // one slice per CTA
+        const int defer = plan_launch(ctx, fp.write(span_of(scratch, kCounterBytes + units * sizeof(V))));
         const cudaError_t e =
             vec ? launch_pdl(k_reduce_seg<T, OT, OP, true>, dim3(static_cast<unsigned>(grid)), dim3(kRT), 0,
-                             ctx->stream, x, outer, k, P, out, scale, counters, partials)
+                             ctx->stream, x, outer, k, P, out, scale, counters, partials, defer)
                 : launch_pdl(k_reduce_seg<T, OT, OP, false>, dim3(static_cast<unsigned>(grid)), dim3(kRT), 0,
-                             ctx->stream, x, outer, k, P, out, scale, counters, partials);
+                             ctx->stream, x, outer, k, P, out, scale, counters, partials, defer);
         if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_seg");
         return after_launch(ctx, "k_reduce_seg");
     }
@@ -528,11 +562,12 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
         int64_t grid = (outer + 7) / 8;  // 8 warps per CTA
         int64_t cap = static_cast<int64_t>(ctx->num_sms) * 32;
         if (grid > cap) grid = cap;
+        const int defer = plan_launch(ctx, fp);
         const cudaError_t e =
             vec ? launch_pdl(k_reduce_rows<T, OT, OP, true>, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
-                             ctx->stream, x, outer, k, out, scale)
+                             ctx->stream, x, outer, k, out, scale, defer)
                 : launch_pdl(k_reduce_rows<T, OT, OP, false>, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
-                             ctx->stream, x, outer, k, out, scale);
+                             ctx->stream, x, outer, k, out, scale, defer);
         if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_rows");
         return after_launch(ctx, "k_reduce_rows");
     }
@@ -543,9 +578,10 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
         const int64_t groups_per_o = (tiles_per_o + 7) / 8;
         const int64_t groups = groups_per_o * outer;
         if (groups >= 2 * static_cast<int64_t>(ctx->num_sms) && groups <= INT32_MAX) {
+            const int defer = plan_launch(ctx, fp);
             const cudaError_t e = launch_pdl(k_reduce_cols_wide<T, OT, OP>, dim3(static_cast<unsigned>(groups)),
                                              dim3(32, 8), 0, ctx->stream, x, outer, k, inner, tiles_per_o,
-                                             groups_per_o, out, scale);
+                                             groups_per_o, out, scale, defer);
             if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_cols_wide");
             return after_launch(ctx, "k_reduce_cols_wide");
         }
@@ -566,10 +602,12 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
                                         &scratch));
             unsigned* counters = static_cast<unsigned*>(scratch);
             V* partials = reinterpret_cast<V*>(static_cast<char*>(scratch) + kCounterBytes);
+            const int defer = plan_launch(
+                ctx, fp.write(span_of(scratch, kCounterBytes + static_cast<size_t>(tiles * S) * 32 * PV * sizeof(V))));
             const cudaError_t e =
                 launch_pdl(k_reduce_cols_split<T, OT, OP>, dim3(static_cast<unsigned>(tiles * S)),
                            dim3(32, static_cast<unsigned>(W)), static_cast<size_t>(W) * 32 * PV * sizeof(V),
-                           ctx->stream, x, outer, k, inner, tiles_per_o, S, out, scale, counters, partials);
+                           ctx->stream, x, outer, k, inner, tiles_per_o, S, out, scale, counters, partials, defer);
             if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_cols_split");
             return after_launch(ctx, "k_reduce_cols_split");
         }
@@ -583,11 +621,12 @@ qsml_status_t run_reduce(Context* ctx, const T* x, int64_t outer, int64_t k, int
     dim3 block(32, static_cast<unsigned>(W));
     size_t smem = static_cast<size_t>(W) * 32 * pv * sizeof(V);
     if (tiles > INT32_MAX) return set_error(ctx, QSML_E_UNSUPPORTED, "reduction too large");
+    const int defer = plan_launch(ctx, fp);
     const cudaError_t e =
         vec ? launch_pdl(k_reduce_cols<T, OT, OP, true>, dim3(static_cast<unsigned>(tiles)), block, smem, ctx->stream,
-                         x, outer, k, inner, tiles_per_o, out, scale)
+                         x, outer, k, inner, tiles_per_o, out, scale, defer)
             : launch_pdl(k_reduce_cols<T, OT, OP, false>, dim3(static_cast<unsigned>(tiles)), block, smem,
-                         ctx->stream, x, outer, k, inner, tiles_per_o, out, scale);
+                         ctx->stream, x, outer, k, inner, tiles_per_o, out, scale, defer);
     if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_cols");
     return after_launch(ctx, "k_reduce_cols");
 }
@@ -635,9 +674,9 @@ __device__ __forceinline__ int64_t strided_base(const StridedPlan& p, int64_t o)
 
 template <typename T, typename OT, int OP>
 __global__ void __launch_bounds__(256) k_reduce_strided_lanes(const T* __restrict__ x, StridedPlan p, int64_t nout,
-                                                              OT* __restrict__ out, float scale) {
+                                                              OT* __restrict__ out, float scale, int defer) {
     using R = Red<OP>;
-    pdl_begin();
+    pdl_start(defer);
     const int lane = threadIdx.x & 31;
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t o = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); o < nout; o += nw) {
@@ -656,6 +695,7 @@ __global__ void __launch_bounds__(256) k_reduce_strided_lanes(const T* __restric
         acc = warp_reduce<OP>(acc);
         if (lane == 0) from_f(R::fin(acc, scale), &out[o]);
     }
+    pdl_end(defer);
 }
 
 // Column-block kernel: block (32, W); lane l owns output 32 g + l of the
@@ -669,7 +709,7 @@ template <typename T, typename OT, int OP>
 __global__ void __launch_bounds__(512) k_reduce_strided_cols(const T* __restrict__ x, StridedPlan p, int64_t nout,
                                                              int64_t S, OT* __restrict__ out, float scale,
                                                              unsigned* __restrict__ counters,
-                                                             typename Red<OP>::V* __restrict__ partials) {
+                                                             typename Red<OP>::V* __restrict__ partials, int defer) {
     using R = Red<OP>;
     using V = typename R::V;
     constexpr int U = 8;
@@ -683,7 +723,7 @@ __global__ void __launch_bounds__(512) k_reduce_strided_cols(const T* __restrict
     const int64_t ks = s * kc, ke = ks + kc < p.k ? ks + kc : p.k;
     const int64_t kper = (kc + W - 1) / W;
     const int64_t k0 = ks + w * kper, k1 = k0 + kper < ke ? k0 + kper : ke;
-    pdl_begin();
+    pdl_start(defer);
     V acc = R::ident();
     if (o < nout) {
         const T* col = x + strided_base(p, o);
@@ -693,9 +733,9 @@ __global__ void __launch_bounds__(512) k_reduce_strided_cols(const T* __restrict
 #pragma unroll
             for (int u = 0; u < U; ++u) v[u] = col[(kk + u) * p.sk];
 #pragma unroll
-            for (int u = 0; u < U; ++u) acc = R::comb(acc, R::lift(to_f(v[u])));
+            for (int u = 0; u < U; ++u) acc = accum<OP>(acc, v[u]);
         }
-        for (; kk < k1; ++kk) acc = R::comb(acc, R::lift(to_f(col[kk * p.sk])));
+        for (; kk < k1; ++kk) acc = accum<OP>(acc, col[kk * p.sk]);
     }
     red[w][lane] = acc;
     __syncthreads();
@@ -708,20 +748,21 @@ __global__ void __launch_bounds__(512) k_reduce_strided_cols(const T* __restrict
             partials[(g * S + s) * 32 + lane] = a;
         }
     }
-    if (S == 1) return;
-    __threadfence();
-    __syncthreads();
-    if (w == 0 && lane == 0) s_last = atomicAdd(&counters[g], 1u) == static_cast<unsigned>(S - 1);
-    __syncthreads();
-    if (!s_last) return;
-    // This CTA completed the group: combine its S partials in chunk order.
-    __threadfence();
-    if (w == 0) {
-        V a = __ldcg(&partials[g * S * 32 + lane]);
-        for (int64_t j = 1; j < S; ++j) a = R::comb(a, __ldcg(&partials[(g * S + j) * 32 + lane]));
-        if (o < nout) from_f(R::fin(a, scale), &out[o]);
-        if (lane == 0) counters[g] = 0;  // ready for the next launch on this stream
+    if (S > 1) {
+        __threadfence();
+        __syncthreads();
+        if (w == 0 && lane == 0) s_last = atomicAdd(&counters[g], 1u) == static_cast<unsigned>(S - 1);
+        __syncthreads();
+        if (s_last && w == 0) {
+            // This CTA completed the group: combine its S partials in chunk order.
+            __threadfence();
+            V a = __ldcg(&partials[g * S * 32 + lane]);
+            for (int64_t j = 1; j < S; ++j) a = R::comb(a, __ldcg(&partials[(g * S + j) * 32 + lane]));
+            if (o < nout) from_f(R::fin(a, scale), &out[o]);
+            if (lane == 0) counters[g] = 0;  // ready for the next launch on this stream
+        }
     }
+    pdl_end(defer);
 }
 
 // The plan of a reduction of view `a` over dim `ax`: false if its other dims
@@ -764,12 +805,24 @@ qsml_status_t launch_strided(Context* ctx, const T* x, const StridedPlan& p, int
                              bool lanes) {
     int64_t grid;
     cudaError_t e;
+    // the bytes the plan can touch (its lowest to its highest element)
+    int64_t lo = 0, hi = 0;
+    for (int d = 0; d < p.nd; ++d) {
+        const int64_t ext = (p.oshape[d] - 1) * p.ostride[d];
+        if (ext < 0) lo += ext; else hi += ext;
+    }
+    const int64_t ext_k = (p.k - 1) * p.sk;
+    if (ext_k < 0) lo += ext_k; else hi += ext_k;
+    Footprint fp;
+    fp.read(Span{reinterpret_cast<uintptr_t>(x + lo), reinterpret_cast<uintptr_t>(x + hi + 1)})
+        .write(span_of(out, static_cast<size_t>(nout) * sizeof(OT)));
     if (lanes) {
         grid = (nout + 7) / 8;
         const int64_t cap = static_cast<int64_t>(ctx->num_sms) * 32;
         if (grid > cap) grid = cap;
+        const int defer = plan_launch(ctx, fp);
         e = launch_pdl(k_reduce_strided_lanes<T, OT, OP>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, ctx->stream,
-                       x, p, nout, out, scale);
+                       x, p, nout, out, scale, defer);
         if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_strided_lanes");
         return after_launch(ctx, "k_reduce_strided_lanes");
     }
@@ -796,9 +849,12 @@ qsml_status_t launch_strided(Context* ctx, const T* x, const StridedPlan& p, int
         QSML_TRY_STATUS(get_scratch(ctx, kCounterBytes + static_cast<size_t>(groups * S) * 32 * sizeof(V), &scratch));
         counters = static_cast<unsigned*>(scratch);
         partials = reinterpret_cast<V*>(static_cast<char*>(scratch) + kCounterBytes);
+        fp.write(span_of(scratch, kCounterBytes + static_cast<size_t>(groups * S) * 32 * sizeof(V)));
     }
+    const int defer = plan_launch(ctx, fp);
     e = launch_pdl(k_reduce_strided_cols<T, OT, OP>, dim3(static_cast<unsigned>(groups * S)),
-                   dim3(32, static_cast<unsigned>(W)), 0, ctx->stream, x, p, nout, S, out, scale, counters, partials);
+                   dim3(32, static_cast<unsigned>(W)), 0, ctx->stream, x, p, nout, S, out, scale, counters, partials,
+                   defer);
     if (e != cudaSuccess) return check_cuda(ctx, e, "k_reduce_strided_cols");
     return after_launch(ctx, "k_reduce_strided_cols");
 }
@@ -1069,10 +1125,10 @@ qsml_status_t run_noalloc(cudaStream_t stream, const T* x, int64_t rows, int64_t
     const int64_t grid = units;  // one slice per CTA
     if (vec)
         k_reduce_seg<T, OT, OP, true><<<static_cast<unsigned>(grid), kRT, 0, stream>>>(x, rows, k, P, out, scale,
-                                                                                        counters, partials);
+                                                                                        counters, partials, 0);
     else
         k_reduce_seg<T, OT, OP, false><<<static_cast<unsigned>(grid), kRT, 0, stream>>>(x, rows, k, P, out, scale,
-                                                                                         counters, partials);
+                                                                                         counters, partials, 0);
     e = cudaGetLastError();
     if (e != cudaSuccess)
         return set_error(nullptr, QSML_E_CUDA, std::string("qsml_reduce_noalloc: launch: ") + cudaGetErrorString(e));

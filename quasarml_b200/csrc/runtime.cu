@@ -9,6 +9,7 @@
 #include "qsml_internal.cuh"
 
 #include <cstdlib>
+#include <vector>
 
 namespace qsml {
 
@@ -27,19 +28,97 @@ qsml_status_t set_error(Context* ctx, qsml_status_t st, const std::string& msg) 
 qsml_status_t check_cuda(Context* ctx, cudaError_t e, const char* what) {
     if (e == cudaSuccess) return QSML_OK;
     cudaGetLastError();  // clear a non-sticky error
+    if (ctx) {
+        // a launch planned but refused: forget the plan and the window
+        ctx->planned_for = 0;
+        end_window(ctx->stream);
+    }
     std::string m = std::string(what) + ": " + cudaGetErrorString(e);
     return set_error(ctx, e == cudaErrorMemoryAllocation ? QSML_E_OOM : QSML_E_CUDA, m);
 }
 
 qsml_status_t after_launch(Context* ctx, const char* kernel) {
+    // a launch that plan_launch did not see closes the stream's window
+    const bool planned = ctx->planned_for != 0 && ctx->planned_for == ctx->launches + 1;
+    ctx->planned_for = 0;
     ctx->launches++;
     ctx->last_kernel = kernel;
     cudaError_t e = cudaGetLastError();
+    if (!planned || e != cudaSuccess) end_window(ctx->stream);
     if (e != cudaSuccess) {
         return set_error(ctx, QSML_E_CUDA,
                          std::string("launch of ") + kernel + " failed: " + cudaGetErrorString(e));
     }
     return QSML_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Windows of kernels that may run together on a stream (see plan_launch in
+// qsml_internal.cuh).
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kMaxWindow = 16;  // deferring kernels in flight behind one that waited
+
+struct Window {
+    bool open = false;
+    std::vector<Footprint> kernels;
+};
+
+std::mutex g_window_mu;
+std::unordered_map<cudaStream_t, Window> g_windows;
+
+bool overlap(const Span& a, const Span& b) { return a.lo < b.hi && b.lo < a.hi; }
+
+// True if kernel n may not run beside kernel r.
+bool conflict(const Footprint& n, const Footprint& r) {
+    for (int i = 0; i < n.nw; ++i) {
+        for (int j = 0; j < r.nr; ++j)
+            if (overlap(n.writes[i], r.reads[j])) return true;
+        for (int j = 0; j < r.nw; ++j)
+            if (overlap(n.writes[i], r.writes[j])) return true;
+    }
+    for (int i = 0; i < n.nr; ++i)
+        for (int j = 0; j < r.nw; ++j)
+            if (overlap(n.reads[i], r.writes[j])) return true;
+    return false;
+}
+
+}  // namespace
+
+int plan_launch(Context* ctx, const Footprint& f) {
+    std::lock_guard<std::mutex> lk(g_window_mu);
+    Window& w = g_windows[ctx->stream];
+    bool defer = ctx->overlap && w.open && w.kernels.size() < kMaxWindow;
+    for (size_t i = 0; defer && i < w.kernels.size(); ++i) defer = !conflict(f, w.kernels[i]);
+    if (!defer) w.kernels.clear();  // this kernel waits: nothing before it is still running
+    w.kernels.push_back(f);
+    w.open = true;
+    ctx->planned_for = ctx->launches + 1;
+    ctx->planned++;
+    if (defer) ctx->deferred++;
+    return defer ? 1 : 0;
+}
+
+void end_window(cudaStream_t stream) {
+    std::lock_guard<std::mutex> lk(g_window_mu);
+    auto it = g_windows.find(stream);
+    if (it != g_windows.end()) {
+        it->second.open = false;
+        it->second.kernels.clear();
+    }
+}
+
+Span view_span(const qsml_tdesc* d) {
+    const int64_t es = static_cast<int64_t>(dtype_size(d->dtype));
+    int64_t lo = 0, hi = 0;
+    for (int i = 0; i < d->ndim; ++i) {
+        if (d->shape[i] == 0) return Span{};
+        const int64_t e = (d->shape[i] - 1) * d->stride[i];
+        if (e < 0) lo += e; else hi += e;
+    }
+    const uintptr_t base = reinterpret_cast<uintptr_t>(d->data);
+    return Span{base + static_cast<uintptr_t>(lo * es), base + static_cast<uintptr_t>((hi + 1) * es)};
 }
 
 qsml_status_t check_desc(Context* ctx, const qsml_tdesc* d, const char* name) {
@@ -245,7 +324,9 @@ CachingAllocator::~CachingAllocator() {
 
 qsml_status_t get_scratch(Context* ctx, size_t bytes, void** ptr) {
     bytes += 256;
-    if (ctx->scratch_bytes < bytes) {
+    bytes = (bytes + 255) & ~size_t(255);
+    // kScratchSlots slots of scratch_bytes / kScratchSlots each, in turn
+    if (ctx->scratch_bytes / kScratchSlots < bytes) {
         if (ctx->scratch) {
             // The old scratch may still be read by enqueued kernels.
             QSML_TRY_STATUS(check_cuda(ctx, cudaStreamSynchronize(ctx->stream), "scratch resize sync"));
@@ -253,12 +334,17 @@ qsml_status_t get_scratch(Context* ctx, size_t bytes, void** ptr) {
             ctx->scratch = nullptr;
             ctx->scratch_bytes = 0;
         }
-        size_t sz = CachingAllocator::round_size(bytes < (size_t(1) << 20) ? (size_t(1) << 20) : bytes);
+        size_t slot = CachingAllocator::round_size(bytes < (size_t(1) << 20) ? (size_t(1) << 20) : bytes);
+        const size_t sz = slot * kScratchSlots;
         QSML_TRY_STATUS(check_cuda(ctx, cudaMalloc(&ctx->scratch, sz), "scratch allocation"));
         QSML_TRY_STATUS(check_cuda(ctx, cudaMemsetAsync(ctx->scratch, 0, sz, ctx->stream), "scratch clear"));
         ctx->scratch_bytes = sz;
+        ctx->scratch_slot = 0;
+        end_window(ctx->stream);  // the memset: kernels after it wait for it
     }
-    *ptr = ctx->scratch;
+    const size_t slot = ctx->scratch_bytes / kScratchSlots;
+    *ptr = static_cast<char*>(ctx->scratch) + static_cast<size_t>(ctx->scratch_slot) * slot;
+    ctx->scratch_slot = (ctx->scratch_slot + 1) % kScratchSlots;
     return QSML_OK;
 }
 
@@ -351,12 +437,27 @@ qsml_status_t qsml_destroy(qsml_ctx* handle) {
     QSML_CTX(handle);
     cudaStreamSynchronize(C_->stream);
     if (C_->stream != C_->own_stream) cudaStreamSynchronize(C_->own_stream);
+    qsml::end_window(C_->stream);
+    qsml::end_window(C_->own_stream);
     qsml::staging_free(C_);
     delete C_->allocator;
     if (C_->scratch) cudaFree(C_->scratch);
     if (C_->status) cudaFree(C_->status);
     cudaStreamDestroy(C_->own_stream);
     delete C_;
+    return QSML_OK;
+}
+
+qsml_status_t qsml_set_overlap(qsml_ctx* handle, int32_t enable) {
+    QSML_CTX(handle);
+    C_->overlap = enable != 0;
+    return QSML_OK;
+}
+
+qsml_status_t qsml_overlap_stats(qsml_ctx* handle, uint64_t* planned, uint64_t* deferred) {
+    QSML_CTX(handle);
+    if (planned) *planned = C_->planned;
+    if (deferred) *deferred = C_->deferred;
     return QSML_OK;
 }
 

@@ -1,0 +1,192 @@
+"""Overlap of independent reductions on one stream (qsml_set_overlap).
+
+A reduction that shares no buffer with the library kernels still running on
+the stream starts reading at once and waits for them only at its end.  These
+tests check that:
+* a burst of independent reductions (every reduction kernel: segment, rows,
+  columns, wide columns, split columns, strided lanes and column blocks)
+  gives the same bits with overlap as without, eagerly and from a CUDA graph,
+  and that the launches after the first did overlap;
+* reductions that depend on one another (one reads what the previous wrote,
+  or writes what the previous reads) wait, and give the right results;
+* any other library kernel on the stream (an elementwise op) closes the
+  window, so a reduction of its output waits for it.
+"""
+import numpy as np
+import pytest
+
+from helpers import d, dev, empty, host
+from quasarml_b200 import abi, datagen
+
+pytestmark = pytest.mark.gpu
+
+# (shape, axis, dtype, kernel)
+CASES = [((64, 512, 1024), None, np.float16, "k_reduce_seg"),
+         ((64, 512, 1024), 2, np.float32, "k_reduce_rows"),
+         ((64, 512, 1024), 1, np.float16, "k_reduce_cols"),
+         ((64, 512, 1024), 0, np.float32, "k_reduce_cols_wide"),
+         ((4096, 2048), 0, np.float32, "k_reduce_cols_split"),
+         ((64, 512, 1024), 0, np.float16, "k_reduce_cols")]
+
+
+def _inputs():
+    import torch
+    xs = []
+    for i, (shape, axis, dt, _) in enumerate(CASES):
+        x = dev(datagen.normal(70 + i, shape, 0.5, 1.0).astype(dt))
+        tdt = torch.float32 if dt == np.float32 else torch.float16
+        out = torch.empty(abi.reduced_shape(shape, axis, False), dtype=tdt, device="cuda")
+        xs.append((x, out))
+    # two strided views of one X[2048, 4096] fp32: rows along k, column blocks
+    base = dev(datagen.normal(79, (2048, 4096), 0.5, 1.0))
+    v = abi.make_desc(base.data_ptr() + (5 * 4096 + 1) * 4, abi.F32, (681, 2048), (3 * 4096, 2))
+    o_rows = torch.empty((681,), device="cuda")
+    o_cols = torch.empty((2048,), device="cuda")
+    return xs, base, v, o_rows, o_cols
+
+
+def _burst(ctx, xs, v, o_rows, o_cols, op):
+    kernels = []
+    for (x, out), (_, axis, _, _) in zip(xs, CASES):
+        ctx.reduce(op, d(x), abi.AXIS_ALL if axis is None else axis, False, d(out))
+        kernels.append(ctx.last_kernel())
+    ctx.reduce(op, v, 1, False, d(o_rows))
+    kernels.append(ctx.last_kernel())
+    ctx.reduce(op, v, 0, False, d(o_cols))
+    kernels.append(ctx.last_kernel())
+    return kernels
+
+
+def _results(xs, o_rows, o_cols):
+    return [host(o).copy() for _, o in xs] + [host(o_rows).copy(), host(o_cols).copy()]
+
+
+@pytest.mark.parametrize("op", [abi.RED_SUM, abi.RED_MEAN, abi.RED_MAX])
+def test_independent_burst_same_bits(op):
+    import torch
+    xs, base, v, o_rows, o_cols = _inputs()
+    ref_ctx = abi.Context(0)
+    _burst(ref_ctx, xs, v, o_rows, o_cols, op)
+    torch.cuda.synchronize()
+    want = _results(xs, o_rows, o_cols)
+    for _, o in xs:
+        o.fill_(-7.0)
+    o_rows.fill_(-7.0)
+    o_cols.fill_(-7.0)
+
+    ctx = abi.Context(0)
+    ctx.set_overlap(True)
+    p0, d0 = ctx.overlap_stats()
+    kernels = _burst(ctx, xs, v, o_rows, o_cols, op)
+    torch.cuda.synchronize()
+    p1, d1 = ctx.overlap_stats()
+    assert [c[3] for c in CASES] == kernels[:len(CASES)]
+    assert kernels[-2:] == ["k_reduce_strided_lanes", "k_reduce_strided_cols"]
+    assert p1 - p0 == len(kernels)
+    assert d1 - d0 == len(kernels) - 1, "every launch after the first shares no buffer with those before it"
+    got = _results(xs, o_rows, o_cols)
+    for g, w, k in zip(got, want, kernels):
+        assert np.array_equal(g.view(np.uint8), w.view(np.uint8)), k
+
+    # the same burst captured in a CUDA graph and replayed
+    for _, o in xs:
+        o.fill_(-7.0)
+    s = torch.cuda.Stream()
+    ctx.set_stream(s.cuda_stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        _burst(ctx, xs, v, o_rows, o_cols, op)  # warm-up outside the graph
+        s.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            _burst(ctx, xs, v, o_rows, o_cols, op)
+    for _ in range(3):
+        for _, o in xs:
+            o.fill_(-7.0)
+        g.replay()
+        torch.cuda.synchronize()
+        got = _results(xs, o_rows, o_cols)
+        for gg, w, k in zip(got, want, kernels):
+            assert np.array_equal(gg.view(np.uint8), w.view(np.uint8)), k
+
+
+def test_dependent_reductions_wait():
+    """Read-after-write (a reduction of the previous one's output) and
+    write-after-read (a reduction whose output lies in the bytes the previous
+    one reads): each waits, over many rounds with no host sync in between."""
+    import torch
+    ctx = abi.Context(0)
+    ctx.set_overlap(True)
+    x = datagen.normal(81, (512, 8192), 0.5, 1.0)
+    tx = dev(x)
+    rows = empty((512,), np.float32)
+    total = empty((1,), np.float32)
+    y = datagen.normal(82, (1024, 4), 0.5, 1.0)
+    ty = dev(y)
+    want_rows = x.astype(np.float64).sum(axis=1)
+    outs = []
+    _, d0 = ctx.overlap_stats()
+    for i in range(20):
+        ctx.reduce(abi.RED_SUM, d(tx), 1, False, d(rows))          # reads X, writes rows
+        ctx.reduce(abi.RED_SUM, d(rows), abi.AXIS_ALL, False, d(total))  # reads rows: waits
+        t = empty((1,), np.float32)
+        ctx.reduce(abi.RED_MAX, d(total), abi.AXIS_ALL, False, d(t))   # reads total: waits
+        outs.append(t)
+    torch.cuda.synchronize()
+    _, d1 = ctx.overlap_stats()
+    # the second and third reduction of a round read their predecessor's
+    # output and wait; the first of the next round shares no buffer with the
+    # third (the one kernel that may still run: it waited for the second) and
+    # overlaps it
+    assert d1 - d0 == 19
+    for t in outs:
+        assert abs(float(host(t)[0]) - want_rows.sum()) <= 1e-5 * np.abs(x).sum()
+
+    # write-after-read: the second reduction's output is the first 4 KiB of X
+    # while the first reduction reads all of X
+    for _ in range(10):
+        tx.copy_(torch.from_numpy(x).cuda())
+        ctx.reduce(abi.RED_SUM, d(tx), 1, False, d(rows))
+        over = abi.make_desc(tx.data_ptr(), abi.F32, (1024,), (1,))
+        ctx.reduce(abi.RED_SUM, d(ty), 1, False, over)
+        torch.cuda.synchronize()
+        assert np.all(np.abs(host(rows).astype(np.float64) - want_rows) <= 1e-5 * np.abs(x).sum(axis=1))
+        np.testing.assert_allclose(host(tx).reshape(-1)[:1024], y.sum(axis=1), rtol=1e-5)
+
+
+def test_other_kernels_close_the_window():
+    """An elementwise kernel between two reductions is not tracked: the
+    reduction after it waits, and reads what it wrote."""
+    import torch
+    ctx = abi.Context(0)
+    ctx.set_overlap(True)
+    a = dev(datagen.normal(83, (2048, 4096), 0.0, 1.0))
+    b = dev(datagen.normal(84, (2048, 4096), 0.0, 1.0))
+    s = empty((2048,), np.float32)
+    first = empty((2048,), np.float32)
+    for i in range(5):
+        ctx.reduce(abi.RED_SUM, d(b), 1, False, d(first))
+        _, d0 = ctx.overlap_stats()
+        ctx.binary_scalar(abi.OP_ADD, d(a), float(i + 1), d(a))  # a += i + 1
+        ctx.reduce(abi.RED_SUM, d(a), 1, False, d(s))
+        _, d1 = ctx.overlap_stats()
+        assert d1 == d0
+    torch.cuda.synchronize()
+    a0 = datagen.normal(83, (2048, 4096), 0.0, 1.0).astype(np.float64) + 15.0
+    assert np.all(np.abs(host(s) - a0.sum(axis=1)) <= 1e-5 * np.abs(a0).sum(axis=1))
+
+
+def test_long_burst_is_capped():
+    """More independent reductions than the window holds: still right."""
+    import torch
+    ctx = abi.Context(0)
+    ctx.set_overlap(True)
+    xs = [dev(datagen.normal(90 + i, (256, 4096), 0.5, 1.0)) for i in range(40)]
+    outs = [empty((256,), np.float32) for _ in xs]
+    for x, o in zip(xs, outs):
+        ctx.reduce(abi.RED_SUM, d(x), 1, False, d(o))
+    torch.cuda.synchronize()
+    p, dd = ctx.overlap_stats()
+    assert 0 < dd < p
+    for i, o in enumerate(outs):
+        x = datagen.normal(90 + i, (256, 4096), 0.5, 1.0).astype(np.float64)
+        assert np.all(np.abs(host(o) - x.sum(axis=1)) <= 1e-5 * np.abs(x).sum(axis=1))
