@@ -162,11 +162,12 @@ QSML_API qsml_status_t qsml_synchronize(qsml_ctx* ctx);
 QSML_API qsml_status_t qsml_set_wait_limit(qsml_ctx* ctx, int64_t cycles);
 
 /* Overlap of independent reductions on the context's stream (off by default).
- * With enable = 1, a reduction (qsml_reduce) whose input, output and scratch
- * share no byte with the library kernels that may still be running on the
- * stream starts reading at once instead of waiting for them to finish; it
- * waits for them only at its end, so kernels still complete in stream order
- * and every other call sees the same results as without overlap.  A
+ * With enable = 1, a reduction (qsml_reduce, qsml_arg_reduce) whose input,
+ * output and scratch share no byte with the library kernels that may still
+ * be running on the stream starts reading at once instead of waiting for
+ * them to finish; it waits for them only at its end, so kernels still
+ * complete in stream order and every other call sees the same results as
+ * without overlap.  A
  * reduction that reads what such a kernel writes (or writes what it reads or
  * writes) waits at its start as usual.  The library tracks its own kernels
  * only: enable this when nothing else on the stream launches kernels that

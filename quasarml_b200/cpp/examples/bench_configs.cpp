@@ -129,30 +129,36 @@ int main() {
         const double outs[4] = {1, 512.0 * 1024, 64.0 * 1024, 64.0 * 512};  // all, axis 0, 1, 2
         for (int es : {4, 2})
             for (double o : outs) bytes += 4 * 8 * (n * es + o * es);
+        std::vector<TensorPtr> results;  // the step's results, kept until the next step
+        results.reserve(256);
+        qsml::set_overlap(true);
         report("reductions", "reductions X[64,512,1024] fp32 and fp16: sum/mean/max/min over axis 0, 1, 2 and all "
-               "(256 qsml:: calls)",
+               "(256 qsml:: calls, qsml::set_overlap(true))",
                bytes, "GB/s", 2, 10, [&] {
+                   results.clear();
                    for (auto* xs : {&X32, &X16}) {
                        for (int ax = -1; ax < 3; ++ax) {
                            for (int op = 0; op < 4; ++op) {
                                for (int b = 0; b < 8; ++b) {
                                    TensorPtr x = (*xs)[b];
                                    if (ax < 0) {
-                                       if (op == 0) qsml::sum(x);
-                                       else if (op == 1) qsml::mean(x);
-                                       else if (op == 2) qsml::max(x);
-                                       else qsml::min(x);
+                                       if (op == 0) results.push_back(qsml::sum(x));
+                                       else if (op == 1) results.push_back(qsml::mean(x));
+                                       else if (op == 2) results.push_back(qsml::max(x));
+                                       else results.push_back(qsml::min(x));
                                    } else {
-                                       if (op == 0) qsml::sum(x, ax);
-                                       else if (op == 1) qsml::mean(x, ax);
-                                       else if (op == 2) qsml::max(x, ax);
-                                       else qsml::min(x, ax);
+                                       if (op == 0) results.push_back(qsml::sum(x, ax));
+                                       else if (op == 1) results.push_back(qsml::mean(x, ax));
+                                       else if (op == 2) results.push_back(qsml::max(x, ax));
+                                       else results.push_back(qsml::min(x, ax));
                                    }
                                }
                            }
                        }
                    }
                });
+        qsml::set_overlap(false);
+        results.clear();
     }
 
     {  // C3: X[5::3, 1::2] and X.T[::4, :] of X[8192,8192], int32 and fp32

@@ -36,6 +36,10 @@ public:
     // results that evaluate as one fused kernel on first access.
     void set_fusion(bool on);
     bool fusion() const { return _fusion; }
+    // Overlap of independent reductions on the device's stream (a reduction
+    // sharing no buffer with the kernels still running before it starts at
+    // once; qsml_set_overlap).  Off by default.
+    void set_overlap(bool on);
     bool defer_elementwise() const { return _fusion || _in_batch; }
 
     // Work is enqueued in order on one stream; a batch additionally defers

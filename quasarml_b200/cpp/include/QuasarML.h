@@ -204,6 +204,9 @@ inline std::vector<TensorPtr> sharded_reduce(const std::vector<TensorPtr>& block
 inline void set_fusion(bool on) { device().set_fusion(on); }
 inline bool fusion_enabled() { return device().fusion(); }
 
+// Overlap of independent reductions on the device's stream (off by default).
+inline void set_overlap(bool on) { device().set_overlap(on); }
+
 inline u64 cpu_fallback_count() {
     uint64_t n = 0;
     device().check(qsml_cpu_fallback_count(device().ctx(), &n));

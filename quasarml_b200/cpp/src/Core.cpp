@@ -353,6 +353,8 @@ std::shared_ptr<Tensor> Device::create_tensor(const std::vector<u32>& shape, Dat
 
 void Device::set_fusion(bool on) { _fusion = on; }
 
+void Device::set_overlap(bool on) { check(qsml_set_overlap(_ctx, on ? 1 : 0)); }
+
 void Device::begin_batch() {
     QS_ASSERT(!_in_batch, "Already in batch");
     _in_batch = true;

@@ -192,8 +192,8 @@ __device__ __forceinline__ void half_cols_to_best(const HalfBest<OP>& hb, int64_
 template <typename T, int OP, bool VEC>
 __global__ void __launch_bounds__(kAT) k_arg_seg(const T* __restrict__ x, int64_t nseg, int64_t len, int64_t P,
                                                  uint32_t* __restrict__ out, unsigned* __restrict__ counters,
-                                                 unsigned long long* __restrict__ partials) {
-    pdl_begin();
+                                                 unsigned long long* __restrict__ partials, int defer) {
+    pdl_start(defer);
     using C = typename Cmp<T>::C;
     constexpr int PV = APack<T>::N;
     __shared__ bool s_last;
@@ -250,6 +250,7 @@ __global__ void __launch_bounds__(kAT) k_arg_seg(const T* __restrict__ x, int64_
         }
         __syncthreads();
     }
+    pdl_end(defer);
 }
 
 // ---------------------------------------------------------------------------
@@ -257,8 +258,8 @@ __global__ void __launch_bounds__(kAT) k_arg_seg(const T* __restrict__ x, int64_
 // ---------------------------------------------------------------------------
 template <typename T, int OP, bool VEC>
 __global__ void __launch_bounds__(256) k_arg_rows(const T* __restrict__ x, int64_t rows, int64_t len,
-                                                  uint32_t* __restrict__ out) {
-    pdl_begin();
+                                                  uint32_t* __restrict__ out, int defer) {
+    pdl_start(defer);
     using C = typename Cmp<T>::C;
     constexpr int PV = APack<T>::N;
     const int lane = threadIdx.x & 31;
@@ -300,8 +301,8 @@ __global__ void __launch_bounds__(256) k_arg_rows(const T* __restrict__ x, int64
 // ---------------------------------------------------------------------------
 template <typename T, int OP, bool VEC>
 __global__ void k_arg_cols(const T* __restrict__ x, int64_t outer, int64_t k, int64_t inner, int64_t tiles_per_o,
-                           uint32_t* __restrict__ out) {
-    pdl_begin();
+                           uint32_t* __restrict__ out, int defer) {
+    pdl_start(defer);
     using C = typename Cmp<T>::C;
     constexpr int PV = VEC ? APack<T>::N : 1;
     extern __shared__ unsigned long long red[];
@@ -370,6 +371,7 @@ __global__ void k_arg_cols(const T* __restrict__ x, int64_t outer, int64_t k, in
         const int64_t ci = (tile - o * tiles_per_o) * (32 * PV) + col;
         if (o < outer && ci < inner) out[o * inner + ci] = key_index(a);
     }
+    pdl_end(defer);
 }
 
 // ---------------------------------------------------------------------------
@@ -379,6 +381,10 @@ template <typename T, int OP>
 qsml_status_t run_arg(Context* ctx, const T* x, int64_t outer, int64_t k, int64_t inner, uint32_t* out) {
     constexpr int PV = APack<T>::N;
     const bool x_al = aligned16(x);
+    // what the launch reads and writes, for overlap with the kernels before it
+    Footprint fp;
+    fp.read(span_of(x, static_cast<size_t>(outer * k * inner) * sizeof(T)))
+        .write(span_of(out, static_cast<size_t>(outer * inner) * sizeof(uint32_t)));
     if (inner == 1 && (outer == 1 || (outer < 592 && k >= 8192))) {
         if (outer > kArgMaxSegments) return set_error(ctx, QSML_E_UNSUPPORTED, "qsml_arg_reduce: too many segments");
         const bool vec = x_al && (outer == 1 || (k * static_cast<int64_t>(sizeof(T))) % 16 == 0);
@@ -393,11 +399,12 @@ qsml_status_t run_arg(Context* ctx, const T* x, int64_t outer, int64_t k, int64_
         auto* partials = reinterpret_cast<unsigned long long*>(static_cast<char*>(scratch) + kArgCounterBytes);
         int64_t grid = static_cast<int64_t>(ctx->num_sms) * 8;
         if (grid > units) grid = units;
+        const int defer = plan_launch(ctx, fp.write(span_of(scratch, kArgCounterBytes + static_cast<size_t>(units) * 8)));
         const cudaError_t e =
             vec ? launch_pdl(k_arg_seg<T, OP, true>, dim3(static_cast<unsigned>(grid)), dim3(kAT), 0, ctx->stream, x,
-                             outer, k, P, out, counters, partials)
+                             outer, k, P, out, counters, partials, defer)
                 : launch_pdl(k_arg_seg<T, OP, false>, dim3(static_cast<unsigned>(grid)), dim3(kAT), 0, ctx->stream, x,
-                             outer, k, P, out, counters, partials);
+                             outer, k, P, out, counters, partials, defer);
         if (e != cudaSuccess) return check_cuda(ctx, e, "k_arg_seg");
         return after_launch(ctx, "k_arg_seg");
     }
@@ -406,11 +413,12 @@ qsml_status_t run_arg(Context* ctx, const T* x, int64_t outer, int64_t k, int64_
         int64_t grid = (outer + 7) / 8;  // 8 warps per CTA
         const int64_t cap = static_cast<int64_t>(ctx->num_sms) * 32;
         if (grid > cap) grid = cap;
+        const int defer = plan_launch(ctx, fp);
         const cudaError_t e =
             vec ? launch_pdl(k_arg_rows<T, OP, true>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, ctx->stream, x,
-                             outer, k, out)
+                             outer, k, out, defer)
                 : launch_pdl(k_arg_rows<T, OP, false>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, ctx->stream, x,
-                             outer, k, out);
+                             outer, k, out, defer);
         if (e != cudaSuccess) return check_cuda(ctx, e, "k_arg_rows");
         return after_launch(ctx, "k_arg_rows");
     }
@@ -433,11 +441,12 @@ qsml_status_t run_arg(Context* ctx, const T* x, int64_t outer, int64_t k, int64_
     if (W < 1) W = 1;
     dim3 block(32, static_cast<unsigned>(W));
     const size_t smem = static_cast<size_t>(W) * 32 * pv * 8;
+    const int defer = plan_launch(ctx, fp);
     const cudaError_t e =
         vec ? launch_pdl(k_arg_cols<T, OP, true>, dim3(static_cast<unsigned>(tiles)), block, smem, ctx->stream, x,
-                         outer, k, inner, tiles_per_o, out)
+                         outer, k, inner, tiles_per_o, out, defer)
             : launch_pdl(k_arg_cols<T, OP, false>, dim3(static_cast<unsigned>(tiles)), block, smem, ctx->stream, x,
-                         outer, k, inner, tiles_per_o, out);
+                         outer, k, inner, tiles_per_o, out, defer);
     if (e != cudaSuccess) return check_cuda(ctx, e, "k_arg_cols");
     return after_launch(ctx, "k_arg_cols");
 }

@@ -190,3 +190,39 @@ def test_long_burst_is_capped():
     for i, o in enumerate(outs):
         x = datagen.normal(90 + i, (256, 4096), 0.5, 1.0).astype(np.float64)
         assert np.all(np.abs(host(o) - x.sum(axis=1)) <= 1e-5 * np.abs(x).sum(axis=1))
+
+
+def test_arg_reductions_overlap_same_indices():
+    """argmax/argmin bursts (segment, rows and column kernels) give the same
+    indices with overlap, and the launches after the first overlap."""
+    import torch
+    shapes = [((64, 512, 1024), None, np.float16), ((64, 512, 1024), 2, np.float32),
+              ((64, 512, 1024), 1, np.float16), ((64, 512, 1024), 0, np.float32)]
+    xs = [dev(datagen.normal(100 + i, s, 0.0, 1.0).astype(dt)) for i, (s, _, dt) in enumerate(shapes)]
+    outs = [empty((1,) if ax is None else abi.reduced_shape(s, ax, False), np.int32) for s, ax, _ in shapes]
+
+    def burst(ctx):
+        names = []
+        for op in (abi.ARG_MAX, abi.ARG_MIN):
+            for x, o, (_, ax, _) in zip(xs, outs, shapes):
+                ctx.arg_reduce(op, d(x), abi.AXIS_ALL if ax is None else ax, False, d(o))
+                names.append(ctx.last_kernel())
+        return names
+
+    ref = abi.Context(0)
+    burst(ref)
+    torch.cuda.synchronize()
+    want = [host(o).copy() for o in outs]
+    for o in outs:
+        o.fill_(-1)
+    ctx = abi.Context(0)
+    ctx.set_overlap(True)
+    names = burst(ctx)
+    torch.cuda.synchronize()
+    p, dd = ctx.overlap_stats()
+    assert names[:4] == ["k_arg_seg", "k_arg_rows", "k_arg_cols", "k_arg_cols"]
+    # the second op's first launch writes what the first op's first launch
+    # wrote (still in the window) and waits; the other six overlap
+    assert (p, dd) == (8, 6)
+    for g, w in zip([host(o) for o in outs], want):
+        assert np.array_equal(g, w)
