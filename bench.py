@@ -338,7 +338,7 @@ class ReduceWorkload(Workload):
             return
         import torch
         abi = self.abi
-        self.xstream = torch.cuda.Stream()
+        self.xstream = torch.cuda.Stream(priority=-1)  # NCCL CTAs ahead of the local reductions
         self.xctx = abi.Context(torch.cuda.current_device(), use_torch_stream=False)
         self.xctx.set_stream(self.xstream.cuda_stream)
         uid = [abi.group_unique_id() if self.dist.rank == 0 else None]
@@ -362,8 +362,13 @@ class ReduceWorkload(Workload):
         self.init_exchange()
         self.ev_ready.record(torch.cuda.current_stream())
         self.xstream.wait_event(self.ev_ready)
-        for g, op in (("sum", abi.RED_SUM), ("max", abi.RED_MAX), ("min", abi.RED_MIN)):
-            self.group.allreduce_partials(0, op, self.flat[g].data_ptr(), self.flat[g].numel())
+        # one NCCL group for the three combines (launched together)
+        abi.group_start()
+        try:
+            for g, op in (("sum", abi.RED_SUM), ("max", abi.RED_MAX), ("min", abi.RED_MIN)):
+                self.group.allreduce_partials(0, op, self.flat[g].data_ptr(), self.flat[g].numel())
+        finally:
+            abi.group_end()
         self.ev_done.record(self.xstream)
         return self.ev_done
 

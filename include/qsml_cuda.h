@@ -161,22 +161,22 @@ QSML_API qsml_status_t qsml_synchronize(qsml_ctx* ctx);
  * QuasarML/src/Backend/Vulkan/VulkanBackend.cpp:613-658). */
 QSML_API qsml_status_t qsml_set_wait_limit(qsml_ctx* ctx, int64_t cycles);
 
-/* Overlap of independent reductions on the context's stream (off by default).
- * With enable = 1, a reduction (qsml_reduce, qsml_arg_reduce) whose input,
- * output and scratch share no byte with the library kernels that may still
- * be running on the stream starts reading at once instead of waiting for
- * them to finish; it waits for them only at its end, so kernels still
- * complete in stream order and every other call sees the same results as
- * without overlap.  A
- * reduction that reads what such a kernel writes (or writes what it reads or
- * writes) waits at its start as usual.  The library tracks its own kernels
+/* Overlap of independent calls on the context's stream (off by default).
+ * With enable = 1, a memory-bound call (qsml_reduce, qsml_arg_reduce,
+ * qsml_layer_norm, qsml_softmax, qsml_gather) whose inputs, outputs and
+ * scratch share no byte with the library kernels that may still be running
+ * on the stream starts reading at once instead of waiting for them to
+ * finish; it waits for them only at its end, so kernels still complete in
+ * stream order and every other call sees the same results as without
+ * overlap.  A call that reads what such a kernel writes (or writes what it
+ * reads or writes) waits at its start as usual.  The library tracks its own kernels
  * only: enable this when nothing else on the stream launches kernels that
  * trigger programmatic dependent launch early (plain kernel launches,
  * copies, memsets and events are fine).  Measured on B200: binary16 column
  * reductions of 64 MiB 13.2 -> 10.5 us per launch.  No reference counterpart
  * (its dispatches each end with a fence wait, VulkanBackend.cpp:613-658). */
 QSML_API qsml_status_t qsml_set_overlap(qsml_ctx* ctx, int32_t enable);
-/* Reduction launches planned on this context so far, and how many of them
+/* Launches planned for overlap on this context so far, and how many of them
  * overlapped the kernels before them (either pointer may be NULL). */
 QSML_API qsml_status_t qsml_overlap_stats(qsml_ctx* ctx, uint64_t* planned, uint64_t* deferred);
 

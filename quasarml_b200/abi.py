@@ -351,14 +351,15 @@ class Context:
         self.check(self.lib.qsml_set_wait_limit(self.h, cycles))
 
     def set_overlap(self, enable: bool) -> None:
-        """Let independent reductions on this context's stream overlap (each
-        starts reading while the library kernels before it that share no
-        buffer with it still run).  Only for streams on which nothing else
-        launches kernels that trigger programmatic dependent launch early."""
+        """Let independent reductions, arg-reductions, layer norms, softmaxes
+        and gathers on this context's stream overlap (each starts reading
+        while the library kernels before it that share no buffer with it
+        still run).  Only for streams on which nothing else launches kernels
+        that trigger programmatic dependent launch early."""
         self.check(self.lib.qsml_set_overlap(self.h, 1 if enable else 0))
 
     def overlap_stats(self) -> tuple:
-        """(reduction launches planned, of which overlapped the kernels before them)."""
+        """(launches planned for overlap, of which overlapped the kernels before them)."""
         p, d = ctypes.c_uint64(), ctypes.c_uint64()
         self.check(self.lib.qsml_overlap_stats(self.h, ctypes.byref(p), ctypes.byref(d)))
         return p.value, d.value

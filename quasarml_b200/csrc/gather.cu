@@ -58,8 +58,8 @@ constexpr int kGU = 4;
 // Inner stride 1: copy rows, VEC = whole 16-byte packs.
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(kGT) k_gather_rows(const T* __restrict__ src, T* __restrict__ dst, GPlan p,
-                                                     int64_t items, int64_t per_row) {
-    pdl_begin();
+                                                     int64_t items, int64_t per_row, int defer) {
+    pdl_start(defer);
     const int64_t base = static_cast<int64_t>(blockIdx.x) * (kGT * kGU) + threadIdx.x;
     if (VEC) {
         constexpr int PV = 16 / sizeof(T);
@@ -89,14 +89,15 @@ __global__ void __launch_bounds__(kGT) k_gather_rows(const T* __restrict__ src, 
         for (int u = 0; u < kGU; ++u)
             if (it[u] < items) dst[it[u]] = v[u];
     }
+    pdl_end(defer);
 }
 
 // Small inner stride: G consecutive outputs per item from G loads spaced by
 // the inner stride; one G-element store (16 bytes when G*sizeof(T) == 16).
 template <typename T, int G>
 __global__ void __launch_bounds__(kGT) k_gather_small(const T* __restrict__ src, T* __restrict__ dst, GPlan p,
-                                                      int64_t items, int64_t per_row) {
-    pdl_begin();
+                                                      int64_t items, int64_t per_row, int defer) {
+    pdl_start(defer);
     struct alignas(G * sizeof(T)) Out { T v[G]; };
     const int64_t s = p.st[p.nd - 1];
     const int64_t base = static_cast<int64_t>(blockIdx.x) * (kGT * 2) + threadIdx.x;
@@ -114,14 +115,15 @@ __global__ void __launch_bounds__(kGT) k_gather_small(const T* __restrict__ src,
 #pragma unroll
     for (int u = 0; u < 2; ++u)
         if (it[u] < items) reinterpret_cast<Out*>(dst)[it[u]] = o[u];
+    pdl_end(defer);
 }
 
 // Transpose-like: tile over (P = small-stride dim, Q = innermost dim).
 constexpr int kTile = 64;
 template <typename T>
 __global__ void __launch_bounds__(256) k_gather_tiled(const T* __restrict__ src, T* __restrict__ dst, GPlan p,
-                                                      int dP, int64_t ptiles, int64_t qtiles) {
-    pdl_begin();
+                                                      int dP, int64_t ptiles, int64_t qtiles, int defer) {
+    pdl_start(defer);
     __shared__ T tile[kTile][kTile + 1];
     const int tx = threadIdx.x, ty = threadIdx.y;  // (32, 8)
     const int dQ = p.nd - 1;
@@ -170,6 +172,7 @@ __global__ void __launch_bounds__(256) k_gather_tiled(const T* __restrict__ src,
             if (pp < P && qq < Q) dst[ooff + pp * oP + qq] = tile[qi][pi];
         }
     }
+    pdl_end(defer);
 }
 
 template <typename T>
@@ -224,7 +227,8 @@ qsml_status_t copy_strided_typed(Context* ctx, const CopyPlan& p, const void* sr
 }
 
 template <int ES>
-qsml_status_t gather_typed(Context* ctx, const GPlan& p, const void* srcv, void* dstv, int64_t n) {
+qsml_status_t gather_typed(Context* ctx, const GPlan& p, const void* srcv, void* dstv, int64_t n,
+                           const Footprint& fp) {
     using T = typename EType<ES>::T;
     const T* src = static_cast<const T*>(srcv);
     T* dst = static_cast<T*>(dstv);
@@ -241,15 +245,17 @@ qsml_status_t gather_typed(Context* ctx, const GPlan& p, const void* srcv, void*
             int64_t per_row = C / PV, items = n / PV;
             int64_t blocks = (items + kGT * kGU - 1) / (kGT * kGU);
             {
+                const int defer = plan_launch(ctx, fp);
                 const cudaError_t e = launch_pdl(k_gather_rows<T, true>, dim3(static_cast<unsigned>(blocks)),
-                                                 dim3(kGT), 0, ctx->stream, src, dst, p, items, per_row);
+                                                 dim3(kGT), 0, ctx->stream, src, dst, p, items, per_row, defer);
                 if (e != cudaSuccess) return check_cuda(ctx, e, "k_gather_rows");
             }
         } else {
             int64_t blocks = (n + kGT * kGU - 1) / (kGT * kGU);
             {
+                const int defer = plan_launch(ctx, fp);
                 const cudaError_t e = launch_pdl(k_gather_rows<T, false>, dim3(static_cast<unsigned>(blocks)),
-                                                 dim3(kGT), 0, ctx->stream, src, dst, p, n, C);
+                                                 dim3(kGT), 0, ctx->stream, src, dst, p, n, C, defer);
                 if (e != cudaSuccess) return check_cuda(ctx, e, "k_gather_rows");
             }
         }
@@ -270,8 +276,9 @@ qsml_status_t gather_typed(Context* ctx, const GPlan& p, const void* srcv, void*
         int64_t blocks = ptiles * qtiles * batch;
         if (blocks > INT32_MAX) return set_error(ctx, QSML_E_UNSUPPORTED, "gather too large");
         {
+            const int defer = plan_launch(ctx, fp);
             const cudaError_t e = launch_pdl(k_gather_tiled<T>, dim3(static_cast<unsigned>(blocks)), dim3(32, 8), 0,
-                                             ctx->stream, src, dst, p, dP, ptiles, qtiles);
+                                             ctx->stream, src, dst, p, dP, ptiles, qtiles, defer);
             if (e != cudaSuccess) return check_cuda(ctx, e, "k_gather_tiled");
         }
         return after_launch(ctx, "k_gather_tiled");
@@ -281,8 +288,9 @@ qsml_status_t gather_typed(Context* ctx, const GPlan& p, const void* srcv, void*
         int64_t per_row = C / PV, items = n / PV;
         int64_t blocks = (items + kGT * 2 - 1) / (kGT * 2);
         {
+            const int defer = plan_launch(ctx, fp);
             const cudaError_t e = launch_pdl(k_gather_small<T, PV>, dim3(static_cast<unsigned>(blocks)), dim3(kGT), 0,
-                                             ctx->stream, src, dst, p, items, per_row);
+                                             ctx->stream, src, dst, p, items, per_row, defer);
             if (e != cudaSuccess) return check_cuda(ctx, e, "k_gather_small");
         }
         return after_launch(ctx, "k_gather_small");
@@ -348,15 +356,17 @@ extern "C" qsml_status_t qsml_gather(qsml_ctx* handle, const qsml_tdesc* src, co
         nd = 1;
     }
     p.nd = nd;
+    Footprint fp;  // what the launch reads and writes, for overlap
+    fp.read(view_span(src)).write(span_of(out->data, static_cast<size_t>(n) * es));
     if (nd == 1 && p.st[0] == 1)
         return check_cuda(C_, cudaMemcpyAsync(out->data, src->data, static_cast<size_t>(n) * es,
                                               cudaMemcpyDeviceToDevice, C_->stream),
                           "qsml_gather copy");
     switch (es) {
-        case 1: return gather_typed<1>(C_, p, src->data, out->data, n);
-        case 2: return gather_typed<2>(C_, p, src->data, out->data, n);
-        case 4: return gather_typed<4>(C_, p, src->data, out->data, n);
-        case 8: return gather_typed<8>(C_, p, src->data, out->data, n);
+        case 1: return gather_typed<1>(C_, p, src->data, out->data, n, fp);
+        case 2: return gather_typed<2>(C_, p, src->data, out->data, n, fp);
+        case 4: return gather_typed<4>(C_, p, src->data, out->data, n, fp);
+        case 8: return gather_typed<8>(C_, p, src->data, out->data, n, fp);
     }
     return set_error(C_, QSML_E_DTYPE, "qsml_gather: unsupported element size");
 }

@@ -133,8 +133,8 @@ __device__ __forceinline__ float block_sum(float v, float* slot) {
 template <typename T, typename GT, int NV>
 __global__ void __launch_bounds__(256) k_layer_norm_reg(const T* __restrict__ x, const GT* __restrict__ gamma,
                                                         const GT* __restrict__ beta, T* __restrict__ y,
-                                                        int64_t rows, int cols, float eps) {
-    pdl_begin();
+                                                        int64_t rows, int cols, float eps, int defer) {
+    pdl_start(defer);
     constexpr int PV = Pack<T>::N;
     constexpr int E = NV * PV;  // elements per thread
     extern __shared__ float4 ln_smem[];
@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(256) k_layer_norm_reg(const T* __restrict__ x,
         process(C, row);
         row += G;
     }
+    pdl_end(defer);
 }
 
 // Rows streamed through shared memory (row_pipe.cuh), one warp per row:
@@ -220,8 +221,8 @@ __global__ void __launch_bounds__(256) k_layer_norm_reg(const T* __restrict__ x,
 template <typename T, typename GT>
 __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
     k_layer_norm_pipe(const T* __restrict__ x, const GT* __restrict__ gamma, const GT* __restrict__ beta,
-                      T* __restrict__ y, int64_t rows, int cols, float eps, int slots, int* status) {
-    pdl_begin();
+                      T* __restrict__ y, int64_t rows, int cols, float eps, int slots, int* status, int defer) {
+    pdl_start(defer);
     constexpr int PV = Pack<T>::N;
     extern __shared__ float4 ln_pipe_smem[];
     __shared__ uint64_t bars[rowpipe::kMaxWarps * rowpipe::kMaxSlots];
@@ -286,6 +287,7 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
             }
         });
     if (!ok && lane == 0) atomicExch(status, QSML_E_TIMEOUT);
+    pdl_end(defer);
 }
 
 // Binary16 rows of 8-108 KiB and binary32 rows of 32-108 KiB: one CTA of TH
@@ -298,8 +300,8 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
 template <typename T, typename GT, int REG, int TH>
 __global__ void __launch_bounds__(TH) k_layer_norm_wide(const T* __restrict__ x, const GT* __restrict__ gamma,
                                                          const GT* __restrict__ beta, T* __restrict__ y,
-                                                         int64_t rows, int cols, float eps, int* status) {
-    pdl_begin();
+                                                         int64_t rows, int cols, float eps, int* status, int defer) {
+    pdl_start(defer);
     constexpr int PV = Pack<T>::N;
     float rg[REG > 0 ? REG : 1][PV], rb[REG > 0 ? REG : 1][PV];
     if constexpr (REG > 0) {
@@ -381,6 +383,7 @@ __global__ void __launch_bounds__(TH) k_layer_norm_wide(const T* __restrict__ x,
             }
         });
     if (!ok && t == 0) atomicExch(status, QSML_E_TIMEOUT);
+    pdl_end(defer);
 }
 
 template <typename T, typename GT>
@@ -440,6 +443,15 @@ __global__ void __launch_bounds__(256) k_layer_norm_generic(const T* __restrict_
     }
 }
 
+// What a layer-norm launch reads (x, gamma, beta) and writes (y), for overlap.
+template <typename T, typename GT>
+Footprint ln_footprint(const T* x, const GT* g, const GT* b, const T* y, int64_t rows, int cols) {
+    Footprint f;
+    const size_t n = static_cast<size_t>(rows) * cols * sizeof(T);
+    f.read(span_of(x, n)).read(span_of(g, cols * sizeof(GT))).read(span_of(b, cols * sizeof(GT))).write(span_of(y, n));
+    return f;
+}
+
 template <typename T, typename GT, int NV>
 qsml_status_t launch_reg(Context* ctx, const T* x, const GT* g, const GT* b, T* y, int64_t rows, int cols,
                          float eps, unsigned th) {
@@ -474,8 +486,9 @@ qsml_status_t launch_reg(Context* ctx, const T* x, const GT* g, const GT* b, T* 
     int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
     if (grid > rows) grid = rows;
     {
+        const int defer = plan_launch(ctx, ln_footprint(x, g, b, y, rows, cols));
         const cudaError_t e = launch_pdl(k_layer_norm_reg<T, GT, NV>, dim3(static_cast<unsigned>(grid)), dim3(th),
-                                         smem, ctx->stream, x, g, b, y, rows, cols, eps);
+                                         smem, ctx->stream, x, g, b, y, rows, cols, eps, defer);
         if (e != cudaSuccess) return check_cuda(ctx, e, "k_layer_norm_reg");
     }
     return after_launch(ctx, "k_layer_norm_reg");
@@ -498,8 +511,9 @@ qsml_status_t launch_pipe(Context* ctx, const T* x, const GT* g, const GT* b, T*
         }
     }
     {
+        const int defer = plan_launch(ctx, ln_footprint(x, g, b, y, rows, cols));
         const cudaError_t e = launch_pdl(k_layer_norm_pipe<T, GT>, dim3(p.grid), dim3(p.warps * 32), p.smem,
-                                         ctx->stream, x, g, b, y, rows, cols, eps, p.slots, ctx->status);
+                                         ctx->stream, x, g, b, y, rows, cols, eps, p.slots, ctx->status, defer);
         if (e != cudaSuccess) return check_cuda(ctx, e, "k_layer_norm_pipe");
     }
     return after_launch(ctx, "k_layer_norm_pipe");
@@ -538,8 +552,9 @@ qsml_status_t launch_wide_as(Context* ctx, const T* x, const GT* g, const GT* b,
     }
     int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
     if (grid > rows) grid = rows;
+    const int defer = plan_launch(ctx, ln_footprint(x, g, b, y, rows, cols));
     const cudaError_t e = launch_pdl(k_layer_norm_wide<T, GT, REG, TH>, dim3(static_cast<unsigned>(grid)), dim3(TH),
-                                     smem, ctx->stream, x, g, b, y, rows, cols, eps, ctx->status);
+                                     smem, ctx->stream, x, g, b, y, rows, cols, eps, ctx->status, defer);
     if (e != cudaSuccess) return check_cuda(ctx, e, "k_layer_norm_wide");
     return after_launch(ctx, "k_layer_norm_wide");
 }

@@ -110,8 +110,8 @@ __device__ __forceinline__ Pack<T> to_pack(const float* z) {
 // change roles without register copies.
 template <typename T, int NV>
 __global__ void __launch_bounds__(256) k_softmax_rows(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
-                                                      int cols) {
-    pdl_begin();
+                                                      int cols, int defer) {
+    pdl_start(defer);
     constexpr int PV = Pack<T>::N;
     constexpr int E = NV * PV;
     __shared__ float sh_max[8], sh_sum[8];
@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(256) k_softmax_rows(const T* __restrict__ x, T
         process(C, row);
         row += G;
     }
+    pdl_end(defer);
 }
 
 // Rows streamed through shared memory (row_pipe.cuh), one warp per row:
@@ -215,8 +216,8 @@ __device__ __forceinline__ float pack_max(const Pack<T>* xs, int packs, int lane
 
 template <typename T>
 __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
-    k_softmax_pipe(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int cols, int slots, int* status) {
-    pdl_begin();
+    k_softmax_pipe(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int cols, int slots, int* status, int defer) {
+    pdl_start(defer);
     constexpr int PV = Pack<T>::N;
     constexpr bool F32 = sizeof(T) == 4;
     extern __shared__ float4 sm_pipe_smem[];
@@ -261,6 +262,7 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
             }
         });
     if (!ok && lane == 0) atomicExch(status, QSML_E_TIMEOUT);
+    pdl_end(defer);
 }
 
 // Binary16 rows of 8-108 KiB and binary32 rows of 32-108 KiB: one CTA of TH
@@ -270,8 +272,8 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
 // 16-byte packs.
 template <typename T, int TH>
 __global__ void __launch_bounds__(TH) k_softmax_wide(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
-                                                      int cols, int* status) {
-    pdl_begin();
+                                                      int cols, int* status, int defer) {
+    pdl_start(defer);
     constexpr int PV = Pack<T>::N;
     constexpr bool F32 = sizeof(T) == 4;
     extern __shared__ float4 sm_wide_smem[];
@@ -315,6 +317,7 @@ __global__ void __launch_bounds__(TH) k_softmax_wide(const T* __restrict__ x, T*
             }
         });
     if (!ok && t == 0) atomicExch(status, QSML_E_TIMEOUT);
+    pdl_end(defer);
 }
 
 template <typename T>
@@ -449,6 +452,15 @@ qsml_status_t run_long_rows(Context* ctx, const T* x, T* y, int64_t rows, int64_
     return after_launch(ctx, "k_softmax_long_out");
 }
 
+// What a softmax launch reads (x) and writes (y), for overlap.
+template <typename T>
+Footprint sm_footprint(const T* x, const T* y, int64_t rows, int cols) {
+    Footprint f;
+    const size_t n = static_cast<size_t>(rows) * cols * sizeof(T);
+    f.read(span_of(x, n)).write(span_of(y, n));
+    return f;
+}
+
 template <typename T, int NV>
 qsml_status_t launch_rows(Context* ctx, const T* x, T* y, int64_t rows, int cols, unsigned th) {
     static std::mutex mu;
@@ -468,8 +480,9 @@ qsml_status_t launch_rows(Context* ctx, const T* x, T* y, int64_t rows, int cols
     int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
     if (grid > rows) grid = rows;
     {
+        const int defer = plan_launch(ctx, sm_footprint(x, y, rows, cols));
         const cudaError_t e = launch_pdl(k_softmax_rows<T, NV>, dim3(static_cast<unsigned>(grid)), dim3(th), 0,
-                                         ctx->stream, x, y, rows, cols);
+                                         ctx->stream, x, y, rows, cols, defer);
         if (e != cudaSuccess) return check_cuda(ctx, e, "k_softmax_rows");
     }
     return after_launch(ctx, "k_softmax_rows");
@@ -490,8 +503,9 @@ qsml_status_t launch_pipe(Context* ctx, const T* x, T* y, int64_t rows, int cols
         }
     }
     {
+        const int defer = plan_launch(ctx, sm_footprint(x, y, rows, cols));
         const cudaError_t e = launch_pdl(k_softmax_pipe<T>, dim3(p.grid), dim3(p.warps * 32), p.smem, ctx->stream, x,
-                                         y, rows, cols, p.slots, ctx->status);
+                                         y, rows, cols, p.slots, ctx->status, defer);
         if (e != cudaSuccess) return check_cuda(ctx, e, "k_softmax_pipe");
     }
     return after_launch(ctx, "k_softmax_pipe");
@@ -529,8 +543,9 @@ qsml_status_t launch_wide_as(Context* ctx, const T* x, T* y, int64_t rows, int c
     }
     int64_t grid = static_cast<int64_t>(ctx->num_sms) * per_sm;
     if (grid > rows) grid = rows;
+    const int defer = plan_launch(ctx, sm_footprint(x, y, rows, cols));
     const cudaError_t e = launch_pdl(k_softmax_wide<T, TH>, dim3(static_cast<unsigned>(grid)), dim3(TH), smem,
-                                     ctx->stream, x, y, rows, cols, ctx->status);
+                                     ctx->stream, x, y, rows, cols, ctx->status, defer);
     if (e != cudaSuccess) return check_cuda(ctx, e, "k_softmax_wide");
     return after_launch(ctx, "k_softmax_wide");
 }

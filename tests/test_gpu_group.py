@@ -95,6 +95,50 @@ def test_two_gpus_one_process():
             c.close()
 
 
+@pytest.mark.skipif(n_gpus() < 2, reason="needs two GPUs")
+def test_partials_in_one_group_bracket():
+    """The three partial combines of a sharded step (sum, max, min) issued
+    inside one group bracket, as bench.py does: max/min keys are decoded
+    after the bracket closes; results equal the binary32 sum and the IEEE
+    754-2019 maximum/minimum (NaN wins as 0x7fffffff, -0 < +0)."""
+    import torch
+    ctxs = [abi.Context(i, use_torch_stream=False) for i in range(2)]
+    g = abi.Group.init_all(ctxs)
+    try:
+        rng = np.random.default_rng(5)
+        vals = [rng.normal(0, 1, 4099).astype(np.float32) for _ in range(2)]
+        vals[0][:4] = [np.nan, -0.0, 0.0, 1.0]
+        vals[1][:4] = [2.0, 0.0, -0.0, np.nan]
+        bufs = {op: [torch.from_numpy(v.copy()).to(f"cuda:{i}") for i, v in enumerate(vals)]
+                for op in (abi.RED_SUM, abi.RED_MAX, abi.RED_MIN)}
+        for i in range(2):
+            torch.cuda.synchronize(i)
+        abi.group_start()
+        try:
+            for op, bs in bufs.items():
+                for i in range(2):
+                    g.allreduce_partials(i, op, bs[i].data_ptr(), bs[i].numel())
+        finally:
+            abi.group_end()
+        for c in ctxs:
+            c.synchronize()
+        nan = np.array([0x7fffffff], np.uint32).view(np.float32)[0]
+        want_max = np.maximum(vals[0], vals[1])
+        want_min = np.minimum(vals[0], vals[1])
+        for w in (want_max, want_min):
+            w[np.isnan(w)] = nan
+        want_max[1:3] = [0.0, 0.0]
+        want_min[1:3] = [-0.0, -0.0]
+        for i in range(2):
+            np.testing.assert_array_equal(bufs[abi.RED_SUM][i].cpu().numpy(), vals[0] + vals[1])
+            assert np.array_equal(bufs[abi.RED_MAX][i].cpu().numpy().view(np.uint32), want_max.view(np.uint32))
+            assert np.array_equal(bufs[abi.RED_MIN][i].cpu().numpy().view(np.uint32), want_min.view(np.uint32))
+    finally:
+        g.destroy()
+        for c in ctxs:
+            c.close()
+
+
 def _rank_main(rank, uid, q):
     import torch
     sys.path.insert(0, ROOT)

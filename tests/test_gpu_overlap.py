@@ -226,3 +226,49 @@ def test_arg_reductions_overlap_same_indices():
     assert (p, dd) == (8, 6)
     for g, w in zip([host(o) for o in outs], want):
         assert np.array_equal(g, w)
+
+
+def test_row_ops_and_gathers_overlap_same_bits():
+    """Layer norm, softmax and gathers of distinct tensors overlap like the
+    reductions, with the same bits as without overlap."""
+    import torch
+    X32 = dev(datagen.normal(110, (16384, 4096), 0.5, 2.0))
+    X16 = dev(datagen.normal(111, (16384, 4096), 0.5, 2.0).astype(np.float16))
+    g = dev(datagen.normal(112, (4096,), 1.0, 0.1))
+    b = dev(datagen.normal(113, (4096,), 0.0, 0.1))
+    G = dev(datagen.uniform(114, (8192, 8192), -1, 1))
+    v1 = abi.make_desc(G.data_ptr() + (5 * 8192 + 1) * 4, abi.F32, (2729, 4096), (3 * 8192, 2))
+    v2 = abi.make_desc(G.data_ptr(), abi.F32, (2048, 8192), (4, 8192))
+    outs = [torch.empty_like(X32), torch.empty_like(X16), torch.empty_like(X32), torch.empty_like(X16),
+            torch.empty((2729, 4096), device="cuda"), torch.empty((2048, 8192), device="cuda")]
+
+    def burst(ctx):
+        names = []
+        ctx.layer_norm(d(X32), d(g), d(b), 1e-5, d(outs[0]))
+        names.append(ctx.last_kernel())
+        ctx.layer_norm(d(X16), d(g), d(b), 1e-5, d(outs[1]))
+        names.append(ctx.last_kernel())
+        ctx.softmax(d(X32), -1, d(outs[2]))
+        names.append(ctx.last_kernel())
+        ctx.softmax(d(X16), -1, d(outs[3]))
+        names.append(ctx.last_kernel())
+        ctx.gather(v1, d(outs[4]))
+        names.append(ctx.last_kernel())
+        ctx.gather(v2, d(outs[5]))
+        names.append(ctx.last_kernel())
+        return names
+
+    ref = abi.Context(0)
+    burst(ref)
+    torch.cuda.synchronize()
+    want = [host(o).copy() for o in outs]
+    for o in outs:
+        o.zero_()
+    ctx = abi.Context(0)
+    ctx.set_overlap(True)
+    names = burst(ctx)
+    torch.cuda.synchronize()
+    p, dd = ctx.overlap_stats()
+    assert (p, dd) == (6, 5), names
+    for gg, w, k in zip([host(o) for o in outs], want, names):
+        assert np.array_equal(gg.view(np.uint8), w.view(np.uint8)), k
