@@ -163,7 +163,8 @@ QSML_API qsml_status_t qsml_set_wait_limit(qsml_ctx* ctx, int64_t cycles);
 
 /* Overlap of independent calls on the context's stream (off by default).
  * With enable = 1, a memory-bound call (qsml_reduce, qsml_arg_reduce,
- * qsml_layer_norm, qsml_softmax, qsml_gather) whose inputs, outputs and
+ * qsml_layer_norm, qsml_softmax, qsml_gather, and qsml_elementwise_fused
+ * when it runs a runtime-compiled kernel) whose inputs, outputs and
  * scratch share no byte with the library kernels that may still be running
  * on the stream starts reading at once instead of waiting for them to
  * finish; it waits for them only at its end, so kernels still complete in

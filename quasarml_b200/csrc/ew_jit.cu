@@ -146,10 +146,12 @@ std::string generate(const qsml_fuse_node* nodes, int n, const JitInput* ins, in
     if (half) s << kHalfHelpers;
     s << "extern \"C\" __global__ void __launch_bounds__(" << kJitThreads << ") qsml_fused_kernel(";
     for (int j = 0; j < nin; ++j) s << "const " << T << "* __restrict__ p" << j << ", long long r" << j << ", ";
-    s << T << "* __restrict__ out, unsigned items, unsigned cpr, unsigned magic, unsigned sh1, unsigned sh2) {\n";
-    // programmatic dependent launch: wait for the previous kernel on the stream
-    // before touching memory, then let the next one launch
-    s << "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
+    s << T << "* __restrict__ out, unsigned items, unsigned cpr, unsigned magic, unsigned sh1, unsigned sh2, "
+         "int defer) {\n";
+    // programmatic dependent launch: wait for the previous kernel on the
+    // stream before touching memory (at the end instead when the launch
+    // overlaps it, see plan_launch), then let the next one launch
+    s << "  if (!defer) asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n";
     s << "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n";
     s << "  const int V = " << V << ", U = " << U << ";\n";
     s << "  const unsigned base = blockIdx.x * (" << kJitThreads << "u * U) + threadIdx.x;\n";
@@ -213,7 +215,8 @@ std::string generate(const qsml_fuse_node* nodes, int n, const JitInput* ins, in
         s << "    uint4 w = make_uint4(__float_as_uint(y[u * V + 0]), __float_as_uint(y[u * V + 1]), "
              "__float_as_uint(y[u * V + 2]), __float_as_uint(y[u * V + 3]));\n";
     }
-    s << "    *reinterpret_cast<uint4*>(out + (long long)its[u] * V) = w;\n  }\n}\n";
+    s << "    *reinterpret_cast<uint4*>(out + (long long)its[u] * V) = w;\n  }\n";
+    s << "  if (defer) asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n}\n";
     return s.str();
 }
 
@@ -321,6 +324,16 @@ qsml_status_t fused_jit(Context* ctx, const qsml_fuse_node* nodes, int n_nodes, 
     args.push_back(&sh2);
     const int per_block = kJitThreads * (kJitElems / (half ? 8 : 4));
     const int64_t blocks = (items + per_block - 1) / per_block;
+    // what the launch reads and writes, for overlap with the kernels before it
+    const size_t es = half ? 2 : 4;
+    const int64_t rows = items / cpr;
+    Footprint fp;
+    for (int j = 0; j < nin; ++j)
+        fp.read(span_of(ins[j].ptr, static_cast<size_t>((rows - 1) * ins[j].row_stride +
+                                                        (ins[j].vec ? cpr * (half ? 8 : 4) : 1)) * es));
+    fp.write(span_of(out, static_cast<size_t>(items) * (half ? 8 : 4) * es));
+    int defer = r.launch_ex ? plan_launch(ctx, fp) : 0;
+    args.push_back(&defer);
     CUresult lr;
     if (r.launch_ex) {
         CUlaunchAttribute attr[1];
@@ -342,12 +355,13 @@ qsml_status_t fused_jit(Context* ctx, const qsml_fuse_node* nodes, int n_nodes, 
         lr = r.launch(fn, static_cast<unsigned>(blocks), 1, 1, kJitThreads, 1, 1, 0,
                       reinterpret_cast<CUstream>(ctx->stream), args.data(), nullptr);
     }
-    ctx->launches++;
-    ctx->last_kernel = "qsml_fused_kernel";
-    if (lr != CUDA_SUCCESS)
+    if (lr != CUDA_SUCCESS) {
+        ctx->planned_for = 0;
+        end_window(ctx->stream);
         return set_error(ctx, QSML_E_CUDA, "launch of the fused kernel failed (CUresult " + std::to_string(lr) + ")");
+    }
     *ran = true;
-    return QSML_OK;
+    return after_launch(ctx, "qsml_fused_kernel");
 }
 
 }  // namespace qsml

@@ -272,3 +272,48 @@ def test_row_ops_and_gathers_overlap_same_bits():
     assert (p, dd) == (6, 5), names
     for gg, w, k in zip([host(o) for o in outs], want, names):
         assert np.array_equal(gg.view(np.uint8), w.view(np.uint8)), k
+
+
+def test_fused_kernels_overlap_and_readers_wait():
+    """Runtime-compiled fused kernels of distinct batch entries overlap; a
+    reduction of a fused kernel's output waits for it (read-after-write)."""
+    import torch
+    A = [dev(datagen.uniform(120 + i, (4096, 4096), -1.0, 1.0)) for i in range(4)]
+    B = dev(datagen.uniform(125, (1, 4096), -1.0, 1.0))
+    D = dev(datagen.uniform(126, (4096, 1), 0.5, 2.0))
+    outs = [empty((4096, 4096), np.float32) for _ in A]
+    sums = [empty((4096,), np.float32) for _ in A]
+    e = abi.Expr()
+    a, b, dd = e.input(0), e.input(1), e.input(2)
+    t = e.binary(abi.OP_SUB, e.binary(abi.OP_MUL, e.binary(abi.OP_ADD, a, b), b), a)
+    e.unary(abi.UN_RELU, e.binary(abi.OP_DIV, e.binary(abi.OP_POW, t, e.const(2.0)), dd))
+
+    def run(ctx, with_sums):
+        for i in range(4):
+            ctx.elementwise_fused(e.nodes, [d(A[i]), d(B), d(D)], d(outs[i]))
+            if with_sums:
+                ctx.reduce(abi.RED_SUM, d(outs[i]), 1, False, d(sums[i]))
+
+    ref = abi.Context(0)
+    ref.set_fuse_mode(abi.FUSE_MODE_JIT)
+    run(ref, True)
+    torch.cuda.synchronize()
+    want = [host(o).copy() for o in outs]
+    want_s = [host(s).copy() for s in sums]
+    for o in outs + sums:
+        o.zero_()
+    ctx = abi.Context(0)
+    ctx.set_fuse_mode(abi.FUSE_MODE_JIT)
+    ctx.set_overlap(True)
+    run(ctx, False)  # four independent fused kernels
+    torch.cuda.synchronize()
+    p, dd0 = ctx.overlap_stats()
+    assert (p, dd0) == (4, 3)
+    for o in outs:
+        o.zero_()
+    run(ctx, True)  # each reduction reads the fused kernel just before it
+    torch.cuda.synchronize()
+    for g, w in zip([host(o) for o in outs], want):
+        assert np.array_equal(g.view(np.uint32), w.view(np.uint32))
+    for g, w in zip([host(s) for s in sums], want_s):
+        assert np.array_equal(g.view(np.uint32), w.view(np.uint32))
