@@ -762,7 +762,7 @@ def _launches(wl) -> int:
     return n
 
 
-def time_steps(wl, dist: Dist, stream, steps: int, warmup: int, sampler=None, use_graph=True):
+def time_steps(wl, dist: Dist, stream, steps: int, warmup: int, sampler=None, use_graph=True, timeline=None):
     """Times `steps` steps on `stream` with CUDA events; returns the max over
     ranks (ms), the kernel launches in the timed steps and the graph(s).
 
@@ -770,7 +770,11 @@ def time_steps(wl, dist: Dist, stream, steps: int, warmup: int, sampler=None, us
     with an exchange (ReduceWorkload under sharding) replays two graphs --
     the partials of the exchanged reductions, then the local reductions --
     with the combine started between them on its own stream and the
-    finishing calls issued after it."""
+    finishing calls issued after it.  With a `timeline` dict (sharded
+    workloads), it also receives rank 0's median per-step times (ms from the
+    step's start) at which the partials, the combines, the local reductions
+    and the finishing calls ended (CUDA events; the events themselves sit
+    between the graphs and do not change the work)."""
     import torch
     with torch.cuda.stream(stream):
         for _ in range(warmup):
@@ -794,12 +798,25 @@ def time_steps(wl, dist: Dist, stream, steps: int, warmup: int, sampler=None, us
         if sampler:
             sampler.__enter__()
         start.record(stream)
+        marks = []
         for _ in range(steps):
             if split:
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)] if timeline is not None else None
+                if ev:
+                    ev[0].record(stream)
                 g[0].replay()
+                if ev:
+                    ev[1].record(stream)
                 done = wl.exchange_start()
+                if ev:
+                    ev[2].record(wl.xstream)
                 g[1].replay()
+                if ev:
+                    ev[3].record(stream)
                 wl.exchange_finish(done)
+                if ev:
+                    ev[4].record(stream)
+                    marks.append(ev)
             elif g is not None:
                 g.replay()
                 wl.exchange()
@@ -810,6 +827,11 @@ def time_steps(wl, dist: Dist, stream, steps: int, warmup: int, sampler=None, us
         if sampler:
             sampler.__exit__()
     ms = start.elapsed_time(end)
+    if marks and timeline is not None:
+        rows = [[e[0].elapsed_time(x) for x in e[1:]] for e in marks]
+        med = [sorted(r[i] for r in rows)[len(rows) // 2] for i in range(4)]
+        timeline.update({k: round(v, 3) for k, v in zip(
+            ("partials_end_ms", "combines_end_ms", "local_end_ms", "finish_end_ms"), med)})
     dist.barrier()
     return dist.max(ms), per_step * steps, g
 
@@ -1107,6 +1129,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="reduce",
                     choices=["reduce", "chain", "gather", "layernorm", "matmul_f16", "matmul_f32"])
+    ap.add_argument("--timeline", action="store_true",
+                    help="sharded runs: add rank 0's median per-step timeline (partials, combines, local, finish)")
     ap.add_argument("--no-overlap", action="store_true",
                     help="reductions wait for the previous kernel at their start (qsml_set_overlap off)")
     ap.add_argument("--single", default=None,
@@ -1154,7 +1178,8 @@ def main():
           "matmul_f32": lambda: MatmulWorkload(ctx, dist, "f32", False)}[args.workload]()
 
     sampler = ClockSampler(dist.local)
-    ms, launches, graph = time_steps(wl, dist, stream, args.steps, args.warmup, sampler=sampler)
+    timeline = {} if args.timeline else None
+    ms, launches, graph = time_steps(wl, dist, stream, args.steps, args.warmup, sampler=sampler, timeline=timeline)
     del graph
     units = wl.units_per_step * args.steps * dist.world
     value = units / (ms / 1e3) / (1e9 if wl.unit == "GB/s" else 1e12)
@@ -1184,6 +1209,8 @@ def main():
         line["roofline"] = roofline_from_families(family_times(wl, stream), hbm, peak_kind)
         if sharded:
             line["exchange"] = exchange_alone(wl, dist, stream)
+            if timeline:
+                line["exchange"]["timeline_rank0"] = timeline
     if hasattr(wl, "e2e_step"):
         e_steps = max(2, min(args.steps, 5))
         ems = time_e2e(wl, dist, stream, e_steps, 1)
