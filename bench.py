@@ -707,7 +707,7 @@ class MatmulWorkload(Workload):
     sharded)."""
 
     def __init__(self, ctx, dist: Dist, dtype: str, batched: bool, fp32_precision: str = "3xtf32",
-                 scale: str = "weak"):
+                 scale: str = "weak", out16: bool = False):
         import torch
         from quasarml_b200 import abi, datagen
         self.ctx, self.abi = ctx, abi
@@ -716,7 +716,7 @@ class MatmulWorkload(Workload):
             e0, E, _ = row_block(32, dist, scale)
             A = _t(datagen.uniform(datagen.SEEDS["mm_Ab"], (E, 2048, 1024), -s, s, offset=e0 * 2048 * 1024))
             B = _t(datagen.uniform(datagen.SEEDS["mm_Bb"], (E, 1024, 2048), -s, s, offset=e0 * 1024 * 2048))
-            C = torch.empty((E, 2048, 2048), device="cuda")
+            C = torch.empty((E, 2048, 2048), device="cuda", dtype=torch.float16 if out16 else torch.float32)
             self.flops = 2.0 * E * 2048 * 2048 * 1024
             self.name = f"batched matmul [32,2048,1024]x[32,1024,2048] {dtype}"
         else:
@@ -724,12 +724,14 @@ class MatmulWorkload(Workload):
             r0, R, _ = row_block(8192, dist, scale)
             A = _t(datagen.uniform(datagen.SEEDS["mm_A"], (R, 8192), -s, s, offset=r0 * 8192))
             B = _t(datagen.uniform(datagen.SEEDS["mm_B"], (8192, 8192), -s, s))
-            C = torch.empty((R, 8192), device="cuda")
+            C = torch.empty((R, 8192), device="cuda", dtype=torch.float16 if out16 else torch.float32)
             self.flops = 2.0 * R * 8192 * 8192
             self.name = f"matmul 8192x8192x8192 {dtype}"
         if dtype == "f16":
             A, B = A.half(), B.half()
             self.prec = abi.MM_FP16_F32ACC
+            self.name += (" (fp32 accumulate, fp16 out: the input dtype, as the drop-in batch_matmul returns)"
+                          if out16 else " (fp32 accumulate, fp32 out)")
         else:
             self.prec = abi.MM_FP32_3XTF32 if fp32_precision == "3xtf32" else abi.MM_FP32_FFMA
             self.name += f" ({fp32_precision})"
@@ -1307,6 +1309,7 @@ EXTRAS = (("elementwise_chain", lambda c, d, s: ChainWorkload(c, d, scale=s), 10
           ("matmul_f32_8192_3xtf32", lambda c, d, s: MatmulWorkload(c, d, "f32", False, scale=s), 5),
           ("matmul_f32_8192_ffma", lambda c, d, s: MatmulWorkload(c, d, "f32", False, "ffma", scale=s), 3),
           ("batched_matmul_f16", lambda c, d, s: MatmulWorkload(c, d, "f16", True, scale=s), 5),
+          ("batched_matmul_f16_out16", lambda c, d, s: MatmulWorkload(c, d, "f16", True, scale=s, out16=True), 5),
           ("batched_matmul_f32_3xtf32", lambda c, d, s: MatmulWorkload(c, d, "f32", True, scale=s), 5))
 
 
