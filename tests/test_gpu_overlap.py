@@ -317,3 +317,88 @@ def test_fused_kernels_overlap_and_readers_wait():
         assert np.array_equal(g.view(np.uint32), w.view(np.uint32))
     for g, w in zip([host(s) for s in sums], want_s):
         assert np.array_equal(g.view(np.uint32), w.view(np.uint32))
+
+
+def _random_program(seed, nops):
+    """A seeded sequence of ops over a pool of 6 buffers of [1024, 1024]
+    binary32, each op reading and writing 256-row blocks (or whole buffers)
+    chosen at random, so that reads-after-writes, writes-after-reads and
+    writes-after-writes between consecutive and nearby ops are frequent."""
+    rng = np.random.default_rng(seed)
+    prog = []
+    for _ in range(nops):
+        kind = rng.choice(["red_rows", "red_cols", "red_all", "arg_rows", "gather_t", "layer_norm", "softmax",
+                           "add", "fused"])
+        src, dst = int(rng.integers(6)), int(rng.integers(6))
+        qs, qd = int(rng.integers(4)), int(rng.integers(4))
+        if kind in ("gather_t", "red_rows", "red_cols", "red_all", "arg_rows") and src == dst:
+            dst = (dst + 1) % 6  # no kernel writes into what it reads
+        if kind in ("layer_norm", "softmax", "fused", "add") and src == dst and qs == qd:
+            qd = (qd + 1) % 4
+        prog.append((str(kind), src, dst, qs, qd, int(rng.integers(6)), int(rng.integers(2))))
+    return prog
+
+
+def _run_program(ctx, pool, g, b, prog):
+    import torch
+    R, C = 256, 1024
+    blk = R * C
+
+    def view(i, q, rows=R):
+        return abi.make_desc(pool[i].data_ptr() + q * blk * 4, abi.F32, (rows, C), (C, 1))
+
+    e = abi.Expr()
+    x0, x1 = e.input(0), e.input(1)
+    e.binary(abi.OP_ADD, e.binary(abi.OP_MUL, x0, e.const(0.5)), e.unary(abi.UN_RELU, x1))
+    for kind, src, dst, qs, qd, other, opbit in prog:
+        op = abi.RED_MAX if opbit else abi.RED_MEAN
+        if kind == "red_rows":
+            out = abi.make_desc(pool[dst].data_ptr() + qd * blk * 4, abi.F32, (R,), (1,))
+            ctx.reduce(op, view(src, qs), 1, False, out)
+        elif kind == "red_cols":
+            out = abi.make_desc(pool[dst].data_ptr() + qd * blk * 4, abi.F32, (C,), (1,))
+            ctx.reduce(op, view(src, qs), 0, False, out)
+        elif kind == "red_all":
+            out = abi.make_desc(pool[dst].data_ptr() + (qd * blk + 7) * 4, abi.F32, (1,), (1,))
+            ctx.reduce(op, abi.make_desc(pool[src].data_ptr(), abi.F32, (1024, C), (C, 1)), abi.AXIS_ALL, False, out)
+        elif kind == "arg_rows":
+            out = abi.make_desc(pool[dst].data_ptr() + qd * blk * 4, abi.I32, (R,), (1,))
+            ctx.arg_reduce(abi.ARG_MAX if opbit else abi.ARG_MIN, view(src, qs), 1, False, out)
+            # the indices land as floats' bits: small integers, harmless inputs
+        elif kind == "gather_t":
+            t = abi.make_desc(pool[src].data_ptr(), abi.F32, (1024, C), (1, C))
+            ctx.gather(t, abi.make_desc(pool[dst].data_ptr(), abi.F32, (1024, C), (C, 1)))
+        elif kind == "layer_norm":
+            ctx.layer_norm(view(src, qs), d(g), d(b), 1e-5, view(dst, qd))
+        elif kind == "softmax":
+            ctx.softmax(view(src, qs), -1, view(dst, qd))
+        elif kind == "add":
+            ctx.binary(abi.OP_ADD, view(src, qs), view(other, (qs + 1) % 4), view(dst, qd))
+        else:
+            ctx.elementwise_fused(e.nodes, [view(src, qs), view(other, qd)], view(dst, (qd + 2) % 4))
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_random_programs_same_bits_with_overlap(seed):
+    """Seeded random programs of reductions, arg-reductions, gathers, layer
+    norms, softmaxes, adds and fused expressions over a small pool of
+    buffers, so that dependent and independent neighbours mix: with overlap
+    on, every buffer ends bit-identical to the run without it."""
+    import torch
+    init = [datagen.uniform(200 + i, (1024, 1024), -1.0, 1.0) for i in range(6)]
+    g = dev(datagen.normal(210, (1024,), 1.0, 0.1))
+    b = dev(datagen.normal(211, (1024,), 0.0, 0.1))
+    prog = _random_program(seed, 300)
+    results = []
+    for overlap in (False, True):
+        pool = [dev(x) for x in init]
+        ctx = abi.Context(0)
+        ctx.set_overlap(overlap)
+        _run_program(ctx, pool, g, b, prog)
+        results.append([host(p).copy() for p in pool])
+        if overlap:
+            planned, deferred = ctx.overlap_stats()
+            assert deferred > 0, (planned, deferred)
+    for i, (r0, r1) in enumerate(zip(*results)):
+        assert np.array_equal(r0.view(np.uint32), r1.view(np.uint32)), f"buffer {i}"
