@@ -163,7 +163,8 @@ QSML_API qsml_status_t qsml_set_wait_limit(qsml_ctx* ctx, int64_t cycles);
 
 /* Overlap of independent calls on the context's stream (off by default).
  * With enable = 1, a memory-bound call (qsml_reduce, qsml_arg_reduce,
- * qsml_layer_norm, qsml_softmax, qsml_gather, and qsml_elementwise_fused
+ * qsml_layer_norm, qsml_softmax, qsml_gather, qsml_binary, qsml_unary,
+ * qsml_binary_scalar on vectorisable layouts, and qsml_elementwise_fused
  * when it runs a runtime-compiled kernel) whose inputs, outputs and
  * scratch share no byte with the library kernels that may still be running
  * on the stream starts reading at once instead of waiting for them to

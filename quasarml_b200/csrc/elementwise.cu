@@ -42,8 +42,9 @@ __device__ __forceinline__ C apply(const Op& op, C a, C b) {
 // Row kernel: out is [R, Cn] with Cn % VEC == 0; each input's inner stride is
 // 0 (one value per row, splatted) or 1 (16-byte vectors).
 template <typename T, int NIN, typename Op, typename IDX>
-__global__ void __launch_bounds__(kThreads) k_ew_rows(Ptrs<T, NIN> P, EwPlan plan, IDX items, IDX cpr, Op op) {
-    pdl_begin();
+__global__ void __launch_bounds__(kThreads) k_ew_rows(Ptrs<T, NIN> P, EwPlan plan, IDX items, IDX cpr, Op op,
+                                                      int defer) {
+    pdl_start(defer);
     using E = Elem<T>;
     using CT = typename E::C;
     constexpr int V = Pack<T>::N;
@@ -83,12 +84,13 @@ __global__ void __launch_bounds__(kThreads) k_ew_rows(Ptrs<T, NIN> P, EwPlan pla
         }
         reinterpret_cast<Pack<T>*>(P.out)[outoff[u]] = o;
     }
+    pdl_end(defer);
 }
 
 // 1-D contiguous (or scalar-broadcast) operands: vector body + scalar tail.
 template <typename T, int NIN, typename Op, bool VEC>
-__global__ void __launch_bounds__(kThreads) k_ew_flat(Ptrs<T, NIN> P, EwPlan plan, int64_t n, Op op) {
-    pdl_begin();
+__global__ void __launch_bounds__(kThreads) k_ew_flat(Ptrs<T, NIN> P, EwPlan plan, int64_t n, Op op, int defer) {
+    pdl_start(defer);
     using E = Elem<T>;
     using CT = typename E::C;
     constexpr int V = VEC ? Pack<T>::N : 1;
@@ -151,6 +153,7 @@ __global__ void __launch_bounds__(kThreads) k_ew_flat(Ptrs<T, NIN> P, EwPlan pla
             P.out[i] = E::st(apply<CT, NIN>(op, a, b));
         }
     }
+    pdl_end(defer);
 }
 
 // Any strides, one element per thread (grid-stride).
@@ -177,6 +180,14 @@ __global__ void __launch_bounds__(kThreads) k_ew_generic(Ptrs<T, NIN> P, EwPlan 
 // Host planning
 // ---------------------------------------------------------------------------
 
+// What an elementwise launch reads (its inputs' spans) and writes, for overlap.
+inline Footprint ew_footprint(const qsml_tdesc* const* ins, int nin, const qsml_tdesc* out) {
+    Footprint f;
+    for (int j = 0; j < nin; ++j) f.read(view_span(ins[j]));
+    f.write(view_span(out));
+    return f;
+}
+
 template <typename T, int NIN, typename Op>
 qsml_status_t launch_ew(Context* ctx, const EwPlan& p, const qsml_tdesc* const* ins, const qsml_tdesc* out, Op op) {
     constexpr int V = Pack<T>::N;
@@ -201,15 +212,17 @@ qsml_status_t launch_ew(Context* ctx, const EwPlan& p, const qsml_tdesc* const* 
             int64_t blocks = (npk + kThreads * kUnroll - 1) / (kThreads * kUnroll);
             if (blocks < 1) blocks = 1;
             {
+                const int defer = plan_launch(ctx, ew_footprint(ins, NIN, out));
                 const cudaError_t e = launch_pdl(k_ew_flat<T, NIN, Op, true>, dim3(static_cast<unsigned>(blocks)),
-                                                 dim3(kThreads), 0, ctx->stream, P, p, n, op);
+                                                 dim3(kThreads), 0, ctx->stream, P, p, n, op, defer);
                 if (e != cudaSuccess) return check_cuda(ctx, e, "k_ew_flat");
             }
         } else {
             int64_t blocks = (n + kThreads * kUnroll - 1) / (kThreads * kUnroll);
             {
+                const int defer = plan_launch(ctx, ew_footprint(ins, NIN, out));
                 const cudaError_t e = launch_pdl(k_ew_flat<T, NIN, Op, false>, dim3(static_cast<unsigned>(blocks)),
-                                                 dim3(kThreads), 0, ctx->stream, P, p, n, op);
+                                                 dim3(kThreads), 0, ctx->stream, P, p, n, op, defer);
                 if (e != cudaSuccess) return check_cuda(ctx, e, "k_ew_flat");
             }
         }
@@ -233,17 +246,19 @@ qsml_status_t launch_ew(Context* ctx, const EwPlan& p, const qsml_tdesc* const* 
                 if (p.shape[d] >= (int64_t(1) << 31)) small = false;
             if (small) {
                 {
+                    const int defer = plan_launch(ctx, ew_footprint(ins, NIN, out));
                     const cudaError_t e = launch_pdl(k_ew_rows<T, NIN, Op, uint32_t>,
                                                      dim3(static_cast<unsigned>(blocks)), dim3(kThreads), 0,
                                                      ctx->stream, P, p, static_cast<uint32_t>(items),
-                                                     static_cast<uint32_t>(cpr), op);
+                                                     static_cast<uint32_t>(cpr), op, defer);
                     if (e != cudaSuccess) return check_cuda(ctx, e, "k_ew_rows");
                 }
             } else {
                 {
+                    const int defer = plan_launch(ctx, ew_footprint(ins, NIN, out));
                     const cudaError_t e = launch_pdl(k_ew_rows<T, NIN, Op, int64_t>,
                                                      dim3(static_cast<unsigned>(blocks)), dim3(kThreads), 0,
-                                                     ctx->stream, P, p, items, cpr, op);
+                                                     ctx->stream, P, p, items, cpr, op, defer);
                     if (e != cudaSuccess) return check_cuda(ctx, e, "k_ew_rows");
                 }
             }

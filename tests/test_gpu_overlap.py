@@ -154,8 +154,10 @@ def test_dependent_reductions_wait():
 
 
 def test_other_kernels_close_the_window():
-    """An elementwise kernel between two reductions is not tracked: the
-    reduction after it waits, and reads what it wrote."""
+    """A kernel that does not plan its launch (here qsml_fill) between two
+    reductions closes the window: the reduction after it waits, and reads
+    what it wrote.  An elementwise op plans its own launch: it overlaps an
+    independent reduction before it, and a reduction of its output waits."""
     import torch
     ctx = abi.Context(0)
     ctx.set_overlap(True)
@@ -165,14 +167,24 @@ def test_other_kernels_close_the_window():
     first = empty((2048,), np.float32)
     for i in range(5):
         ctx.reduce(abi.RED_SUM, d(b), 1, False, d(first))
+        ctx.fill(a.data_ptr(), np.float32(i + 1).tobytes(), a.numel())
         _, d0 = ctx.overlap_stats()
-        ctx.binary_scalar(abi.OP_ADD, d(a), float(i + 1), d(a))  # a += i + 1
         ctx.reduce(abi.RED_SUM, d(a), 1, False, d(s))
         _, d1 = ctx.overlap_stats()
         assert d1 == d0
     torch.cuda.synchronize()
-    a0 = datagen.normal(83, (2048, 4096), 0.0, 1.0).astype(np.float64) + 15.0
-    assert np.all(np.abs(host(s) - a0.sum(axis=1)) <= 1e-5 * np.abs(a0).sum(axis=1))
+    assert np.all(host(s) == 5.0 * 4096)
+    es = [torch.zeros((2048, 4096), device="cuda") for _ in range(5)]
+    for e in es:
+        ctx.reduce(abi.RED_SUM, d(b), 1, False, d(first))
+        _, d0 = ctx.overlap_stats()
+        ctx.binary_scalar(abi.OP_ADD, d(e), 1.0, d(e))  # e += 1: nothing in flight touches e
+        _, d1 = ctx.overlap_stats()
+        ctx.reduce(abi.RED_SUM, d(e), 1, False, d(s))  # reads e: waits
+        _, d2 = ctx.overlap_stats()
+        assert (d1 - d0, d2 - d1) == (1, 0)
+    torch.cuda.synchronize()
+    assert np.all(host(s) == 4096.0)
 
 
 def test_long_burst_is_capped():
