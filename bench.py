@@ -886,7 +886,29 @@ def time_e2e(wl, dist: Dist, stream, steps: int, warmup: int):
     return dist.max(start.elapsed_time(end))
 
 
-def roofline_from_families(fam, hbm_peak, peak_kind):
+def read_only_reference(stream, reps: int = 10) -> dict:
+    """A read-only HBM stream for comparison with the copy peak: torch's sum
+    over 2 GiB of binary32 (a library kernel, not this project's), CUDA
+    events around `reps` launches after warm-up."""
+    import torch
+    x = torch.ones(1 << 29, device="cuda")
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            x.sum()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            x.sum()
+        b.record(stream)
+        torch.cuda.synchronize()
+    gbs = x.numel() * 4 * reps / (a.elapsed_time(b) / 1e3) / 1e9
+    del x
+    torch.cuda.empty_cache()
+    return {"gbs": round(gbs, 1), "how": "torch.sum over 2 GiB fp32 (reads only), CUDA events, 10 launches"}
+
+
+def roofline_from_families(fam, hbm_peak, peak_kind, read_ref=None):
     total = sum(f["ms"] for f in fam.values())
     dom = max(fam, key=lambda k: fam[k]["ms"])
     f = fam[dom]
@@ -905,6 +927,8 @@ def roofline_from_families(fam, hbm_peak, peak_kind):
             "avg_launch_us": round(per_launch_ms * 1e3, 2),
             "share_of_step": round(f["ms"] / total, 3),
             "timing": "CUDA events around replays of a graph holding one step's launches of this kernel",
+            "read_only_reference": read_ref,
+            "frac_of_read_only": round(achieved / read_ref["gbs"], 4) if read_ref else None,
             "families": {k: {"share": round(v["ms"] / total, 3),
                              "gbs": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1),
                              "frac": round(v["bytes"] / (v["ms"] / 1e3) / 1e9 / hbm_peak, 4),
@@ -1208,7 +1232,8 @@ def main():
                                  "qsml_set_overlap(ctx, 1): a reduction sharing no buffer with the library kernels "
                                  "still running on the stream starts at once and waits for them at its end")
     if args.workload == "reduce":
-        line["roofline"] = roofline_from_families(family_times(wl, stream), hbm, peak_kind)
+        line["roofline"] = roofline_from_families(family_times(wl, stream), hbm, peak_kind,
+                                                  read_only_reference(stream))
         if sharded:
             line["exchange"] = exchange_alone(wl, dist, stream)
             if timeline:

@@ -131,9 +131,8 @@ int main() {
             for (double o : outs) bytes += 4 * 8 * (n * es + o * es);
         std::vector<TensorPtr> results;  // the step's results, kept until the next step
         results.reserve(256);
-        qsml::set_overlap(true);
         report("reductions", "reductions X[64,512,1024] fp32 and fp16: sum/mean/max/min over axis 0, 1, 2 and all "
-               "(256 qsml:: calls, qsml::set_overlap(true))",
+               "(256 qsml:: calls)",
                bytes, "GB/s", 2, 10, [&] {
                    results.clear();
                    for (auto* xs : {&X32, &X16}) {
@@ -157,7 +156,6 @@ int main() {
                        }
                    }
                });
-        qsml::set_overlap(false);
         results.clear();
     }
 

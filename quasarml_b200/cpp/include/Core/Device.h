@@ -36,9 +36,11 @@ public:
     // results that evaluate as one fused kernel on first access.
     void set_fusion(bool on);
     bool fusion() const { return _fusion; }
-    // Overlap of independent reductions, layer norms, softmaxes and gathers
-    // on the device's stream (a call sharing no buffer with the kernels still
-    // running before it starts at once; qsml_set_overlap).  Off by default.
+    // Overlap of independent reductions, layer norms, softmaxes, gathers and
+    // elementwise ops on the device's stream (a call sharing no buffer with
+    // the kernels still running before it starts at once; qsml_set_overlap).
+    // On by default (the stream is the library's own; QSML_OVERLAP=0 at
+    // start-up, or set_overlap(false), turns it off).
     void set_overlap(bool on);
     bool defer_elementwise() const { return _fusion || _in_batch; }
 

@@ -204,7 +204,7 @@ inline std::vector<TensorPtr> sharded_reduce(const std::vector<TensorPtr>& block
 inline void set_fusion(bool on) { device().set_fusion(on); }
 inline bool fusion_enabled() { return device().fusion(); }
 
-// Overlap of independent reductions on the device's stream (off by default).
+// Overlap of independent calls on the device's stream (on by default).
 inline void set_overlap(bool on) { device().set_overlap(on); }
 
 inline u64 cpu_fallback_count() {

@@ -331,6 +331,11 @@ Device::Device(const std::string& name, u32 device_index)
     qsml_ctx* c = nullptr;
     if (qsml_init(static_cast<int32_t>(device_index), &c) == QSML_OK) {
         _ctx = c;
+        // The device's stream is the library's own (qsml_init creates it) and
+        // carries only library work, so independent calls may overlap on it;
+        // QSML_OVERLAP=0 turns that off.
+        const char* env = std::getenv("QSML_OVERLAP");
+        qsml_set_overlap(_ctx, env && env[0] == '0' ? 0 : 1);
     } else {
         LOG_WARN("device %u unavailable: %s", device_index, qsml_last_error(nullptr));
     }

@@ -370,6 +370,9 @@ qsml_status_t qsml_allreduce(qsml_group* g, int32_t local, void* buf, int64_t co
     if (!map_op(op, &o)) return set_error(C_, QSML_E_INVALID, "qsml_allreduce: unknown op");
     const ncclResult_t r =
         nccl().all_reduce(buf, buf, static_cast<size_t>(count), t, o, g->comms[local], C_->stream);
+    // NCCL's kernel is not one of the library's: the next library kernel on the
+    // stream waits for it at its start (no overlap across a collective)
+    end_window(C_->stream);
     if (r != ncclSuccess && r != ncclInProgress) {
         g->failed = true;
         return nccl_error(C_, r, "ncclAllReduce");
@@ -398,6 +401,7 @@ qsml_status_t qsml_allreduce_partials(qsml_group* g, int32_t local, int32_t op, 
     const ncclResult_t r = nccl().all_reduce(buf, buf, static_cast<size_t>(count), keys ? ncclUint32 : ncclFloat32,
                                              op == QSML_RED_MAX ? ncclMax : op == QSML_RED_MIN ? ncclMin : ncclSum,
                                              g->comms[local], C_->stream);
+    end_window(C_->stream);  // the next library kernel waits for the collective
     if (r != ncclSuccess && r != ncclInProgress) {
         g->failed = true;
         return nccl_error(C_, r, "ncclAllReduce (partials)");

@@ -186,13 +186,16 @@ static void test_views_and_gathers() {
     check("sum over a transposed view", st0.size() == 6 && st0[0] == 0 + 6 + 12 + 18 + 24 + 30 + 36 + 42);
     check("max of a sliced view", get(qsml::max(s))[0] == 47 && get(qsml::min(s))[0] == 7);
     check("mean of a transposed view", near(get(qsml::mean(T))[0], 23.5f, 1e-5f));
-    // with overlap on, independent reductions give the same results
+    // independent reductions give the same results with overlap on (the
+    // default) and off
+    for (bool ov : {true, false}) {
+        qsml::set_overlap(ov);
+        auto o1 = qsml::sum(X, 1), o2 = qsml::max(X, 0), o3 = qsml::sum(s, 1), o4 = qsml::sum(o1);
+        auto v1 = get(o1), v2 = get(o2), v3 = get(o3), v4 = get(o4);
+        check(ov ? "overlapped reductions" : "reductions without overlap",
+              v1[0] == 15 && v1[7] == 42 * 6 + 15 && v2[5] == 47 && v3[1] == 81 && v4[0] == 47.0f * 48.0f / 2.0f);
+    }
     qsml::set_overlap(true);
-    auto o1 = qsml::sum(X, 1), o2 = qsml::max(X, 0), o3 = qsml::sum(s, 1), o4 = qsml::sum(o1);
-    auto v1 = get(o1), v2 = get(o2), v3 = get(o3), v4 = get(o4);
-    qsml::set_overlap(false);
-    check("overlapped reductions", v1[0] == 15 && v1[7] == 42 * 6 + 15 && v2[5] == 47 && v3[1] == 81 &&
-                                       v4[0] == 47.0f * 48.0f / 2.0f);
     // argmax over an axis of a transpose reads it in place; of a slice, a copy
     auto idx = [](const qsml::TensorPtr& t) {
         vector<int32_t> v(t->numel());
