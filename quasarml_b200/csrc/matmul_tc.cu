@@ -230,6 +230,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// One 32-row x 128-byte box of C (32 fp32 or 64 fp16 columns; lane = row):
+// the row goes to a staging buffer in the 128-byte swizzle the C tensor map
+// expects, then lane 0 issues one TMA store of the box (clipped at the matrix
+// edges by the hardware) as its own bulk group.  Each epilogue warp alternates
+// between two buffers by the count of stores it has issued, so the store that
+// last read this buffer is the second newest group: wait_group.read 1 leaves
+// only the newest (the other buffer) reading.
+__device__ __forceinline__ void stage_and_store(uint32_t stage, const uint32_t (&words)[32], int lane,
+                                                const CUtensorMap* tmC, int col, int row0, int b) {
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t a = stage + lane * 128 + ((j ^ (lane & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(words[4 * j]), "r"(words[4 * j + 1]),
+                     "r"(words[4 * j + 2]), "r"(words[4 * j + 3])
+                     : "memory");
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+        asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                     ::"l"(reinterpret_cast<uint64_t>(tmC)), "r"(col), "r"(row0), "r"(b), "r"(stage)
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+}
+
 // Operand maps: tmA[0..NA), tmB[0..NB) (hi then lo for 3xTF32).
 struct OperandMaps {
     CUtensorMap a[2];
@@ -397,6 +425,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int quarter = warp & 3;
         int acc = 0;
         uint32_t acc_phase = 0;
+        uint32_t stores = 0;  // bulk stores this warp has issued: picks the staging buffer
         for (int t = blockIdx.x; t < total; t += gridDim.x) {
             // one lane waits, the warp follows its result (tcgen05.ld needs
             // the whole warp converged)
@@ -410,16 +439,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int row0 = mt * BM + quarter * 32;  // first of this warp's 32 rows
             const uint32_t taddr =
                 tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            // Each chunk is 32 rows x 128 bytes (32 fp32 or 64 fp16 columns):
-            // lane = row; the row goes to a staging buffer in the 128-byte
-            // swizzle the C tensor map expects, then one TMA store writes the
-            // box (clipped at the matrix edges by the hardware).
+            // Chunks of 32 rows x 128 bytes, up to the last column of the matrix.
             constexpr int CHUNK_COLS = OUT_F16 ? 64 : 32;
-            for (int c0 = 0; c0 < BN; c0 += CHUNK_COLS) {
-                // Past the last column nothing is stored; stopping here also
-                // keeps "one bulk group per buffer use" true, which the
-                // wait_group.read accounting below relies on.
-                if (nt * BN + c0 >= N) break;
+            const int cend = min(BN, N - nt * BN);
+            for (int c0 = 0; c0 < cend; c0 += CHUNK_COLS) {
                 uint32_t words[32];  // the row's 128 bytes
                 if (OUT_F16) {
                     uint32_t r0[32], r1[32];
@@ -435,32 +458,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 } else {
                     tmem_ld32(taddr + c0, words);
                 }
-                const int buf = (c0 / CHUNK_COLS) & 1;
-                const uint32_t stage = sC_stage + static_cast<uint32_t>((quarter * 2 + buf) * C_BOX_BYTES);
-                // the store issued from this buffer two chunks ago has read it
-                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-                __syncwarp();
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t a = stage + lane * 128 + ((j ^ (lane & 7)) << 4);
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(words[4 * j]),
-                                 "r"(words[4 * j + 1]), "r"(words[4 * j + 2]), "r"(words[4 * j + 3])
-                                 : "memory");
+                if (c0 + CHUNK_COLS >= cend) {
+                    // the warp's last columns of this accumulator are in
+                    // registers: release it before storing them
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(tempty_bar(acc));
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                const int col = nt * BN + c0;
-                if (lane == 0 && row0 < M && col < N) {
-                    asm volatile(
-                        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
-                        ::"l"(reinterpret_cast<uint64_t>(&tmC)), "r"(col), "r"(row0), "r"(b), "r"(stage)
-                        : "memory");
-                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                }
+                if (row0 >= M) continue;  // rows past the matrix: nothing to store
+                stage_and_store(sC_stage + static_cast<uint32_t>((quarter * 2 + (stores & 1u)) * C_BOX_BYTES), words,
+                                lane, &tmC, nt * BN + c0, row0, b);
+                ++stores;
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty_bar(acc));
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
@@ -696,6 +705,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int quarter = warp & 3;
         int acc = 0;
         uint32_t acc_phase = 0;
+        uint32_t stores = 0;  // bulk stores this warp has issued: picks the staging buffer
         const uint32_t tempty_leader0 = map_to_rank(tempty_bar(0), 0);
         const uint32_t tempty_leader1 = map_to_rank(tempty_bar(1), 0);
         for (int t = cid; t < total; t += nclusters) {
@@ -710,8 +720,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t taddr =
                 tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * P_BN);
             constexpr int CHUNK_COLS = OUT_F16 ? 64 : 32;
-            for (int c0 = 0; c0 < P_BN; c0 += CHUNK_COLS) {
-                if (nt * P_BN + c0 >= N) break;
+            const int cend = min(P_BN, N - nt * P_BN);  // the tile's columns inside the matrix
+            const uint32_t tempty_leader = acc == 0 ? tempty_leader0 : tempty_leader1;
+            for (int c0 = 0; c0 < cend; c0 += CHUNK_COLS) {
                 uint32_t words[32];
                 if (OUT_F16) {
                     uint32_t r0[32], r1[32];
@@ -727,31 +738,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 } else {
                     tmem_ld32(taddr + c0, words);
                 }
-                const int buf = (c0 / CHUNK_COLS) & 1;
-                const uint32_t stage = sC_stage + static_cast<uint32_t>((quarter * 2 + buf) * C_BOX_BYTES);
-                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-                __syncwarp();
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t a = stage + lane * 128 + ((j ^ (lane & 7)) << 4);
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(words[4 * j]),
-                                 "r"(words[4 * j + 1]), "r"(words[4 * j + 2]), "r"(words[4 * j + 3])
-                                 : "memory");
+                if (c0 + CHUNK_COLS >= cend) {
+                    // the warp's last columns of this accumulator are in
+                    // registers: release it before storing them
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_remote(tempty_leader);
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                const int col = nt * P_BN + c0;
-                if (lane == 0 && row0 < M && col < N) {
-                    asm volatile(
-                        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
-                        ::"l"(reinterpret_cast<uint64_t>(&tmC)), "r"(col), "r"(row0), "r"(b), "r"(stage)
-                        : "memory");
-                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                }
+                if (row0 >= M) continue;  // rows past the matrix: nothing to store
+                stage_and_store(sC_stage + static_cast<uint32_t>((quarter * 2 + (stores & 1u)) * C_BOX_BYTES), words,
+                                lane, &tmC, nt * P_BN + c0, row0, b);
+                ++stores;
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_remote(acc == 0 ? tempty_leader0 : tempty_leader1);
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;

@@ -96,3 +96,30 @@ def test_auto_choice(ctx, monkeypatch):
     small = dev(np.zeros((512, 64), np.float16)), dev(np.zeros((64, 512), np.float16))
     mm(ctx, small[0], d(small[1]), (512, 512), np.float32)
     assert ctx.last_kernel().startswith("k_gemm_tc<"), ctx.last_kernel()
+
+
+# Column counts whose last tile holds an odd number of 128-byte output chunks
+# (8 and 160 columns past the last full 256-column tile), with rows that end
+# inside a tile (900: whole 32-row warps of the last tile lie past M), over
+# enough tiles that every epilogue warp stores many tiles in a row.  Each
+# epilogue warp alternates two staging buffers under in-flight TMA stores;
+# this is the case where a buffer choice restarted per tile would overwrite a
+# buffer a store is still reading.  Repeated calls into NaN-filled outputs.
+@pytest.mark.parametrize("mkn", [(900, 520, 776), (1000, 264, 416)])
+@pytest.mark.parametrize("out", [np.float32, np.float16])
+def test_ragged_tiles_repeated(ctx, kernel, mkn, out):
+    M, K, N = mkn
+    E = 20
+    a = datagen.uniform(71, (E, M, K), -1, 1).astype(np.float16)
+    b = datagen.uniform(72, (E, K, N), -1, 1).astype(np.float16)
+    ta, tb = dev(a), dev(b)
+    ref = np.matmul(a.astype(np.float64), b.astype(np.float64))
+    scale = np.max(np.abs(ref))
+    for call in range(6):
+        c = empty((E, M, N), out)
+        c.fill_(float("nan"))
+        ctx.matmul(d(ta), d(tb), d(c), abi.MM_FP16_F32ACC)
+        got = host(c).astype(np.float64)
+        assert ctx.last_kernel().startswith("k_gemm_tc2<" if kernel == "1" else "k_gemm_tc<"), ctx.last_kernel()
+        err = np.max(np.abs(got - ref)) / scale  # NaN (an unwritten output) fails too
+        assert err <= (1e-5 if out == np.float32 else 1e-3), (kernel, call, err)
