@@ -9,8 +9,13 @@
 // per thread.  The next slice's global loads are in flight while this one is
 // computed (16-byte loads for interior tiles of binary32 operands), and each
 // thread's fragments for step kk+1 are read from shared memory while the 64
-// fmas of step kk issue.  Used for QSML_MM_FP32_FFMA and as the fp16-input
-// fallback for shapes the tensor-core kernel does not take.
+// fmas of step kk issue.  The fmas are issued two at a time as sm_100's packed
+// fma.rn.f32x2 (outputs (i, 2j) and (i, 2j+1) in one instruction, A's value in
+// both lanes): each lane is one IEEE fma rounded to nearest even, exactly what
+// fmaf does, so the per-output chain and its bits are unchanged while the
+// kernel, issue-bound with scalar fmas, issues a third fewer instructions.
+// Used for QSML_MM_FP32_FFMA and as the fp16-input fallback for shapes the
+// tensor-core kernel does not take.
 #include "qsml_internal.cuh"
 
 #include "matmul.cuh"
@@ -19,6 +24,21 @@ namespace qsml {
 namespace {
 
 constexpr int BM = 128, BN = 128, BK = 16, TM = 8, TN = 8;
+
+// Two fp32 values as one 64-bit operand of a packed instruction (lo = first).
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// d = a * b + d in each of the two lanes, each lane rounded once to nearest
+// even (per lane the operation of fmaf).
+__device__ __forceinline__ void fma2(uint64_t& d, uint64_t a, uint64_t b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(a), "l"(b));
+}
 
 __device__ __forceinline__ float ldf(const float* p) { return *p; }
 __device__ __forceinline__ float ldf(const __half* p) { return __half2float(*p); }
@@ -92,11 +112,24 @@ __global__ void __launch_bounds__(256, 2) k_matmul_simt(const TI* __restrict__ A
         b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
     };
 
-    float acc[TM][TN];
+    // acc2[i][j] holds outputs (i, 2j) and (i, 2j+1) of the thread's 8 x 8.
+    uint64_t acc2[TM][TN / 2];
 #pragma unroll
     for (int i = 0; i < TM; ++i)
 #pragma unroll
-        for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
+        for (int j = 0; j < TN / 2; ++j) acc2[i][j] = 0;  // both lanes +0.0f
+    // One k step: acc(i, c) = fma(a[i], b[c], acc(i, c)) for the 8 x 8 outputs.
+    auto step = [&](const float* a, const float* b) {
+        uint64_t b2[TN / 2];
+#pragma unroll
+        for (int j = 0; j < TN / 2; ++j) b2[j] = pack2(b[2 * j], b[2 * j + 1]);
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+            const uint64_t a2 = pack2(a[i], a[i]);
+#pragma unroll
+            for (int j = 0; j < TN / 2; ++j) fma2(acc2[i][j], a2, b2[j]);
+        }
+    };
 
     const int nslices = (K + BK - 1) / BK;
     load_slice(0);
@@ -112,25 +145,24 @@ __global__ void __launch_bounds__(256, 2) k_matmul_simt(const TI* __restrict__ A
 #pragma unroll
             for (int kk = 0; kk < BK; ++kk) {
                 if (kk + 1 < BK) load_frag(buf, kk + 1, fa[(kk + 1) & 1], fb[(kk + 1) & 1]);
-#pragma unroll
-                for (int i = 0; i < TM; ++i)
-#pragma unroll
-                    for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(fa[kk & 1][i], fb[kk & 1][j], acc[i][j]);
+                step(fa[kk & 1], fb[kk & 1]);
             }
         } else {
             // the last, partial slice: only the valid k (no fma with padding)
             for (int kk = 0; kk < kn; ++kk) {
                 float a[TM], b[TN];
                 load_frag(buf, kk, a, b);
-#pragma unroll
-                for (int i = 0; i < TM; ++i)
-#pragma unroll
-                    for (int j = 0; j < TN; ++j) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+                step(a, b);
             }
         }
         if (s + 1 < nslices) store_slice(buf ^ 1);
         __syncthreads();
     }
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN / 2; ++j) unpack2(acc2[i][j], acc[i][2 * j], acc[i][2 * j + 1]);
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
         const int r = row0 + ty * 4 + (i & 3) + (i >> 2) * 64;
