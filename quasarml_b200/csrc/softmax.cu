@@ -87,6 +87,88 @@ __device__ __forceinline__ float row_exp(float x, float m, float mk) {
     }
 }
 
+// Binary16 rows two columns at a time: row_exp and the __fadd_rn /
+// __fmul_rn around it issued as packed binary32 instructions
+// (fma/add/mul.rn.f32x2, each lane rounded to nearest even exactly like the
+// scalar instruction), so the results are bit-identical and the kernels,
+// issue-bound on these rows, issue fewer instructions.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// {2^(x0*log2(e) - mk), 2^(x1*log2(e) - mk)} for the pair h = {x0, x1};
+// l2e = {log2(e), log2(e)}, nmk = {-mk, -mk}.  Per lane row_exp<__half>.
+__device__ __forceinline__ uint64_t exp_pair(__half2 h, uint64_t l2e, uint64_t nmk) {
+    const float2 f = __half22float2(h);
+    uint64_t a;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(a) : "l"(f2pack(f.x, f.y)), "l"(l2e), "l"(nmk));
+    float a0, a1, r0, r1;
+    f2unpack(a, a0, a1);
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(a0));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(a1));
+    return f2pack(r0, r1);
+}
+
+// Sum pass of a binary16 row from shared memory: per-column partials (the
+// same per-column order as the scalar loop), combined in column order.
+__device__ __forceinline__ float half_exp_sum(const Pack<__half>* xs, int packs, int t, int stride, float mk) {
+    constexpr int PV = Pack<__half>::N;
+    const uint64_t l2e = f2pack(1.4426950408889634f, 1.4426950408889634f), nmk = f2pack(-mk, -mk);
+    uint64_t part2[PV / 2];
+#pragma unroll
+    for (int e = 0; e < PV / 2; ++e) part2[e] = 0;  // both lanes +0.0f
+#pragma unroll 4
+    for (int p = t; p < packs; p += stride) {
+        const Pack<__half> v = xs[p];
+        const __half2* h = reinterpret_cast<const __half2*>(v.v);
+#pragma unroll
+        for (int e = 0; e < PV / 2; ++e) part2[e] = add2(part2[e], exp_pair(h[e], l2e, nmk));
+    }
+    float part[PV];
+#pragma unroll
+    for (int e = 0; e < PV / 2; ++e) f2unpack(part2[e], part[2 * e], part[2 * e + 1]);
+    float s = part[0];
+#pragma unroll
+    for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
+    return s;
+}
+
+// Output pass of a binary16 row: y = exp(x - m) * inv, rounded to binary16.
+__device__ __forceinline__ void half_exp_out(const Pack<__half>* xs, Pack<__half>* yr, int packs, int t, int stride,
+                                             float mk, float inv) {
+    constexpr int PV = Pack<__half>::N;
+    const uint64_t l2e = f2pack(1.4426950408889634f, 1.4426950408889634f), nmk = f2pack(-mk, -mk);
+    const uint64_t inv2 = f2pack(inv, inv);
+#pragma unroll 2
+    for (int p = t; p < packs; p += stride) {
+        const Pack<__half> v = xs[p];
+        const __half2* h = reinterpret_cast<const __half2*>(v.v);
+        Pack<__half> o;
+        __half2* oh = reinterpret_cast<__half2*>(o.v);
+#pragma unroll
+        for (int e = 0; e < PV / 2; ++e) {
+            float z0, z1;
+            f2unpack(mul2(exp_pair(h[e], l2e, nmk), inv2), z0, z1);
+            oh[e] = __floats2half2_rn(z0, z1);
+        }
+        yr[p] = o;
+    }
+}
+
 // Binary32 values to a pack (binary16: two at a time).
 template <typename T>
 __device__ __forceinline__ Pack<T> to_pack(const float* z) {
@@ -232,33 +314,41 @@ __global__ void __launch_bounds__(rowpipe::kMaxWarps * 32, 1)
 #pragma unroll
             for (int k = 16; k >= 1; k >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, k));
             const float mk = __fmul_rn(m, 1.4426950408889634f);
-            float part[PV];
+            float s;
+            if constexpr (F32) {
+                float part[PV];
 #pragma unroll
-            for (int e = 0; e < PV; ++e) part[e] = 0.0f;
+                for (int e = 0; e < PV; ++e) part[e] = 0.0f;
 #pragma unroll 4
-            for (int p = lane; p < packs; p += 32) {
-                Pack<T> v = xs[p];
+                for (int p = lane; p < packs; p += 32) {
+                    Pack<T> v = xs[p];
 #pragma unroll
-                for (int e = 0; e < PV; ++e) {
-                    const float ex = row_exp<T>(to_f(v.v[e]), m, mk);
-                    part[e] = __fadd_rn(part[e], ex);
-                    if constexpr (F32) from_f(ex, &v.v[e]);
+                    for (int e = 0; e < PV; ++e) {
+                        const float ex = row_exp<T>(to_f(v.v[e]), m, mk);
+                        part[e] = __fadd_rn(part[e], ex);
+                        from_f(ex, &v.v[e]);
+                    }
+                    xs[p] = v;
                 }
-                if constexpr (F32) xs[p] = v;
-            }
-            float s = part[0];
+                s = part[0];
 #pragma unroll
-            for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
+                for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
+            } else {
+                s = half_exp_sum(xs, packs, lane, 32, mk);
+            }
             const float inv = __frcp_rn(rowpipe::warp_sum(s));
             Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
+            if constexpr (F32) {
 #pragma unroll 2
-            for (int p = lane; p < packs; p += 32) {
-                const Pack<T> v = xs[p];
-                float z[PV];
+                for (int p = lane; p < packs; p += 32) {
+                    const Pack<T> v = xs[p];
+                    float z[PV];
 #pragma unroll
-                for (int e = 0; e < PV; ++e)
-                    z[e] = __fmul_rn(F32 ? to_f(v.v[e]) : row_exp<T>(to_f(v.v[e]), m, mk), inv);
-                yr[p] = to_pack<T>(z);
+                    for (int e = 0; e < PV; ++e) z[e] = __fmul_rn(to_f(v.v[e]), inv);
+                    yr[p] = to_pack<T>(z);
+                }
+            } else {
+                half_exp_out(xs, yr, packs, lane, 32, mk, inv);
             }
         });
     if (!ok && lane == 0) atomicExch(status, QSML_E_TIMEOUT);
@@ -287,33 +377,41 @@ __global__ void __launch_bounds__(TH) k_softmax_wide(const T* __restrict__ x, T*
             Pack<T>* xs = reinterpret_cast<Pack<T>*>(buf);
             const float m = rowpipe::cta_combine<true>(pack_max<T>(xs, packs, t, th), s_max);
             const float mk = __fmul_rn(m, 1.4426950408889634f);
-            float part[PV];
+            float s;
+            if constexpr (F32) {
+                float part[PV];
 #pragma unroll
-            for (int e = 0; e < PV; ++e) part[e] = 0.0f;
+                for (int e = 0; e < PV; ++e) part[e] = 0.0f;
 #pragma unroll 2
-            for (int p = t; p < packs; p += th) {
-                Pack<T> v = xs[p];
+                for (int p = t; p < packs; p += th) {
+                    Pack<T> v = xs[p];
 #pragma unroll
-                for (int e = 0; e < PV; ++e) {
-                    const float ex = row_exp<T>(to_f(v.v[e]), m, mk);
-                    part[e] = __fadd_rn(part[e], ex);
-                    if constexpr (F32) from_f(ex, &v.v[e]);
+                    for (int e = 0; e < PV; ++e) {
+                        const float ex = row_exp<T>(to_f(v.v[e]), m, mk);
+                        part[e] = __fadd_rn(part[e], ex);
+                        from_f(ex, &v.v[e]);
+                    }
+                    xs[p] = v;
                 }
-                if constexpr (F32) xs[p] = v;
-            }
-            float s = part[0];
+                s = part[0];
 #pragma unroll
-            for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
+                for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
+            } else {
+                s = half_exp_sum(xs, packs, t, th, mk);
+            }
             const float inv = __frcp_rn(rowpipe::cta_combine<false>(s, s_sum));
             Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
+            if constexpr (F32) {
 #pragma unroll 2
-            for (int p = t; p < packs; p += th) {
-                const Pack<T> v = xs[p];
-                float z[PV];
+                for (int p = t; p < packs; p += th) {
+                    const Pack<T> v = xs[p];
+                    float z[PV];
 #pragma unroll
-                for (int e = 0; e < PV; ++e)
-                    z[e] = __fmul_rn(F32 ? to_f(v.v[e]) : row_exp<T>(to_f(v.v[e]), m, mk), inv);
-                yr[p] = to_pack<T>(z);
+                    for (int e = 0; e < PV; ++e) z[e] = __fmul_rn(to_f(v.v[e]), inv);
+                    yr[p] = to_pack<T>(z);
+                }
+            } else {
+                half_exp_out(xs, yr, packs, t, th, mk, inv);
             }
         });
     if (!ok && t == 0) atomicExch(status, QSML_E_TIMEOUT);
