@@ -1338,6 +1338,26 @@ EXTRAS = (("elementwise_chain", lambda c, d, s: ChainWorkload(c, d, scale=s), 10
           ("batched_matmul_f32_3xtf32", lambda c, d, s: MatmulWorkload(c, d, "f32", True, scale=s), 5))
 
 
+def fp32_ceiling(w, tf_burst: float):
+    """(TFLOP/s, what) for the binary32 matmul paths, whose ceiling is not the
+    fp16 tensor rate: the FFMA pipe (SMs x 128 lanes x 2 flops x the maximum
+    SM clock) for the CUDA-core kernel, one sixth of the fp16 rate for 3xTF32
+    (tf32 runs at half the fp16 rate and each product is three MMAs)."""
+    import torch
+    from quasarml_b200 import abi
+    prec = getattr(w, "prec", None)
+    if prec == abi.MM_FP32_FFMA:
+        mhz = 1965.0
+        p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+        if os.path.exists(p):
+            mhz = float(json.load(open(p)).get("sm_max_mhz", mhz))
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        return (round(sms * 128 * 2 * mhz * 1e6 / 1e12, 1), f"FFMA pipe: {sms} SMs x 128 x 2 x {mhz:.0f} MHz")
+    if prec == abi.MM_FP32_3XTF32:
+        return (round(tf_burst / 6.0, 1), "3xTF32: measured fp16 tensor rate / 2 (tf32) / 3 (products)")
+    return None
+
+
 def run_extras(ctx, dist: Dist, stream, hbm: float, tf_burst: float) -> dict:
     """The other configurations, each row-sharded over the ranks: weak
     scaling at every N (each rank the configuration's size), and at N>1 also
@@ -1398,6 +1418,10 @@ def run_extras(ctx, dist: Dist, stream, hbm: float, tf_burst: float) -> dict:
                             "per_gpu": round(v / dist.world, 2), "unit": w.unit,
                             "frac_of_peak": round(v / dist.world / peak, 4), "peak": peak,
                             "ms_per_step": round(ms_x / st, 3), "launches_per_step": l_x // st}
+            ceiling = fp32_ceiling(w, tf_burst)
+            if ceiling:
+                extras[name]["ceiling"] = ceiling
+                extras[name]["frac_of_ceiling"] = round(v / dist.world / ceiling[0], 4)
             if alone:
                 extras[name]["one_gpu_same_run"] = round(alone, 2)
                 extras[name]["efficiency_vs_one_gpu"] = round(v / dist.world / alone, 4)
