@@ -52,7 +52,10 @@ __global__ void __launch_bounds__(256, 2) k_matmul_simt(const TI* __restrict__ A
     __shared__ __align__(16) float As[2][BK][BM];
     __shared__ __align__(16) float Bs[2][BK][BN];
     const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;
+    // Threads as a 16 x 16 grid (tx, ty); each warp is a 4 (ty) x 8 (tx) block of
+    // it, so a warp's fragment reads below are 64 bytes of A and 128 bytes of B:
+    // one shared-memory wavefront each.
+    const int tx = 8 * ((tid >> 5) & 1) + (tid & 7), ty = 4 * (tid >> 6) + ((tid >> 3) & 3);
     const int bz = blockIdx.z;
     A += bz * sA;
     B += bz * sB;
