@@ -169,6 +169,62 @@ __device__ __forceinline__ void half_exp_out(const Pack<__half>* xs, Pack<__half
     }
 }
 
+// Binary16 rows of which each thread holds at most KP packs: the sum pass
+// keeps its exponentials in registers (ex), and the output pass multiplies
+// those instead of reading the row again and recomputing them -- the same
+// values, so the same bits, with one pass over shared memory less.
+template <int KP>
+__device__ __forceinline__ float half_exp_sum_keep(const Pack<__half>* xs, int packs, int t, int stride, float mk,
+                                                   uint64_t (&ex)[KP][Pack<__half>::N / 2]) {
+    constexpr int PV = Pack<__half>::N;
+    const uint64_t l2e = f2pack(1.4426950408889634f, 1.4426950408889634f), nmk = f2pack(-mk, -mk);
+    uint64_t part2[PV / 2];
+#pragma unroll
+    for (int e = 0; e < PV / 2; ++e) part2[e] = 0;  // both lanes +0.0f
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+        const int p = t + k * stride;
+        if (p < packs) {
+            const Pack<__half> v = xs[p];
+            const __half2* h = reinterpret_cast<const __half2*>(v.v);
+#pragma unroll
+            for (int e = 0; e < PV / 2; ++e) {
+                ex[k][e] = exp_pair(h[e], l2e, nmk);
+                part2[e] = add2(part2[e], ex[k][e]);
+            }
+        }
+    }
+    float part[PV];
+#pragma unroll
+    for (int e = 0; e < PV / 2; ++e) f2unpack(part2[e], part[2 * e], part[2 * e + 1]);
+    float s = part[0];
+#pragma unroll
+    for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
+    return s;
+}
+
+template <int KP>
+__device__ __forceinline__ void half_exp_out_keep(Pack<__half>* yr, int packs, int t, int stride, float inv,
+                                                  const uint64_t (&ex)[KP][Pack<__half>::N / 2]) {
+    constexpr int PV = Pack<__half>::N;
+    const uint64_t inv2 = f2pack(inv, inv);
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+        const int p = t + k * stride;
+        if (p < packs) {
+            Pack<__half> o;
+            __half2* oh = reinterpret_cast<__half2*>(o.v);
+#pragma unroll
+            for (int e = 0; e < PV / 2; ++e) {
+                float z0, z1;
+                f2unpack(mul2(ex[k][e], inv2), z0, z1);
+                oh[e] = __floats2half2_rn(z0, z1);
+            }
+            yr[p] = o;
+        }
+    }
+}
+
 // Binary32 values to a pack (binary16: two at a time).
 template <typename T>
 __device__ __forceinline__ Pack<T> to_pack(const float* z) {
@@ -377,6 +433,10 @@ __global__ void __launch_bounds__(TH) k_softmax_wide(const T* __restrict__ x, T*
             Pack<T>* xs = reinterpret_cast<Pack<T>*>(buf);
             const float m = rowpipe::cta_combine<true>(pack_max<T>(xs, packs, t, th), s_max);
             const float mk = __fmul_rn(m, 1.4426950408889634f);
+            // binary16 rows of at most KP packs per thread keep their exponentials
+            constexpr int KP = 4;
+            uint64_t ex[KP][Pack<__half>::N / 2];
+            const bool keep = !F32 && packs <= KP * th;
             float s;
             if constexpr (F32) {
                 float part[PV];
@@ -397,7 +457,7 @@ __global__ void __launch_bounds__(TH) k_softmax_wide(const T* __restrict__ x, T*
 #pragma unroll
                 for (int e = 1; e < PV; ++e) s = __fadd_rn(s, part[e]);
             } else {
-                s = half_exp_sum(xs, packs, t, th, mk);
+                s = keep ? half_exp_sum_keep<KP>(xs, packs, t, th, mk, ex) : half_exp_sum(xs, packs, t, th, mk);
             }
             const float inv = __frcp_rn(rowpipe::cta_combine<false>(s, s_sum));
             Pack<T>* yr = reinterpret_cast<Pack<T>*>(y + row * cols);
@@ -410,6 +470,8 @@ __global__ void __launch_bounds__(TH) k_softmax_wide(const T* __restrict__ x, T*
                     for (int e = 0; e < PV; ++e) z[e] = __fmul_rn(to_f(v.v[e]), inv);
                     yr[p] = to_pack<T>(z);
                 }
+            } else if (keep) {
+                half_exp_out_keep<KP>(yr, packs, t, th, inv, ex);
             } else {
                 half_exp_out(xs, yr, packs, t, th, mk, inv);
             }
