@@ -16,7 +16,8 @@
 //                                      32-byte sectors, so DRAM reads are the
 //                                      sector footprint and no more;
 //   * large inner stride, another dim with a smaller one (a transpose)
-//                                   -> k_gather_tiled: a 64x64 tile staged in
+//                                   -> k_gather_tiled: a 128 (small-stride
+//                                      dim) x 32 (output dim) tile staged in
 //                                      shared memory, read along the
 //                                      small-stride dim and written along the
 //                                      contiguous output dim;
@@ -118,13 +119,16 @@ __global__ void __launch_bounds__(kGT) k_gather_small(const T* __restrict__ src,
     pdl_end(defer);
 }
 
-// Transpose-like: tile over (P = small-stride dim, Q = innermost dim).
-constexpr int kTile = 64;
+// Transpose-like: tile over (P = small-stride dim, Q = innermost dim).  128
+// along P: each of a tile's 32 source lines is read over 128 elements (2 KiB
+// of X.T[::4, :]'s int32 rows), which measured 5 % faster on that gather than
+// 64 x 64 tiles (32 x 32: 8 % slower).
+constexpr int kTileP = 128, kTileQ = 32;
 template <typename T>
 __global__ void __launch_bounds__(256) k_gather_tiled(const T* __restrict__ src, T* __restrict__ dst, GPlan p,
                                                       int dP, int64_t ptiles, int64_t qtiles, int defer) {
     pdl_start(defer);
-    __shared__ T tile[kTile][kTile + 1];
+    __shared__ T tile[kTileQ][kTileP + 1];
     const int tx = threadIdx.x, ty = threadIdx.y;  // (32, 8)
     const int dQ = p.nd - 1;
     int64_t bid = blockIdx.x;
@@ -148,13 +152,13 @@ __global__ void __launch_bounds__(256) k_gather_tiled(const T* __restrict__ src,
         ooff += c * ostr[d];
     }
     const int64_t P = p.shape[dP], Q = p.shape[dQ];
-    const int64_t p0 = pt * kTile, q0 = qt * kTile;
+    const int64_t p0 = pt * kTileP, q0 = qt * kTileQ;
     const int64_t sP = p.st[dP], sQ = p.st[dQ];
     // Load: lanes walk P (the small source stride).
 #pragma unroll
-    for (int qi = ty; qi < kTile; qi += 8) {
+    for (int qi = ty; qi < kTileQ; qi += 8) {
 #pragma unroll
-        for (int ph = 0; ph < kTile; ph += 32) {
+        for (int ph = 0; ph < kTileP; ph += 32) {
             int pi = tx + ph;
             int64_t pp = p0 + pi, qq = q0 + qi;
             if (pp < P && qq < Q) tile[qi][pi] = src[soff + pp * sP + qq * sQ];
@@ -164,9 +168,9 @@ __global__ void __launch_bounds__(256) k_gather_tiled(const T* __restrict__ src,
     // Store: lanes walk Q (contiguous in the output).
     const int64_t oP = ostr[dP];
 #pragma unroll
-    for (int pi = ty; pi < kTile; pi += 8) {
+    for (int pi = ty; pi < kTileP; pi += 8) {
 #pragma unroll
-        for (int qh = 0; qh < kTile; qh += 32) {
+        for (int qh = 0; qh < kTileQ; qh += 32) {
             int qi = tx + qh;
             int64_t pp = p0 + pi, qq = q0 + qi;
             if (pp < P && qq < Q) dst[ooff + pp * oP + qq] = tile[qi][pi];
@@ -271,7 +275,7 @@ qsml_status_t gather_typed(Context* ctx, const GPlan& p, const void* srcv, void*
         if (p.shape[d] >= 8 && ad < as && (dP < 0 || ad < (p.st[dP] < 0 ? -p.st[dP] : p.st[dP]))) dP = d;
     }
     if (as > 32 && dP >= 0) {
-        int64_t ptiles = (p.shape[dP] + kTile - 1) / kTile, qtiles = (C + kTile - 1) / kTile;
+        int64_t ptiles = (p.shape[dP] + kTileP - 1) / kTileP, qtiles = (C + kTileQ - 1) / kTileQ;
         int64_t batch = n / (p.shape[dP] * C);
         int64_t blocks = ptiles * qtiles * batch;
         if (blocks > INT32_MAX) return set_error(ctx, QSML_E_UNSUPPORTED, "gather too large");
